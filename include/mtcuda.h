@@ -1,0 +1,259 @@
+/*
+ * mtcuda.h — C ABI of the B200 (sm_100a) CUDA backend for MiniTensor.
+ *
+ * Every entry point here replaces one CPU kernel (a `KernelFn` registered under
+ * `KernelKey{PrimitiveId, DeviceType}`, src/tensor/dispatch/kernel_registry.hpp:15-16)
+ * or one `DeviceRuntime` method (src/tensor/backend/device_runtime.hpp:13-29) of the
+ * MiniTensor reference.  The C++ adapter that registers these under
+ * `DeviceType::Cuda` lives in minitensor_cpp_b200/host/; any other host language
+ * can bind the same symbols (ctypes, cgo, JNI) because the signatures carry only
+ * plain pointers, integers and the POD descriptor below.
+ *
+ * Conventions
+ *  - A tensor operand is an `mtc_desc`: base pointer of the device buffer, plus
+ *    shape, strides and offset counted in ELEMENTS, exactly like the reference
+ *    `Layout{strides, offset}` (src/tensor/storage/layout.hpp:18-42).  Strides may be
+ *    zero (broadcast views) or negative (reversed slices); offsets are >= 0.
+ *  - `capacity` is the buffer size in elements.  Every entry point checks on the
+ *    host that every reachable element of every view lies inside [0, capacity),
+ *    like `Materialization::validate` (src/tensor/storage/materialization.cpp:77-129),
+ *    and returns MTC_ERR_OUT_OF_RANGE otherwise; no kernel is launched then.
+ *  - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default stream)
+ *    and returns without synchronising.  Data-dependent failures that can only be
+ *    seen on the device (a gather index outside its axis) are recorded in a
+ *    per-device error word and reported by mtc_check_device_errors().
+ *  - Return value: MTC_OK or one of the MTC_ERR_* codes; mtc_last_error() gives a
+ *    thread-local message.  No C++ exception crosses this boundary.  The codes map
+ *    one-to-one onto the reference's exception types (invalid_argument,
+ *    out_of_range, runtime_error, logic_error, overflow_error).
+ */
+#ifndef MTCUDA_H
+#define MTCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MTC_MAX_RANK 8
+#define MTC_MAX_FUSED_OPERANDS 12
+#define MTC_MAX_FUSED_OUTPUTS 4
+#define MTC_MAX_FUSED_INSTRUCTIONS 96
+#define MTC_MAX_CONCAT_INPUTS 64
+
+/* Status codes (reference exception type in brackets). */
+enum {
+    MTC_OK = 0,
+    MTC_ERR_INVALID_ARGUMENT = 1, /* std::invalid_argument */
+    MTC_ERR_OUT_OF_RANGE = 2,     /* std::out_of_range      */
+    MTC_ERR_RUNTIME = 3,          /* std::runtime_error (CUDA / NCCL failure) */
+    MTC_ERR_LOGIC = 4,            /* std::logic_error       */
+    MTC_ERR_OVERFLOW = 5,         /* std::overflow_error    */
+    MTC_ERR_UNSUPPORTED = 6       /* no kernel for this case (std::runtime_error) */
+};
+
+/* Element types: the numbering of minitensor::DType (include/minitensor/types.hpp:55-59). */
+enum { MTC_FLOAT32 = 0, MTC_INT64 = 1 };
+
+/* Operation codes.  Codes of reference primitives equal their PrimitiveId value
+ * (src/tensor/primitives/<family>/<op>.hpp: `static constexpr PrimitiveId ID{...}`);
+ * codes >= 0x..80 within a family are additions of this backend. */
+enum {
+    /* unary elementwise, src/tensor/backend/cpu/kernels/elementwise/kernels.cpp:58-125 */
+    MTC_OP_ABS = 0x0101,
+    MTC_OP_SIGN = 0x0102,
+    MTC_OP_NEGATE = 0x0103,
+    MTC_OP_EXP = 0x0104,
+    MTC_OP_LOG = 0x0105,
+    MTC_OP_SQRT = 0x0106,
+    MTC_OP_TANH = 0x0107,
+    MTC_OP_SIGMOID = 0x0108,
+    MTC_OP_RELU = 0x0180, /* new: max(x, 0), NaN propagates */
+    /* binary elementwise, elementwise/kernels.cpp:127-167 */
+    MTC_OP_ADD = 0x0110,
+    MTC_OP_SUBTRACT = 0x0111,
+    MTC_OP_MULTIPLY = 0x0112,
+    MTC_OP_DIVIDE = 0x0113,
+    MTC_OP_LOGADDEXP = 0x0114,
+    /* fused-program pseudo ops */
+    MTC_OP_CONST = 0x01F0, /* dst = imm */
+    /* reductions, src/tensor/backend/cpu/kernels/reduction/kernels.cpp:22-42 */
+    MTC_OP_SUM = 0x0301,
+    MTC_OP_LOGSUMEXP = 0x0302,
+    MTC_OP_MAX = 0x0380,    /* new: NaN propagates, empty -> -inf */
+    MTC_OP_ARGMAX = 0x0381  /* new: Int64 output, first maximum; a NaN counts as the maximum */
+};
+
+/* Strided view of a device buffer (reference TensorView, src/tensor/dispatch/tensor_view.hpp:15-45). */
+typedef struct mtc_desc {
+    void *data;       /* base address of the buffer (element 0 of the storage) */
+    int64_t offset;   /* Layout::offset(), in elements, >= 0 */
+    int64_t capacity; /* buffer size in elements */
+    int32_t dtype;    /* MTC_FLOAT32 / MTC_INT64 */
+    int32_t rank;     /* 0..MTC_MAX_RANK */
+    int64_t shape[MTC_MAX_RANK];
+    int64_t strides[MTC_MAX_RANK]; /* Layout::strides(), in elements */
+} mtc_desc;
+
+/* One instruction of a fused elementwise program (see mtc_fused). */
+typedef struct mtc_instr {
+    int32_t op;  /* MTC_OP_* unary/binary code, or MTC_OP_CONST */
+    int16_t dst; /* destination register */
+    int16_t a;   /* first source register */
+    int16_t b;   /* second source register (binary ops) */
+    int16_t pad;
+    float imm;   /* MTC_OP_CONST value */
+} mtc_instr;
+
+/* ---------------------------------------------------------------- library -- */
+
+/* Thread-local text of the last failure on this thread ("" when none). */
+const char *mtc_last_error(void);
+/* Version string of the library and the architecture it was compiled for. */
+const char *mtc_version(void);
+/* Number of visible CUDA devices (0 when no driver/GPU is present). */
+int mtc_device_count(int *count);
+/* Streaming-multiprocessor count of `device` (grid sizing; 148 on B200). */
+int mtc_device_sm_count(int device, int *count);
+/* Makes `device` current for the calling thread (kernels launch on the current device). */
+int mtc_set_device(int device);
+
+/* ------------------------------------------------------ DeviceRuntime (A2) --
+ * Replaces CpuRuntime/CpuBuffer (src/tensor/backend/cpu/cpu_runtime.cpp:31-87,
+ * cpu_buffer.cpp:13-32).  Memory comes from a per-device stream-ordered pool
+ * (cudaMallocAsync with an unbounded release threshold), so freed blocks are
+ * reused by later work on the same stream without a device synchronisation. */
+
+/* Per-device work stream created on first use (non-blocking w.r.t. the legacy stream). */
+int mtc_device_stream(int device, void **stream);
+/* Stream-ordered allocation of `bytes` on `device`; *ptr = NULL for 0 bytes
+ * (the reference hands out a valid empty buffer, runtime_test.cpp:85-94). */
+int mtc_alloc(int device, size_t bytes, void *stream, void **ptr);
+/* Stream-ordered release of a block from mtc_alloc. */
+int mtc_free(int device, void *ptr, void *stream);
+/* Host -> device copy, ordered on `stream`; `src` must stay valid until the
+ * stream reaches the copy (pageable sources are staged by the driver before return). */
+int mtc_copy_from_host(int device, void *dst, const void *src, size_t bytes, void *stream);
+/* Device -> host copy; returns after the data is in `dst` (synchronises `stream`). */
+int mtc_copy_to_host(int device, void *dst, const void *src, size_t bytes, void *stream);
+/* Wait for all work queued on `stream`. */
+int mtc_stream_synchronize(void *stream);
+/* Bytes reserved by / in use in the device pool. */
+int mtc_pool_stats(int device, uint64_t *reserved_bytes, uint64_t *used_bytes);
+/* Return cached-but-unused pool memory to the driver. */
+int mtc_pool_trim(int device);
+
+/* Device-side error word: synchronises `stream`, then returns MTC_ERR_OUT_OF_RANGE
+ * (and the offending index in *detail) if a gather/scatter kernel met an index
+ * outside its axis since the last check, MTC_OK otherwise; the word is cleared. */
+int mtc_check_device_errors(int device, void *stream, int64_t *detail);
+
+/* --------------------------------------------------- elementwise (A4, A5) -- */
+
+/* out = f(in), Negate/Exp/Log/Sqrt/Tanh/Abs/Sign/Sigmoid (+ReLU);
+ * replaces unary_elementwise (elementwise/loops.hpp:19-67).  Float32 only;
+ * in.shape == out.shape. */
+int mtc_unary(int32_t op, const mtc_desc *in, const mtc_desc *out, void *stream);
+
+/* out = g(lhs, rhs) with right-aligned broadcasting of lhs/rhs to out.shape,
+ * Add/Subtract/Multiply/Divide/LogAddExp; replaces binary_elementwise
+ * (elementwise/loops.hpp:69-153).  Float32 only. */
+int mtc_binary(int32_t op, const mtc_desc *lhs, const mtc_desc *rhs, const mtc_desc *out, void *stream);
+
+/* Fused elementwise program over one index space (the shape of every output).
+ * Registers 0..n_inputs-1 hold the inputs (each broadcast to the output shape);
+ * instruction k writes register `dst`; outputs[j] receives register out_regs[j].
+ * Every instruction rounds to float32 exactly as the unfused op does (no FMA
+ * contraction across instructions), so a fused chain equals the chain of single
+ * kernels bit for bit.  The kernel for a new program is generated and compiled
+ * for sm_100a on first use and cached for the life of the process. */
+int mtc_fused(const mtc_instr *program, int32_t n_instr, const mtc_desc *inputs, int32_t n_inputs,
+              const int32_t *out_regs, const mtc_desc *outputs, int32_t n_outputs, void *stream);
+
+/* ---------------------------------------------------------- copies (A7, A13) -- */
+
+/* dst[i] = src[i] over src.shape; dst is any same-shape view (Contiguous 0x0201 and
+ * Reshape 0x0202, copy/loops.hpp:22-88).  Float32 and Int64. */
+int mtc_copy(const mtc_desc *src, const mtc_desc *dst, void *stream);
+
+/* out = concatenate(inputs, axis) (Concatenate 0x0205, copy/loops.hpp:90-127). */
+int mtc_concat(const mtc_desc *inputs, int32_t n_inputs, int64_t axis, const mtc_desc *out, void *stream);
+
+/* out = 0, then the view `dst_view` of out's buffer receives `in`
+ * (BasicIndexScatter 0x0207, copy/loops.hpp:129-153). */
+int mtc_index_scatter(const mtc_desc *in, const mtc_desc *dst_view, const mtc_desc *out, void *stream);
+
+/* --------------------------------------------------- Int64 indexing (A11, A12) -- */
+
+/* take-along-axis: out[..i..] = src[..idx[..i..]..] (Gather 0x0208, copy/loops.hpp:155-220).
+ * idx.shape == out.shape, same rank as src.  An index outside [0, src.shape[axis])
+ * writes nothing for that element and sets the device error word. */
+int mtc_gather(const mtc_desc *src, const mtc_desc *idx, int64_t axis, const mtc_desc *out, void *stream);
+
+/* out = 0; out[..idx[..i..]..] += upd[..i..] (GatherScatterAdd 0x0209,
+ * copy/loops.hpp:222-303).  Duplicate indices accumulate with float32 atomics:
+ * bit-exact against the sequential CPU loop whenever the partial sums are exact
+ * (integer-valued updates below 2^24), otherwise equal up to summation order. */
+int mtc_gather_scatter_add(const mtc_desc *upd, const mtc_desc *idx, int64_t axis, const mtc_desc *out,
+                           void *stream);
+
+/* -------------------------------------------------------- reductions (A8, A9) -- */
+
+/* Reduce `in` over `axes` (normalised, distinct).  `out` is contiguous and holds the
+ * kept dimensions in order (keep_dim only changes out.shape).  SUM (0x0301,
+ * reduce_values, reduction/loops.hpp:21-57), LOGSUMEXP (0x0302, reduce_logsumexp,
+ * reduction/loops.hpp:59-136), MAX, ARGMAX (one axis, Int64 out). */
+int mtc_reduce(int32_t op, const mtc_desc *in, const int64_t *axes, int32_t n_axes, const mtc_desc *out,
+               void *stream);
+
+/* out = in - logsumexp(in, {axis}, keep_dim=true), one pass over HBM per row
+ * (the composite of reduce_logsumexp and Subtract). */
+int mtc_log_softmax(const mtc_desc *in, int64_t axis, const mtc_desc *out, void *stream);
+
+/* ---------------------------------------------------------------- GEMM (A10) -- */
+
+enum {
+    MTC_GEMM_AUTO = 0,     /* tensor-core 3xTF32 where the shape suits it, else SIMT */
+    MTC_GEMM_SIMT = 1,     /* exact float32 FFMA kernel, any strides */
+    MTC_GEMM_3XTF32 = 2    /* tcgen05/TMEM kernel, split-float32 (hi+lo) operands */
+};
+
+/* matmul with the reference's full semantics (Matmul 0x0401, matmul_dispatch,
+ * linalg/loops.hpp:288-324; shape rules src/tensor/primitives/linalg/matmul.cpp:18-52):
+ * 1-D x 1-D dot, matrix x vector, vector x matrix, batched matrices with broadcast
+ * batch dimensions and arbitrary strides.  Float32 in, float32 accumulate. */
+int mtc_matmul(const mtc_desc *lhs, const mtc_desc *rhs, const mtc_desc *out, int32_t algo, void *stream);
+
+/* --------------------------------------------------------- creation (A14) -- */
+
+/* out[...] = value; `value` points at 4 bytes (Float32) or 8 bytes (Int64)
+ * (Full 0x0001, creation/loops.hpp:21-37). */
+int mtc_fill(const mtc_desc *out, const void *value, void *stream);
+
+/* Philox-4x32-10 counter RNG keyed by RandomKey words {key0, key1}
+ * (src/tensor/backend/cpu/detail/random_engine.cpp:14-64).  Uniform
+ * (creation/loops.hpp:39-86) is bit-exact; Normal (creation/loops.hpp:88-141)
+ * uses double Box-Muller like the CPU and matches it to float32 rounding. */
+int mtc_uniform(const mtc_desc *out, float low, float high, uint64_t key0, uint64_t key1, void *stream);
+int mtc_normal(const mtc_desc *out, float mean, float std_dev, uint64_t key0, uint64_t key1, void *stream);
+
+/* -------------------------------------------------- data parallel (config 5) --
+ * Gradient all-reduce between the ranks of a data-parallel job, one process per
+ * GPU; NCCL over NVLink/NVSwitch.  No reference counterpart: the reference is
+ * single-process (it has no collective at all). */
+
+/* Writes NCCL_UNIQUE_ID_BYTES (128) bytes of a fresh communicator id into `id`. */
+int mtc_comm_unique_id(void *id, size_t id_bytes);
+int mtc_comm_init(int device, int rank, int n_ranks, const void *id, size_t id_bytes, void **comm);
+/* In-place sum all-reduce of `n` float32 buffers, then scale by `scale`, all on `stream`. */
+int mtc_comm_allreduce_f32(void *comm, void *const *buffers, const size_t *counts, int32_t n, float scale,
+                           void *stream);
+int mtc_comm_destroy(void *comm);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MTCUDA_H */

@@ -1,0 +1,530 @@
+// Data movement kernels: strided copy (Contiguous/Reshape), concatenation,
+// basic-index scatter, Int64 gather and gather-scatter-add, fill.
+// Reference: src/tensor/backend/cpu/kernels/copy/loops.hpp:22-303 and
+// creation/loops.hpp:21-37.
+#include <cstring>
+
+#include "common.cuh"
+
+namespace mtc {
+
+__device__ unsigned long long g_device_error[2];
+
+__device__ __forceinline__ void record_device_error(int code, long long detail) {
+    if (atomicCAS(&g_device_error[0], 0ull, static_cast<unsigned long long>(code)) == 0ull) {
+        atomicExch(&g_device_error[1], static_cast<unsigned long long>(detail));
+    }
+}
+
+namespace {
+
+constexpr int kOps = 3;
+
+struct MoveArgs {
+    long long numel;
+    int rank;
+    unsigned int shape[MTC_MAX_RANK];
+    FastDiv div[MTC_MAX_RANK];
+    char *ptr[kOps];  // 0 = destination, 1 = source / updates, 2 = indices
+    long long off[kOps];
+    long long str[kOps][MTC_MAX_RANK];
+    long long axis_extent;  // gather / scatter: extent of the indexed axis
+    long long axis_stride;  // gather / scatter: stride of the indexed axis in the indexed tensor
+};
+
+// Coordinates of linear index i over the simplified shape -> per-operand offsets.
+template <int NOPS>
+__device__ __forceinline__ void offsets_of(const MoveArgs &a, unsigned int i, long long (&o)[NOPS]) {
+#pragma unroll
+    for (int k = 0; k < NOPS; ++k) o[k] = a.off[k];
+    unsigned int rem = i;
+#pragma unroll
+    for (int d = MTC_MAX_RANK - 1; d >= 1; --d) {
+        if (d < a.rank) {
+            const unsigned int q = fastdiv(rem, a.div[d]);
+            const long long c = static_cast<long long>(rem - q * a.shape[d]);
+            rem = q;
+#pragma unroll
+            for (int k = 0; k < NOPS; ++k) o[k] += c * a.str[k][d];
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < NOPS; ++k) o[k] += static_cast<long long>(rem) * a.str[k][0];
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_copy_strided(const MoveArgs a) {
+    const unsigned int n = static_cast<unsigned int>(a.numel);
+    for (unsigned int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        long long o[2];
+        offsets_of<2>(a, i, o);
+        reinterpret_cast<T *>(a.ptr[0])[o[0]] = reinterpret_cast<const T *>(a.ptr[1])[o[1]];
+    }
+}
+
+// Transposing copy through a 64x64 shared-memory tile: the destination is
+// contiguous along the last axis, the source along the second-to-last one.
+template <typename T>
+__global__ void __launch_bounds__(256) k_copy_tiled(const MoveArgs a) {
+    constexpr int TT = 64;
+    __shared__ T tile[TT][TT + 1];
+    const int r = a.rank;
+    const unsigned int rows = a.shape[r - 2], cols = a.shape[r - 1];
+    const unsigned int r0 = blockIdx.y * TT, c0 = blockIdx.x * TT;
+    long long ob = a.off[0], ib = a.off[1];
+    unsigned int rem = blockIdx.z;
+    for (int d = r - 3; d >= 0; --d) {
+        const unsigned int c = rem % a.shape[d];
+        rem /= a.shape[d];
+        ob += static_cast<long long>(c) * a.str[0][d];
+        ib += static_cast<long long>(c) * a.str[1][d];
+    }
+    const T *src = reinterpret_cast<const T *>(a.ptr[1]);
+    T *dst = reinterpret_cast<T *>(a.ptr[0]);
+    const int tx = threadIdx.x % TT, ty = threadIdx.x / TT;
+#pragma unroll 4
+    for (int s = 0; s < 16; ++s) {
+        const unsigned int lr = tx, lc = ty + s * 4;
+        if (r0 + lr < rows && c0 + lc < cols)
+            tile[lc][lr] = src[ib + static_cast<long long>(r0 + lr) * a.str[1][r - 2] +
+                               static_cast<long long>(c0 + lc) * a.str[1][r - 1]];
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int s = 0; s < 16; ++s) {
+        const unsigned int lc = tx, lr = ty + s * 4;
+        if (r0 + lr < rows && c0 + lc < cols)
+            dst[ob + static_cast<long long>(r0 + lr) * a.str[0][r - 2] + static_cast<long long>(c0 + lc) * a.str[0][r - 1]] =
+                tile[lc][lr];
+    }
+}
+
+// Row copy: rank-2 space whose inner axis is contiguous for both operands and a
+// multiple of 16 bytes; one 128-bit lane per 16 bytes.
+__global__ void __launch_bounds__(256) k_copy_rows16(const MoveArgs a, long long row_vec) {
+    const long long total = static_cast<long long>(a.shape[0]) * row_vec;
+    for (long long v = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+         v += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long row = v / row_vec, col = v - row * row_vec;
+        const uint4 *s = reinterpret_cast<const uint4 *>(a.ptr[1] + (a.off[1] + row * a.str[1][0]) * 4) + col;
+        uint4 *d = reinterpret_cast<uint4 *>(a.ptr[0] + (a.off[0] + row * a.str[0][0]) * 4) + col;
+        *d = __ldg(s);
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_fill_flat(T *out, long long n, T value) {
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<long long>(gridDim.x) * blockDim.x)
+        out[i] = value;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_fill_strided(const MoveArgs a, T value) {
+    const unsigned int n = static_cast<unsigned int>(a.numel);
+    for (unsigned int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        long long o[1];
+        offsets_of<1>(a, i, o);
+        reinterpret_cast<T *>(a.ptr[0])[o[0]] = value;
+    }
+}
+
+// take-along-axis gather, one element per thread.  Operand 0 = out, 1 = source
+// base (indexed axis stride zeroed), 2 = indices.
+template <typename T>
+__global__ void __launch_bounds__(256) k_gather(const MoveArgs a) {
+    const unsigned int n = static_cast<unsigned int>(a.numel);
+    const long long *idx = reinterpret_cast<const long long *>(a.ptr[2]);
+    for (unsigned int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        long long o[3];
+        offsets_of<3>(a, i, o);
+        const long long j = idx[o[2]];
+        if (j < 0 || j >= a.axis_extent) {
+            record_device_error(MTC_ERR_OUT_OF_RANGE, j);
+            continue;
+        }
+        reinterpret_cast<T *>(a.ptr[0])[o[0]] = reinterpret_cast<const T *>(a.ptr[1])[o[1] + j * a.axis_stride];
+    }
+}
+
+// Row gather: the innermost axis is contiguous in out and source and broadcast
+// (stride 0) in the indices, so every index selects a whole row of `row_vec`
+// 16-byte vectors.  One index load per row; 128-bit copies.
+__global__ void __launch_bounds__(256) k_gather_rows16(const MoveArgs a, long long rows, long long row_vec) {
+    const long long *idx = reinterpret_cast<const long long *>(a.ptr[2]);
+    const long long total = rows * row_vec;
+    for (long long v = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+         v += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long row = v / row_vec, col = v - row * row_vec;
+        // outer coordinates of this row (all axes but the innermost)
+        long long o[3];
+        offsets_of<3>(a, static_cast<unsigned int>(row * a.shape[a.rank - 1]), o);
+        const long long j = __ldg(idx + o[2]);
+        if (j < 0 || j >= a.axis_extent) {
+            if (col == 0) record_device_error(MTC_ERR_OUT_OF_RANGE, j);
+            continue;
+        }
+        const uint4 *s = reinterpret_cast<const uint4 *>(a.ptr[1] + (o[1] + j * a.axis_stride) * 4) + col;
+        uint4 *d = reinterpret_cast<uint4 *>(a.ptr[0] + o[0] * 4) + col;
+        *d = __ldg(s);
+    }
+}
+
+// Scatter-add: operand 0 = target base (indexed axis stride zeroed), 1 = updates, 2 = indices.
+__global__ void __launch_bounds__(256) k_scatter_add(const MoveArgs a) {
+    const unsigned int n = static_cast<unsigned int>(a.numel);
+    const long long *idx = reinterpret_cast<const long long *>(a.ptr[2]);
+    for (unsigned int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        long long o[3];
+        offsets_of<3>(a, i, o);
+        const long long j = idx[o[2]];
+        if (j < 0 || j >= a.axis_extent) {
+            record_device_error(MTC_ERR_OUT_OF_RANGE, j);
+            continue;
+        }
+        atomicAdd(reinterpret_cast<float *>(a.ptr[0]) + o[0] + j * a.axis_stride,
+                  reinterpret_cast<const float *>(a.ptr[1])[o[1]]);
+    }
+}
+
+// Row scatter-add with 128-bit vector reductions into L2 (sm_90+ red.v4.f32).
+__global__ void __launch_bounds__(256) k_scatter_add_rows16(const MoveArgs a, long long rows, long long row_vec) {
+    const long long *idx = reinterpret_cast<const long long *>(a.ptr[2]);
+    const long long total = rows * row_vec;
+    for (long long v = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; v < total;
+         v += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long row = v / row_vec, col = v - row * row_vec;
+        long long o[3];
+        offsets_of<3>(a, static_cast<unsigned int>(row * a.shape[a.rank - 1]), o);
+        const long long j = __ldg(idx + o[2]);
+        if (j < 0 || j >= a.axis_extent) {
+            if (col == 0) record_device_error(MTC_ERR_OUT_OF_RANGE, j);
+            continue;
+        }
+        const float4 u = __ldg(reinterpret_cast<const float4 *>(a.ptr[1] + o[1] * 4) + col);
+        float4 *t = reinterpret_cast<float4 *>(a.ptr[0] + (o[0] + j * a.axis_stride) * 4) + col;
+        atomicAdd(t, u);
+    }
+}
+
+int grid_for(long long work, int per_block = 256) {
+    const int sms = sm_count(current_device());
+    long long b = (work + per_block - 1) / per_block;
+    if (b > static_cast<long long>(sms) * 8) b = static_cast<long long>(sms) * 8;
+    return b < 1 ? 1 : static_cast<int>(b);
+}
+
+void fill_divs(MoveArgs &a, const IterSpace &s) {
+    a.numel = s.numel;
+    a.rank = s.rank;
+    for (int d = 0; d < s.rank; ++d) {
+        a.shape[d] = static_cast<unsigned int>(s.shape[d]);
+        a.div[d] = make_fastdiv(static_cast<uint32_t>(s.shape[d]));
+        for (int k = 0; k < s.nops; ++k) a.str[k][d] = s.stride[k][d];
+    }
+    for (int k = 0; k < s.nops; ++k) a.off[k] = s.offset[k];
+}
+
+bool aligned16(const void *p, long long off_elems, int elem) {
+    return (reinterpret_cast<uintptr_t>(static_cast<const char *>(p) + off_elems * elem) % 16) == 0;
+}
+
+// Strided copy of src into dst (same shape, same dtype).
+int copy_impl(const mtc_desc &src, const mtc_desc &dst, cudaStream_t stream) {
+    IterSpace s;
+    s.rank = src.rank;
+    s.nops = 2;
+    for (int d = 0; d < src.rank; ++d) {
+        s.shape[d] = src.shape[d];
+        s.stride[0][d] = dst.strides[d];
+        s.stride[1][d] = src.strides[d];
+    }
+    s.offset[0] = dst.offset;
+    s.offset[1] = src.offset;
+    simplify(s);
+    if (s.numel == 0) return MTC_OK;
+    const int es = static_cast<int>(dtype_size(src.dtype));
+    if (s.rank == 1 && s.stride[0][0] == 1 && s.stride[1][0] == 1) {
+        MTC_CUDA_TRY(cudaMemcpyAsync(static_cast<char *>(dst.data) + s.offset[0] * es,
+                                     static_cast<const char *>(src.data) + s.offset[1] * es,
+                                     static_cast<size_t>(s.numel) * es, cudaMemcpyDeviceToDevice, stream));
+        return MTC_OK;
+    }
+    if (s.numel >= (int64_t{1} << 32)) return fail(MTC_ERR_UNSUPPORTED, "strided copy of 2^32 or more elements");
+    MoveArgs a;
+    std::memset(&a, 0, sizeof(a));
+    fill_divs(a, s);
+    a.ptr[0] = static_cast<char *>(dst.data);
+    a.ptr[1] = static_cast<char *>(const_cast<void *>(src.data));
+    const int r = s.rank;
+    // contiguous rows, 16-byte multiples: vector row copy
+    if (r == 2 && s.stride[0][1] == 1 && s.stride[1][1] == 1 && (s.shape[1] * es) % 16 == 0 &&
+        (s.stride[0][0] * es) % 16 == 0 && (s.stride[1][0] * es) % 16 == 0 && aligned16(dst.data, s.offset[0], es) &&
+        aligned16(src.data, s.offset[1], es)) {
+        const long long row_vec = s.shape[1] * es / 16;
+        k_copy_rows16<<<grid_for(s.shape[0] * row_vec), 256, 0, stream>>>(a, row_vec);
+        return check_launch("row copy");
+    }
+    if (r >= 2 && s.stride[0][r - 1] == 1 && s.stride[1][r - 2] == 1 && s.stride[1][r - 1] != 1) {
+        int64_t batch = 1;
+        for (int d = 0; d < r - 2; ++d) batch *= s.shape[d];
+        const int64_t ty = (s.shape[r - 2] + 63) / 64;
+        if (batch <= 65535 && ty <= 65535) {
+            dim3 grid(static_cast<unsigned>((s.shape[r - 1] + 63) / 64), static_cast<unsigned>(ty),
+                      static_cast<unsigned>(batch));
+            if (es == 4) k_copy_tiled<uint32_t><<<grid, 256, 0, stream>>>(a);
+            else k_copy_tiled<unsigned long long><<<grid, 256, 0, stream>>>(a);
+            return check_launch("tiled copy");
+        }
+    }
+    if (es == 4) k_copy_strided<uint32_t><<<grid_for(s.numel), 256, 0, stream>>>(a);
+    else k_copy_strided<unsigned long long><<<grid_for(s.numel), 256, 0, stream>>>(a);
+    return check_launch("strided copy");
+}
+
+int fill_impl(const mtc_desc &out, const void *value, cudaStream_t stream) {
+    const int es = static_cast<int>(dtype_size(out.dtype));
+    IterSpace s;
+    s.rank = out.rank;
+    s.nops = 1;
+    for (int d = 0; d < out.rank; ++d) {
+        s.shape[d] = out.shape[d];
+        s.stride[0][d] = out.strides[d];
+    }
+    s.offset[0] = out.offset;
+    simplify(s);
+    if (s.numel == 0) return MTC_OK;
+    uint64_t bits = 0;
+    std::memcpy(&bits, value, es);
+    char *base = static_cast<char *>(out.data);
+    if (s.rank == 1 && (s.stride[0][0] == 1 || s.numel == 1)) {
+        if (bits == 0) {
+            MTC_CUDA_TRY(cudaMemsetAsync(base + s.offset[0] * es, 0, static_cast<size_t>(s.numel) * es, stream));
+            return MTC_OK;
+        }
+        if (es == 4)
+            k_fill_flat<uint32_t><<<grid_for(s.numel), 256, 0, stream>>>(
+                reinterpret_cast<uint32_t *>(base) + s.offset[0], s.numel, static_cast<uint32_t>(bits));
+        else
+            k_fill_flat<unsigned long long><<<grid_for(s.numel), 256, 0, stream>>>(
+                reinterpret_cast<unsigned long long *>(base) + s.offset[0], s.numel, static_cast<unsigned long long>(bits));
+        return check_launch("fill");
+    }
+    if (s.numel >= (int64_t{1} << 32)) return fail(MTC_ERR_UNSUPPORTED, "strided fill of 2^32 or more elements");
+    MoveArgs a;
+    std::memset(&a, 0, sizeof(a));
+    fill_divs(a, s);
+    a.ptr[0] = base;
+    if (es == 4) k_fill_strided<uint32_t><<<grid_for(s.numel), 256, 0, stream>>>(a, static_cast<uint32_t>(bits));
+    else k_fill_strided<unsigned long long><<<grid_for(s.numel), 256, 0, stream>>>(a, static_cast<unsigned long long>(bits));
+    return check_launch("strided fill");
+}
+
+bool same_shape(const mtc_desc &x, const mtc_desc &y) {
+    if (x.rank != y.rank) return false;
+    for (int d = 0; d < x.rank; ++d)
+        if (x.shape[d] != y.shape[d]) return false;
+    return true;
+}
+
+// Shared set-up of gather (role 0 = out, 1 = src, 2 = idx) and scatter-add
+// (role 0 = target, 1 = updates, 2 = idx): the indexed tensor's axis stride is
+// zeroed and supplied separately, the walk runs over idx.shape.
+int index_space(const mtc_desc &indexed, const mtc_desc &walked, const mtc_desc &idx, int64_t axis, bool indexed_is_out,
+                MoveArgs &a, IterSpace &s) {
+    const int rank = idx.rank;
+    s.rank = rank;
+    s.nops = 3;
+    for (int d = 0; d < rank; ++d) {
+        s.shape[d] = idx.shape[d];
+        const int64_t st = (d == axis) ? 0 : indexed.strides[d];
+        s.stride[indexed_is_out ? 0 : 1][d] = st;
+        s.stride[indexed_is_out ? 1 : 0][d] = walked.strides[d];
+        s.stride[2][d] = idx.strides[d];
+    }
+    s.offset[indexed_is_out ? 0 : 1] = indexed.offset;
+    s.offset[indexed_is_out ? 1 : 0] = walked.offset;
+    s.offset[2] = idx.offset;
+    // Keep the innermost axis separate from the coalescing so the row kernels can
+    // recognise it: simplification still merges the outer axes.
+    simplify(s);
+    if (s.numel >= (int64_t{1} << 32)) return fail(MTC_ERR_UNSUPPORTED, "index space of 2^32 or more elements");
+    std::memset(&a, 0, sizeof(a));
+    fill_divs(a, s);
+    a.axis_extent = indexed.shape[axis];
+    a.axis_stride = indexed.strides[axis];
+    return MTC_OK;
+}
+
+}  // namespace
+}  // namespace mtc
+
+using namespace mtc;
+
+extern "C" {
+
+int mtc_copy(const mtc_desc *src, const mtc_desc *dst, void *stream) {
+    clear_error();
+    MTC_TRY(validate(src, "source"));
+    MTC_TRY(validate(dst, "destination"));
+    if (src->dtype != dst->dtype) return fail(MTC_ERR_INVALID_ARGUMENT, "copy between different dtypes");
+    if (!same_shape(*src, *dst)) return fail(MTC_ERR_INVALID_ARGUMENT, "copy between different shapes");
+    return copy_impl(*src, *dst, static_cast<cudaStream_t>(stream));
+}
+
+int mtc_concat(const mtc_desc *inputs, int32_t n_inputs, int64_t axis, const mtc_desc *out, void *stream) {
+    clear_error();
+    MTC_TRY(validate(out, "output"));
+    if (n_inputs < 1 || inputs == nullptr) return fail(MTC_ERR_INVALID_ARGUMENT, "concatenate needs inputs");
+    if (axis < 0 || axis >= out->rank) return fail(MTC_ERR_OUT_OF_RANGE, "concatenate axis out of range");
+    int64_t start = 0;
+    for (int i = 0; i < n_inputs; ++i) {
+        MTC_TRY(validate(&inputs[i], "input"));
+        const mtc_desc &in = inputs[i];
+        if (in.dtype != out->dtype || in.rank != out->rank)
+            return fail(MTC_ERR_INVALID_ARGUMENT, "concatenate input %d does not match the output", i);
+        for (int d = 0; d < out->rank; ++d)
+            if (d != axis && in.shape[d] != out->shape[d])
+                return fail(MTC_ERR_INVALID_ARGUMENT, "concatenate input %d has a mismatched extent", i);
+        start += in.shape[axis];
+    }
+    if (start != out->shape[axis]) return fail(MTC_ERR_INVALID_ARGUMENT, "concatenate extents do not sum to the output");
+    start = 0;
+    for (int i = 0; i < n_inputs; ++i) {
+        const mtc_desc &in = inputs[i];
+        mtc_desc section = *out;
+        for (int d = 0; d < out->rank; ++d) section.shape[d] = in.shape[d];
+        section.offset = out->offset + start * out->strides[axis];
+        start += in.shape[axis];
+        int64_t n = 1;
+        for (int d = 0; d < in.rank; ++d) n *= in.shape[d];
+        if (n == 0) continue;
+        MTC_TRY(copy_impl(in, section, static_cast<cudaStream_t>(stream)));
+    }
+    return MTC_OK;
+}
+
+int mtc_index_scatter(const mtc_desc *in, const mtc_desc *dst_view, const mtc_desc *out, void *stream) {
+    clear_error();
+    MTC_TRY(validate(in, "input"));
+    MTC_TRY(validate(dst_view, "destination view"));
+    MTC_TRY(validate(out, "output"));
+    if (dst_view->data != out->data) return fail(MTC_ERR_INVALID_ARGUMENT, "scatter view must alias the output buffer");
+    if (!same_shape(*in, *dst_view)) return fail(MTC_ERR_INVALID_ARGUMENT, "scatter view shape differs from input");
+    if (in->dtype != out->dtype) return fail(MTC_ERR_INVALID_ARGUMENT, "scatter dtype mismatch");
+    const uint64_t zero = 0;
+    MTC_TRY(fill_impl(*out, &zero, static_cast<cudaStream_t>(stream)));
+    return copy_impl(*in, *dst_view, static_cast<cudaStream_t>(stream));
+}
+
+int mtc_fill(const mtc_desc *out, const void *value, void *stream) {
+    clear_error();
+    MTC_TRY(validate(out, "output"));
+    if (value == nullptr) return fail(MTC_ERR_INVALID_ARGUMENT, "null fill value");
+    return fill_impl(*out, value, static_cast<cudaStream_t>(stream));
+}
+
+int mtc_gather(const mtc_desc *src, const mtc_desc *idx, int64_t axis, const mtc_desc *out, void *stream) {
+    clear_error();
+    MTC_TRY(validate(src, "source"));
+    MTC_TRY(validate(idx, "indices"));
+    MTC_TRY(validate(out, "output"));
+    if (idx->dtype != MTC_INT64) return fail(MTC_ERR_INVALID_ARGUMENT, "gather indices must be Int64");
+    if (src->dtype != out->dtype) return fail(MTC_ERR_INVALID_ARGUMENT, "gather dtype mismatch");
+    if (src->rank != idx->rank || !same_shape(*idx, *out))
+        return fail(MTC_ERR_INVALID_ARGUMENT, "gather shapes are inconsistent");
+    if (axis < 0 || axis >= src->rank) return fail(MTC_ERR_OUT_OF_RANGE, "gather axis out of range");
+    for (int d = 0; d < src->rank; ++d)
+        if (d != axis && idx->shape[d] != src->shape[d])
+            return fail(MTC_ERR_INVALID_ARGUMENT, "gather index extent differs from source off the axis");
+    MoveArgs a;
+    IterSpace s;
+    MTC_TRY(index_space(*src, *out, *idx, axis, false, a, s));
+    if (s.numel == 0) return MTC_OK;
+    a.ptr[0] = static_cast<char *>(out->data);
+    a.ptr[1] = static_cast<char *>(const_cast<void *>(src->data));
+    a.ptr[2] = static_cast<char *>(const_cast<void *>(idx->data));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int r = s.rank;
+    const int es = static_cast<int>(dtype_size(src->dtype));
+    if (r >= 2 && es == 4 && s.stride[0][r - 1] == 1 && s.stride[1][r - 1] == 1 && s.stride[2][r - 1] == 0 &&
+        (s.shape[r - 1] * 4) % 16 == 0 && (a.axis_stride * 4) % 16 == 0) {
+        bool ok = aligned16(out->data, 0, 4) && aligned16(src->data, 0, 4);
+        for (int d = 0; d < r - 1 && ok; ++d) ok = (s.stride[0][d] * 4) % 16 == 0 && (s.stride[1][d] * 4) % 16 == 0;
+        ok = ok && (s.offset[0] * 4) % 16 == 0 && (s.offset[1] * 4) % 16 == 0;
+        if (ok) {
+            const long long rows = s.numel / s.shape[r - 1];
+            const long long row_vec = s.shape[r - 1] / 4;
+            k_gather_rows16<<<grid_for(rows * row_vec), 256, 0, st>>>(a, rows, row_vec);
+            return check_launch("row gather");
+        }
+    }
+    if (es == 4) k_gather<uint32_t><<<grid_for(s.numel), 256, 0, st>>>(a);
+    else k_gather<unsigned long long><<<grid_for(s.numel), 256, 0, st>>>(a);
+    return check_launch("gather");
+}
+
+int mtc_gather_scatter_add(const mtc_desc *upd, const mtc_desc *idx, int64_t axis, const mtc_desc *out, void *stream) {
+    clear_error();
+    MTC_TRY(validate(upd, "updates"));
+    MTC_TRY(validate(idx, "indices"));
+    MTC_TRY(validate(out, "output"));
+    if (idx->dtype != MTC_INT64) return fail(MTC_ERR_INVALID_ARGUMENT, "scatter indices must be Int64");
+    if (upd->dtype != MTC_FLOAT32 || out->dtype != MTC_FLOAT32)
+        return fail(MTC_ERR_LOGIC, "scatter-add requires Float32");
+    if (upd->rank != idx->rank || upd->rank != out->rank || !same_shape(*upd, *idx))
+        return fail(MTC_ERR_INVALID_ARGUMENT, "scatter-add shapes are inconsistent");
+    if (axis < 0 || axis >= out->rank) return fail(MTC_ERR_OUT_OF_RANGE, "scatter-add axis out of range");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const float zero = 0.0f;
+    MTC_TRY(fill_impl(*out, &zero, st));
+    MoveArgs a;
+    IterSpace s;
+    MTC_TRY(index_space(*out, *upd, *idx, axis, true, a, s));
+    if (s.numel == 0) return MTC_OK;
+    a.ptr[0] = static_cast<char *>(out->data);
+    a.ptr[1] = static_cast<char *>(const_cast<void *>(upd->data));
+    a.ptr[2] = static_cast<char *>(const_cast<void *>(idx->data));
+    const int r = s.rank;
+    if (r >= 2 && s.stride[0][r - 1] == 1 && s.stride[1][r - 1] == 1 && s.stride[2][r - 1] == 0 &&
+        (s.shape[r - 1] * 4) % 16 == 0 && (a.axis_stride * 4) % 16 == 0) {
+        bool ok = aligned16(out->data, 0, 4) && aligned16(upd->data, 0, 4);
+        for (int d = 0; d < r - 1 && ok; ++d) ok = (s.stride[0][d] * 4) % 16 == 0 && (s.stride[1][d] * 4) % 16 == 0;
+        ok = ok && (s.offset[0] * 4) % 16 == 0 && (s.offset[1] * 4) % 16 == 0;
+        if (ok) {
+            const long long rows = s.numel / s.shape[r - 1];
+            const long long row_vec = s.shape[r - 1] / 4;
+            k_scatter_add_rows16<<<grid_for(rows * row_vec), 256, 0, st>>>(a, rows, row_vec);
+            return check_launch("row scatter-add");
+        }
+    }
+    k_scatter_add<<<grid_for(s.numel), 256, 0, st>>>(a);
+    return check_launch("scatter-add");
+}
+
+int mtc_check_device_errors(int device, void *stream, int64_t *detail) {
+    clear_error();
+    int prev = 0;
+    MTC_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != device) MTC_CUDA_TRY(cudaSetDevice(device));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned long long word[2] = {0, 0};
+    int rc = MTC_OK;
+    if (cudaMemcpyFromSymbolAsync(word, g_device_error, sizeof(word), 0, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
+        rc = fail(MTC_ERR_RUNTIME, "reading the device error word failed: %s", cudaGetErrorString(cudaGetLastError()));
+    } else {
+        if (detail) *detail = static_cast<int64_t>(word[1]);
+        if (word[0] != 0) {
+            const unsigned long long zero[2] = {0, 0};
+            cudaMemcpyToSymbolAsync(g_device_error, zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s);
+            cudaStreamSynchronize(s);
+            rc = fail(static_cast<int>(word[0]), "an index kernel met index %lld outside its axis",
+                      static_cast<long long>(word[1]));
+        }
+    }
+    if (prev != device) cudaSetDevice(prev);
+    return rc;
+}
+
+}  // extern "C"

@@ -1,0 +1,307 @@
+// Elementwise kernel templates of libmtcuda.
+//
+// This header is compiled twice: by nvcc into the precompiled single-op kernels
+// (elementwise.cu), and, embedded as text, by NVRTC into the kernels generated
+// for fused elementwise programs (fused.cu).  It therefore uses only builtin
+// types and CUDA device intrinsics (no host or standard-library headers).
+//
+// Op semantics follow the reference CPU kernels
+// (src/tensor/backend/cpu/kernels/elementwise/kernels.cpp:58-167).  Every
+// arithmetic step uses an explicitly rounded intrinsic (__fadd_rn, __fmul_rn,
+// ...) so the compiler cannot contract a multiply and an add of two different
+// graph nodes into one FMA: a fused chain then rounds exactly like the chain of
+// materialised single ops the CPU evaluates.
+#ifndef MTC_EW_KERNELS_CUH
+#define MTC_EW_KERNELS_CUH
+
+#define MTC_EW_MAX_RANK 8
+#define MTC_EW_MAX_IN 12
+#define MTC_EW_MAX_OUT 4
+#define MTC_EW_TILE 64
+#define MTC_EW_TILE_THREADS 256
+
+// ------------------------------------------------------------------- ops --
+
+template <int OP>
+__device__ __forceinline__ float mtc_unary(float x);
+
+template <> __device__ __forceinline__ float mtc_unary<0x0101>(float x) { return fabsf(x); }
+template <> __device__ __forceinline__ float mtc_unary<0x0102>(float x) {
+    // sign keeps +-0 and NaN (kernels.cpp:96-107)
+    return x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : x);
+}
+template <> __device__ __forceinline__ float mtc_unary<0x0103>(float x) { return -x; }
+template <> __device__ __forceinline__ float mtc_unary<0x0104>(float x) { return expf(x); }
+template <> __device__ __forceinline__ float mtc_unary<0x0105>(float x) { return logf(x); }
+template <> __device__ __forceinline__ float mtc_unary<0x0106>(float x) { return __fsqrt_rn(x); }
+template <> __device__ __forceinline__ float mtc_unary<0x0107>(float x) { return tanhf(x); }
+template <> __device__ __forceinline__ float mtc_unary<0x0108>(float x) {
+    // branch form of the CPU sigmoid (kernels.cpp:113-124)
+    if (x >= 0.0f) {
+        const float e = expf(-x);
+        return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+    }
+    const float e = expf(x);
+    return __fdiv_rn(e, __fadd_rn(1.0f, e));
+}
+template <> __device__ __forceinline__ float mtc_unary<0x0180>(float x) {
+    // relu: NaN propagates, -0 -> +0 (equal to the composite (x + |x|) * 0.5)
+    return x > 0.0f ? x : (x != x ? x : 0.0f);
+}
+
+template <int OP>
+__device__ __forceinline__ float mtc_binary(float a, float b);
+
+template <> __device__ __forceinline__ float mtc_binary<0x0110>(float a, float b) { return __fadd_rn(a, b); }
+template <> __device__ __forceinline__ float mtc_binary<0x0111>(float a, float b) { return __fsub_rn(a, b); }
+template <> __device__ __forceinline__ float mtc_binary<0x0112>(float a, float b) { return __fmul_rn(a, b); }
+template <> __device__ __forceinline__ float mtc_binary<0x0113>(float a, float b) { return __fdiv_rn(a, b); }
+template <> __device__ __forceinline__ float mtc_binary<0x0114>(float a, float b) {
+    // logaddexp with the CPU's NaN and infinity rules (kernels.cpp:150-167)
+    if (a != a || b != b) return __fadd_rn(a, b);
+    const float m = (a < b) ? b : a;  // std::max(a, b)
+    if (isinf(m)) return m;
+    return __fadd_rn(m, log1pf(expf(-fabsf(__fsub_rn(a, b)))));
+}
+
+template <int OP>
+struct MtcUnaryOp {
+    static constexpr int kIn = 1;
+    static constexpr int kOut = 1;
+    __device__ __forceinline__ void operator()(const float *x, float *y) const { y[0] = mtc_unary<OP>(x[0]); }
+};
+
+template <int OP>
+struct MtcBinaryOp {
+    static constexpr int kIn = 2;
+    static constexpr int kOut = 1;
+    __device__ __forceinline__ void operator()(const float *x, float *y) const { y[0] = mtc_binary<OP>(x[0], x[1]); }
+};
+
+// ------------------------------------------------------------ arguments --
+
+struct MtcFastDiv {
+    unsigned int d;
+    unsigned int mul;
+    unsigned int shift;
+};
+
+// Division by an invariant divisor (Granlund & Montgomery 1994, round-up variant).
+__device__ __forceinline__ unsigned int mtc_fastdiv(unsigned int n, const MtcFastDiv &f) {
+    if (f.d <= 1u) return n;
+    const unsigned int t = __umulhi(n, f.mul);
+    return (t + ((n - t) >> 1)) >> (f.shift - 1u);
+}
+
+// One launch's operands over a common (simplified) logical shape.
+struct MtcEwArgs {
+    long long numel;
+    int rank;
+    unsigned int shape[MTC_EW_MAX_RANK];
+    MtcFastDiv div[MTC_EW_MAX_RANK];
+    const float *in[MTC_EW_MAX_IN];
+    long long in_off[MTC_EW_MAX_IN];
+    long long in_str[MTC_EW_MAX_IN][MTC_EW_MAX_RANK];
+    float *out[MTC_EW_MAX_OUT];
+    long long out_off[MTC_EW_MAX_OUT];
+    long long out_str[MTC_EW_MAX_OUT][MTC_EW_MAX_RANK];
+    unsigned int transposed;  // tiled kernel: bit k set when input k is read through shared memory
+    unsigned int batch_rank;  // tiled kernel: number of leading (batch) axes
+};
+
+// ------------------------------------------------------------ flat kernel --
+// Every operand is contiguous (stride 1) or a broadcast scalar (stride 0) over
+// a single axis.  VEC = 4 uses 128-bit loads/stores (all pointers 16-byte aligned).
+
+template <class Op, int VEC>
+__global__ void __launch_bounds__(256) mtc_ew_flat(const MtcEwArgs a) {
+    constexpr int NIN = Op::kIn;
+    constexpr int NOUT = Op::kOut;
+    const Op op;
+    const long long nvec = a.numel / VEC;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long v = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
+        float x[VEC][NIN > 0 ? NIN : 1];
+        float y[VEC][NOUT];
+#pragma unroll
+        for (int k = 0; k < NIN; ++k) {
+            if (a.in_str[k][0] == 0) {
+                const float s = __ldg(a.in[k] + a.in_off[k]);
+#pragma unroll
+                for (int l = 0; l < VEC; ++l) x[l][k] = s;
+            } else if (VEC == 4) {
+                const float4 q = __ldg(reinterpret_cast<const float4 *>(a.in[k] + a.in_off[k]) + v);
+                x[0][k] = q.x;
+                x[1][k] = q.y;
+                x[2][k] = q.z;
+                x[3][k] = q.w;
+            } else {
+#pragma unroll
+                for (int l = 0; l < VEC; ++l) x[l][k] = __ldg(a.in[k] + a.in_off[k] + v * VEC + l);
+            }
+        }
+#pragma unroll
+        for (int l = 0; l < VEC; ++l) op(x[l], y[l]);
+#pragma unroll
+        for (int j = 0; j < NOUT; ++j) {
+            if (VEC == 4) {
+                float4 q;
+                q.x = y[0][j];
+                q.y = y[1][j];
+                q.z = y[2][j];
+                q.w = y[3][j];
+                reinterpret_cast<float4 *>(a.out[j] + a.out_off[j])[v] = q;
+            } else {
+#pragma unroll
+                for (int l = 0; l < VEC; ++l) a.out[j][a.out_off[j] + v * VEC + l] = y[l][j];
+            }
+        }
+    }
+    // scalar tail (numel not a multiple of VEC)
+    const long long tail = nvec * VEC;
+    const long long t = tail + static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (VEC > 1 && t < a.numel) {
+        float x[NIN > 0 ? NIN : 1];
+        float y[NOUT];
+#pragma unroll
+        for (int k = 0; k < NIN; ++k) x[k] = __ldg(a.in[k] + a.in_off[k] + (a.in_str[k][0] == 0 ? 0 : t));
+        op(x, y);
+#pragma unroll
+        for (int j = 0; j < NOUT; ++j) a.out[j][a.out_off[j] + t] = y[j];
+    }
+}
+
+// --------------------------------------------------------- strided kernel --
+// Any strides (zero, negative, transposed); the linear index is decomposed into
+// coordinates with precomputed divisors.  numel < 2^32.
+
+template <class Op>
+__global__ void __launch_bounds__(256) mtc_ew_strided(const MtcEwArgs a) {
+    constexpr int NIN = Op::kIn;
+    constexpr int NOUT = Op::kOut;
+    const Op op;
+    const unsigned int n = static_cast<unsigned int>(a.numel);
+    const unsigned int stride = gridDim.x * blockDim.x;
+    for (unsigned int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        long long io[NIN > 0 ? NIN : 1];
+        long long oo[NOUT];
+#pragma unroll
+        for (int k = 0; k < NIN; ++k) io[k] = a.in_off[k];
+#pragma unroll
+        for (int j = 0; j < NOUT; ++j) oo[j] = a.out_off[j];
+        unsigned int rem = i;
+#pragma unroll
+        for (int d = MTC_EW_MAX_RANK - 1; d >= 1; --d) {
+            if (d < a.rank) {
+                const unsigned int q = mtc_fastdiv(rem, a.div[d]);
+                const long long c = static_cast<long long>(rem - q * a.shape[d]);
+                rem = q;
+#pragma unroll
+                for (int k = 0; k < NIN; ++k) io[k] += c * a.in_str[k][d];
+#pragma unroll
+                for (int j = 0; j < NOUT; ++j) oo[j] += c * a.out_str[j][d];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < NIN; ++k) io[k] += static_cast<long long>(rem) * a.in_str[k][0];
+#pragma unroll
+        for (int j = 0; j < NOUT; ++j) oo[j] += static_cast<long long>(rem) * a.out_str[j][0];
+        float x[NIN > 0 ? NIN : 1];
+        float y[NOUT];
+#pragma unroll
+        for (int k = 0; k < NIN; ++k) x[k] = __ldg(a.in[k] + io[k]);
+        op(x, y);
+#pragma unroll
+        for (int j = 0; j < NOUT; ++j) a.out[j][oo[j]] = y[j];
+    }
+}
+
+// ----------------------------------------------------------- tiled kernel --
+// For spaces whose innermost output axis is contiguous while some inputs are
+// contiguous along the second-innermost axis instead (a transposed view, e.g.
+// B^T in A * B^T).  A 64x64 output tile is produced per CTA; every transposed
+// input is first staged through shared memory with loads coalesced along its own
+// contiguous axis, so both the reads and the writes are full 128-byte lines.
+// grid = (ceil(cols/64), ceil(rows/64), batch).
+
+template <class Op, int NT>
+__global__ void __launch_bounds__(MTC_EW_TILE_THREADS) mtc_ew_tiled(const MtcEwArgs a) {
+    constexpr int NIN = Op::kIn;
+    constexpr int NOUT = Op::kOut;
+    constexpr int T = MTC_EW_TILE;
+    __shared__ float stage[NT > 0 ? NT : 1][T][T + 1];
+    const Op op;
+    const int r = a.rank;
+    const unsigned int rows = a.shape[r - 2];
+    const unsigned int cols = a.shape[r - 1];
+    const unsigned int r0 = blockIdx.y * T;
+    const unsigned int c0 = blockIdx.x * T;
+
+    long long ib[NIN > 0 ? NIN : 1];
+    long long ob[NOUT];
+#pragma unroll
+    for (int k = 0; k < NIN; ++k) ib[k] = a.in_off[k];
+#pragma unroll
+    for (int j = 0; j < NOUT; ++j) ob[j] = a.out_off[j];
+    unsigned int rem = blockIdx.z;
+    for (int d = static_cast<int>(a.batch_rank) - 1; d >= 0; --d) {
+        const unsigned int c = rem % a.shape[d];
+        rem /= a.shape[d];
+#pragma unroll
+        for (int k = 0; k < NIN; ++k) ib[k] += static_cast<long long>(c) * a.in_str[k][d];
+#pragma unroll
+        for (int j = 0; j < NOUT; ++j) ob[j] += static_cast<long long>(c) * a.out_str[j][d];
+    }
+
+    const int tx = threadIdx.x % T;
+    const int ty = threadIdx.x / T;  // 0..3
+    constexpr int STEPS = T * T / MTC_EW_TILE_THREADS;
+
+    if (NT > 0) {
+        int slot = 0;
+#pragma unroll
+        for (int k = 0; k < NIN; ++k) {
+            if (a.transposed & (1u << k)) {
+#pragma unroll 4
+                for (int s = 0; s < STEPS; ++s) {
+                    const unsigned int lr = tx;                  // along the input's contiguous axis
+                    const unsigned int lc = ty + s * (T / STEPS);
+                    if (r0 + lr < rows && c0 + lc < cols) {
+                        stage[slot][lc][lr] = __ldg(a.in[k] + ib[k] + static_cast<long long>(r0 + lr) * a.in_str[k][r - 2] +
+                                                    static_cast<long long>(c0 + lc) * a.in_str[k][r - 1]);
+                    }
+                }
+                ++slot;
+            }
+        }
+        __syncthreads();
+    }
+
+#pragma unroll 4
+    for (int s = 0; s < STEPS; ++s) {
+        const unsigned int lc = tx;
+        const unsigned int lr = ty + s * (T / STEPS);
+        if (r0 + lr < rows && c0 + lc < cols) {
+            float x[NIN > 0 ? NIN : 1];
+            float y[NOUT];
+            int slot = 0;
+#pragma unroll
+            for (int k = 0; k < NIN; ++k) {
+                if (NT > 0 && (a.transposed & (1u << k))) {
+                    x[k] = stage[slot][lc][lr];
+                    ++slot;
+                } else {
+                    x[k] = __ldg(a.in[k] + ib[k] + static_cast<long long>(r0 + lr) * a.in_str[k][r - 2] +
+                                 static_cast<long long>(c0 + lc) * a.in_str[k][r - 1]);
+                }
+            }
+            op(x, y);
+#pragma unroll
+            for (int j = 0; j < NOUT; ++j)
+                a.out[j][ob[j] + static_cast<long long>(r0 + lr) * a.out_str[j][r - 2] +
+                         static_cast<long long>(c0 + lc) * a.out_str[j][r - 1]] = y[j];
+        }
+    }
+}
+
+#endif  // MTC_EW_KERNELS_CUH

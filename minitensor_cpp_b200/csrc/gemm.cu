@@ -1,0 +1,233 @@
+// mtc_matmul: reference matmul semantics and the exact float32 SIMT GEMM.
+//
+// Shape and stride rules follow matmul_dispatch / MatmulPlan
+// (src/tensor/backend/cpu/kernels/linalg/loops.hpp:288-324,
+//  src/tensor/backend/cpu/iteration/matmul.cpp:32-82): 1-D operands become a
+// row (lhs) or column (rhs) of stride 0, batch axes are right-aligned and
+// broadcast with stride 0.  The SIMT kernel computes each product in float32
+// and accumulates with FFMA (one rounding per step instead of the CPU's two),
+// so it matches the CPU to rounding, not bit for bit.
+#include <cstring>
+
+#include "gemm.cuh"
+
+namespace mtc {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 8, PAD = 4;
+
+struct SimtArgs {
+    GemmProblem p;
+    int a_kmajor;  // A is contiguous along k (row-major A)
+    int b_nmajor;  // B is contiguous along n (row-major B)
+};
+
+__global__ void __launch_bounds__(256, 2) k_gemm_simt(const SimtArgs args) {
+    const GemmProblem &p = args.p;
+    __shared__ __align__(16) float As[2][BK][BM + PAD];
+    __shared__ __align__(16) float Bs[2][BK][BN + PAD];
+
+    // batch offsets
+    long long ao = p.a_off, bo = p.b_off, co = p.c_off;
+    {
+        unsigned int rem = blockIdx.z;
+        for (int d = p.batch_rank - 1; d >= 0; --d) {
+            const unsigned int e = static_cast<unsigned int>(p.batch_shape[d]);
+            const unsigned int c = rem % e;
+            rem /= e;
+            ao += static_cast<long long>(c) * p.a_bs[d];
+            bo += static_cast<long long>(c) * p.b_bs[d];
+            co += static_cast<long long>(c) * p.c_bs[d];
+        }
+    }
+    const long long m0 = static_cast<long long>(blockIdx.y) * BM;
+    const long long n0 = static_cast<long long>(blockIdx.x) * BN;
+    const int t = threadIdx.x;
+
+    // global -> register staging of one k-tile: 4 A values and 4 B values per thread
+    float ra[4], rb[4];
+    auto load_tile = [&](long long k0) {
+        if (args.a_kmajor) {  // row m = t/2, k = (t%2)*4 + i
+            const long long m = m0 + t / 2;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const long long k = k0 + (t % 2) * 4 + i;
+                ra[i] = (m < p.M && k < p.K) ? __ldg(p.A + ao + m * p.a_rs + k * p.a_cs) : 0.0f;
+            }
+        } else {  // k = t/32, m = (t%32)*4 + i
+            const long long k = k0 + t / 32;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const long long m = m0 + (t % 32) * 4 + i;
+                ra[i] = (m < p.M && k < p.K) ? __ldg(p.A + ao + m * p.a_rs + k * p.a_cs) : 0.0f;
+            }
+        }
+        if (args.b_nmajor) {  // k = t/32, n = (t%32)*4 + i
+            const long long k = k0 + t / 32;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const long long n = n0 + (t % 32) * 4 + i;
+                rb[i] = (n < p.N && k < p.K) ? __ldg(p.B + bo + k * p.b_rs + n * p.b_cs) : 0.0f;
+            }
+        } else {  // n = t/2, k = (t%2)*4 + i
+            const long long n = n0 + t / 2;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const long long k = k0 + (t % 2) * 4 + i;
+                rb[i] = (n < p.N && k < p.K) ? __ldg(p.B + bo + k * p.b_rs + n * p.b_cs) : 0.0f;
+            }
+        }
+    };
+    auto store_tile = [&](int buf) {
+        if (args.a_kmajor) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) As[buf][(t % 2) * 4 + i][t / 2] = ra[i];
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) As[buf][t / 32][(t % 32) * 4 + i] = ra[i];
+        }
+        if (args.b_nmajor) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) Bs[buf][t / 32][(t % 32) * 4 + i] = rb[i];
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) Bs[buf][(t % 2) * 4 + i][t / 2] = rb[i];
+        }
+    };
+
+    float acc[8][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+
+    const int tx = t % 16, ty = t / 16;
+    const long long ktiles = (p.K + BK - 1) / BK;
+    load_tile(0);
+    store_tile(0);
+    __syncthreads();
+    for (long long kt = 0; kt < ktiles; ++kt) {
+        const int buf = static_cast<int>(kt & 1);
+        if (kt + 1 < ktiles) load_tile((kt + 1) * BK);
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+            const float4 a0 = *reinterpret_cast<const float4 *>(&As[buf][k][ty * 4]);
+            const float4 a1 = *reinterpret_cast<const float4 *>(&As[buf][k][64 + ty * 4]);
+            const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[buf][k][tx * 4]);
+            const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[buf][k][64 + tx * 4]);
+            const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        if (kt + 1 < ktiles) store_tile(buf ^ 1);
+        __syncthreads();
+    }
+
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const long long m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
+        if (m >= p.M) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const long long n = n0 + (j < 4 ? tx * 4 + j : 64 + tx * 4 + (j - 4));
+            if (n < p.N) p.C[co + m * p.c_rs + n * p.c_cs] = acc[i][j];
+        }
+    }
+}
+
+}  // namespace
+
+int gemm_simt(const GemmProblem &p, cudaStream_t stream) {
+    if (p.M == 0 || p.N == 0 || p.batch == 0) return MTC_OK;
+    SimtArgs args;
+    args.p = p;
+    args.a_kmajor = (p.a_cs == 1 || p.a_rs != 1) ? 1 : 0;
+    args.b_nmajor = (p.b_cs == 1 || p.b_rs != 1) ? 1 : 0;
+    const int64_t gx = (p.N + BN - 1) / BN, gy = (p.M + BM - 1) / BM;
+    if (gy > 65535) return fail(MTC_ERR_UNSUPPORTED, "matmul with more than %d row tiles", 65535);
+    if (p.batch > 65535) return fail(MTC_ERR_UNSUPPORTED, "matmul with more than 65535 batch entries");
+    dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), static_cast<unsigned>(p.batch));
+    k_gemm_simt<<<grid, 256, 0, stream>>>(args);
+    MTC_TRY(check_launch("SIMT GEMM"));
+    return MTC_OK;
+}
+
+// Builds the GEMM problem from the three descriptors with the reference's
+// matmul shape rules; fails with the reference's exception kinds.
+static int build_problem(const mtc_desc &lhs, const mtc_desc &rhs, const mtc_desc &out, GemmProblem &p) {
+    if (lhs.rank < 1 || rhs.rank < 1) return fail(MTC_ERR_INVALID_ARGUMENT, "matmul operands must have rank >= 1");
+    const bool lv = lhs.rank == 1, rv = rhs.rank == 1;
+    const int lb = lv ? 0 : lhs.rank - 2, rb = rv ? 0 : rhs.rank - 2;
+    const int ob = lb > rb ? lb : rb;
+    std::memset(&p, 0, sizeof(p));
+    p.M = lv ? 1 : lhs.shape[lhs.rank - 2];
+    p.K = lhs.shape[lhs.rank - 1];
+    const int64_t rk = rv ? rhs.shape[0] : rhs.shape[rhs.rank - 2];
+    if (rk != p.K) return fail(MTC_ERR_INVALID_ARGUMENT, "matmul contraction extents differ");
+    p.N = rv ? 1 : rhs.shape[rhs.rank - 1];
+    // expected output shape: batch..., [M], [N]
+    const int out_rank = ob + (lv ? 0 : 1) + (rv ? 0 : 1);
+    if (out.rank != out_rank) return fail(MTC_ERR_INVALID_ARGUMENT, "matmul output rank mismatch");
+    p.batch = 1;
+    p.batch_rank = ob;
+    for (int d = 0; d < ob; ++d) {
+        const int la = d - (ob - lb), ra = d - (ob - rb);
+        const int64_t le = la >= 0 ? lhs.shape[la] : 1, re = ra >= 0 ? rhs.shape[ra] : 1;
+        if (le != re && le != 1 && re != 1) return fail(MTC_ERR_INVALID_ARGUMENT, "matmul batch extents do not broadcast");
+        const int64_t e = le == 1 ? re : le;
+        if (out.shape[d] != e) return fail(MTC_ERR_INVALID_ARGUMENT, "matmul output batch extent mismatch");
+        p.batch_shape[d] = e;
+        p.batch *= e;
+        p.a_bs[d] = (la >= 0 && lhs.shape[la] != 1) ? lhs.strides[la] : 0;
+        p.b_bs[d] = (ra >= 0 && rhs.shape[ra] != 1) ? rhs.strides[ra] : 0;
+        p.c_bs[d] = out.strides[d];
+    }
+    if (!lv && out.shape[ob] != p.M) return fail(MTC_ERR_INVALID_ARGUMENT, "matmul output row extent mismatch");
+    if (!rv && out.shape[ob + (lv ? 0 : 1)] != p.N) return fail(MTC_ERR_INVALID_ARGUMENT, "matmul output column extent mismatch");
+    p.A = static_cast<const float *>(lhs.data);
+    p.B = static_cast<const float *>(rhs.data);
+    p.C = static_cast<float *>(out.data);
+    p.a_off = lhs.offset;
+    p.a_rs = lv ? 0 : lhs.strides[lhs.rank - 2];
+    p.a_cs = lhs.strides[lhs.rank - 1];
+    p.b_off = rhs.offset;
+    p.b_rs = rv ? rhs.strides[0] : rhs.strides[rhs.rank - 2];
+    p.b_cs = rv ? 0 : rhs.strides[rhs.rank - 1];
+    p.c_off = out.offset;
+    p.c_rs = lv ? 0 : out.strides[ob];
+    p.c_cs = rv ? 0 : out.strides[ob + (lv ? 0 : 1)];
+    return MTC_OK;
+}
+
+}  // namespace mtc
+
+using namespace mtc;
+
+extern "C" int mtc_matmul(const mtc_desc *lhs, const mtc_desc *rhs, const mtc_desc *out, int32_t algo, void *stream) {
+    clear_error();
+    MTC_TRY(validate(lhs, "lhs"));
+    MTC_TRY(validate(rhs, "rhs"));
+    MTC_TRY(validate(out, "output"));
+    if (lhs->dtype != MTC_FLOAT32 || rhs->dtype != MTC_FLOAT32 || out->dtype != MTC_FLOAT32)
+        return fail(MTC_ERR_LOGIC, "matmul requires Float32");
+    GemmProblem p;
+    MTC_TRY(build_problem(*lhs, *rhs, *out, p));
+    if (numel_of(*out) == 0) return MTC_OK;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (p.K == 0) {
+        // empty contraction: every output element is 0 (the CPU zero-fills, loops.hpp:224)
+        const float zero = 0.0f;
+        return mtc_fill(out, &zero, stream);
+    }
+    if (algo == MTC_GEMM_SIMT) return gemm_simt(p, s);
+    if (algo == MTC_GEMM_3XTF32 || algo == MTC_GEMM_AUTO) {
+        const int rc = gemm_3xtf32(p, s);
+        if (rc != MTC_ERR_UNSUPPORTED || algo == MTC_GEMM_3XTF32) return rc;
+        clear_error();
+        return gemm_simt(p, s);
+    }
+    return fail(MTC_ERR_INVALID_ARGUMENT, "unknown matmul algorithm %d", algo);
+}

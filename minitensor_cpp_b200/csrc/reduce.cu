@@ -1,0 +1,552 @@
+// Axis reductions: Sum (0x0301), LogSumExp (0x0302), Max, ArgMax, and the
+// single-pass log-softmax.  Reference: reduce_values / reduce_logsumexp
+// (src/tensor/backend/cpu/kernels/reduction/loops.hpp:21-136) over ReductionPlan
+// (src/tensor/backend/cpu/iteration/reduction.cpp:14-121).
+//
+// Two kernel shapes:
+//  - row kernel: the reduced elements of one output form one run (stride +-1
+//    after folding), e.g. sum over the last axis; a warp (short rows) or a CTA
+//    (long rows) reduces a row with 128-bit loads, shuffle and shared-memory trees.
+//  - per-output kernel: one thread per output and reduction chunk; consecutive
+//    threads own consecutive outputs, so reducing a strided axis (sum over axis
+//    0 of a row-major matrix) reads full 128-byte lines.  Long reductions are cut
+//    into chunks whose partial states are merged in order by a second kernel.
+// The CPU accumulates sequentially in float; the GPU order is a fixed tree, so
+// results agree to rounding (parity tolerance 1e-5 * sqrt(K) relative).
+#include <cfloat>
+#include <cmath>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace mtc {
+namespace {
+
+constexpr long long kEmpty = 0x7fffffffffffffffLL;
+
+// Accumulator state shared by every reduction op.
+struct State {
+    float a;      // sum / running max
+    float b;      // logsumexp: running sum of exp(x - a)
+    long long i;  // argmax: index of the best element, kEmpty when none
+    int flags;    // logsumexp: bit0 = NaN seen, bit1 = +inf seen
+    int pad;
+};
+
+template <int OP>
+struct Reducer;
+
+template <>
+struct Reducer<MTC_OP_SUM> {
+    __device__ static State init() { return State{0.0f, 0.0f, kEmpty, 0, 0}; }
+    __device__ static void add(State &s, float x, long long) { s.a += x; }
+    __device__ static void merge(State &s, const State &o) { s.a += o.a; }
+    __device__ static float result(const State &s) { return s.a; }
+};
+
+template <>
+struct Reducer<MTC_OP_MAX> {
+    // NaN propagates; an empty reduction gives -inf.
+    __device__ static State init() { return State{-INFINITY, 0.0f, kEmpty, 0, 0}; }
+    __device__ static void add(State &s, float x, long long) {
+        if (s.a == s.a && (x != x || x > s.a)) s.a = x;
+    }
+    __device__ static void merge(State &s, const State &o) { add(s, o.a, 0); }
+    __device__ static float result(const State &s) { return s.a; }
+};
+
+template <>
+struct Reducer<MTC_OP_ARGMAX> {
+    // First index of the maximum; a NaN counts as the maximum (first NaN wins).
+    __device__ static State init() { return State{-INFINITY, 0.0f, kEmpty, 0, 0}; }
+    __device__ static void add(State &s, float x, long long idx) {
+        if (s.i == kEmpty || (s.a == s.a && (x != x || x > s.a))) {
+            s.a = x;
+            s.i = idx;
+        }
+    }
+    __device__ static void merge(State &s, const State &o) {
+        if (o.i == kEmpty) return;
+        if (s.i == kEmpty) {
+            s = o;
+            return;
+        }
+        const bool sn = s.a != s.a, on = o.a != o.a;
+        bool take;
+        if (sn || on) take = (sn && on) ? (o.i < s.i) : on;
+        else take = (o.a > s.a) || (o.a == s.a && o.i < s.i);
+        if (take) s = o;
+    }
+    __device__ static long long result(const State &s) { return s.i == kEmpty ? 0 : s.i; }
+};
+
+template <>
+struct Reducer<MTC_OP_LOGSUMEXP> {
+    // Online (max, sum) form of the two-pass CPU loop; NaN -> NaN, a +inf element
+    // or an all -inf / empty input returns the maximum (loops.hpp:59-136).
+    __device__ static State init() { return State{-INFINITY, 0.0f, kEmpty, 0, 0}; }
+    __device__ static void add(State &s, float x, long long) {
+        if (x != x) {
+            s.flags |= 1;
+        } else if (x == INFINITY) {
+            s.flags |= 2;
+        } else if (x == -INFINITY) {
+        } else if (x > s.a) {
+            s.b = s.b * expf(s.a - x) + 1.0f;
+            s.a = x;
+        } else {
+            s.b += expf(x - s.a);
+        }
+    }
+    __device__ static void merge(State &s, const State &o) {
+        s.flags |= o.flags;
+        if (o.a == -INFINITY) return;
+        if (s.a == -INFINITY) {
+            s.a = o.a;
+            s.b = o.b;
+            return;
+        }
+        if (o.a > s.a) {
+            s.b = s.b * expf(s.a - o.a) + o.b;
+            s.a = o.a;
+        } else {
+            s.b += o.b * expf(o.a - s.a);
+        }
+    }
+    __device__ static float result(const State &s) {
+        if (s.flags & 1) return NAN;
+        if (s.flags & 2) return INFINITY;
+        if (s.a == -INFINITY) return -INFINITY;
+        return s.a + logf(s.b);
+    }
+};
+
+__device__ __forceinline__ State shfl_down(const State &s, int delta) {
+    State o;
+    o.a = __shfl_down_sync(0xffffffffu, s.a, delta);
+    o.b = __shfl_down_sync(0xffffffffu, s.b, delta);
+    o.i = __shfl_down_sync(0xffffffffu, s.i, delta);
+    o.flags = __shfl_down_sync(0xffffffffu, s.flags, delta);
+    o.pad = 0;
+    return o;
+}
+
+template <int OP>
+__device__ __forceinline__ State warp_reduce(State s) {
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) {
+        const State o = shfl_down(s, d);
+        Reducer<OP>::merge(s, o);
+    }
+    return s;
+}
+
+struct RedArgs {
+    const float *in;
+    long long in_off;
+    void *out;
+    long long out_off;
+    long long nout;
+    long long R;
+    int krank;
+    unsigned int kshape[MTC_MAX_RANK];
+    FastDiv kdiv[MTC_MAX_RANK];
+    long long kstr[MTC_MAX_RANK];
+    int rrank;
+    unsigned int rshape[MTC_MAX_RANK];
+    long long rstr[MTC_MAX_RANK];
+    long long rrun_stride;  // row kernel: stride of the single reduced run
+    int vec4;               // row kernel: 128-bit loads allowed
+    int chunks;             // per-output kernel: reduction chunks per output
+    State *partial;         // chunks > 1: partial states [nout][chunks]
+    float *out_f;           // log-softmax output
+    long long out_row_stride;
+};
+
+__device__ __forceinline__ long long kept_offset(const RedArgs &a, unsigned int o) {
+    long long off = a.in_off;
+    unsigned int rem = o;
+#pragma unroll
+    for (int d = MTC_MAX_RANK - 1; d >= 1; --d) {
+        if (d < a.krank) {
+            const unsigned int q = fastdiv(rem, a.kdiv[d]);
+            off += static_cast<long long>(rem - q * a.kshape[d]) * a.kstr[d];
+            rem = q;
+        }
+    }
+    if (a.krank > 0) off += static_cast<long long>(rem) * a.kstr[0];
+    return off;
+}
+
+template <int OP>
+__device__ __forceinline__ void store_result(const RedArgs &a, long long o, const State &s) {
+    if constexpr (OP == MTC_OP_ARGMAX) {
+        static_cast<long long *>(a.out)[a.out_off + o] = Reducer<OP>::result(s);
+    } else {
+        static_cast<float *>(a.out)[a.out_off + o] = Reducer<OP>::result(s);
+    }
+}
+
+// Accumulates the run [base, base + R*stride) handled by `lane` of `lanes`.
+template <int OP>
+__device__ __forceinline__ State accumulate_row(const RedArgs &a, long long base, int lane, int lanes) {
+    State s = Reducer<OP>::init();
+    const long long R = a.R;
+    if (a.vec4) {
+        const float4 *p = reinterpret_cast<const float4 *>(a.in + base);
+        const long long nv = R / 4;
+        for (long long v = lane; v < nv; v += lanes) {
+            const float4 q = __ldg(p + v);
+            Reducer<OP>::add(s, q.x, 4 * v);
+            Reducer<OP>::add(s, q.y, 4 * v + 1);
+            Reducer<OP>::add(s, q.z, 4 * v + 2);
+            Reducer<OP>::add(s, q.w, 4 * v + 3);
+        }
+    } else {
+        const long long st = a.rrun_stride;
+        for (long long j = lane; j < R; j += lanes) Reducer<OP>::add(s, __ldg(a.in + base + j * st), j);
+    }
+    return s;
+}
+
+template <int OP>
+__device__ __forceinline__ State block_reduce(State s, State *shared) {
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    s = warp_reduce<OP>(s);
+    if (lane == 0) shared[warp] = s;
+    __syncthreads();
+    if (warp == 0) {
+        s = lane < static_cast<int>(blockDim.x / 32) ? shared[lane] : Reducer<OP>::init();
+        s = warp_reduce<OP>(s);
+        if (lane == 0) shared[0] = s;
+    }
+    __syncthreads();
+    s = shared[0];
+    __syncthreads();
+    return s;
+}
+
+// One warp per row (short rows).
+template <int OP>
+__global__ void __launch_bounds__(256) k_row_warp(const RedArgs a) {
+    const int lane = threadIdx.x % 32;
+    const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x / 32);
+    for (long long o = static_cast<long long>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32; o < a.nout; o += warps) {
+        const long long base = kept_offset(a, static_cast<unsigned int>(o));
+        State s = accumulate_row<OP>(a, base, lane, 32);
+        s = warp_reduce<OP>(s);
+        if (lane == 0) store_result<OP>(a, o, s);
+    }
+}
+
+// One CTA per row (long rows).
+template <int OP>
+__global__ void __launch_bounds__(512) k_row_block(const RedArgs a) {
+    __shared__ State shared[32];
+    for (long long o = blockIdx.x; o < a.nout; o += gridDim.x) {
+        const long long base = kept_offset(a, static_cast<unsigned int>(o));
+        State s = accumulate_row<OP>(a, base, threadIdx.x, blockDim.x);
+        s = block_reduce<OP>(s, shared);
+        if (threadIdx.x == 0) store_result<OP>(a, o, s);
+    }
+}
+
+// One thread per (output, chunk); reduced coordinates walked with an odometer.
+template <int OP>
+__global__ void __launch_bounds__(256) k_per_output(const RedArgs a) {
+    const long long total = a.nout * a.chunks;
+    for (long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
+         t += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long c = t / a.nout;  // chunk-major: neighbouring threads share a chunk
+        const long long o = t - c * a.nout;
+        const long long per = (a.R + a.chunks - 1) / a.chunks;
+        const long long r0 = c * per;
+        const long long r1 = r0 + per < a.R ? r0 + per : a.R;
+        State s = Reducer<OP>::init();
+        if (r0 < r1) {
+            const long long base = kept_offset(a, static_cast<unsigned int>(o));
+            unsigned int coord[MTC_MAX_RANK];
+            long long off = base;
+            long long rem = r0;
+            for (int d = a.rrank - 1; d >= 0; --d) {
+                coord[d] = static_cast<unsigned int>(rem % a.rshape[d]);
+                rem /= a.rshape[d];
+                off += static_cast<long long>(coord[d]) * a.rstr[d];
+            }
+            const int inner = a.rrank - 1;
+            for (long long r = r0; r < r1; ++r) {
+                Reducer<OP>::add(s, __ldg(a.in + off), r);
+                // advance the odometer
+                if (++coord[inner] < a.rshape[inner]) {
+                    off += a.rstr[inner];
+                } else {
+                    off -= static_cast<long long>(a.rshape[inner] - 1) * a.rstr[inner];
+                    coord[inner] = 0;
+                    for (int d = inner - 1; d >= 0; --d) {
+                        if (++coord[d] < a.rshape[d]) {
+                            off += a.rstr[d];
+                            break;
+                        }
+                        off -= static_cast<long long>(a.rshape[d] - 1) * a.rstr[d];
+                        coord[d] = 0;
+                    }
+                }
+            }
+        }
+        if (a.chunks == 1) store_result<OP>(a, o, s);
+        else a.partial[o * a.chunks + c] = s;
+    }
+}
+
+// Merges the chunk partials of every output in chunk order.
+template <int OP>
+__global__ void __launch_bounds__(256) k_finalize(const RedArgs a) {
+    for (long long o = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; o < a.nout;
+         o += static_cast<long long>(gridDim.x) * blockDim.x) {
+        State s = a.partial[o * a.chunks];
+        for (int c = 1; c < a.chunks; ++c) Reducer<OP>::merge(s, a.partial[o * a.chunks + c]);
+        store_result<OP>(a, o, s);
+    }
+}
+
+// log-softmax of contiguous rows: online (max, sum) pass, then x - lse written
+// in a second pass that re-reads the row from L2.
+__global__ void __launch_bounds__(512) k_log_softmax_rows(const RedArgs a) {
+    __shared__ State shared[32];
+    for (long long o = blockIdx.x; o < a.nout; o += gridDim.x) {
+        const long long base = kept_offset(a, static_cast<unsigned int>(o));
+        State s = accumulate_row<MTC_OP_LOGSUMEXP>(a, base, threadIdx.x, blockDim.x);
+        s = block_reduce<MTC_OP_LOGSUMEXP>(s, shared);
+        const float lse = Reducer<MTC_OP_LOGSUMEXP>::result(s);
+        float *dst = a.out_f + a.out_off + o * a.out_row_stride;
+        if (a.vec4) {
+            const float4 *p = reinterpret_cast<const float4 *>(a.in + base);
+            float4 *q = reinterpret_cast<float4 *>(dst);
+            for (long long v = threadIdx.x; v < a.R / 4; v += blockDim.x) {
+                float4 x = __ldg(p + v);
+                x.x = __fsub_rn(x.x, lse);
+                x.y = __fsub_rn(x.y, lse);
+                x.z = __fsub_rn(x.z, lse);
+                x.w = __fsub_rn(x.w, lse);
+                q[v] = x;
+            }
+        } else {
+            for (long long j = threadIdx.x; j < a.R; j += blockDim.x)
+                dst[j] = __fsub_rn(__ldg(a.in + base + j * a.rrun_stride), lse);
+        }
+    }
+}
+
+struct RedPlan {
+    RedArgs args;
+    bool row = false;
+    bool empty_out = false;
+};
+
+int plan_reduction(const mtc_desc *in, const int64_t *axes, int n_axes, RedPlan &plan) {
+    RedArgs &a = plan.args;
+    std::memset(&a, 0, sizeof(a));
+    bool reduced[MTC_MAX_RANK] = {};
+    for (int i = 0; i < n_axes; ++i) {
+        if (axes[i] < 0 || axes[i] >= in->rank) return fail(MTC_ERR_OUT_OF_RANGE, "reduction axis out of range");
+        if (reduced[axes[i]]) return fail(MTC_ERR_INVALID_ARGUMENT, "reduction axes contain a duplicate");
+        reduced[axes[i]] = true;
+    }
+    // kept and reduced axes, extent-1 axes dropped, then folded where strides chain
+    long long nout = 1, R = 1;
+    int kr = 0, rr = 0;
+    int64_t kshape[MTC_MAX_RANK], kstr[MTC_MAX_RANK], rshape[MTC_MAX_RANK], rstr[MTC_MAX_RANK];
+    for (int d = 0; d < in->rank; ++d) {
+        const int64_t e = in->shape[d];
+        if (reduced[d]) R *= e; else nout *= e;
+        if (e == 1) continue;
+        if (reduced[d]) {
+            if (rr > 0 && rstr[rr - 1] == in->strides[d] * e) {
+                rshape[rr - 1] *= e;
+                rstr[rr - 1] = in->strides[d];
+            } else {
+                rshape[rr] = e;
+                rstr[rr] = in->strides[d];
+                ++rr;
+            }
+        } else {
+            if (kr > 0 && kstr[kr - 1] == in->strides[d] * e) {
+                kshape[kr - 1] *= e;
+                kstr[kr - 1] = in->strides[d];
+            } else {
+                kshape[kr] = e;
+                kstr[kr] = in->strides[d];
+                ++kr;
+            }
+        }
+    }
+    a.nout = nout;
+    a.R = R;
+    a.in = static_cast<const float *>(in->data);
+    a.in_off = in->offset;
+    plan.empty_out = (nout == 0);
+    if (nout >= (1ll << 32)) return fail(MTC_ERR_UNSUPPORTED, "reduction with 2^32 or more outputs");
+    a.krank = kr;
+    for (int d = 0; d < kr; ++d) {
+        a.kshape[d] = static_cast<unsigned int>(kshape[d]);
+        a.kdiv[d] = make_fastdiv(static_cast<uint32_t>(kshape[d]));
+        a.kstr[d] = kstr[d];
+    }
+    a.rrank = rr;
+    for (int d = 0; d < rr; ++d) {
+        if (rshape[d] >= (1ll << 32)) return fail(MTC_ERR_UNSUPPORTED, "reduced extent of 2^32 or more");
+        a.rshape[d] = static_cast<unsigned int>(rshape[d]);
+        a.rstr[d] = rstr[d];
+    }
+    plan.row = (rr == 1 && (rstr[0] == 1 || rstr[0] == -1) && R >= 32);
+    if (a.rrank == 0) {
+        // every reduced axis has extent 1 (or there is none): a one-element walk
+        a.rrank = 1;
+        a.rshape[0] = 1;
+        a.rstr[0] = 0;
+    }
+    if (plan.row) {
+        a.rrun_stride = rstr[0];
+        bool vec = rstr[0] == 1 && R % 4 == 0 && (reinterpret_cast<uintptr_t>(a.in + a.in_off) % 16) == 0;
+        for (int d = 0; d < kr && vec; ++d) vec = (kstr[d] % 4) == 0;
+        a.vec4 = vec ? 1 : 0;
+    }
+    return MTC_OK;
+}
+
+template <int OP>
+int run_reduction(RedPlan &p, cudaStream_t stream) {
+    RedArgs &a = p.args;
+    if (p.empty_out) return MTC_OK;
+    const int sms = sm_count(current_device());
+    if (p.row) {
+        if (a.R <= 2048) {
+            long long blocks = (a.nout + 7) / 8;
+            if (blocks > static_cast<long long>(sms) * 8) blocks = static_cast<long long>(sms) * 8;
+            k_row_warp<OP><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+        } else {
+            long long blocks = a.nout;
+            if (blocks > static_cast<long long>(sms) * 4) blocks = static_cast<long long>(sms) * 4;
+            k_row_block<OP><<<static_cast<unsigned>(blocks), 512, 0, stream>>>(a);
+        }
+        return check_launch("row reduction");
+    }
+    // per-output kernel: split the reduction so the grid fills the machine
+    const long long target = static_cast<long long>(sms) * 2048;
+    long long chunks = 1;
+    if (a.nout < target && a.R > 64) {
+        chunks = (target + a.nout - 1) / a.nout;
+        const long long max_chunks = (a.R + 63) / 64;
+        if (chunks > max_chunks) chunks = max_chunks;
+        if (chunks > 4096) chunks = 4096;
+    }
+    a.chunks = static_cast<int>(chunks);
+    void *scratch = nullptr;
+    if (chunks > 1) {
+        MTC_TRY(scratch_alloc(static_cast<size_t>(a.nout * chunks) * sizeof(State), stream, &scratch));
+        a.partial = static_cast<State *>(scratch);
+    }
+    long long blocks = (a.nout * a.chunks + 255) / 256;
+    if (blocks > static_cast<long long>(sms) * 8) blocks = static_cast<long long>(sms) * 8;
+    if (blocks < 1) blocks = 1;
+    k_per_output<OP><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+    int rc = check_launch("reduction");
+    if (rc == MTC_OK && a.chunks > 1) {
+        long long fb = (a.nout + 255) / 256;
+        if (fb > static_cast<long long>(sms) * 8) fb = static_cast<long long>(sms) * 8;
+        k_finalize<OP><<<static_cast<unsigned>(fb), 256, 0, stream>>>(a);
+        rc = check_launch("reduction finalize");
+    }
+    scratch_free(scratch, stream);
+    return rc;
+}
+
+bool contiguous(const mtc_desc &d) {
+    int64_t expect = 1;
+    for (int i = d.rank - 1; i >= 0; --i) {
+        if (d.shape[i] != 1 && d.strides[i] != expect) return false;
+        expect *= d.shape[i];
+    }
+    return true;
+}
+
+}  // namespace
+}  // namespace mtc
+
+using namespace mtc;
+
+extern "C" int mtc_reduce(int32_t op, const mtc_desc *in, const int64_t *axes, int32_t n_axes, const mtc_desc *out,
+                          void *stream) {
+    clear_error();
+    MTC_TRY(validate(in, "input"));
+    MTC_TRY(validate(out, "output"));
+    if (in->dtype != MTC_FLOAT32) return fail(MTC_ERR_LOGIC, "reductions require a Float32 input");
+    const int want = op == MTC_OP_ARGMAX ? MTC_INT64 : MTC_FLOAT32;
+    if (out->dtype != want) return fail(MTC_ERR_INVALID_ARGUMENT, "reduction output has the wrong dtype");
+    if (n_axes < 0 || n_axes > in->rank || (n_axes > 0 && axes == nullptr))
+        return fail(MTC_ERR_INVALID_ARGUMENT, "bad reduction axes");
+    if (!contiguous(*out)) return fail(MTC_ERR_INVALID_ARGUMENT, "reduction output must be contiguous");
+    RedPlan p;
+    MTC_TRY(plan_reduction(in, axes, n_axes, p));
+    if (numel_of(*out) != p.args.nout) return fail(MTC_ERR_INVALID_ARGUMENT, "reduction output size mismatch");
+    if (op == MTC_OP_ARGMAX && n_axes != 1) return fail(MTC_ERR_INVALID_ARGUMENT, "argmax reduces exactly one axis");
+    if (op == MTC_OP_ARGMAX && p.args.R == 0 && p.args.nout > 0)
+        return fail(MTC_ERR_INVALID_ARGUMENT, "argmax of an empty axis");
+    p.args.out = out->data;
+    p.args.out_off = out->offset;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (op) {
+    case MTC_OP_SUM: return run_reduction<MTC_OP_SUM>(p, s);
+    case MTC_OP_LOGSUMEXP: return run_reduction<MTC_OP_LOGSUMEXP>(p, s);
+    case MTC_OP_MAX: return run_reduction<MTC_OP_MAX>(p, s);
+    case MTC_OP_ARGMAX: return run_reduction<MTC_OP_ARGMAX>(p, s);
+    default: return fail(MTC_ERR_INVALID_ARGUMENT, "unknown reduction op 0x%04x", op);
+    }
+}
+
+extern "C" int mtc_log_softmax(const mtc_desc *in, int64_t axis, const mtc_desc *out, void *stream) {
+    clear_error();
+    MTC_TRY(validate(in, "input"));
+    MTC_TRY(validate(out, "output"));
+    if (in->dtype != MTC_FLOAT32 || out->dtype != MTC_FLOAT32) return fail(MTC_ERR_LOGIC, "log-softmax requires Float32");
+    if (axis < 0 || axis >= in->rank) return fail(MTC_ERR_OUT_OF_RANGE, "log-softmax axis out of range");
+    if (in->rank != out->rank) return fail(MTC_ERR_INVALID_ARGUMENT, "log-softmax shape mismatch");
+    for (int d = 0; d < in->rank; ++d)
+        if (in->shape[d] != out->shape[d]) return fail(MTC_ERR_INVALID_ARGUMENT, "log-softmax shape mismatch");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool last = (axis == in->rank - 1);
+    if (last && contiguous(*out) && in->shape[axis] >= 32) {
+        RedPlan p;
+        MTC_TRY(plan_reduction(in, &axis, 1, p));
+        if (p.empty_out) return MTC_OK;
+        if (p.row) {
+            RedArgs &a = p.args;
+            a.out_f = static_cast<float *>(out->data);
+            a.out_off = out->offset;
+            a.out_row_stride = in->shape[axis];
+            if (a.vec4) a.vec4 = ((reinterpret_cast<uintptr_t>(a.out_f + a.out_off) % 16) == 0) ? 1 : 0;
+            const int sms = sm_count(current_device());
+            long long blocks = a.nout;
+            if (blocks > static_cast<long long>(sms) * 4) blocks = static_cast<long long>(sms) * 4;
+            k_log_softmax_rows<<<static_cast<unsigned>(blocks), 512, 0, s>>>(a);
+            return check_launch("log-softmax");
+        }
+    }
+    // general layout: logsumexp into scratch (kept dimension of extent 1), then subtract
+    mtc_desc lse = *in;
+    int64_t n = 1;
+    for (int d = in->rank - 1; d >= 0; --d) {
+        lse.shape[d] = (d == axis) ? 1 : in->shape[d];
+        lse.strides[d] = n;
+        n *= lse.shape[d];
+    }
+    lse.offset = 0;
+    lse.capacity = n;
+    void *buf = nullptr;
+    MTC_TRY(scratch_alloc(static_cast<size_t>(n > 0 ? n : 1) * 4, s, &buf));
+    lse.data = buf;
+    int rc = mtc_reduce(MTC_OP_LOGSUMEXP, in, &axis, 1, &lse, stream);
+    if (rc == MTC_OK) rc = mtc_binary(MTC_OP_SUBTRACT, in, &lse, out, stream);
+    scratch_free(buf, s);
+    return rc;
+}

@@ -1,0 +1,150 @@
+"""ctypes binding of the workload entry points (host/workloads.hpp).
+
+`Frontend()` loads libminitensor_b200.so: MiniTensor's own C++ front-end
+(Tensor / lazy graph / autograd / nn / AdamW) built with the CUDA backend, so a
+workload placed on `device >= 0` runs on cuda:device through the backend and
+`device = -1` runs the reference CPU kernels.  The same API is exported by the
+oracle library (oracle/_ref/libmtref.so, CPU only) for baselines and parity.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import numpy as np
+
+LIB = Path(__file__).resolve().parent / "lib" / "libminitensor_b200.so"
+
+
+class Frontend:
+    def __init__(self, path: Path | str = LIB):
+        path = Path(path)
+        if not path.exists():
+            raise FileNotFoundError(f"{path} is not built; run __graft_entry__.build()")
+        try:  # PyTorch's CUDA runtime and NCCL first, so one copy of each serves the process
+            import torch  # noqa: F401
+        except ImportError:
+            pass
+        self.lib = ctypes.CDLL(str(path), mode=os.RTLD_GLOBAL)
+        L = self.lib
+        P = ctypes.POINTER
+        vp, i32, i64, u64, f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64, ctypes.c_float
+        sigs = {
+            "mtb_last_error": ([], ctypes.c_char_p),
+            "mtb_has_cuda": ([], ctypes.c_int),
+            "mtb_spiral_train": ([ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, u64, f32, ctypes.c_int,
+                                  P(f32), P(ctypes.c_double)], ctypes.c_int),
+            "mtb_mlp_create": ([ctypes.c_int, i64, i64, i32, i64, u64, f32, P(vp)], ctypes.c_int),
+            "mtb_mlp_destroy": ([vp], None),
+            "mtb_mlp_set_comm": ([vp, vp, i32], ctypes.c_int),
+            "mtb_mlp_load_batch": ([vp, vp, vp, i64], ctypes.c_int),
+            "mtb_mlp_step_resident": ([vp, i32, P(f32)], ctypes.c_int),
+            "mtb_mlp_step_host": ([vp, vp, vp, i64, P(f32)], ctypes.c_int),
+            "mtb_mlp_parameters": ([vp, P(f32), i64], ctypes.c_int),
+            "mtb_mlp_parameter_count": ([vp], i64),
+            "mtb_mlp_synchronize": ([vp], ctypes.c_int),
+            "mtb_mlp_stream": ([vp], vp),
+            "mtb_chain": ([ctypes.c_int, i64, i64, P(f32), P(f32), P(f32), P(f32), P(f32), P(f32)], ctypes.c_int),
+            "mtb_evaluator_stats": ([P(u64)], None),
+            "mtb_evaluator_reset_stats": ([], None),
+        }
+        for name, (args, res) in sigs.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+
+    def _check(self, rc: int, what: str):
+        if rc == 0:
+            return
+        msg = self.lib.mtb_last_error().decode(errors="replace")
+        exc = {1: ValueError, 2: IndexError, 5: OverflowError}.get(rc, RuntimeError)
+        raise exc(f"{what}: {msg}")
+
+    @property
+    def has_cuda(self) -> bool:
+        return bool(self.lib.mtb_has_cuda())
+
+    def spiral_train(self, device: int, steps: int, points: int = 100, hidden: int = 64, seed: int = 0,
+                     lr: float = 1e-2, loss_every: int = 1):
+        losses = np.full(max(steps, 1), np.nan, dtype=np.float32)
+        secs = ctypes.c_double(0.0)
+        self._check(self.lib.mtb_spiral_train(device, steps, points, hidden, seed, lr, loss_every,
+                                              losses.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                              ctypes.byref(secs)), "spiral_train")
+        return losses[:steps], secs.value
+
+    def chain(self, device: int, a, b_storage, row, col, reductions: bool = False):
+        n, m = a.shape
+        out = np.empty((n, m), dtype=np.float32)
+        red = np.empty(m + 2 * n, dtype=np.float32) if reductions else None
+        f = lambda x: np.ascontiguousarray(x, dtype=np.float32).ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        keep = [np.ascontiguousarray(x, dtype=np.float32) for x in (a, b_storage, row, col)]
+        self._check(self.lib.mtb_chain(device, n, m, *[k.ctypes.data_as(ctypes.POINTER(ctypes.c_float)) for k in keep],
+                                       out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                       red.ctypes.data_as(ctypes.POINTER(ctypes.c_float)) if red is not None else None),
+                    "chain")
+        if red is None:
+            return out
+        return out, red[:m], red[m:m + n], red[m + n:]
+
+    def stats(self) -> dict:
+        buf = (ctypes.c_uint64 * 6)()
+        self.lib.mtb_evaluator_stats(buf)
+        keys = ("kernel_steps", "fused_launches", "fused_nodes", "folded_constants", "view_steps", "evaluations")
+        return dict(zip(keys, list(buf)))
+
+    def reset_stats(self):
+        self.lib.mtb_evaluator_reset_stats()
+
+
+class MlpTrainer:
+    """The wide-MLP trainer of host/workloads.cpp on one device."""
+
+    def __init__(self, fe: Frontend, device: int, in_features: int, hidden: int, hidden_layers: int, classes: int,
+                 seed: int, lr: float):
+        self.fe = fe
+        self.in_features = in_features
+        self.h = ctypes.c_void_p()
+        fe._check(fe.lib.mtb_mlp_create(device, in_features, hidden, hidden_layers, classes, seed, lr,
+                                        ctypes.byref(self.h)), "mlp_create")
+
+    def close(self):
+        if self.h:
+            self.fe.lib.mtb_mlp_destroy(self.h)
+            self.h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_comm(self, comm, world: int):
+        self.fe._check(self.fe.lib.mtb_mlp_set_comm(self.h, comm, world), "mlp_set_comm")
+
+    def load_batch(self, x_ptr: int, y_ptr: int, batch: int):
+        self.fe._check(self.fe.lib.mtb_mlp_load_batch(self.h, x_ptr, y_ptr, batch), "mlp_load_batch")
+
+    def step_resident(self, read_loss: bool = False) -> float:
+        loss = ctypes.c_float(0.0)
+        self.fe._check(self.fe.lib.mtb_mlp_step_resident(self.h, int(read_loss), ctypes.byref(loss)), "mlp_step")
+        return loss.value
+
+    def step_host(self, x_ptr: int, y_ptr: int, batch: int) -> float:
+        loss = ctypes.c_float(0.0)
+        self.fe._check(self.fe.lib.mtb_mlp_step_host(self.h, x_ptr, y_ptr, batch, ctypes.byref(loss)), "mlp_step_host")
+        return loss.value
+
+    def parameters(self) -> np.ndarray:
+        n = self.fe.lib.mtb_mlp_parameter_count(self.h)
+        out = np.empty(n, dtype=np.float32)
+        self.fe._check(self.fe.lib.mtb_mlp_parameters(self.h, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n),
+                       "mlp_parameters")
+        return out
+
+    def synchronize(self):
+        self.fe._check(self.fe.lib.mtb_mlp_synchronize(self.h), "mlp_synchronize")
+
+    def stream(self) -> int:
+        return self.fe.lib.mtb_mlp_stream(self.h) or 0

@@ -1,0 +1,436 @@
+// Benchmark and parity workloads over MiniTensor's public API (see workloads.hpp).
+#include "workloads.hpp"
+
+#include <chrono>
+#include <cmath>
+#include <limits>
+#include <memory>
+#include <optional>
+#include <span>
+#include <stdexcept>
+#include <string>
+#include <string_view>
+#include <vector>
+
+#include <minitensor/data.hpp>
+#include <minitensor/evaluation.hpp>
+#include <minitensor/nn/gradients.hpp>
+#include <minitensor/nn/leafification.hpp>
+#include <minitensor/nn/loss.hpp>
+#include <minitensor/nn/module.hpp>
+#include <minitensor/nn/modules/linear.hpp>
+#include <minitensor/nn/optimizers/adamw.hpp>
+#include <minitensor/nn/parameters.hpp>
+#include <minitensor/ops.hpp>
+#include <minitensor/random.hpp>
+#include <minitensor/tensor.hpp>
+
+#include "mtcuda.h"
+
+#ifndef MTB_CPU_ONLY
+#include "cuda_backend.hpp"
+#include "ops_ext.hpp"
+#include "tensor/execution/environment.hpp"
+#include "tensor/graph/value.hpp"
+#include "tensor/storage/materialization.hpp"
+#include "tensor/tensor_access.hpp"
+#endif
+
+namespace mt = minitensor;
+
+namespace {
+
+thread_local std::string t_error;
+
+template <typename F>
+int guarded(F &&f) {
+    t_error.clear();
+    try {
+        f();
+        return MTC_OK;
+    } catch (const std::out_of_range &e) {
+        t_error = e.what();
+        return MTC_ERR_OUT_OF_RANGE;
+    } catch (const std::invalid_argument &e) {
+        t_error = e.what();
+        return MTC_ERR_INVALID_ARGUMENT;
+    } catch (const std::overflow_error &e) {
+        t_error = e.what();
+        return MTC_ERR_OVERFLOW;
+    } catch (const std::logic_error &e) {
+        t_error = e.what();
+        return MTC_ERR_LOGIC;
+    } catch (const std::exception &e) {
+        t_error = e.what();
+        return MTC_ERR_RUNTIME;
+    }
+}
+
+mt::Device device_of(int device) {
+    if (device < 0) return mt::Device::cpu();
+#ifdef MTB_CPU_ONLY
+    throw std::invalid_argument{"this build has no CUDA device"};
+#else
+    return mt::Device::cuda(static_cast<std::uint32_t>(device));
+#endif
+}
+
+// ReLU as the exact composite of reference ops (gradient 0.5 at 0); the CUDA
+// evaluator fuses it into one kernel with its neighbours.
+mt::Tensor relu(const mt::Tensor &x) { return (x + mt::abs(x)) * 0.5F; }
+
+// Dense MLP: Linear layers with ReLU between them (none after the last).
+class DenseMlp final {
+  public:
+    class ParameterTree final {
+      public:
+        [[nodiscard]] const std::vector<mt::nn::Linear::ParameterTree> &layers() const noexcept { return layers_; }
+
+      private:
+        explicit ParameterTree(std::vector<mt::nn::Linear::ParameterTree> layers) : layers_{std::move(layers)} {}
+
+        template <typename Self, typename Visitor>
+        static void visit_members(Self &self, Visitor &visitor) {
+            static constexpr std::string_view names[] = {"layer0", "layer1", "layer2", "layer3",
+                                                         "layer4", "layer5", "layer6", "layer7"};
+            for (std::size_t i = 0; i < self.layers_.size(); ++i) visitor.child(names[i], self.layers_[i]);
+        }
+
+        std::vector<mt::nn::Linear::ParameterTree> layers_;
+        friend class DenseMlp;
+        friend class minitensor::nn::ParameterTreeAccess;
+    };
+
+    explicit DenseMlp(std::vector<mt::Extent> widths) {
+        if (widths.size() < 2 || widths.size() > 9) throw std::invalid_argument{"MLP needs 1 to 8 layers"};
+        for (std::size_t i = 0; i + 1 < widths.size(); ++i) layers_.emplace_back(widths[i], widths[i + 1]);
+    }
+
+    [[nodiscard]] ParameterTree initialize(mt::nn::ParameterBuilder &builder, mt::RandomKey key,
+                                           mt::TensorOptions options = {}) const {
+        // one key per layer: split off the first, keep splitting the rest
+        std::vector<mt::nn::Linear::ParameterTree> trees;
+        mt::RandomKey rest = key;
+        for (std::size_t i = 0; i < layers_.size(); ++i) {
+            auto [layer_key, next] = mt::split(rest);
+            trees.push_back(layers_[i].initialize(builder, layer_key, options));
+            rest = next;
+        }
+        return ParameterTree{std::move(trees)};
+    }
+
+    [[nodiscard]] mt::Tensor operator()(const mt::nn::ParameterMap &parameters, const ParameterTree &tree,
+                                        const mt::Tensor &input) const {
+        mt::Tensor h = input;
+        for (std::size_t i = 0; i < layers_.size(); ++i) {
+            h = layers_[i](parameters, tree.layers()[i], h);
+            if (i + 1 < layers_.size()) h = relu(h);
+        }
+        return h;
+    }
+
+    [[nodiscard]] std::size_t depth() const noexcept { return layers_.size(); }
+
+  private:
+    std::vector<mt::nn::Linear> layers_;
+};
+
+using Snapshot = mt::nn::ParameterSnapshot<DenseMlp::ParameterTree>;
+
+}  // namespace
+
+extern "C" {
+
+const char *mtb_last_error(void) { return t_error.c_str(); }
+
+int mtb_has_cuda(void) {
+#ifdef MTB_CPU_ONLY
+    return 0;
+#else
+    return 1;
+#endif
+}
+
+int mtb_spiral_train(int device, int steps, int points, int hidden, uint64_t seed, float lr, int loss_every,
+                     float *losses, double *seconds) {
+    return guarded([&] {
+        if (points < 2 || steps < 0 || hidden < 1) throw std::invalid_argument{"bad spiral configuration"};
+        const mt::Device dev = device_of(device);
+        // keys as in demo.cpp:163-164
+        auto [dataset_key, model_key] = mt::split(mt::RandomKey{seed});
+        auto [train_key, test_key] = mt::split(dataset_key);
+        (void)test_key;
+        constexpr int classes = 3;
+        const int n = classes * points;
+        const std::vector<float> noise = mt::to_vector(mt::normal(mt::Shape{n}, 0.0F, 0.2F, train_key));
+        std::vector<float> xs(static_cast<std::size_t>(n) * 2);
+        std::vector<std::int64_t> ys(static_cast<std::size_t>(n));
+        for (int k = 0; k < classes; ++k) {
+            for (int i = 0; i < points; ++i) {
+                const int s = k * points + i;
+                const float r = static_cast<float>(i) / static_cast<float>(points - 1);  // linspace(0, 1)
+                const float theta = 4.0F * static_cast<float>(k) + 4.0F * r + noise[static_cast<std::size_t>(s)];
+                xs[2 * s] = r * std::sin(theta);
+                xs[2 * s + 1] = r * std::cos(theta);
+                ys[s] = k;
+            }
+        }
+        const mt::Tensor x = mt::from_data(xs, mt::Shape{n, 2}, dev);
+        const mt::Tensor y = mt::from_data(ys, mt::Shape{n}, dev);
+        const DenseMlp model({2, hidden, hidden, classes});
+        auto params = mt::nn::initialize(model, model_key, mt::TensorOptions{mt::DType::Float32, dev});
+        const mt::nn::AdamW optimizer(lr, 0.0F);
+        auto state = optimizer.initialize(params);
+        const auto t0 = std::chrono::steady_clock::now();
+        for (int step = 0; step < steps; ++step) {
+            const mt::Tensor logits = mt::nn::forward(model, params, x);
+            const mt::Tensor loss = mt::nn::categorical_cross_entropy_with_logits(logits, y);
+            if (losses) {
+                losses[step] = (loss_every > 0 && step % loss_every == 0) ? mt::item<float>(loss)
+                                                                          : std::numeric_limits<float>::quiet_NaN();
+            }
+            auto grads = mt::nn::parameter_gradients(loss, params);
+            auto [next_params, next_state] = optimizer.step(std::move(params), std::move(state), grads);
+            params = mt::nn::leafify_parameter_values(std::move(next_params));
+            state = mt::nn::leafify_optimizer_state(std::move(next_state));
+        }
+        // the final parameters are the step's result: wait for them
+        for (const auto &[id, p] : params.parameters()) {
+            (void)id;
+            (void)mt::to_vector(mt::reshape(p.value, mt::Shape{static_cast<mt::Extent>(p.value.numel())}));
+            break;
+        }
+        if (seconds) seconds[0] = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    });
+}
+
+}  // extern "C"
+
+namespace {
+
+struct MlpTrainer {
+    mt::Device device;
+    DenseMlp model;
+    Snapshot params;
+    mt::nn::AdamW optimizer;
+    mt::nn::AdamW::State state;
+    std::vector<mt::nn::ParameterId> order;  // layer order: weight, bias, ...
+    void *comm = nullptr;
+    int world = 1;
+    std::optional<mt::Tensor> x_resident;
+    std::optional<mt::Tensor> y_resident;
+
+    MlpTrainer(mt::Device dev, std::vector<mt::Extent> widths, uint64_t seed, float lr)
+        : device{dev}, model{std::move(widths)},
+          params{mt::nn::initialize(model, mt::RandomKey{seed}, mt::TensorOptions{mt::DType::Float32, dev})},
+          optimizer{lr, 0.0F}, state{optimizer.initialize(params)} {
+        for (const auto &layer : params.tree().layers()) {
+            order.push_back(layer.weight());
+            if (layer.bias()) order.push_back(*layer.bias());
+        }
+    }
+
+    float step(const mt::Tensor &x, const mt::Tensor &y, bool read_loss) {
+        const mt::Tensor logits = mt::nn::forward(model, params, x);
+        const mt::Tensor loss = mt::nn::categorical_cross_entropy_with_logits(logits, y);
+        auto grads = mt::nn::parameter_gradients(loss, params);
+        if (world > 1) allreduce(grads, loss);
+        auto [next_params, next_state] = optimizer.step(std::move(params), std::move(state), grads);
+        grads.clear();
+        params = mt::nn::leafify_parameter_values(std::move(next_params));
+        state = mt::nn::leafify_optimizer_state(std::move(next_state));
+        return read_loss ? mt::item<float>(loss) : 0.0F;
+    }
+
+    void allreduce(mt::nn::ParameterGradients &grads, const mt::Tensor &loss) {
+#ifdef MTB_CPU_ONLY
+        (void)grads;
+        (void)loss;
+        throw std::invalid_argument{"data parallelism needs the CUDA build"};
+#else
+        // materialise loss and gradients (one evaluation), then sum them in place
+        std::vector<mt::Tensor> roots{loss};
+        for (const auto &id : order) roots.push_back(grads.at(id));
+        std::vector<mt::Tensor> leaves = mt::leafify(roots);
+        std::vector<void *> buffers;
+        std::vector<std::size_t> counts;
+        for (std::size_t i = 0; i < order.size(); ++i) {
+            mt::Tensor g = leaves[i + 1];
+            const auto &value = mt::detail::TensorAccess::value(g);
+            const auto *m = value->materialization();
+            // the region of a permuted dense layout is [offset, offset + numel)
+            const auto &layout = m->layout();
+            std::int64_t span = 1;
+            for (std::size_t d = 0; d < g.rank(); ++d)
+                span += (g.shape()[d] - 1) * std::abs(layout.stride(d));
+            if (span != static_cast<std::int64_t>(g.numel())) {
+                g = mt::leafify(mt::contiguous(g));
+            }
+            const auto &v2 = mt::detail::TensorAccess::value(g);
+            const auto *m2 = v2->materialization();
+            auto *buf = dynamic_cast<mt::detail::cuda::CudaBuffer *>(m2->buffer_ref().get());
+            std::int64_t lo = m2->layout().offset();
+            for (std::size_t d = 0; d < g.rank(); ++d)
+                if (m2->layout().stride(d) < 0) lo += (g.shape()[d] - 1) * m2->layout().stride(d);
+            buffers.push_back(static_cast<float *>(buf->data()) + lo);
+            counts.push_back(g.numel());
+            grads.at(order[i]) = g;
+        }
+        auto &rt = dynamic_cast<mt::detail::cuda::CudaRuntime &>(
+            mt::detail::environment().runtime_for(device));
+        mt::detail::cuda::check(mtc_comm_allreduce_f32(comm, buffers.data(), counts.data(),
+                                                       static_cast<int32_t>(buffers.size()), 1.0F / world, rt.stream()),
+                                "gradient all-reduce");
+#endif
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+int mtb_mlp_create(int device, int64_t in_features, int64_t hidden, int32_t hidden_layers, int64_t classes,
+                   uint64_t seed, float lr, void **handle) {
+    return guarded([&] {
+        std::vector<mt::Extent> widths{in_features};
+        for (int i = 0; i < hidden_layers; ++i) widths.push_back(hidden);
+        widths.push_back(classes);
+        *handle = new MlpTrainer(device_of(device), std::move(widths), seed, lr);
+    });
+}
+
+void mtb_mlp_destroy(void *handle) { delete static_cast<MlpTrainer *>(handle); }
+
+int mtb_mlp_set_comm(void *handle, void *comm, int32_t world) {
+    return guarded([&] {
+        auto *t = static_cast<MlpTrainer *>(handle);
+        t->comm = comm;
+        t->world = world;
+    });
+}
+
+int mtb_mlp_load_batch(void *handle, const float *x, const int64_t *labels, int64_t batch) {
+    return guarded([&] {
+        auto *t = static_cast<MlpTrainer *>(handle);
+        const mt::Extent in = t->params.parameters().get(t->order.front()).value.shape()[1];
+        t->x_resident = mt::from_data(std::span<const float>(x, static_cast<std::size_t>(batch * in)),
+                                      mt::Shape{batch, in}, t->device);
+        t->y_resident = mt::from_data(std::span<const std::int64_t>(labels, static_cast<std::size_t>(batch)),
+                                      mt::Shape{batch}, t->device);
+    });
+}
+
+int mtb_mlp_step_resident(void *handle, int32_t read_loss, float *loss) {
+    return guarded([&] {
+        auto *t = static_cast<MlpTrainer *>(handle);
+        if (!t->x_resident) throw std::logic_error{"no resident batch loaded"};
+        const float l = t->step(*t->x_resident, *t->y_resident, read_loss != 0);
+        if (loss) *loss = l;
+    });
+}
+
+int mtb_mlp_step_host(void *handle, const float *x, const int64_t *labels, int64_t batch, float *loss) {
+    return guarded([&] {
+        auto *t = static_cast<MlpTrainer *>(handle);
+        const mt::Extent in = t->params.parameters().get(t->order.front()).value.shape()[1];
+        const mt::Tensor xt = mt::from_data(std::span<const float>(x, static_cast<std::size_t>(batch * in)),
+                                            mt::Shape{batch, in}, t->device);
+        const mt::Tensor yt = mt::from_data(std::span<const std::int64_t>(labels, static_cast<std::size_t>(batch)),
+                                            mt::Shape{batch}, t->device);
+        const float l = t->step(xt, yt, true);
+        if (loss) *loss = l;
+    });
+}
+
+int64_t mtb_mlp_parameter_count(void *handle) {
+    auto *t = static_cast<MlpTrainer *>(handle);
+    int64_t n = 0;
+    for (const auto &id : t->order) n += static_cast<int64_t>(t->params.parameters().get(id).value.numel());
+    return n;
+}
+
+int mtb_mlp_parameters(void *handle, float *out, int64_t capacity) {
+    return guarded([&] {
+        auto *t = static_cast<MlpTrainer *>(handle);
+        int64_t pos = 0;
+        for (const auto &id : t->order) {
+            const mt::Tensor &v = t->params.parameters().get(id).value;
+            const std::vector<float> host = mt::to_vector(v);
+            if (pos + static_cast<int64_t>(host.size()) > capacity) throw std::out_of_range{"parameter buffer too small"};
+            std::copy(host.begin(), host.end(), out + pos);
+            pos += static_cast<int64_t>(host.size());
+        }
+    });
+}
+
+int mtb_mlp_synchronize(void *handle) {
+    return guarded([&] {
+        auto *t = static_cast<MlpTrainer *>(handle);
+#ifndef MTB_CPU_ONLY
+        if (t->device.type() == mt::DeviceType::Cuda) {
+            auto &rt = dynamic_cast<mt::detail::cuda::CudaRuntime &>(mt::detail::environment().runtime_for(t->device));
+            mt::detail::cuda::check(mtc_stream_synchronize(rt.stream()), "synchronize");
+        }
+#else
+        (void)t;
+#endif
+    });
+}
+
+void *mtb_mlp_stream(void *handle) {
+#ifndef MTB_CPU_ONLY
+    auto *t = static_cast<MlpTrainer *>(handle);
+    if (t->device.type() != mt::DeviceType::Cuda) return nullptr;
+    auto &rt = dynamic_cast<mt::detail::cuda::CudaRuntime &>(mt::detail::environment().runtime_for(t->device));
+    return rt.stream();
+#else
+    (void)handle;
+    return nullptr;
+#endif
+}
+
+int mtb_chain(int device, int64_t n, int64_t m, const float *a, const float *b_storage, const float *row,
+              const float *col, float *out, float *reductions) {
+    return guarded([&] {
+        const mt::Device dev = device_of(device);
+        const auto N = static_cast<std::size_t>(n), M = static_cast<std::size_t>(m);
+        const mt::Tensor A = mt::from_data(std::span<const float>(a, N * M), mt::Shape{n, m}, dev);
+        const mt::Tensor Bs = mt::from_data(std::span<const float>(b_storage, N * M), mt::Shape{m, n}, dev);
+        const mt::Tensor B = mt::transpose(Bs);  // [n, m] view with strides {1, n}
+        const mt::Tensor r = mt::from_data(std::span<const float>(row, M), mt::Shape{1, m}, dev);
+        const mt::Tensor c = mt::from_data(std::span<const float>(col, N), mt::Shape{n, 1}, dev);
+        const mt::Tensor Y = relu(A * B + r) * mt::exp(-c);
+        const std::vector<float> y = mt::to_vector(Y);
+        std::copy(y.begin(), y.end(), out);
+        if (reductions) {
+            const std::vector<float> s0 = mt::to_vector(mt::sum(Y, {0}));
+            const std::vector<float> s1 = mt::to_vector(mt::sum(Y, {1}));
+            const std::vector<float> l1 = mt::to_vector(mt::logsumexp(Y, {1}));
+            std::copy(s0.begin(), s0.end(), reductions);
+            std::copy(s1.begin(), s1.end(), reductions + M);
+            std::copy(l1.begin(), l1.end(), reductions + M + N);
+        }
+    });
+}
+
+void mtb_evaluator_stats(uint64_t *out6) {
+#ifndef MTB_CPU_ONLY
+    const auto &s = mt::detail::cuda::evaluator_stats();
+    out6[0] = s.kernel_steps;
+    out6[1] = s.fused_launches;
+    out6[2] = s.fused_nodes;
+    out6[3] = s.folded_constants;
+    out6[4] = s.view_steps;
+    out6[5] = s.evaluations;
+#else
+    for (int i = 0; i < 6; ++i) out6[i] = 0;
+#endif
+}
+
+void mtb_evaluator_reset_stats(void) {
+#ifndef MTB_CPU_ONLY
+    mt::detail::cuda::evaluator_stats() = {};
+#endif
+}
+
+}  // extern "C"

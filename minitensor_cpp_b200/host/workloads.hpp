@@ -1,0 +1,65 @@
+// Benchmark and parity workloads written against MiniTensor's unchanged public
+// API (the way a user program such as demo.cpp is written).  The same source is
+// compiled into libminitensor_b200.so (any device) and, with MTB_CPU_ONLY, into
+// the oracle library built from the unmodified reference (CPU device only), so
+// both sides run exactly the same graphs.  C ABI for the Python drivers.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// Thread-local message of the last failing call.
+const char *mtb_last_error(void);
+// Status codes follow include/mtcuda.h (0 = ok).
+
+// Spiral classification (3 classes x `points` points, seed 0 keys split as in
+// demo.cpp:163-164), MLP 2 -> hidden -> hidden -> 3 with ReLU, softmax cross
+// entropy, Adam (AdamW(lr, 0)), full batch.  device < 0 = CPU, else cuda:device.
+// losses[s] receives the loss of step s when (s % loss_every == 0), or NaN.
+int mtb_spiral_train(int device, int steps, int points, int hidden, uint64_t seed, float lr, int loss_every,
+                     float *losses, double *seconds);
+
+// Wide MLP trainer: in -> hidden (x layers) -> classes, ReLU, softmax cross
+// entropy, Adam(lr).  Parameters initialised from `seed` (identical on every rank).
+int mtb_mlp_create(int device, int64_t in_features, int64_t hidden, int32_t hidden_layers, int64_t classes,
+                   uint64_t seed, float lr, void **handle);
+void mtb_mlp_destroy(void *handle);
+// Attach a data-parallel communicator (from mtc_comm_init) of `world` ranks:
+// gradients are summed over ranks and scaled by 1/world before the update.
+int mtb_mlp_set_comm(void *handle, void *comm, int32_t world);
+// Upload one batch (host memory; copied to the device) that mtb_mlp_step_resident reuses.
+int mtb_mlp_load_batch(void *handle, const float *x, const int64_t *labels, int64_t batch);
+// One training step on the resident batch; *loss receives the step's loss when read_loss != 0.
+int mtb_mlp_step_resident(void *handle, int32_t read_loss, float *loss);
+// One end-to-end training step from host buffers: the batch is copied host -> device,
+// the step runs, and the loss is read back to the host.
+int mtb_mlp_step_host(void *handle, const float *x, const int64_t *labels, int64_t batch, float *loss);
+// Copies the current parameters (layer by layer: weight [out, in] then bias [out]) to host.
+int mtb_mlp_parameters(void *handle, float *out, int64_t capacity);
+int64_t mtb_mlp_parameter_count(void *handle);
+// Blocks until the device finished all work of this trainer.
+int mtb_mlp_synchronize(void *handle);
+// The CUDA stream the trainer's kernels run on (NULL on the CPU).
+void *mtb_mlp_stream(void *handle);
+
+// relu(A * B^T + row) * exp(-col) through the API on `device` (inputs uploaded
+// from host; B given as the [n, m] storage whose transpose view is used), result
+// copied to `out` [n, m].  reductions (optional, may be NULL) receive
+// sum(Y, 0) [m], sum(Y, 1) [n] and logsumexp(Y, 1) [n].
+int mtb_chain(int device, int64_t n, int64_t m, const float *a, const float *b_storage, const float *row,
+              const float *col, float *out, float *reductions);
+
+// Counters of the fusing evaluator (zeros in the CPU-only build):
+// kernel_steps, fused_launches, fused_nodes, folded_constants, view_steps, evaluations.
+void mtb_evaluator_stats(uint64_t *out6);
+void mtb_evaluator_reset_stats(void);
+// 1 when the library has the CUDA backend, 0 for the CPU-only build.
+int mtb_has_cuda(void);
+
+#ifdef __cplusplus
+}
+#endif

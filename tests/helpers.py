@@ -1,0 +1,56 @@
+"""Shared helpers of the parity tests."""
+from __future__ import annotations
+
+import numpy as np
+
+F32 = np.float32
+
+
+def ordered(x: np.ndarray) -> np.ndarray:
+    """Maps float32 bit patterns onto a monotone int64 line (ulp distance = difference)."""
+    i = np.asarray(x, dtype=F32).view(np.int32).astype(np.int64)
+    return np.where(i < 0, -(i & 0x7FFFFFFF), i)
+
+
+def ulp_diff(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """ulp distance of two float32 arrays; NaN==NaN counts as 0, NaN vs number as huge."""
+    a = np.asarray(a, dtype=F32)
+    b = np.asarray(b, dtype=F32)
+    d = np.abs(ordered(a) - ordered(b))
+    both_nan = np.isnan(a) & np.isnan(b)
+    one_nan = np.isnan(a) ^ np.isnan(b)
+    d = np.where(both_nan, 0, d)
+    return np.where(one_nan, np.iinfo(np.int64).max, d)
+
+
+def assert_ulp(actual, expected, max_ulp: int, what: str = ""):
+    d = ulp_diff(actual, expected)
+    worst = int(d.max()) if d.size else 0
+    assert worst <= max_ulp, f"{what}: {worst} ulp > {max_ulp} (first bad at {np.argmax(d.reshape(-1))})"
+
+
+def assert_bits(actual, expected, what: str = ""):
+    a = np.asarray(actual)
+    e = np.asarray(expected)
+    assert a.shape == e.shape, f"{what}: shape {a.shape} != {e.shape}"
+    if a.dtype == np.float32:
+        ok = (a.view(np.int32) == e.view(np.int32)) | (np.isnan(a) & np.isnan(e))
+    else:
+        ok = a == e
+    assert ok.all(), f"{what}: {int((~ok).sum())} of {ok.size} elements differ; first at {np.argmax(~ok.reshape(-1))}"
+
+
+def assert_rel_sqrtk(actual, expected, k: int, scale=None, what: str = ""):
+    """Reduction / GEMM parity bound: |a - e| <= 1e-5 * sqrt(K) * scale (scale = |e| when None,
+    floored at 1e-30); NaN/inf positions must agree exactly."""
+    a = np.asarray(actual, dtype=np.float64)
+    e = np.asarray(expected, dtype=np.float64)
+    finite = np.isfinite(e)
+    assert (np.isnan(a) == np.isnan(e)).all(), f"{what}: NaN positions differ"
+    assert (a[~finite & ~np.isnan(e)] == e[~finite & ~np.isnan(e)]).all(), f"{what}: infinities differ"
+    s = np.abs(e) if scale is None else np.asarray(scale, dtype=np.float64)
+    tol = 1e-5 * np.sqrt(max(k, 1)) * np.maximum(s, 1e-30)
+    err = np.abs(a - e)
+    bad = finite & (err > tol)
+    assert not bad.any(), (f"{what}: {int(bad.sum())} elements exceed 1e-5*sqrt({k}); worst ratio "
+                           f"{float(np.max(np.where(finite, err / tol, 0))):.3g}")

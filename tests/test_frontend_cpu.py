@@ -1,0 +1,56 @@
+"""The MiniTensor front-end built with the backend behaves exactly like the
+unmodified reference on the CPU device (same graphs, same kernels, same bits),
+and a CUDA device without a GPU is reported the reference's way. CPU only."""
+import numpy as np
+import pytest
+
+from minitensor_cpp_b200.frontend import Frontend, MlpTrainer
+from oracle import refkernels as rk
+
+F = np.float32
+
+
+@pytest.fixture(scope="module")
+def fe():
+    return Frontend()
+
+
+@pytest.fixture(scope="module")
+def ref():
+    return Frontend(rk.LIB_PATH)
+
+
+def test_cpu_device_is_bit_identical_to_reference(fe, ref):
+    a, _ = fe.spiral_train(-1, 30)
+    b, _ = ref.spiral_train(-1, 30)
+    assert np.array_equal(a.view(np.int32), b.view(np.int32))
+    rng = np.random.default_rng(1)
+    args = (rng.uniform(-1, 1, (20, 30)).astype(F), rng.uniform(-1, 1, (30, 20)).astype(F),
+            rng.uniform(-1, 1, 30).astype(F), rng.uniform(-1, 1, 20).astype(F))
+    assert np.array_equal(fe.chain(-1, *args), ref.chain(-1, *args))
+
+
+def test_mlp_trainer_cpu_identical(fe, ref):
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((32, 12)).astype(F)
+    y = rng.integers(0, 5, 32).astype(np.int64)
+    t1 = MlpTrainer(fe, -1, 12, 16, 2, 5, seed=3, lr=1e-2)
+    t2 = MlpTrainer(ref, -1, 12, 16, 2, 5, seed=3, lr=1e-2)
+    t1.load_batch(x.ctypes.data, y.ctypes.data, 32)
+    t2.load_batch(x.ctypes.data, y.ctypes.data, 32)
+    for _ in range(2):
+        assert t1.step_resident(True) == t2.step_resident(True)
+    assert np.array_equal(t1.parameters(), t2.parameters())
+
+
+def test_cuda_device_without_gpu_raises_runtime_error(fe):
+    import ctypes
+
+    n = ctypes.c_int(0)
+    from minitensor_cpp_b200 import abi
+
+    abi.lib().mtc_device_count(ctypes.byref(n))
+    if n.value > 0:
+        pytest.skip("a GPU is visible")
+    with pytest.raises(RuntimeError, match="no runtime is registered"):
+        fe.spiral_train(0, 1)

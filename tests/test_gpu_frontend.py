@@ -1,0 +1,87 @@
+"""End-to-end parity through MiniTensor's own API with the CUDA backend.
+
+The workloads (minitensor_cpp_b200/host/workloads.cpp) run once on cuda:0
+through libminitensor_b200.so and once on the CPU through the oracle library
+(the unmodified reference compiled from its sources).  Tolerances: loss curves
+within 1e-3 relative (1e-5 at step 0), fused elementwise results within 2 ulp,
+parameters after a training step within 1e-5*sqrt(K) of their magnitude.
+"""
+import numpy as np
+import pytest
+
+from helpers import assert_rel_sqrtk, assert_ulp
+from minitensor_cpp_b200.frontend import Frontend, MlpTrainer
+from oracle import mt_oracle as mo
+from oracle import refkernels as rk
+
+pytestmark = pytest.mark.gpu
+
+F = np.float32
+
+
+@pytest.fixture(scope="module")
+def fe(cuda):
+    return Frontend()
+
+
+@pytest.fixture(scope="module")
+def ref():
+    return Frontend(rk.LIB_PATH)
+
+
+def test_spiral_loss_curve_matches_reference(fe, ref):
+    """Config 1: spiral MLP 2-64-64-3, ReLU, Adam(1e-2), full batch, 2000 steps."""
+    steps = 2000
+    gpu_losses, _ = fe.spiral_train(0, steps, loss_every=1)
+    cpu_losses, _ = ref.spiral_train(-1, steps, loss_every=1)
+    assert np.isfinite(gpu_losses).all()
+    rel = np.abs(gpu_losses.astype(np.float64) - cpu_losses) / np.abs(cpu_losses)
+    assert rel[0] <= 1e-5, rel[0]
+    assert rel[:200].max() <= 1e-3, (int(rel[:200].argmax()), float(rel[:200].max()))
+    assert rel[-1] <= 1e-2, float(rel[-1])
+    assert gpu_losses[-1] < 0.2 * gpu_losses[0]
+
+
+def test_fused_chain_through_api(fe, ref):
+    """Config 2's chain relu(A*B^T + row)*exp(-col): one fused launch on the GPU."""
+    rng = np.random.default_rng(3)
+    n, m = 300, 420
+    a = rng.uniform(-1, 1, (n, m)).astype(F)
+    bs = rng.uniform(-1, 1, (m, n)).astype(F)
+    row = rng.uniform(-1, 1, m).astype(F)
+    col = rng.uniform(-1, 1, n).astype(F)
+    fe.reset_stats()
+    y_gpu, s0, s1, l1 = fe.chain(0, a, bs, row, col, reductions=True)
+    stats = fe.stats()
+    y_cpu, r0, r1, rl = ref.chain(-1, a, bs, row, col, reductions=True)
+    assert_ulp(y_gpu, y_cpu, 2, "chain")
+    assert stats["fused_launches"] >= 1 and stats["fused_nodes"] >= 6, stats
+    scale0 = mo.reduce_sum(np.abs(y_cpu), [0])
+    assert_rel_sqrtk(s0, r0, n, scale0, "sum axis 0")
+    assert_rel_sqrtk(s1, r1, m, mo.reduce_sum(np.abs(y_cpu), [1]), "sum axis 1")
+    assert_rel_sqrtk(l1, rl, m, None, "logsumexp axis 1")
+
+
+def test_mlp_training_steps_match_reference(fe, ref):
+    """Config 5's trainer at reduced width: losses and parameters after 3 steps."""
+    rng = np.random.default_rng(5)
+    batch, fin, hid, cls = 256, 96, 160, 10
+    x = rng.standard_normal((batch, fin)).astype(F)
+    y = rng.integers(0, cls, batch).astype(np.int64)
+    g = MlpTrainer(fe, 0, fin, hid, 3, cls, seed=7, lr=1e-3)
+    c = MlpTrainer(ref, -1, fin, hid, 3, cls, seed=7, lr=1e-3)
+    np.testing.assert_array_equal(g.parameters(), c.parameters())  # identical Philox init
+    g.load_batch(x.ctypes.data, y.ctypes.data, batch)
+    c.load_batch(x.ctypes.data, y.ctypes.data, batch)
+    for step in range(3):
+        lg = g.step_resident(read_loss=True)
+        lc = c.step_resident(read_loss=True)
+        assert abs(lg - lc) <= 1e-5 * abs(lc) * np.sqrt(hid), (step, lg, lc)
+    pg, pc = g.parameters(), c.parameters()
+    # Adam normalises the step, so parameters move by ~lr per step: compare on that scale
+    assert np.max(np.abs(pg - pc)) <= 3 * 1e-3 * 1e-2, float(np.max(np.abs(pg - pc)))
+    lh = g.step_host(x.ctypes.data, y.ctypes.data, batch)
+    lc = c.step_host(x.ctypes.data, y.ctypes.data, batch)
+    assert abs(lh - lc) <= 1e-4 * abs(lc), (lh, lc)
+    g.close()
+    c.close()
