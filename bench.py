@@ -1,0 +1,417 @@
+"""Benchmark: wide-MLP data-parallel training through MiniTensor's API on B200.
+
+Workload (the multi-GPU configuration of the benchmark set): MLP
+1024 -> 8192 -> 8192 -> 8192 -> 1000 with ReLU and softmax cross entropy,
+Adam(lr=1e-3), Float32, global batch 65536 split evenly over the ranks,
+gradients all-reduced with NCCL.  Inputs are seeded synthetic N(0,1) rows with
+Int64 labels uniform in [0, 1000) (no dataset is involved).  A step is one full
+training iteration (forward, backward, all-reduce, Adam update, leafify) of the
+unchanged MiniTensor front-end running on the CUDA backend.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`value` times K steps on device-resident inputs (CUDA events on the backend's
+stream, barrier + synchronize on both sides, max over ranks).  `e2e` times steps
+through the public workload API from pinned host buffers: every step copies its
+inputs host -> device and reads the loss back.  `--impl reference` runs the
+reference CPU backend (oracle/_ref, built from the unmodified sources) on the
+host cores.  One JSON line is printed by rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "wide_mlp_train_samples_per_s"
+WIDTHS = (1024, 8192, 8192, 8192, 1000)
+GLOBAL_BATCH = 65536
+LR = 1e-3
+SEED = 2026
+
+
+def flops_per_sample(widths=WIDTHS) -> float:
+    macs = sum(a * b for a, b in zip(widths[:-1], widths[1:]))
+    # forward 2*MACs, backward 4*MACs except no input gradient for the first layer
+    return 6.0 * macs - 2.0 * widths[0] * widths[1]
+
+
+def config(n_gpus: int) -> dict:
+    return {
+        "workload": "wide MLP 1024-8192-8192-8192-1000 ReLU + softmax CE, Adam lr=1e-3, global batch 65536 "
+                    "split over ranks, NCCL gradient all-reduce",
+        "global_batch": GLOBAL_BATCH,
+        "per_rank_batch": GLOBAL_BATCH // n_gpus,
+        "parameters": sum(a * b + b for a, b in zip(WIDTHS[:-1], WIDTHS[1:])),
+        "flop_per_step": flops_per_sample() * GLOBAL_BATCH,
+        "parallelism": f"dp{n_gpus}",
+        "l2": "inputs and weights larger than the 126 MB L2 (no flush needed)",
+    }
+
+
+# ---------------------------------------------------------------- helpers --
+
+def make_batch(rank: int, batch: int):
+    import numpy as np
+    import torch
+
+    rng = np.random.default_rng([SEED, rank])
+    x = torch.empty((batch, WIDTHS[0]), dtype=torch.float32, pin_memory=True)
+    y = torch.empty((batch,), dtype=torch.int64, pin_memory=True)
+    x.numpy()[:] = rng.standard_normal((batch, WIDTHS[0]), dtype=np.float32)
+    y.numpy()[:] = rng.integers(0, WIDTHS[-1], batch)
+    return x, y
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.out = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        if not self.out:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measure_tf32_peak() -> float:
+    """Dense TF32 tensor throughput of cuBLAS (torch.matmul, 8192^3, best of 10): the
+    3xTF32 roofline is a third of it.  TF32 is not in the driver's peak file."""
+    import torch
+
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    n = 8192
+    a = torch.randn(n, n, device="cuda")
+    b = torch.randn(n, n, device="cuda")
+    for _ in range(3):
+        torch.matmul(a, b)
+    best = float("inf")
+    for _ in range(10):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch.matmul(a, b)
+        e.record()
+        torch.cuda.synchronize()
+        best = min(best, s.elapsed_time(e))
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b
+    return 2 * n ** 3 / (best * 1e-3) / 1e12
+
+
+def read_traffic(name: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    path = ROOT / "profiles" / "traffic.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith(name + " "):
+            try:
+                return float(line.split()[1])
+            except (IndexError, ValueError):
+                return None
+    return None
+
+
+def cpu_reference_sample(batch: int, steps: int) -> dict:
+    """The reference CPU backend (oracle/_ref) training the same model on one core."""
+    import numpy as np
+
+    from minitensor_cpp_b200.frontend import Frontend, MlpTrainer
+    from oracle import refkernels
+
+    fe = Frontend(refkernels.LIB_PATH)
+    tr = MlpTrainer(fe, -1, WIDTHS[0], WIDTHS[1], len(WIDTHS) - 2, WIDTHS[-1], seed=SEED, lr=LR)
+    tr.materialize()
+    rng = np.random.default_rng([SEED, 99])
+    x = rng.standard_normal((batch, WIDTHS[0]), dtype=np.float32)
+    y = rng.integers(0, WIDTHS[-1], batch).astype(np.int64)
+    tr.load_batch(x.ctypes.data, y.ctypes.data, batch)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        tr.step_resident(read_loss=True)
+    dt = time.perf_counter() - t0
+    tr.close()
+    return {"samples": batch * steps, "seconds": dt}
+
+
+def _worker(args):
+    batch, steps = args
+    return cpu_reference_sample(batch, steps)
+
+
+# ----------------------------------------------------------------- our arm --
+
+def run_ours(args) -> None:
+    import ctypes
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+
+    from minitensor_cpp_b200 import abi
+    from minitensor_cpp_b200.frontend import Frontend, MlpTrainer
+
+    fe = Frontend()
+    batch = GLOBAL_BATCH // world
+    tr = MlpTrainer(fe, local, WIDTHS[0], WIDTHS[1], len(WIDTHS) - 2, WIDTHS[-1], seed=SEED, lr=LR)
+    comm = None
+    if world > 1:
+        uid = (ctypes.c_char * 128)()
+        if rank == 0:
+            abi.check(abi.lib().mtc_comm_unique_id(uid, 128), "nccl id")
+        payload = [bytes(uid) if rank == 0 else None]
+        dist.broadcast_object_list(payload, src=0)
+        uid = (ctypes.c_char * 128).from_buffer_copy(payload[0])
+        comm = ctypes.c_void_p()
+        abi.check(abi.lib().mtc_comm_init(local, rank, world, uid, 128, ctypes.byref(comm)), "nccl init")
+        tr.set_comm(comm, world)
+
+    x, y = make_batch(rank, batch)
+    tr.load_batch(x.data_ptr(), y.data_ptr(), batch)
+    stream = torch.cuda.ExternalStream(tr.stream(), device=torch.device("cuda", local))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        tr.step_resident(read_loss=False)
+    tr.synchronize()
+
+    # ---- value: device-resident inputs
+    launches0 = abi.launch_count()
+    abi.profile_gemm(reset=True)
+    abi.profile_enable(True)
+    barrier()
+    torch.cuda.synchronize()
+    tr.synchronize()
+    with ClockSampler(local) as clocks:
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            tr.step_resident(read_loss=False)
+        stop.record(stream)
+        tr.synchronize()
+        torch.cuda.synchronize()
+    abi.profile_enable(False)
+    launches = abi.launch_count() - launches0
+    ms_local = start.elapsed_time(stop)
+    ms = max_over_ranks(ms_local)
+    barrier()
+    gemm_n, gemm_ms, gemm_flops = abi.profile_gemm(reset=True)
+
+    # ---- e2e: host buffers through the public API, loss read back every step
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    loss = 0.0
+    for _ in range(e2e_steps):
+        loss = tr.step_host(x.data_ptr(), y.data_ptr(), batch)
+    e_stop.record(stream)
+    tr.synchronize()
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_stop))
+    wall_e2e = time.perf_counter() - t0
+
+    tf32 = measure_tf32_peak() if rank == 0 else None
+    if comm is not None:
+        barrier()
+        abi.lib().mtc_comm_destroy(comm)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    peaks = json.loads(peaks_path.read_text()) if peaks_path.exists() else {}
+    value = GLOBAL_BATCH * args.steps / (ms * 1e-3)
+    gemm_tflops = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+    peak = tf32 / 3.0 if tf32 else None
+    roofline = {
+        "kernel": "3xTF32 tcgen05 GEMM (matmul of every Linear forward/backward)",
+        "bound": "tensor",
+        "achieved": gemm_tflops,
+        "peak": peak,
+        "unit": "TFLOP/s",
+        "frac": (gemm_tflops / peak) if (gemm_tflops and peak) else None,
+        "peak_source": f"measured cuBLAS TF32 {tf32:.1f} TFLOP/s / 3 (3xTF32); bf16 burst in MEASURED_PEAKS.json "
+                       f"{peaks.get('bf16_tflops')}" if tf32 else None,
+        "launches": gemm_n,
+        "avg_launch_ms": gemm_ms / gemm_n if gemm_n else None,
+        "traffic": read_traffic("gemm_3xtf32"),
+    }
+    cpu = None
+    if world == 1 and not args.skip_cpu:
+        s = cpu_reference_sample(args.cpu_batch, 1)
+        cpu = {"value": s["samples"] / s["seconds"], "unit": "samples/s", "cores": 1, "kind": "reference",
+               "sample": f"1 training step at batch {args.cpu_batch} (same model, Adam) on the reference CPU "
+                         f"backend, {s['seconds']:.1f} s"}
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "samples/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) inputs, uniform Int64 labels)",
+        "config": config(world),
+        "tflops": flops_per_sample() * GLOBAL_BATCH * args.steps / (ms * 1e-3) / 1e12,
+        "e2e": {"value": GLOBAL_BATCH * e2e_steps / (e2e_ms * 1e-3), "unit": "samples/s",
+                "steps": e2e_steps, "wall_s": wall_e2e, "last_loss": loss,
+                "h2d_bytes_per_step": world * (x.numel() * 4 + y.numel() * 8),
+                "d2h_bytes_per_step": world * 4},
+        "gpu_launches": launches,
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------- reference arm --
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import refkernels
+
+    if not refkernels.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libmtref.so was not built"}))
+        return
+    import multiprocessing as mp
+
+    cores = os.cpu_count() or 1
+    try:
+        avail_gb = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE") / 2 ** 30
+    except (ValueError, OSError):
+        avail_gb = 64.0
+    # each single-threaded reference process holds the 151M-parameter model,
+    # its Adam moments and the step's intermediates (~10 GB peak)
+    workers = max(1, min(cores, int(avail_gb // 12), 16))
+    batch = args.cpu_batch
+    steps = 1  # one ~30-60 s training step per worker bounds the whole run to minutes
+    ctx = mp.get_context("spawn")
+    t0 = time.perf_counter()
+    with ctx.Pool(workers) as pool:
+        results = pool.map(_worker, [(batch, steps)] * workers)
+    wall = time.perf_counter() - t0
+    samples = sum(r["samples"] for r in results)
+    busiest = max(r["seconds"] for r in results)
+    value = samples / busiest
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "samples/s",
+        "impl": "reference",
+        "n_gpus": args.gpus,
+        "steps": steps,
+        "steps_requested": args.steps,
+        "warmup": 0,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) inputs, uniform Int64 labels)",
+        "config": config(args.gpus),
+        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": workers, "kind": "reference",
+                         "sample": f"{workers} single-threaded reference processes x {steps} training step at "
+                                   f"batch {batch} each (the reference is single-threaded); wall {wall:.1f} s"},
+        "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--cpu-batch", type=int, default=4)
+    p.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline sample")
+    args = p.parse_args()
+    if args.warmup < 3:
+        p.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -239,6 +239,17 @@ int mtc_fill(const mtc_desc *out, const void *value, void *stream);
 int mtc_uniform(const mtc_desc *out, float low, float high, uint64_t key0, uint64_t key1, void *stream);
 int mtc_normal(const mtc_desc *out, float mean, float std_dev, uint64_t key0, uint64_t key1, void *stream);
 
+/* ------------------------------------------------------------ instrumentation -- */
+
+/* Number of kernels this library has launched in this process (all devices). */
+int mtc_launch_count(uint64_t *count);
+/* While enabled, every GEMM launch is bracketed by CUDA events on its stream. */
+int mtc_profile_enable(int on);
+/* Totals since the last reset for GEMM launches: launch count, summed device
+ * time (ms, from the events; synchronises them) and algorithmic FLOPs (2*M*N*K
+ * per batch entry).  reset != 0 clears the totals afterwards. */
+int mtc_profile_gemm(uint64_t *launches, double *milliseconds, double *flops, int reset);
+
 /* -------------------------------------------------- data parallel (config 5) --
  * Gradient all-reduce between the ranks of a data-parallel job, one process per
  * GPU; NCCL over NVLink/NVSwitch.  No reference counterpart: the reference is

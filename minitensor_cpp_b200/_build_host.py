@@ -142,7 +142,8 @@ def build(verbose: bool = False) -> Path | None:
                 print(proc.stderr)
     mtcuda = LIB / "libmtcuda.so"
     if _newer(lib, objs + [mtcuda]):
-        _run([CXX, "-shared", "-o", str(lib), *map(str, objs), f"-L{LIB}", "-lmtcuda", "-Wl,-rpath,$ORIGIN"])
+        _run([CXX, "-shared", "-Wl,-Bsymbolic", "-o", str(lib), *map(str, objs), f"-L{LIB}", "-lmtcuda",
+              "-Wl,-rpath,$ORIGIN"])
     return lib
 
 

@@ -173,6 +173,9 @@ def _declare(L):
         "mtc_fill": ([P(Desc), c_vp, c_vp], c_int),
         "mtc_uniform": ([P(Desc), c_f, c_f, ctypes.c_uint64, ctypes.c_uint64, c_vp], c_int),
         "mtc_normal": ([P(Desc), c_f, c_f, ctypes.c_uint64, ctypes.c_uint64, c_vp], c_int),
+        "mtc_launch_count": ([P(ctypes.c_uint64)], c_int),
+        "mtc_profile_enable": ([c_int], c_int),
+        "mtc_profile_gemm": ([P(ctypes.c_uint64), P(ctypes.c_double), P(ctypes.c_double), c_int], c_int),
         "mtc_comm_unique_id": ([c_vp, c_sz], c_int),
         "mtc_comm_init": ([c_int, c_int, c_int, c_vp, c_sz, P(c_vp)], c_int),
         "mtc_comm_allreduce_f32": ([c_vp, P(c_vp), P(c_sz), c_i32, c_f, c_vp], c_int),
@@ -189,7 +192,7 @@ EXPORTED = (
     "mtc_free", "mtc_copy_from_host", "mtc_copy_to_host", "mtc_stream_synchronize", "mtc_pool_stats", "mtc_pool_trim",
     "mtc_check_device_errors", "mtc_unary", "mtc_binary", "mtc_fused", "mtc_copy", "mtc_concat", "mtc_index_scatter",
     "mtc_gather", "mtc_gather_scatter_add", "mtc_reduce", "mtc_log_softmax", "mtc_matmul", "mtc_fill", "mtc_uniform",
-    "mtc_normal", "mtc_comm_unique_id", "mtc_comm_init", "mtc_comm_allreduce_f32", "mtc_comm_destroy",
+    "mtc_normal", "mtc_launch_count", "mtc_profile_enable", "mtc_profile_gemm", "mtc_comm_unique_id", "mtc_comm_init", "mtc_comm_allreduce_f32", "mtc_comm_destroy",
 )
 
 
@@ -295,6 +298,23 @@ def uniform(out: View, low: float, high: float, key: tuple, stream=None) -> None
 
 def normal(out: View, mean: float, std: float, key: tuple, stream=None) -> None:
     check(lib().mtc_normal(ctypes.byref(out.desc()), mean, std, key[0], key[1], _stream(stream)), "normal")
+
+
+def launch_count() -> int:
+    n = ctypes.c_uint64(0)
+    check(lib().mtc_launch_count(ctypes.byref(n)))
+    return n.value
+
+
+def profile_enable(on: bool) -> None:
+    check(lib().mtc_profile_enable(int(on)))
+
+
+def profile_gemm(reset: bool = True):
+    """(launches, total ms, total FLOPs) of GEMM launches since the last reset."""
+    n, ms, fl = ctypes.c_uint64(0), ctypes.c_double(0.0), ctypes.c_double(0.0)
+    check(lib().mtc_profile_gemm(ctypes.byref(n), ctypes.byref(ms), ctypes.byref(fl), int(reset)))
+    return n.value, ms.value, fl.value
 
 
 def check_device_errors(device: int = 0, stream=None) -> None:

@@ -35,8 +35,14 @@ void clear_error();
         if (mtc_rc__ != MTC_OK) return mtc_rc__;                                             \
     } while (0)
 
-// Checks the launch that was just enqueued.
+// Checks the launch that was just enqueued (and counts it).
 int check_launch(const char *what);
+// Counts a launch made through the driver API.
+void count_launch();
+// GEMM launch profiling (CUDA events around each launch while enabled).
+bool profiling();
+void *profile_begin(cudaStream_t stream);
+void profile_end(void *begin, cudaStream_t stream, double flops);
 
 inline size_t dtype_size(int32_t dtype) { return dtype == MTC_INT64 ? 8 : 4; }
 

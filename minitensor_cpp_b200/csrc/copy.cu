@@ -16,6 +16,19 @@ __device__ __forceinline__ void record_device_error(int code, long long detail) 
     }
 }
 
+// Device address of the error word on the current device (kernels in other
+// files receive it as an argument).
+unsigned long long *device_error_word() {
+    static unsigned long long *words[64] = {};
+    const int dev = current_device();
+    if (dev < 0 || dev >= 64) return nullptr;
+    if (words[dev] == nullptr) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_error) == cudaSuccess) words[dev] = static_cast<unsigned long long *>(p);
+    }
+    return words[dev];
+}
+
 namespace {
 
 constexpr int kOps = 3;
@@ -519,8 +532,11 @@ int mtc_check_device_errors(int device, void *stream, int64_t *detail) {
             const unsigned long long zero[2] = {0, 0};
             cudaMemcpyToSymbolAsync(g_device_error, zero, sizeof(zero), 0, cudaMemcpyHostToDevice, s);
             cudaStreamSynchronize(s);
-            rc = fail(static_cast<int>(word[0]), "an index kernel met index %lld outside its axis",
-                      static_cast<long long>(word[1]));
+            if (word[0] == MTC_ERR_OUT_OF_RANGE)
+                rc = fail(MTC_ERR_OUT_OF_RANGE, "an index kernel met index %lld outside its axis",
+                          static_cast<long long>(word[1]));
+            else
+                rc = fail(static_cast<int>(word[0]), "a device kernel gave up waiting (error %llu)", word[0]);
         }
     }
     if (prev != device) cudaSetDevice(prev);

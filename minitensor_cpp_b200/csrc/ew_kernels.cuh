@@ -19,6 +19,7 @@
 #define MTC_EW_MAX_OUT 4
 #define MTC_EW_TILE 64
 #define MTC_EW_TILE_THREADS 256
+#define MTC_EW_MAX_IMM 48
 
 // ------------------------------------------------------------------- ops --
 
@@ -68,14 +69,14 @@ template <int OP>
 struct MtcUnaryOp {
     static constexpr int kIn = 1;
     static constexpr int kOut = 1;
-    __device__ __forceinline__ void operator()(const float *x, float *y) const { y[0] = mtc_unary<OP>(x[0]); }
+    __device__ __forceinline__ void operator()(const float *x, float *y, const float *) const { y[0] = mtc_unary<OP>(x[0]); }
 };
 
 template <int OP>
 struct MtcBinaryOp {
     static constexpr int kIn = 2;
     static constexpr int kOut = 1;
-    __device__ __forceinline__ void operator()(const float *x, float *y) const { y[0] = mtc_binary<OP>(x[0], x[1]); }
+    __device__ __forceinline__ void operator()(const float *x, float *y, const float *) const { y[0] = mtc_binary<OP>(x[0], x[1]); }
 };
 
 // ------------------------------------------------------------ arguments --
@@ -107,6 +108,7 @@ struct MtcEwArgs {
     long long out_str[MTC_EW_MAX_OUT][MTC_EW_MAX_RANK];
     unsigned int transposed;  // tiled kernel: bit k set when input k is read through shared memory
     unsigned int batch_rank;  // tiled kernel: number of leading (batch) axes
+    float imm[MTC_EW_MAX_IMM]; // fused programs: constants, passed by value so one compiled program serves all
 };
 
 // ------------------------------------------------------------ flat kernel --
@@ -141,7 +143,7 @@ __global__ void __launch_bounds__(256) mtc_ew_flat(const MtcEwArgs a) {
             }
         }
 #pragma unroll
-        for (int l = 0; l < VEC; ++l) op(x[l], y[l]);
+        for (int l = 0; l < VEC; ++l) op(x[l], y[l], a.imm);
 #pragma unroll
         for (int j = 0; j < NOUT; ++j) {
             if (VEC == 4) {
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(256) mtc_ew_flat(const MtcEwArgs a) {
         float y[NOUT];
 #pragma unroll
         for (int k = 0; k < NIN; ++k) x[k] = __ldg(a.in[k] + a.in_off[k] + (a.in_str[k][0] == 0 ? 0 : t));
-        op(x, y);
+        op(x, y, a.imm);
 #pragma unroll
         for (int j = 0; j < NOUT; ++j) a.out[j][a.out_off[j] + t] = y[j];
     }
@@ -210,7 +212,7 @@ __global__ void __launch_bounds__(256) mtc_ew_strided(const MtcEwArgs a) {
         float y[NOUT];
 #pragma unroll
         for (int k = 0; k < NIN; ++k) x[k] = __ldg(a.in[k] + io[k]);
-        op(x, y);
+        op(x, y, a.imm);
 #pragma unroll
         for (int j = 0; j < NOUT; ++j) a.out[j][oo[j]] = y[j];
     }
@@ -295,7 +297,7 @@ __global__ void __launch_bounds__(MTC_EW_TILE_THREADS) mtc_ew_tiled(const MtcEwA
                                  static_cast<long long>(c0 + lc) * a.in_str[k][r - 1]);
                 }
             }
-            op(x, y);
+            op(x, y, a.imm);
 #pragma unroll
             for (int j = 0; j < NOUT; ++j)
                 a.out[j][ob[j] + static_cast<long long>(r0 + lr) * a.out_str[j][r - 2] +

@@ -9,7 +9,12 @@
 #include <cuda.h>
 #include <nvrtc.h>
 
+#include <sys/stat.h>
+#include <unistd.h>
+
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -62,7 +67,7 @@ const char *const kNameExpr[kVariants] = {"mtc_ew_flat<MtcFused, 4>", "mtc_ew_fl
 
 struct CompiledProgram {
     CUmodule module = nullptr;
-    CUfunction fn[kVariants] = {};
+    CUfunction fn = nullptr;
 };
 
 std::mutex g_cache_mutex;
@@ -99,12 +104,14 @@ int generate(const mtc_instr *program, int n_instr, int n_in, const int32_t *out
         snprintf(line, sizeof(line), "        r%d = x[%d];\n", k, k);
         body += line;
     }
+    int n_imm = 0;
     for (int i = 0; i < n_instr; ++i) {
         const mtc_instr &ins = program[i];
         if (ins.op == MTC_OP_CONST) {
-            uint32_t bits;
-            std::memcpy(&bits, &ins.imm, 4);
-            snprintf(line, sizeof(line), "        r%d = __int_as_float(0x%08xu);\n", ins.dst, bits);
+            // constants are launch arguments, so programs that differ only in their
+            // constants (an optimizer's per-step coefficients) share one kernel
+            if (n_imm >= MTC_EW_MAX_IMM) return fail(MTC_ERR_UNSUPPORTED, "fused program has too many constants");
+            snprintf(line, sizeof(line), "        r%d = imm[%d];\n", ins.dst, n_imm++);
         } else if (is_unary(ins.op)) {
             if (ins.a >= n_reg || !written[ins.a])
                 return fail(MTC_ERR_INVALID_ARGUMENT, "fused instruction %d reads an unwritten register", i);
@@ -128,49 +135,95 @@ int generate(const mtc_instr *program, int n_instr, int n_in, const int32_t *out
              "\nstruct MtcFused {\n    static constexpr int kIn = %d;\n    static constexpr int kOut = %d;\n", n_in,
              n_out);
     src += line;
-    src += "    __device__ __forceinline__ void operator()(const float *x, float *y) const {\n";
+    src += "    __device__ __forceinline__ void operator()(const float *x, float *y, const float *imm) const {\n";
     src += body;
     src += "    }\n};\n";
     return MTC_OK;
 }
 
-int compile(const std::string &src, int n_in, CompiledProgram &out) {
-    nvrtcProgram prog;
-    if (nvrtcCreateProgram(&prog, src.c_str(), "mtc_fused.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS)
-        return fail(MTC_ERR_RUNTIME, "nvrtcCreateProgram failed");
-    const int variants = n_in >= 2 ? kVariants : kVariants - 1;
-    for (int v = 0; v < variants; ++v) nvrtcAddNameExpression(prog, kNameExpr[v]);
-    const char *opts[] = {"--gpu-architecture=sm_100a", "-std=c++17", "-default-device"};
-    nvrtcResult rc = nvrtcCompileProgram(prog, 3, opts);
-    if (rc != NVRTC_SUCCESS) {
-        size_t n = 0;
-        nvrtcGetProgramLogSize(prog, &n);
-        std::string log(n, '\0');
-        nvrtcGetProgramLog(prog, log.data());
-        nvrtcDestroyProgram(&prog);
-        return fail(MTC_ERR_UNSUPPORTED, "NVRTC could not compile the fused program: %s", log.c_str());
+uint64_t fnv1a(const std::string &text) {
+    uint64_t h = 1469598103934665603ull;
+    for (unsigned char c : text) {
+        h ^= c;
+        h *= 1099511628211ull;
     }
-    size_t cubin_size = 0;
-    nvrtcGetCUBINSize(prog, &cubin_size);
-    std::vector<char> cubin(cubin_size);
-    nvrtcGetCUBIN(prog, cubin.data());
-    std::vector<std::string> lowered(variants);
-    for (int v = 0; v < variants; ++v) {
-        const char *name = nullptr;
-        nvrtcGetLoweredName(prog, kNameExpr[v], &name);
-        lowered[v] = name ? name : "";
-    }
-    nvrtcDestroyProgram(&prog);
+    return h;
+}
 
+// On-disk cache of compiled programs: <dir>/<hash>.cubin next to <hash>.src,
+// whose text must equal the program's source (no trust in the hash alone).
+std::string cache_dir() {
+    const char *env = std::getenv("MTB_KERNEL_CACHE");
+    if (env != nullptr) return env;
+    return "/tmp/mtb_kernel_cache";
+}
+
+bool read_file(const std::string &path, std::string &out) {
+    FILE *f = std::fopen(path.c_str(), "rb");
+    if (!f) return false;
+    std::fseek(f, 0, SEEK_END);
+    const long n = std::ftell(f);
+    std::fseek(f, 0, SEEK_SET);
+    out.resize(n > 0 ? static_cast<size_t>(n) : 0);
+    const bool ok = n <= 0 || std::fread(out.data(), 1, out.size(), f) == out.size();
+    std::fclose(f);
+    return ok;
+}
+
+void write_file(const std::string &path, const std::string &data) {
+    const std::string tmp = path + ".tmp" + std::to_string(static_cast<long long>(::getpid()));
+    FILE *f = std::fopen(tmp.c_str(), "wb");
+    if (!f) return;
+    const bool ok = std::fwrite(data.data(), 1, data.size(), f) == data.size();
+    std::fclose(f);
+    if (ok) std::rename(tmp.c_str(), path.c_str());
+    else std::remove(tmp.c_str());
+}
+
+// Compiles one kernel variant of a program (NVRTC, sm_100a) or loads it from the disk cache.
+int compile(const std::string &src, int variant, CompiledProgram &out) {
+    const std::string full = src + "\n// variant " + kNameExpr[variant] + "\n";
+    const std::string dir = cache_dir();
+    char name[32];
+    snprintf(name, sizeof(name), "%016llx", static_cast<unsigned long long>(fnv1a(full)));
+    const std::string base = dir + "/" + name;
+    std::string cubin, lowered, cached_src;
+    if (!(read_file(base + ".src", cached_src) && cached_src == full && read_file(base + ".cubin", cubin) &&
+          read_file(base + ".sym", lowered) && !cubin.empty() && !lowered.empty())) {
+        nvrtcProgram prog;
+        if (nvrtcCreateProgram(&prog, src.c_str(), "mtc_fused.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS)
+            return fail(MTC_ERR_RUNTIME, "nvrtcCreateProgram failed");
+        nvrtcAddNameExpression(prog, kNameExpr[variant]);
+        const char *opts[] = {"--gpu-architecture=sm_100a", "-std=c++17", "-default-device"};
+        const nvrtcResult rc = nvrtcCompileProgram(prog, 3, opts);
+        if (rc != NVRTC_SUCCESS) {
+            size_t n = 0;
+            nvrtcGetProgramLogSize(prog, &n);
+            std::string log(n, '\0');
+            nvrtcGetProgramLog(prog, log.data());
+            nvrtcDestroyProgram(&prog);
+            return fail(MTC_ERR_UNSUPPORTED, "NVRTC could not compile the fused program: %s", log.c_str());
+        }
+        size_t cubin_size = 0;
+        nvrtcGetCUBINSize(prog, &cubin_size);
+        cubin.assign(cubin_size, '\0');
+        nvrtcGetCUBIN(prog, cubin.data());
+        const char *lname = nullptr;
+        nvrtcGetLoweredName(prog, kNameExpr[variant], &lname);
+        lowered = lname ? lname : "";
+        nvrtcDestroyProgram(&prog);
+        ::mkdir(dir.c_str(), 0777);
+        write_file(base + ".cubin", cubin);
+        write_file(base + ".sym", lowered);
+        write_file(base + ".src", full);
+    }
     Driver &d = driver();
     if (!d.ok) return fail(MTC_ERR_RUNTIME, "CUDA driver entry points for module loading are unavailable");
     MTC_CUDA_TRY(cudaFree(nullptr));  // make the primary context current
     if (d.load(&out.module, cubin.data()) != CUDA_SUCCESS)
         return fail(MTC_ERR_RUNTIME, "cuModuleLoadData failed for a fused program");
-    for (int v = 0; v < variants; ++v) {
-        if (d.get(&out.fn[v], out.module, lowered[v].c_str()) != CUDA_SUCCESS)
-            return fail(MTC_ERR_RUNTIME, "fused kernel %s not found in module", kNameExpr[v]);
-    }
+    if (d.get(&out.fn, out.module, lowered.c_str()) != CUDA_SUCCESS)
+        return fail(MTC_ERR_RUNTIME, "fused kernel %s not found in module", kNameExpr[variant]);
     return MTC_OK;
 }
 
@@ -195,19 +248,10 @@ extern "C" int mtc_fused(const mtc_instr *program, int32_t n_instr, const mtc_de
 
     std::string src;
     MTC_TRY(generate(program, n_instr, n_inputs, out_regs, n_outputs, src));
+    int n_imm = 0;
+    for (int i = 0; i < n_instr; ++i)
+        if (program[i].op == MTC_OP_CONST) plan.args.imm[n_imm++] = program[i].imm;
     const int device = current_device();
-    std::string key = std::to_string(device) + "\n" + src.substr(std::strlen(kTemplateSource));
-    CompiledProgram *cp = nullptr;
-    {
-        std::lock_guard<std::mutex> lock(g_cache_mutex);
-        auto it = g_cache.find(key);
-        if (it == g_cache.end()) {
-            auto fresh = std::make_unique<CompiledProgram>();
-            MTC_TRY(compile(src, n_inputs, *fresh));
-            it = g_cache.emplace(key, std::move(fresh)).first;
-        }
-        cp = it->second.get();
-    }
     int v = 0;
     switch (plan.variant) {
     case EwVariant::Flat4: v = 0; break;
@@ -217,10 +261,23 @@ extern "C" int mtc_fused(const mtc_instr *program, int32_t n_instr, const mtc_de
     case EwVariant::Tiled2: v = 4; break;
     default: return MTC_OK;
     }
-    if (cp->fn[v] == nullptr) return fail(MTC_ERR_LOGIC, "fused variant %d was not compiled", v);
+    std::string key = std::to_string(device) + ":" + std::to_string(v) + "\n" + src.substr(std::strlen(kTemplateSource));
+    CompiledProgram *cp = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_cache_mutex);
+        auto it = g_cache.find(key);
+        if (it == g_cache.end()) {
+            auto fresh = std::make_unique<CompiledProgram>();
+            MTC_TRY(compile(src, v, *fresh));
+            it = g_cache.emplace(key, std::move(fresh)).first;
+        }
+        cp = it->second.get();
+    }
+    if (cp->fn == nullptr) return fail(MTC_ERR_LOGIC, "fused variant %d was not compiled", v);
     void *params[] = {&plan.args};
-    CUresult r = driver().launch(cp->fn[v], plan.grid.x, plan.grid.y, plan.grid.z, plan.block.x, plan.block.y,
+    CUresult r = driver().launch(cp->fn, plan.grid.x, plan.grid.y, plan.grid.z, plan.block.x, plan.block.y,
                                  plan.block.z, 0, static_cast<CUstream>(stream), params, nullptr);
     if (r != CUDA_SUCCESS) return fail(MTC_ERR_RUNTIME, "launch of fused kernel failed (CUresult %d)", static_cast<int>(r));
+    count_launch();
     return MTC_OK;
 }

@@ -222,12 +222,19 @@ extern "C" int mtc_matmul(const mtc_desc *lhs, const mtc_desc *rhs, const mtc_de
         const float zero = 0.0f;
         return mtc_fill(out, &zero, stream);
     }
-    if (algo == MTC_GEMM_SIMT) return gemm_simt(p, s);
-    if (algo == MTC_GEMM_3XTF32 || algo == MTC_GEMM_AUTO) {
-        const int rc = gemm_3xtf32(p, s);
-        if (rc != MTC_ERR_UNSUPPORTED || algo == MTC_GEMM_3XTF32) return rc;
-        clear_error();
-        return gemm_simt(p, s);
+    if (algo != MTC_GEMM_SIMT && algo != MTC_GEMM_3XTF32 && algo != MTC_GEMM_AUTO)
+        return fail(MTC_ERR_INVALID_ARGUMENT, "unknown matmul algorithm %d", algo);
+    void *mark = profiling() ? profile_begin(s) : nullptr;
+    int rc;
+    if (algo == MTC_GEMM_SIMT) {
+        rc = gemm_simt(p, s);
+    } else {
+        rc = gemm_3xtf32(p, s);
+        if (rc == MTC_ERR_UNSUPPORTED && algo == MTC_GEMM_AUTO) {
+            clear_error();
+            rc = gemm_simt(p, s);
+        }
     }
-    return fail(MTC_ERR_INVALID_ARGUMENT, "unknown matmul algorithm %d", algo);
+    if (mark != nullptr) profile_end(mark, s, 2.0 * double(p.M) * double(p.N) * double(p.K) * double(p.batch));
+    return rc;
 }

@@ -1,12 +1,527 @@
-// Tensor-core 3xTF32 GEMM for sm_100a (tcgen05 + TMEM + TMA).
-// Placeholder until the kernel lands: every problem is reported unsupported so
-// mtc_matmul's AUTO mode takes the exact SIMT path.
+// Tensor-core GEMM for sm_100a with float32 accuracy: 3xTF32 on tcgen05.
+//
+// Every float32 operand x is split into hi = x with the low 13 mantissa bits
+// cleared (exactly representable in TF32) and lo = x - hi (exact in float32).
+// The product is accumulated in TMEM as Ahi*Bhi + Ahi*Blo + Alo*Bhi; the
+// dropped Alo*Blo term and the TF32 rounding of lo are below 2^-20 relative,
+// well inside the 1e-5*sqrt(K) parity bound of the float32 reference.
+//
+// Pipeline (one persistent CTA per SM, 192 threads):
+//   pack kernel  : A -> Ahi/Alo [batch][M][Kp], B -> Bhi/Blo [batch][N][Kp],
+//                  both K-major (transposing strided views through shared memory).
+//   warp 0       : TMA producer, 128x32 (A) and 256x32 (B) fp32 boxes with the
+//                  128-byte swizzle, into a 2-stage ring of 96 KB stages.
+//   warp 1       : allocates 512 TMEM columns (two 128x256 fp32 accumulators);
+//                  one thread issues tcgen05.mma.kind::tf32 (M=128, N=256, K=8),
+//                  3 per k-step, and tcgen05.commit releases stages / accumulators.
+//   warps 2..5   : epilogue, tcgen05.ld of the accumulator lane quadrant of the
+//                  warp, stores to C (any strides), then frees the accumulator.
+// Every mbarrier wait is bounded; on expiry the CTA records an error in the
+// device error word and leaves its loops (no hang).
+#include <cuda.h>
+
+#include <cstring>
+#include <mutex>
+
 #include "gemm.cuh"
 
 namespace mtc {
 
-int gemm_3xtf32(const GemmProblem &, cudaStream_t) {
-    return fail(MTC_ERR_UNSUPPORTED, "tensor-core 3xTF32 GEMM not built");
+// Device error word (copy.cu) as a device address, for kernels in other files.
+unsigned long long *device_error_word();
+
+namespace {
+
+constexpr int TC_BM = 128;
+constexpr int TC_BN = 256;
+constexpr int TC_BK = 32;  // fp32 elements = 128 bytes = one swizzle row
+constexpr int TC_STAGES = 2;
+constexpr int TC_A_BYTES = TC_BM * TC_BK * 4;                 // 16 KB
+constexpr int TC_B_BYTES = TC_BN * TC_BK * 4;                 // 32 KB
+constexpr int TC_STAGE_BYTES = 2 * TC_A_BYTES + 2 * TC_B_BYTES;  // 96 KB
+constexpr int TC_SMEM_BYTES = TC_STAGES * TC_STAGE_BYTES + 1024 + 256;
+constexpr int TC_THREADS = 192;
+constexpr uint32_t TC_TMEM_COLS = 512;
+constexpr long long kWaitLimit = 20000000;  // bounded spins per wait
+constexpr int kErrTimeout = MTC_ERR_RUNTIME;
+
+struct TcArgs {
+    int64_t M, N, Kp;
+    int64_t batch;
+    int tiles_m, tiles_n;
+    int64_t total_tiles;
+    float *C;
+    int64_t c_off, c_rs, c_cs;
+    int batch_rank;
+    int64_t batch_shape[kMaxBatchRank];
+    int64_t c_bs[kMaxBatchRank];
+    int vec_store;  // C rows contiguous and 16-byte aligned: float4 stores
+    unsigned long long *err;
+};
+
+// ------------------------------------------------------------ PTX helpers --
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: false when the limit expired or another role aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    for (long long i = 0; i < kWaitLimit; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 1023) == 1023 && *abort_flag) return false;
+    }
+    *abort_flag = 1;
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void *tile) {
+    const uint64_t addr = smem_u32(tile);
+    return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | ((1024ull >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor: D=F32, A=B=TF32, both K-major, M=128, N=TC_BN.
+constexpr uint32_t kInstrDesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(TC_BN >> 3) << 17) |
+                                (uint32_t(TC_BM >> 4) << 24);
+
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(kInstrDesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tile_coords(const TcArgs &a, int64_t t, int &tm, int &tn, int &tb) {
+    const int64_t per_batch = static_cast<int64_t>(a.tiles_m) * a.tiles_n;
+    tb = static_cast<int>(t / per_batch);
+    const int64_t r = t - tb * per_batch;
+    // grouped rasterisation: 8 row tiles share each column sweep for L2 reuse
+    constexpr int G = 8;
+    const int64_t group_span = static_cast<int64_t>(G) * a.tiles_n;
+    const int group = static_cast<int>(r / group_span);
+    const int first_m = group * G;
+    const int gsize = (a.tiles_m - first_m) < G ? (a.tiles_m - first_m) : G;
+    const int64_t in_group = r - group * group_span;
+    tm = first_m + static_cast<int>(in_group % gsize);
+    tn = static_cast<int>(in_group / gsize);
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    k_gemm_3xtf32(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
+                  const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
+                  const TcArgs args) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem =
+        reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + TC_STAGES * TC_STAGE_BYTES);
+    uint64_t *full = bars;                       // [TC_STAGES]
+    uint64_t *empty = bars + TC_STAGES;          // [TC_STAGES]
+    uint64_t *acc_full = bars + 2 * TC_STAGES;   // [2]
+    uint64_t *acc_empty = acc_full + 2;          // [2]
+    uint64_t *drain = acc_empty + 2;             // [1] completion of the MMA issuer's work
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const int64_t kblocks = (args.Kp + TC_BK - 1) / TC_BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < TC_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 128);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TC_TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int64_t it = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
+                int tm, tn, tb;
+                tile_coords(args, t, tm, tn, tb);
+                for (int64_t kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = static_cast<int>(it % TC_STAGES);
+                    const uint32_t round = static_cast<uint32_t>(it / TC_STAGES);
+                    if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    unsigned char *st = smem + s * TC_STAGE_BYTES;
+                    mbar_expect_tx(&full[s], TC_STAGE_BYTES);
+                    const int kx = static_cast<int>(kb * TC_BK);
+                    tma_load_3d(st, &tm_ahi, &full[s], kx, tm * TC_BM, tb);
+                    tma_load_3d(st + TC_A_BYTES, &tm_alo, &full[s], kx, tm * TC_BM, tb);
+                    tma_load_3d(st + 2 * TC_A_BYTES, &tm_bhi, &full[s], kx, tn * TC_BN, tb);
+                    tma_load_3d(st + 2 * TC_A_BYTES + TC_B_BYTES, &tm_blo, &full[s], kx, tn * TC_BN, tb);
+                }
+            }
+            if (!ok) atomicCAS(args.err, 0ull, static_cast<unsigned long long>(kErrTimeout));
+            // drain: every issued stage must have landed before the CTA exits
+            for (int64_t d = it > TC_STAGES ? it - TC_STAGES : 0; d < it; ++d) {
+                const int s = static_cast<int>(d % TC_STAGES);
+                const uint32_t round = static_cast<uint32_t>(d / TC_STAGES);
+                for (long long i = 0; i < kWaitLimit && !mbar_try_wait(&full[s], round & 1u); ++i) {
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int64_t it = 0;
+            int64_t local = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x, ++local) {
+                const int b = static_cast<int>(local & 1);
+                const uint32_t use = static_cast<uint32_t>(local >> 1);
+                if (!mbar_wait(&acc_empty[b], (use & 1u) ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * TC_BN);
+                for (int64_t kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = static_cast<int>(it % TC_STAGES);
+                    const uint32_t round = static_cast<uint32_t>(it / TC_STAGES);
+                    if (!mbar_wait(&full[s], round & 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    unsigned char *st = smem + s * TC_STAGE_BYTES;
+                    const uint64_t a_hi = smem_desc_sw128(st);
+                    const uint64_t a_lo = smem_desc_sw128(st + TC_A_BYTES);
+                    const uint64_t b_hi = smem_desc_sw128(st + 2 * TC_A_BYTES);
+                    const uint64_t b_lo = smem_desc_sw128(st + 2 * TC_A_BYTES + TC_B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < TC_BK / 8; ++kk) {
+                        const uint64_t adv = static_cast<uint64_t>(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
+                        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+                        umma_tf32(d_tmem, a_hi + adv, b_hi + adv, acc);
+                        umma_tf32(d_tmem, a_hi + adv, b_lo + adv, 1u);
+                        umma_tf32(d_tmem, a_lo + adv, b_hi + adv, 1u);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                if (!ok) break;
+                umma_commit(&acc_full[b]);
+            }
+            if (!ok) atomicCAS(args.err, 0ull, static_cast<unsigned long long>(kErrTimeout));
+            // drain: all MMAs this thread issued complete before TMEM is released
+            umma_commit(drain);
+            for (long long i = 0; i < kWaitLimit && !mbar_try_wait(drain, 0u); ++i) {
+            }
+        }
+    } else {
+        // epilogue: warps 2..5 cover TMEM lane quadrants (warp % 4)
+        const int quadrant = warp % 4;
+        const int row_in_tile = quadrant * 32 + lane;
+        int64_t local = 0;
+        for (int64_t t = blockIdx.x; t < args.total_tiles; t += gridDim.x, ++local) {
+            const int b = static_cast<int>(local & 1);
+            const uint32_t use = static_cast<uint32_t>(local >> 1);
+            if (!mbar_wait(&acc_full[b], use & 1u, abort_flag)) {
+                atomicCAS(args.err, 0ull, static_cast<unsigned long long>(kErrTimeout));
+                break;
+            }
+            tc_fence_after();
+            int tm, tn, tb;
+            tile_coords(args, t, tm, tn, tb);
+            int64_t co = args.c_off;
+            {
+                int64_t rem = tb;
+                for (int d = args.batch_rank - 1; d >= 0; --d) {
+                    const int64_t c = rem % args.batch_shape[d];
+                    rem /= args.batch_shape[d];
+                    co += c * args.c_bs[d];
+                }
+            }
+            const int64_t m = static_cast<int64_t>(tm) * TC_BM + row_in_tile;
+            const int64_t n0 = static_cast<int64_t>(tn) * TC_BN;
+            const uint32_t taddr_row = tmem_base + (static_cast<uint32_t>(quadrant * 32) << 16) +
+                                       static_cast<uint32_t>(b * TC_BN);
+#pragma unroll 1
+            for (int c = 0; c < TC_BN / 32; ++c) {
+                float v[32];
+                tmem_ld32(taddr_row + static_cast<uint32_t>(c * 32), v);
+                if (m < args.M) {
+                    const int64_t nb = n0 + c * 32;
+                    float *dst = args.C + co + m * args.c_rs;
+                    if (args.vec_store && nb + 32 <= args.N) {
+                        float4 *d4 = reinterpret_cast<float4 *>(dst + nb);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (nb + j < args.N) dst[(nb + j) * args.c_cs] = v[j];
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[b]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TC_TMEM_COLS));
+    }
+}
+
+// ------------------------------------------------------------- split pack --
+// dst_hi/dst_lo: [batch][rows][Kp] row-major.  Source element (batch, r, k) at
+// off + batch offsets + r*sr + k*sk.  A 32x32 tile goes through shared memory so
+// both the strided read and the K-contiguous write are coalesced.
+
+struct PackArgs {
+    const float *src;
+    int64_t off, sr, sk;
+    int64_t rows, K, Kp;
+    int batch_rank;
+    int64_t batch_shape[kMaxBatchRank];
+    int64_t bs[kMaxBatchRank];
+    float *hi;
+    float *lo;
+    int k_contiguous;
+};
+
+__device__ __forceinline__ void split_tf32(float x, float &hi, float &lo) {
+    if (!isfinite(x)) {
+        hi = x;
+        lo = 0.0f;
+        return;
+    }
+    hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+    lo = __fsub_rn(x, hi);
+}
+
+__global__ void __launch_bounds__(256) k_split_pack(const PackArgs a) {
+    __shared__ float tile[32][33];
+    const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32;
+    const int64_t k0 = static_cast<int64_t>(blockIdx.x) * 32;
+    const int64_t b = blockIdx.z;
+    int64_t base = a.off;
+    {
+        int64_t rem = b;
+        for (int d = a.batch_rank - 1; d >= 0; --d) {
+            const int64_t c = rem % a.batch_shape[d];
+            rem /= a.batch_shape[d];
+            base += c * a.bs[d];
+        }
+    }
+    const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
+    for (int i = ty; i < 32; i += 8) {
+        // coalesced along whichever source axis is contiguous
+        const int64_t r = a.k_contiguous ? r0 + i : r0 + tx;
+        const int64_t k = a.k_contiguous ? k0 + tx : k0 + i;
+        float v = 0.0f;
+        if (r < a.rows && k < a.K) v = __ldg(a.src + base + r * a.sr + k * a.sk);
+        if (a.k_contiguous) tile[i][tx] = v;
+        else tile[tx][i] = v;
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int64_t r = r0 + i, k = k0 + tx;
+        if (r < a.rows && k < a.Kp) {
+            float hi, lo;
+            split_tf32(tile[i][tx], hi, lo);
+            const int64_t o = (b * a.rows + r) * a.Kp + k;
+            a.hi[o] = hi;
+            a.lo[o] = lo;
+        }
+    }
+}
+
+using PFN_EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                     const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+PFN_EncodeTiled encode_fn() {
+    static PFN_EncodeTiled fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess)
+            fn = reinterpret_cast<PFN_EncodeTiled>(p);
+    });
+    return fn;
+}
+
+int make_map(CUtensorMap &map, float *base, int64_t Kp, int64_t rows, int64_t batch, uint32_t box_rows) {
+    PFN_EncodeTiled enc = encode_fn();
+    if (enc == nullptr) return fail(MTC_ERR_RUNTIME, "cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(Kp), static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(batch)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(Kp) * 4, static_cast<cuuint64_t>(rows * Kp) * 4};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(TC_BK), box_rows, 1};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, elem,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MTC_ERR_RUNTIME, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return MTC_OK;
+}
+
+int pack(const float *src, int64_t off, int64_t sr, int64_t sk, int64_t rows, int64_t K, int64_t Kp,
+         const GemmProblem &p, const int64_t *bs, float *hi, float *lo, cudaStream_t stream) {
+    PackArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.src = src;
+    a.off = off;
+    a.sr = sr;
+    a.sk = sk;
+    a.rows = rows;
+    a.K = K;
+    a.Kp = Kp;
+    a.batch_rank = p.batch_rank;
+    for (int d = 0; d < p.batch_rank; ++d) {
+        a.batch_shape[d] = p.batch_shape[d];
+        a.bs[d] = bs[d];
+    }
+    a.hi = hi;
+    a.lo = lo;
+    a.k_contiguous = (sk == 1 || sr != 1) ? 1 : 0;
+    dim3 grid(static_cast<unsigned>((Kp + 31) / 32), static_cast<unsigned>((rows + 31) / 32),
+              static_cast<unsigned>(p.batch));
+    k_split_pack<<<grid, 256, 0, stream>>>(a);
+    return check_launch("3xTF32 split pack");
+}
+
+}  // namespace
+
+int gemm_3xtf32(const GemmProblem &p, cudaStream_t stream) {
+    if (p.M < 64 || p.N < 64 || p.K < 16) return fail(MTC_ERR_UNSUPPORTED, "problem too small for the tensor-core path");
+    if (p.batch > 65535 || (p.M + 31) / 32 > 65535 || (p.N + 31) / 32 > 65535)
+        return fail(MTC_ERR_UNSUPPORTED, "problem too large for the tensor-core launch shape");
+    const int64_t Kp = (p.K + 3) / 4 * 4;  // 16-byte row pitch for the tensor maps
+    if (Kp >= (int64_t{1} << 31) || p.M >= (int64_t{1} << 31) || p.N >= (int64_t{1} << 31))
+        return fail(MTC_ERR_UNSUPPORTED, "extent beyond the tensor-map range");
+    const size_t a_elems = static_cast<size_t>(p.batch * p.M * Kp);
+    const size_t b_elems = static_cast<size_t>(p.batch * p.N * Kp);
+    void *scratch = nullptr;
+    MTC_TRY(scratch_alloc((2 * a_elems + 2 * b_elems) * sizeof(float) + 1024, stream, &scratch));
+    float *ahi = static_cast<float *>(scratch);
+    float *alo = ahi + a_elems;
+    float *bhi = alo + a_elems;
+    float *blo = bhi + b_elems;
+    int rc = pack(p.A, p.a_off, p.a_rs, p.a_cs, p.M, p.K, Kp, p, p.a_bs, ahi, alo, stream);
+    // B[k][n] packed as B'[n][k]: rows advance along n (b_cs), k along b_rs
+    if (rc == MTC_OK) rc = pack(p.B, p.b_off, p.b_cs, p.b_rs, p.N, p.K, Kp, p, p.b_bs, bhi, blo, stream);
+    CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+    if (rc == MTC_OK) rc = make_map(m_ahi, ahi, Kp, p.M, p.batch, TC_BM);
+    if (rc == MTC_OK) rc = make_map(m_alo, alo, Kp, p.M, p.batch, TC_BM);
+    if (rc == MTC_OK) rc = make_map(m_bhi, bhi, Kp, p.N, p.batch, TC_BN);
+    if (rc == MTC_OK) rc = make_map(m_blo, blo, Kp, p.N, p.batch, TC_BN);
+    if (rc == MTC_OK) {
+        TcArgs a;
+        std::memset(&a, 0, sizeof(a));
+        a.M = p.M;
+        a.N = p.N;
+        a.Kp = Kp;
+        a.batch = p.batch;
+        a.tiles_m = static_cast<int>((p.M + TC_BM - 1) / TC_BM);
+        a.tiles_n = static_cast<int>((p.N + TC_BN - 1) / TC_BN);
+        a.total_tiles = static_cast<int64_t>(a.tiles_m) * a.tiles_n * p.batch;
+        a.C = p.C;
+        a.c_off = p.c_off;
+        a.c_rs = p.c_rs;
+        a.c_cs = p.c_cs;
+        a.batch_rank = p.batch_rank;
+        for (int d = 0; d < p.batch_rank; ++d) {
+            a.batch_shape[d] = p.batch_shape[d];
+            a.c_bs[d] = p.c_bs[d];
+        }
+        bool vec = p.c_cs == 1 && (p.c_rs % 4) == 0 && (p.c_off % 4) == 0 &&
+                   (reinterpret_cast<uintptr_t>(p.C) % 16) == 0;
+        for (int d = 0; d < p.batch_rank && vec; ++d) vec = (p.c_bs[d] % 4) == 0;
+        a.vec_store = vec ? 1 : 0;
+        a.err = device_error_word();
+        MTC_CUDA_TRY(cudaFuncSetAttribute(k_gemm_3xtf32, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_BYTES));
+        const int sms = sm_count(current_device());
+        const int64_t grid = a.total_tiles < sms ? a.total_tiles : sms;
+        k_gemm_3xtf32<<<static_cast<unsigned>(grid), TC_THREADS, TC_SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, a);
+        rc = check_launch("3xTF32 GEMM");
+    }
+    scratch_free(scratch, stream);
+    return rc;
 }
 
 }  // namespace mtc

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -86,10 +87,72 @@ int fail(int code, const char *fmt, ...) {
 
 void clear_error() { t_last_error.clear(); }
 
+std::atomic<uint64_t> g_launches{0};
+
 int check_launch(const char *what) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(MTC_ERR_RUNTIME, "launch of %s failed: %s", what, cudaGetErrorString(e));
+    g_launches.fetch_add(1, std::memory_order_relaxed);
     return MTC_OK;
+}
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+// ------------------------------------------------------------ GEMM profile --
+
+namespace {
+struct GemmSample {
+    cudaEvent_t start, stop;
+    double flops;
+};
+std::mutex g_profile_mutex;
+std::vector<GemmSample> g_profile_samples;
+std::vector<cudaEvent_t> g_event_pool;
+bool g_profile_on = false;
+uint64_t g_profile_launches = 0;
+double g_profile_ms = 0.0, g_profile_flops = 0.0;
+
+cudaEvent_t take_event() {
+    if (!g_event_pool.empty()) {
+        cudaEvent_t e = g_event_pool.back();
+        g_event_pool.pop_back();
+        return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+
+void drain_samples() {
+    for (GemmSample &s : g_profile_samples) {
+        float ms = 0.0f;
+        if (cudaEventSynchronize(s.stop) == cudaSuccess && cudaEventElapsedTime(&ms, s.start, s.stop) == cudaSuccess) {
+            g_profile_ms += ms;
+            g_profile_flops += s.flops;
+            ++g_profile_launches;
+        }
+        g_event_pool.push_back(s.start);
+        g_event_pool.push_back(s.stop);
+    }
+    g_profile_samples.clear();
+}
+}  // namespace
+
+bool profiling() { return g_profile_on; }
+
+void *profile_begin(cudaStream_t stream) {
+    std::lock_guard<std::mutex> lock(g_profile_mutex);
+    cudaEvent_t e = take_event();
+    cudaEventRecord(e, stream);
+    return e;
+}
+
+void profile_end(void *begin, cudaStream_t stream, double flops) {
+    std::lock_guard<std::mutex> lock(g_profile_mutex);
+    cudaEvent_t e = take_event();
+    cudaEventRecord(e, stream);
+    g_profile_samples.push_back(GemmSample{static_cast<cudaEvent_t>(begin), e, flops});
+    if (g_profile_samples.size() > 4096) drain_samples();
 }
 
 int current_device() {
@@ -231,6 +294,31 @@ int mtc_device_sm_count(int device, int *count) {
     DeviceState *st = nullptr;
     MTC_TRY(ensure_device(device, &st));
     *count = st->sms;
+    return MTC_OK;
+}
+
+int mtc_launch_count(uint64_t *count) {
+    *count = g_launches.load(std::memory_order_relaxed);
+    return MTC_OK;
+}
+
+int mtc_profile_enable(int on) {
+    std::lock_guard<std::mutex> lock(g_profile_mutex);
+    g_profile_on = on != 0;
+    return MTC_OK;
+}
+
+int mtc_profile_gemm(uint64_t *launches, double *milliseconds, double *flops, int reset) {
+    std::lock_guard<std::mutex> lock(g_profile_mutex);
+    drain_samples();
+    if (launches) *launches = g_profile_launches;
+    if (milliseconds) *milliseconds = g_profile_ms;
+    if (flops) *flops = g_profile_flops;
+    if (reset) {
+        g_profile_launches = 0;
+        g_profile_ms = 0.0;
+        g_profile_flops = 0.0;
+    }
     return MTC_OK;
 }
 

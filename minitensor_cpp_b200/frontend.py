@@ -26,7 +26,9 @@ class Frontend:
             import torch  # noqa: F401
         except ImportError:
             pass
-        self.lib = ctypes.CDLL(str(path), mode=os.RTLD_GLOBAL)
+        # RTLD_LOCAL: the backend library and the oracle define the same MiniTensor
+        # symbols; each must bind to its own copy (both are linked -Bsymbolic)
+        self.lib = ctypes.CDLL(str(path), mode=os.RTLD_LOCAL)
         L = self.lib
         P = ctypes.POINTER
         vp, i32, i64, u64, f32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64, ctypes.c_float
@@ -44,6 +46,7 @@ class Frontend:
             "mtb_mlp_parameters": ([vp, P(f32), i64], ctypes.c_int),
             "mtb_mlp_parameter_count": ([vp], i64),
             "mtb_mlp_synchronize": ([vp], ctypes.c_int),
+            "mtb_mlp_materialize": ([vp], ctypes.c_int),
             "mtb_mlp_stream": ([vp], vp),
             "mtb_chain": ([ctypes.c_int, i64, i64, P(f32), P(f32), P(f32), P(f32), P(f32), P(f32)], ctypes.c_int),
             "mtb_evaluator_stats": ([P(u64)], None),
@@ -145,6 +148,9 @@ class MlpTrainer:
 
     def synchronize(self):
         self.fe._check(self.fe.lib.mtb_mlp_synchronize(self.h), "mlp_synchronize")
+
+    def materialize(self):
+        self.fe._check(self.fe.lib.mtb_mlp_materialize(self.h), "mlp_materialize")
 
     def stream(self) -> int:
         return self.fe.lib.mtb_mlp_stream(self.h) or 0

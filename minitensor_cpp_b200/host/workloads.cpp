@@ -363,6 +363,14 @@ int mtb_mlp_parameters(void *handle, float *out, int64_t capacity) {
     });
 }
 
+int mtb_mlp_materialize(void *handle) {
+    return guarded([&] {
+        auto *t = static_cast<MlpTrainer *>(handle);
+        t->params = mt::nn::leafify_parameter_values(std::move(t->params));
+        t->state = mt::nn::leafify_optimizer_state(std::move(t->state));
+    });
+}
+
 int mtb_mlp_synchronize(void *handle) {
     return guarded([&] {
         auto *t = static_cast<MlpTrainer *>(handle);

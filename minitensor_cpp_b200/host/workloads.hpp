@@ -41,6 +41,8 @@ int mtb_mlp_step_host(void *handle, const float *x, const int64_t *labels, int64
 // Copies the current parameters (layer by layer: weight [out, in] then bias [out]) to host.
 int mtb_mlp_parameters(void *handle, float *out, int64_t capacity);
 int64_t mtb_mlp_parameter_count(void *handle);
+// Evaluates the (lazily initialised) parameters and optimizer state.
+int mtb_mlp_materialize(void *handle);
 // Blocks until the device finished all work of this trainer.
 int mtb_mlp_synchronize(void *handle);
 // The CUDA stream the trainer's kernels run on (NULL on the CPU).

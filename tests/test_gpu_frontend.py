@@ -78,8 +78,12 @@ def test_mlp_training_steps_match_reference(fe, ref):
         lc = c.step_resident(read_loss=True)
         assert abs(lg - lc) <= 1e-5 * abs(lc) * np.sqrt(hid), (step, lg, lc)
     pg, pc = g.parameters(), c.parameters()
-    # Adam normalises the step, so parameters move by ~lr per step: compare on that scale
-    assert np.max(np.abs(pg - pc)) <= 3 * 1e-3 * 1e-2, float(np.max(np.abs(pg - pc)))
+    # Adam's first steps move every parameter by ~lr * sign(gradient), so a
+    # gradient within rounding of 0 may flip sign between backends: such
+    # elements differ by up to 2*lr per step, all others agree to rounding.
+    diff = np.abs(pg - pc)
+    assert diff.max() <= 3 * 2 * 1e-3 + 1e-6, float(diff.max())
+    assert np.mean(diff > 1e-5) < 1e-3, float(np.mean(diff > 1e-5))
     lh = g.step_host(x.ctypes.data, y.ctypes.data, batch)
     lc = c.step_host(x.ctypes.data, y.ctypes.data, batch)
     assert abs(lh - lc) <= 1e-4 * abs(lc), (lh, lc)

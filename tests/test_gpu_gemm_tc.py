@@ -1,0 +1,83 @@
+"""Parity of the tcgen05 3xTF32 tensor-core GEMM (forced, no SIMT fallback)
+against the float32 oracle: |C - C_ref| <= 1e-5 * sqrt(K) * (|A| |B|)_ij, the
+normwise per-element form of the 1e-5*sqrt(K) relative bound."""
+import numpy as np
+import pytest
+
+from helpers import assert_rel_sqrtk
+from minitensor_cpp_b200 import abi
+from oracle import mt_oracle as mo
+
+pytestmark = pytest.mark.gpu
+
+F = np.float32
+
+
+def _run(a_st, a_shape, a_strides, b_st, b_shape, b_strides, out_offset=0, algo=abi.GEMM_3XTF32):
+    import torch
+
+    av = mo.view(a_st, a_shape, a_strides, 0)
+    bv = mo.view(b_st, b_shape, b_strides, 0)
+    exp = mo.matmul(av, bv)
+    A = abi.View(torch.from_numpy(a_st).cuda(), tuple(a_shape), tuple(a_strides), 0)
+    B = abi.View(torch.from_numpy(b_st).cuda(), tuple(b_shape), tuple(b_strides), 0)
+    out_st = torch.full((exp.size + out_offset,), -3.0, device="cuda")
+    C = abi.View(out_st, exp.shape, tuple(abi.contiguous_strides(list(exp.shape))), out_offset)
+    abi.matmul(A, B, C, algo)
+    torch.cuda.synchronize()
+    abi.check_device_errors(0)
+    got = out_st.cpu().numpy()
+    assert (got[:out_offset] == -3.0).all(), "wrote before the output offset"
+    scale = mo.matmul(np.abs(av), np.abs(bv))
+    assert_rel_sqrtk(got[out_offset:], exp.reshape(-1), av.shape[-1], scale.reshape(-1),
+                     f"3xTF32 {a_shape}x{b_shape}")
+    return got[out_offset:].reshape(exp.shape), exp
+
+
+def test_tile_aligned_contiguous(cuda):
+    rng = np.random.default_rng(1)
+    M, N, K = 256, 512, 64
+    _run(rng.standard_normal(M * K).astype(F), [M, K], [K, 1], rng.standard_normal(K * N).astype(F), [K, N], [N, 1])
+
+
+def test_ragged_edges_and_k_tail(cuda):
+    rng = np.random.default_rng(2)
+    for M, N, K in ((300, 520, 100), (129, 257, 35), (1000, 700, 513)):
+        _run(rng.standard_normal(M * K).astype(F), [M, K], [K, 1], rng.standard_normal(K * N).astype(F), [K, N],
+             [N, 1], out_offset=3)
+
+
+def test_transposed_operands(cuda):
+    rng = np.random.default_rng(3)
+    M, N, K = 384, 320, 200
+    a = rng.standard_normal(M * K).astype(F)
+    b = rng.standard_normal(N * K).astype(F)
+    _run(a, [M, K], [K, 1], b, [K, N], [1, K])   # x @ W^T (Linear forward)
+    _run(a, [M, K], [1, M], b, [K, N], [N, 1])   # A^T @ B (weight gradient)
+    _run(a, [M, K], [1, M], b, [K, N], [1, K])   # both transposed
+
+
+def test_batched_with_broadcast(cuda):
+    rng = np.random.default_rng(4)
+    a = rng.standard_normal(3 * 2 * 130 * 70).astype(F)
+    b = rng.standard_normal(2 * 70 * 260).astype(F)
+    _run(a, [3, 2, 130, 70], [2 * 130 * 70, 130 * 70, 70, 1], b, [2, 70, 260], [70 * 260, 260, 1])
+
+
+def test_large_values_and_specials_stay_finite(cuda):
+    rng = np.random.default_rng(5)
+    M, N, K = 128, 256, 64
+    a = (rng.standard_normal(M * K) * 1e18).astype(F)
+    b = (rng.standard_normal(K * N) * 1e-18).astype(F)
+    _run(a, [M, K], [K, 1], b, [K, N], [N, 1])
+
+
+def test_auto_uses_tensor_cores_for_large_problems(cuda):
+    rng = np.random.default_rng(6)
+    M = N = K = 512
+    abi.profile_gemm(reset=True)
+    got, exp = _run(rng.standard_normal(M * K).astype(F), [M, K], [K, 1], rng.standard_normal(K * N).astype(F),
+                    [K, N], [N, 1], algo=abi.GEMM_AUTO)
+    simt_got, _ = _run(rng.standard_normal(M * K).astype(F), [M, K], [K, 1], rng.standard_normal(K * N).astype(F),
+                       [K, N], [N, 1], algo=abi.GEMM_SIMT)
+    assert got.shape == exp.shape
