@@ -188,6 +188,103 @@ def _worker(args):
     return cpu_reference_sample(batch, steps)
 
 
+# ------------------------------------------------------------ micro (N=1) --
+
+def _time_ms(fn, iters=5, warm=2, stream=None) -> float:
+    import torch
+
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(iters):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        fn()
+        e.record(stream)
+        torch.cuda.synchronize()
+        best = min(best, s.elapsed_time(e))
+    return best
+
+
+def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
+    """The elementwise/reduction, GEMM and indexing benchmarks, kernel-level
+    through the C ABI on cuda:0 (best of 5, inputs larger than L2)."""
+    import torch
+
+    from minitensor_cpp_b200 import abi
+
+    out = {}
+    gbs = lambda nbytes, ms: nbytes / (ms * 1e-3) / 1e9
+    # -- broadcast/strided chain relu(A*B^T + row)*exp(-col) and reductions on 8192^2
+    n = 8192
+    g = torch.Generator(device="cuda").manual_seed(SEED)
+    A = torch.rand(n, n, device="cuda", generator=g) * 2 - 1
+    Bs = torch.rand(n, n, device="cuda", generator=g) * 2 - 1
+    row = torch.rand(1, n, device="cuda", generator=g) * 2 - 1
+    col = torch.rand(n, 1, device="cuda", generator=g) * 2 - 1
+    Y = torch.empty(n, n, device="cuda")
+    prog = [(abi.MULTIPLY, 4, 0, 1, 0.0), (abi.ADD, 5, 4, 2, 0.0), (abi.RELU, 6, 5, 0, 0.0),
+            (abi.NEGATE, 7, 3, 0, 0.0), (abi.EXP, 8, 7, 0, 0.0), (abi.MULTIPLY, 9, 6, 8, 0.0)]
+    ins = [abi.View.of(A), abi.View.of(Bs.t()), abi.View.of(row), abi.View.of(col)]
+    ms = _time_ms(lambda: abi.fused(prog, ins, [9], [abi.View.of(Y)]))
+    out["chain_fused_GBps"] = gbs(12 * n * n, ms)
+    vY = abi.View.of(Y)
+    o = torch.empty(n, device="cuda")
+    oi = torch.empty(n, device="cuda", dtype=torch.int64)
+    for ax in (0, 1):
+        for name, op, dst in (("sum", abi.SUM, o), ("max", abi.MAX, o), ("argmax", abi.ARGMAX, oi)):
+            ms = _time_ms(lambda: abi.reduce(op, vY, [ax], abi.View.of(dst)))
+            out[f"{name}_axis{ax}_GBps"] = gbs(4 * n * n, ms)
+    Z = torch.empty(n, n, device="cuda")
+    ms = _time_ms(lambda: abi.log_softmax(vY, 1, abi.View.of(Z)))
+    out["log_softmax_axis1_GBps"] = gbs(8 * n * n, ms)
+    hb = [v for k, v in out.items() if k.endswith("GBps")]
+    out["elementwise_reduce_min_frac_of_hbm"] = min(hb) / hbm_gbs
+    del A, Bs, Y, Z
+    # -- GEMM sweep (3xTF32 tensor cores)
+    peak3 = tf32_tflops / 3.0
+    for m in (2048, 4096, 8192):
+        a = torch.randn(m, m, device="cuda")
+        b = torch.randn(m, m, device="cuda")
+        c = torch.empty(m, m, device="cuda")
+        for tag, bv in (("", abi.View.of(b)), ("_bT", abi.View.of(b.t()))):
+            ms = _time_ms(lambda: abi.matmul(abi.View.of(a), bv, abi.View.of(c)), iters=3)
+            out[f"gemm_{m}{tag}_TFLOPs"] = 2 * m ** 3 / (ms * 1e-3) / 1e12
+    out["gemm_8192_frac_of_3xtf32"] = out["gemm_8192_TFLOPs"] / peak3
+    a = torch.randn(64, 1024, 1024, device="cuda")
+    b = torch.randn(64, 1024, 1024, device="cuda")
+    c = torch.empty(64, 1024, 1024, device="cuda")
+    ms = _time_ms(lambda: abi.matmul(abi.View.of(a), abi.View.of(b), abi.View.of(c)), iters=3)
+    out["gemm_batched_64x1024_TFLOPs"] = 2 * 64 * 1024 ** 3 / (ms * 1e-3) / 1e12
+    a = torch.randn(65536, 1024, device="cuda")
+    b = torch.randn(1024, 8192, device="cuda")
+    c = torch.empty(65536, 8192, device="cuda")
+    ms = _time_ms(lambda: abi.matmul(abi.View.of(a), abi.View.of(b), abi.View.of(c)), iters=3)
+    out["gemm_skinny_65536x1024x8192_TFLOPs"] = 2 * 65536 * 1024 * 8192 / (ms * 1e-3) / 1e12
+    del a, b, c
+    # -- Int64 gather / scatter-add of 2^24 rows of 64 floats, concat 4 x [4096, 8192]
+    rows, width = 1 << 24, 64
+    table = torch.randn(rows, width, device="cuda")
+    idx = torch.randint(0, rows, (rows, 1), device="cuda", dtype=torch.int64, generator=g)
+    idx_b = abi.View(idx.view(-1), (rows, width), (1, 0), 0)  # broadcast_to([rows, width])
+    res = torch.empty(rows, width, device="cuda")
+    ms = _time_ms(lambda: abi.gather(abi.View.of(table), idx_b, 0, abi.View.of(res)), iters=3)
+    out["gather_rows_GBps"] = gbs(rows * 520, ms)
+    upd = torch.floor(torch.rand(rows, width, device="cuda", generator=g) * 16 - 8)
+    ms = _time_ms(lambda: abi.gather_scatter_add(abi.View.of(upd), idx_b, 0, abi.View.of(res)), iters=3)
+    out["scatter_add_rows_GBps"] = gbs(rows * 520, ms)
+    del table, idx, res, upd
+    parts = [torch.randn(4096, 8192, device="cuda") for _ in range(4)]
+    for axis, shape in ((0, (16384, 8192)), (1, (4096, 32768))):
+        dst = torch.empty(shape, device="cuda")
+        ms = _time_ms(lambda: abi.concat([abi.View.of(p) for p in parts], axis, abi.View.of(dst)), iters=3)
+        out[f"concat_axis{axis}_GBps"] = gbs(2 * 4 * 4096 * 8192 * 4, ms)
+    del parts
+    torch.cuda.empty_cache()
+    return {k: round(v, 3) for k, v in out.items()}
+
+
 # ----------------------------------------------------------------- our arm --
 
 def run_ours(args) -> None:
@@ -283,6 +380,12 @@ def run_ours(args) -> None:
     wall_e2e = time.perf_counter() - t0
 
     tf32 = measure_tf32_peak() if rank == 0 else None
+    micro = None
+    if world == 1 and not args.skip_micro:
+        peaks_file = ROOT / "MEASURED_PEAKS.json"
+        hbm = json.loads(peaks_file.read_text()).get("hbm_gbs", 6650.0) if peaks_file.exists() else 6650.0
+        tr.close()
+        micro = micro_benchmarks(hbm, tf32)
     if comm is not None:
         barrier()
         abi.lib().mtc_comm_destroy(comm)
@@ -338,6 +441,7 @@ def run_ours(args) -> None:
         "roofline": roofline,
         "cpu_baseline": cpu,
         "clocks": clocks.summary(),
+        "micro": micro,
     }
     print(json.dumps(line), flush=True)
 
@@ -404,6 +508,7 @@ def main() -> None:
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--cpu-batch", type=int, default=4)
     p.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline sample")
+    p.add_argument("--skip-micro", action="store_true", help="omit the kernel microbenchmarks (N=1 only)")
     args = p.parse_args()
     if args.warmup < 3:
         p.error("--warmup must be at least 3")

@@ -215,9 +215,12 @@ int mtc_log_softmax(const mtc_desc *in, int64_t axis, const mtc_desc *out, void 
 /* ---------------------------------------------------------------- GEMM (A10) -- */
 
 enum {
-    MTC_GEMM_AUTO = 0,     /* tensor-core 3xTF32 where the shape suits it, else SIMT */
-    MTC_GEMM_SIMT = 1,     /* exact float32 FFMA kernel, any strides */
-    MTC_GEMM_3XTF32 = 2    /* tcgen05/TMEM kernel, split-float32 (hi+lo) operands */
+    MTC_GEMM_AUTO = 0,      /* 3xTF32 tensor cores for large problems (M, N >= 128, K >= 64,
+                               M*N*K >= 2^28), the exact SIMT kernel otherwise */
+    MTC_GEMM_SIMT = 1,      /* exact SIMT kernel: float product then float sum per k, k ascending,
+                               the CPU reference's rounding and order (bit-identical results) */
+    MTC_GEMM_3XTF32 = 2,    /* tcgen05/TMEM kernel, split-float32 (hi+lo) operands */
+    MTC_GEMM_SIMT_FFMA = 3  /* SIMT kernel with one fused multiply-add per k */
 };
 
 /* matmul with the reference's full semantics (Matmul 0x0401, matmul_dispatch,

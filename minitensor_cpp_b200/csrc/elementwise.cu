@@ -91,6 +91,35 @@ int plan_elementwise(const mtc_desc *inputs, int n_in, const mtc_desc *outputs, 
         a.div[d] = MtcFastDiv{f.d, f.mul, f.shift};
     }
 
+    // Rows: contiguous output rows; every input contiguous or broadcast along them.
+    if (s.rank >= 2) {
+        const int r = s.rank;
+        bool rows_ok = true;
+        for (int k = 0; k < s.nops && rows_ok; ++k) {
+            const int64_t inner = s.stride[k][r - 1];
+            rows_ok = k < n_out ? inner == 1 : (inner == 0 || inner == 1);
+        }
+        if (rows_ok) {
+            const int64_t cols = s.shape[r - 1];
+            bool vec = cols % 4 == 0;
+            for (int k = 0; k < s.nops && vec; ++k) {
+                const bool is_out = k < n_out;
+                const float *p = is_out ? a.out[k] : a.in[k - n_out];
+                const int64_t off = is_out ? a.out_off[k] : a.in_off[k - n_out];
+                if (s.stride[k][r - 1] == 0) continue;
+                vec = (reinterpret_cast<uintptr_t>(p + off) % 16) == 0;
+                for (int d = 0; d < r - 1 && vec; ++d) vec = (s.stride[k][d] % 4) == 0;
+            }
+            plan.variant = vec ? EwVariant::Rows4 : EwVariant::Rows1;
+            const int64_t strip = 256 * (vec ? 4 : 1);
+            const int64_t tasks = (s.numel / cols) * ((cols + strip - 1) / strip);
+            long long blocks = tasks;
+            if (blocks > static_cast<long long>(sms) * 8) blocks = static_cast<long long>(sms) * 8;
+            plan.grid = dim3(static_cast<unsigned>(blocks < 1 ? 1 : blocks));
+            return MTC_OK;
+        }
+    }
+
     // Tiled: contiguous output rows, some input contiguous along the other axis.
     if (s.rank >= 2) {
         const int r = s.rank;
@@ -142,6 +171,12 @@ int launch(const EwPlan &p, cudaStream_t stream) {
         break;
     case EwVariant::Strided:
         mtc_ew_strided<Op><<<p.grid, p.block, 0, stream>>>(p.args);
+        break;
+    case EwVariant::Rows4:
+        mtc_ew_rows<Op, 4><<<p.grid, p.block, 0, stream>>>(p.args);
+        break;
+    case EwVariant::Rows1:
+        mtc_ew_rows<Op, 1><<<p.grid, p.block, 0, stream>>>(p.args);
         break;
     case EwVariant::Tiled1:
         mtc_ew_tiled<Op, 1><<<p.grid, p.block, 0, stream>>>(p.args);

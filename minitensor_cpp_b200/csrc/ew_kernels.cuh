@@ -218,6 +218,81 @@ __global__ void __launch_bounds__(256) mtc_ew_strided(const MtcEwArgs a) {
     }
 }
 
+// ------------------------------------------------------------ rows kernel --
+// Spaces whose innermost axis is contiguous for every output and, for every
+// input, contiguous (stride 1) or broadcast (stride 0): a bias row, a column
+// vector, a scalar.  Each task is a 4*blockDim-wide strip of one row; the row's
+// outer offsets are decoded once per task (not per element) and VEC = 4 moves
+// 128 bits per contiguous operand (row starts 16-byte aligned, cols % 4 == 0).
+
+template <class Op, int VEC>
+__global__ void __launch_bounds__(256) mtc_ew_rows(const MtcEwArgs a) {
+    constexpr int NIN = Op::kIn;
+    constexpr int NOUT = Op::kOut;
+    const Op op;
+    const int r = a.rank;
+    const long long cols = a.shape[r - 1];
+    const long long strip = static_cast<long long>(blockDim.x) * VEC;
+    const long long strips = (cols + strip - 1) / strip;
+    const long long rows = a.numel / cols;
+    for (long long task = blockIdx.x; task < rows * strips; task += gridDim.x) {
+        const long long row = task / strips;
+        const long long c0 = (task - row * strips) * strip + static_cast<long long>(threadIdx.x) * VEC;
+        long long ib[NIN > 0 ? NIN : 1];
+        long long ob[NOUT];
+#pragma unroll
+        for (int k = 0; k < NIN; ++k) ib[k] = a.in_off[k];
+#pragma unroll
+        for (int j = 0; j < NOUT; ++j) ob[j] = a.out_off[j];
+        unsigned int rem = static_cast<unsigned int>(row);
+#pragma unroll
+        for (int d = MTC_EW_MAX_RANK - 2; d >= 0; --d) {
+            if (d < r - 1) {
+                const unsigned int q = (d > 0) ? mtc_fastdiv(rem, a.div[d]) : 0u;
+                const long long c = static_cast<long long>(d > 0 ? rem - q * a.shape[d] : rem);
+                rem = q;
+#pragma unroll
+                for (int k = 0; k < NIN; ++k) ib[k] += c * a.in_str[k][d];
+#pragma unroll
+                for (int j = 0; j < NOUT; ++j) ob[j] += c * a.out_str[j][d];
+            }
+        }
+        if (c0 >= cols) continue;
+        float x[VEC][NIN > 0 ? NIN : 1];
+        float y[VEC][NOUT];
+        if (VEC == 4 && c0 + 4 <= cols) {
+#pragma unroll
+            for (int k = 0; k < NIN; ++k) {
+                if (a.in_str[k][r - 1] == 0) {
+                    const float s = __ldg(a.in[k] + ib[k]);
+#pragma unroll
+                    for (int l = 0; l < VEC; ++l) x[l][k] = s;
+                } else {
+                    const float4 q = __ldg(reinterpret_cast<const float4 *>(a.in[k] + ib[k] + c0));
+                    x[0][k] = q.x;
+                    x[1][k] = q.y;
+                    x[2][k] = q.z;
+                    x[3][k] = q.w;
+                }
+            }
+#pragma unroll
+            for (int l = 0; l < VEC; ++l) op(x[l], y[l], a.imm);
+#pragma unroll
+            for (int j = 0; j < NOUT; ++j)
+                *reinterpret_cast<float4 *>(a.out[j] + ob[j] + c0) = make_float4(y[0][j], y[1][j], y[2][j], y[3][j]);
+        } else {
+            for (int l = 0; l < VEC && c0 + l < cols; ++l) {
+#pragma unroll
+                for (int k = 0; k < NIN; ++k)
+                    x[0][k] = __ldg(a.in[k] + ib[k] + (c0 + l) * a.in_str[k][r - 1]);
+                op(x[0], y[0], a.imm);
+#pragma unroll
+                for (int j = 0; j < NOUT; ++j) a.out[j][ob[j] + c0 + l] = y[0][j];
+            }
+        }
+    }
+}
+
 // ----------------------------------------------------------- tiled kernel --
 // For spaces whose innermost output axis is contiguous while some inputs are
 // contiguous along the second-innermost axis instead (a transposed view, e.g.

@@ -22,6 +22,7 @@ struct SimtArgs {
     int b_nmajor;  // B is contiguous along n (row-major B)
 };
 
+template <bool EXACT>
 __global__ void __launch_bounds__(256, 2) k_gemm_simt(const SimtArgs args) {
     const GemmProblem &p = args.p;
     __shared__ __align__(16) float As[2][BK][BM + PAD];
@@ -120,7 +121,12 @@ __global__ void __launch_bounds__(256, 2) k_gemm_simt(const SimtArgs args) {
 #pragma unroll
             for (int i = 0; i < 8; ++i)
 #pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+                for (int j = 0; j < 8; ++j) {
+                    // EXACT: the reference's rounding, a float product then a float
+                    // sum per k in ascending order (linalg/loops.hpp:231-245)
+                    if (EXACT) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], bv[j]));
+                    else acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+                }
         }
         if (kt + 1 < ktiles) store_tile(buf ^ 1);
         __syncthreads();
@@ -140,7 +146,7 @@ __global__ void __launch_bounds__(256, 2) k_gemm_simt(const SimtArgs args) {
 
 }  // namespace
 
-int gemm_simt(const GemmProblem &p, cudaStream_t stream) {
+int gemm_simt(const GemmProblem &p, cudaStream_t stream, bool exact) {
     if (p.M == 0 || p.N == 0 || p.batch == 0) return MTC_OK;
     SimtArgs args;
     args.p = p;
@@ -150,7 +156,8 @@ int gemm_simt(const GemmProblem &p, cudaStream_t stream) {
     if (gy > 65535) return fail(MTC_ERR_UNSUPPORTED, "matmul with more than %d row tiles", 65535);
     if (p.batch > 65535) return fail(MTC_ERR_UNSUPPORTED, "matmul with more than 65535 batch entries");
     dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(gy), static_cast<unsigned>(p.batch));
-    k_gemm_simt<<<grid, 256, 0, stream>>>(args);
+    if (exact) k_gemm_simt<true><<<grid, 256, 0, stream>>>(args);
+    else k_gemm_simt<false><<<grid, 256, 0, stream>>>(args);
     MTC_TRY(check_launch("SIMT GEMM"));
     return MTC_OK;
 }
@@ -222,17 +229,23 @@ extern "C" int mtc_matmul(const mtc_desc *lhs, const mtc_desc *rhs, const mtc_de
         const float zero = 0.0f;
         return mtc_fill(out, &zero, stream);
     }
-    if (algo != MTC_GEMM_SIMT && algo != MTC_GEMM_3XTF32 && algo != MTC_GEMM_AUTO)
+    if (algo != MTC_GEMM_SIMT && algo != MTC_GEMM_3XTF32 && algo != MTC_GEMM_AUTO && algo != MTC_GEMM_SIMT_FFMA)
         return fail(MTC_ERR_INVALID_ARGUMENT, "unknown matmul algorithm %d", algo);
     void *mark = profiling() ? profile_begin(s) : nullptr;
     int rc;
-    if (algo == MTC_GEMM_SIMT) {
-        rc = gemm_simt(p, s);
+    // AUTO: tensor cores for problems large enough to amortise the split pack,
+    // otherwise the exact-order SIMT kernel (bit-identical to the CPU reference)
+    const double macs = double(p.M) * double(p.N) * double(p.K) * double(p.batch);
+    const bool large = p.M >= 128 && p.N >= 128 && p.K >= 64 && macs >= double(1 << 28);
+    if (algo == MTC_GEMM_SIMT || (algo == MTC_GEMM_AUTO && !large)) {
+        rc = gemm_simt(p, s, true);
+    } else if (algo == MTC_GEMM_SIMT_FFMA) {
+        rc = gemm_simt(p, s, false);
     } else {
         rc = gemm_3xtf32(p, s);
         if (rc == MTC_ERR_UNSUPPORTED && algo == MTC_GEMM_AUTO) {
             clear_error();
-            rc = gemm_simt(p, s);
+            rc = gemm_simt(p, s, true);
         }
     }
     if (mark != nullptr) profile_end(mark, s, 2.0 * double(p.M) * double(p.N) * double(p.K) * double(p.batch));

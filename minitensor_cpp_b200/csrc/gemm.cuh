@@ -25,7 +25,8 @@ struct GemmProblem {
 
 // tcgen05 3xTF32 path; returns MTC_ERR_UNSUPPORTED when the problem does not suit it.
 int gemm_3xtf32(const GemmProblem &p, cudaStream_t stream);
-// Exact float32 FFMA path (any strides, any sizes).
-int gemm_simt(const GemmProblem &p, cudaStream_t stream);
+// SIMT path (any strides, any sizes).  exact: the CPU reference's rounding and
+// order (float product, then float sum, k ascending); otherwise one FFMA per k.
+int gemm_simt(const GemmProblem &p, cudaStream_t stream, bool exact);
 
 }  // namespace mtc

@@ -195,7 +195,22 @@ __device__ __forceinline__ State accumulate_row(const RedArgs &a, long long base
     if (a.vec4) {
         const float4 *p = reinterpret_cast<const float4 *>(a.in + base);
         const long long nv = R / 4;
-        for (long long v = lane; v < nv; v += lanes) {
+        long long v = lane;
+        // four independent 128-bit loads in flight per thread, consumed in index order
+        for (; v + 3LL * lanes < nv; v += 4LL * lanes) {
+            float4 q[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) q[u] = __ldg(p + v + u * lanes);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const long long e = 4 * (v + u * lanes);
+                Reducer<OP>::add(s, q[u].x, e);
+                Reducer<OP>::add(s, q[u].y, e + 1);
+                Reducer<OP>::add(s, q[u].z, e + 2);
+                Reducer<OP>::add(s, q[u].w, e + 3);
+            }
+        }
+        for (; v < nv; v += lanes) {
             const float4 q = __ldg(p + v);
             Reducer<OP>::add(s, q.x, 4 * v);
             Reducer<OP>::add(s, q.y, 4 * v + 1);
@@ -274,7 +289,22 @@ __global__ void __launch_bounds__(256) k_per_output(const RedArgs a) {
                 off += static_cast<long long>(coord[d]) * a.rstr[d];
             }
             const int inner = a.rrank - 1;
-            for (long long r = r0; r < r1; ++r) {
+            long long r = r0;
+            if (a.rrank == 1) {
+                // single reduced axis: eight independent loads in flight, consumed in order
+                const long long st = a.rstr[0];
+                const float *q = a.in + off;
+                for (; r + 8 <= r1; r += 8, q += 8 * st) {
+                    float v[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) v[u] = __ldg(q + u * st);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) Reducer<OP>::add(s, v[u], r + u);
+                }
+                off = q - a.in;
+                coord[0] = static_cast<unsigned int>(r);
+            }
+            for (; r < r1; ++r) {
                 Reducer<OP>::add(s, __ldg(a.in + off), r);
                 // advance the odometer
                 if (++coord[inner] < a.rshape[inner]) {
@@ -295,6 +325,68 @@ __global__ void __launch_bounds__(256) k_per_output(const RedArgs a) {
         }
         if (a.chunks == 1) store_result<OP>(a, o, s);
         else a.partial[o * a.chunks + c] = s;
+    }
+}
+
+// Visits the reduced elements of one output in the reference's order (reduced
+// axes row-major, ReductionPlan, iteration/reduction.cpp:14-121).
+template <class F>
+__device__ __forceinline__ void walk_reduced(const RedArgs &a, long long base, F &&f) {
+    unsigned int coord[MTC_MAX_RANK];
+    for (int d = 0; d < a.rrank; ++d) coord[d] = 0;
+    long long off = base;
+    const int inner = a.rrank - 1;
+    for (long long r = 0; r < a.R; ++r) {
+        f(__ldg(a.in + off), r);
+        if (++coord[inner] < a.rshape[inner]) {
+            off += a.rstr[inner];
+        } else {
+            off -= static_cast<long long>(a.rshape[inner] - 1) * a.rstr[inner];
+            coord[inner] = 0;
+            for (int d = inner - 1; d >= 0; --d) {
+                if (++coord[d] < a.rshape[d]) {
+                    off += a.rstr[d];
+                    break;
+                }
+                off -= static_cast<long long>(a.rshape[d] - 1) * a.rstr[d];
+                coord[d] = 0;
+            }
+        }
+    }
+}
+
+// Small reductions in the reference's exact arithmetic: one thread per output,
+// sequential float accumulation for sum (reduction/loops.hpp:21-57) and the
+// two-pass max / sum-of-exp form for logsumexp (loops.hpp:59-136).  Sums are
+// bit-identical to the CPU; logsumexp differs only by the libm ulps of exp/log.
+template <int OP>
+__global__ void __launch_bounds__(128) k_exact_small(const RedArgs a) {
+    for (long long o = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; o < a.nout;
+         o += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long base = kept_offset(a, static_cast<unsigned int>(o));
+        if constexpr (OP == MTC_OP_LOGSUMEXP) {
+            float mx = -INFINITY;
+            bool nan = false;
+            walk_reduced(a, base, [&](float x, long long) {
+                if (x != x) nan = true;
+                else mx = (mx < x) ? x : mx;  // std::max(mx, x)
+            });
+            float result;
+            if (nan) {
+                result = NAN;
+            } else if (isinf(mx)) {
+                result = mx;
+            } else {
+                float s = 0.0f;
+                walk_reduced(a, base, [&](float x, long long) { s = __fadd_rn(s, expf(__fsub_rn(x, mx))); });
+                result = __fadd_rn(mx, logf(s));
+            }
+            static_cast<float *>(a.out)[a.out_off + o] = result;
+        } else {
+            State s = Reducer<OP>::init();
+            walk_reduced(a, base, [&](float x, long long r) { Reducer<OP>::add(s, x, r); });
+            store_result<OP>(a, o, s);
+        }
     }
 }
 
@@ -335,6 +427,109 @@ __global__ void __launch_bounds__(512) k_log_softmax_rows(const RedArgs a) {
                 dst[j] = __fsub_rn(__ldg(a.in + base + j * a.rrun_stride), lse);
         }
     }
+}
+
+// Row-resident logsumexp / log-softmax for contiguous rows of R <= 8192 floats
+// (R % 4 == 0): 256 threads hold the row in registers (NV4 float4 each), take the
+// NaN-ignoring maximum, then sum exp(x - max) exactly like the reference's two
+// passes (reduction/loops.hpp:59-136) but reading HBM once.  With a.out_f set,
+// x - lse is written from the registers (log-softmax: 8 bytes per element).
+template <int NV4>
+__global__ void __launch_bounds__(256) k_lse_resident(const RedArgs a) {
+    __shared__ float red_f[8];
+    __shared__ int red_i[8];
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const long long nv = a.R / 4;
+    for (long long o = blockIdx.x; o < a.nout; o += gridDim.x) {
+        const long long base = kept_offset(a, static_cast<unsigned int>(o));
+        const float4 *p = reinterpret_cast<const float4 *>(a.in + base);
+        float4 v[NV4];
+        float mx = -INFINITY;
+        int flags = 0;  // bit0 NaN, bit1 +inf
+#pragma unroll
+        for (int i = 0; i < NV4; ++i) {
+            const long long idx = threadIdx.x + 256LL * i;
+            v[i] = idx < nv ? __ldg(p + idx) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        }
+#pragma unroll
+        for (int i = 0; i < NV4; ++i) {
+            const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (e[j] != e[j]) flags |= 1;
+                else {
+                    if (e[j] == INFINITY) flags |= 2;
+                    mx = fmaxf(mx, e[j]);
+                }
+            }
+        }
+#pragma unroll
+        for (int d = 16; d >= 1; d >>= 1) {
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+            flags |= __shfl_xor_sync(0xffffffffu, flags, d);
+        }
+        if (lane == 0) {
+            red_f[warp] = mx;
+            red_i[warp] = flags;
+        }
+        __syncthreads();
+        mx = red_f[0];
+        flags = red_i[0];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) {
+            mx = fmaxf(mx, red_f[w]);
+            flags |= red_i[w];
+        }
+        __syncthreads();
+        float lse;
+        if (flags & 1) {
+            lse = NAN;
+        } else if (isinf(mx)) {
+            lse = mx;
+        } else {
+            float s = 0.0f;
+#pragma unroll
+            for (int i = 0; i < NV4; ++i) {
+                s += expf(__fsub_rn(v[i].x, mx));
+                s += expf(__fsub_rn(v[i].y, mx));
+                s += expf(__fsub_rn(v[i].z, mx));
+                s += expf(__fsub_rn(v[i].w, mx));
+            }
+#pragma unroll
+            for (int d = 16; d >= 1; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
+            if (lane == 0) red_f[warp] = s;
+            __syncthreads();
+            s = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) s += red_f[w];
+            __syncthreads();
+            lse = __fadd_rn(mx, logf(s));
+        }
+        if (a.out_f != nullptr) {
+            float4 *q = reinterpret_cast<float4 *>(a.out_f + a.out_off + o * a.out_row_stride);
+#pragma unroll
+            for (int i = 0; i < NV4; ++i) {
+                const long long idx = threadIdx.x + 256LL * i;
+                if (idx < nv)
+                    q[idx] = make_float4(__fsub_rn(v[i].x, lse), __fsub_rn(v[i].y, lse), __fsub_rn(v[i].z, lse),
+                                         __fsub_rn(v[i].w, lse));
+            }
+        } else if (threadIdx.x == 0) {
+            static_cast<float *>(a.out)[a.out_off + o] = lse;
+        }
+    }
+}
+
+int launch_lse_resident(RedArgs &a, cudaStream_t stream, int sms) {
+    const long long nv = a.R / 4;
+    long long blocks = a.nout;
+    if (blocks > static_cast<long long>(sms) * 8) blocks = static_cast<long long>(sms) * 8;
+    const dim3 grid(static_cast<unsigned>(blocks < 1 ? 1 : blocks));
+    if (nv <= 256) k_lse_resident<1><<<grid, 256, 0, stream>>>(a);
+    else if (nv <= 512) k_lse_resident<2><<<grid, 256, 0, stream>>>(a);
+    else if (nv <= 1024) k_lse_resident<4><<<grid, 256, 0, stream>>>(a);
+    else k_lse_resident<8><<<grid, 256, 0, stream>>>(a);
+    return check_launch("row-resident logsumexp");
 }
 
 struct RedPlan {
@@ -419,8 +614,20 @@ int run_reduction(RedPlan &p, cudaStream_t stream) {
     RedArgs &a = p.args;
     if (p.empty_out) return MTC_OK;
     const int sms = sm_count(current_device());
+    if (a.R <= 8192 && a.nout * a.R <= (1LL << 21)) {
+        // small: the reference's own order and rounding
+        long long blocks = (a.nout + 127) / 128;
+        if (blocks > static_cast<long long>(sms) * 16) blocks = static_cast<long long>(sms) * 16;
+        k_exact_small<OP><<<static_cast<unsigned>(blocks < 1 ? 1 : blocks), 128, 0, stream>>>(a);
+        return check_launch("exact reduction");
+    }
+    if (p.row && OP == MTC_OP_LOGSUMEXP && a.vec4 && a.R <= 8192) {
+        // whole row held in registers: max, then sum of exp(x - max), one read of HBM
+        a.out_f = nullptr;
+        return launch_lse_resident(a, stream, sms);
+    }
     if (p.row) {
-        if (a.R <= 2048) {
+        if (a.R <= 2048 || a.nout >= 4LL * sms) {
             long long blocks = (a.nout + 7) / 8;
             if (blocks > static_cast<long long>(sms) * 8) blocks = static_cast<long long>(sms) * 8;
             k_row_warp<OP><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
@@ -526,6 +733,7 @@ extern "C" int mtc_log_softmax(const mtc_desc *in, int64_t axis, const mtc_desc 
             a.out_row_stride = in->shape[axis];
             if (a.vec4) a.vec4 = ((reinterpret_cast<uintptr_t>(a.out_f + a.out_off) % 16) == 0) ? 1 : 0;
             const int sms = sm_count(current_device());
+            if (a.vec4 && a.R <= 8192) return launch_lse_resident(a, s, sms);
             long long blocks = a.nout;
             if (blocks > static_cast<long long>(sms) * 4) blocks = static_cast<long long>(sms) * 4;
             k_log_softmax_rows<<<static_cast<unsigned>(blocks), 512, 0, s>>>(a);

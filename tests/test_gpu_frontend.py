@@ -34,12 +34,19 @@ def test_spiral_loss_curve_matches_reference(fe, ref):
     steps = 2000
     gpu_losses, _ = fe.spiral_train(0, steps, loss_every=1)
     cpu_losses, _ = ref.spiral_train(-1, steps, loss_every=1)
+    # The reference's own sensitivity: the same CPU run with the learning rate
+    # moved by one float32 ulp.  Adam amplifies last-bit differences (a gradient
+    # within rounding of zero flips sign and moves its parameter by 2*lr), so the
+    # GPU curve is required to stay within 3x of that noise floor.
+    lr_ulp = float(np.nextafter(np.float32(1e-2), np.float32(1)))
+    cpu_perturbed, _ = ref.spiral_train(-1, steps, lr=lr_ulp, loss_every=1)
+    noise = np.abs(cpu_perturbed.astype(np.float64) - cpu_losses) / np.abs(cpu_losses)
     assert np.isfinite(gpu_losses).all()
     rel = np.abs(gpu_losses.astype(np.float64) - cpu_losses) / np.abs(cpu_losses)
-    assert rel[0] <= 1e-5, rel[0]
-    assert rel[:200].max() <= 1e-3, (int(rel[:200].argmax()), float(rel[:200].max()))
-    assert rel[-1] <= 1e-2, float(rel[-1])
-    assert gpu_losses[-1] < 0.2 * gpu_losses[0]
+    assert rel[0] <= 1e-6, rel[0]
+    assert rel[:200].max() <= 3 * noise[:200].max() + 1e-6, (float(rel[:200].max()), float(noise[:200].max()))
+    assert rel[-1] <= max(1e-2, 3 * noise[-1]), (float(rel[-1]), float(noise[-1]))
+    assert gpu_losses[-1] < 0.05 * gpu_losses[0]
 
 
 def test_fused_chain_through_api(fe, ref):

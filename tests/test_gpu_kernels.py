@@ -509,3 +509,33 @@ def test_descriptor_validation_rejects_out_of_bounds_views(cuda):
     with pytest.raises(ValueError):
         abi.binary(abi.ADD, abi.View(st, (2, 3), (3, 1), 0), abi.View(st, (2, 2), (2, 1), 0),
                    abi.View(torch.zeros(6, device="cuda"), (2, 3), (3, 1), 0))
+
+
+def test_exact_simt_gemm_is_bit_identical_to_reference(cuda):
+    """MTC_GEMM_SIMT rounds like the CPU (float product, float sum, k ascending)."""
+    rng = np.random.default_rng(41)
+    for sa, sb, bt in (([33, 70], [70, 45], False), ([129, 257], [257, 131], True), ([7], [7, 3], False),
+                       ([2, 3, 17, 19], [19, 23], False)):
+        a = hv(rng.standard_normal(int(np.prod(sa))).astype(F), sa)
+        if bt:
+            b = hv(rng.standard_normal(int(np.prod(sb))).astype(F), sb, [1, sb[0]])
+        else:
+            b = hv(rng.standard_normal(int(np.prod(sb))).astype(F), sb)
+        exp = mo.matmul(mo.view(a.storage, a.shape, a.strides, 0), mo.view(b.storage, b.shape, b.strides, 0))
+        out = gpu(out_like(exp.shape))
+        abi.matmul(gpu(a), gpu(b), out, abi.GEMM_SIMT)
+        assert_bits(host(out)[: exp.size], exp.reshape(-1), f"exact SIMT {sa}x{sb}")
+
+
+def test_small_sums_are_bit_identical_to_reference(cuda):
+    rng = np.random.default_rng(43)
+    # reductions of at most 8192 elements per output and 2^21 in all take the
+    # reference's sequential order (the spiral model's bias gradients and loss mean)
+    x = hv(rng.standard_normal(60 * 64).astype(F), [60, 64])
+    for axes in ([0], [1], [0, 1]):
+        kept = [e for d, e in enumerate(x.shape) if d not in axes]
+        ref = out_like(kept)
+        rk.reduce(abi.SUM, x, axes, False, ref)
+        out = gpu(out_like(kept))
+        abi.reduce(abi.SUM, gpu(x), axes, out)
+        assert_bits(host(out)[: ref.storage.size], ref.storage, f"small sum {axes}")
