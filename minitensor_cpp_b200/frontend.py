@@ -16,6 +16,9 @@ import numpy as np
 
 LIB = Path(__file__).resolve().parent / "lib" / "libminitensor_b200.so"
 
+# int sum_in_place(void *buffer, size_t count): sums a float buffer over all ranks
+HOST_ALLREDUCE = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t)
+
 
 class Frontend:
     def __init__(self, path: Path | str = LIB):
@@ -40,6 +43,7 @@ class Frontend:
             "mtb_mlp_create": ([ctypes.c_int, i64, i64, i32, i64, u64, f32, P(vp)], ctypes.c_int),
             "mtb_mlp_destroy": ([vp], None),
             "mtb_mlp_set_comm": ([vp, vp, i32], ctypes.c_int),
+            "mtb_mlp_set_host_allreduce": ([vp, HOST_ALLREDUCE, i32], ctypes.c_int),
             "mtb_mlp_load_batch": ([vp, vp, vp, i64], ctypes.c_int),
             "mtb_mlp_step_resident": ([vp, i32, P(f32)], ctypes.c_int),
             "mtb_mlp_step_host": ([vp, vp, vp, i64, P(f32)], ctypes.c_int),
@@ -125,6 +129,21 @@ class MlpTrainer:
 
     def set_comm(self, comm, world: int):
         self.fe._check(self.fe.lib.mtb_mlp_set_comm(self.h, comm, world), "mlp_set_comm")
+
+    def set_host_allreduce(self, sum_in_place, world: int):
+        """CPU-device data parallelism: sum_in_place(ndarray) sums a float32 view over the ranks in place."""
+        import numpy as np
+
+        def _cb(ptr, count):
+            try:
+                arr = np.ctypeslib.as_array(ctypes.cast(ptr, ctypes.POINTER(ctypes.c_float)), shape=(count,))
+                sum_in_place(arr)
+                return 0
+            except Exception:  # reported to C++ as a failed exchange
+                return 1
+
+        self._host_cb = HOST_ALLREDUCE(_cb)  # keep alive while attached
+        self.fe._check(self.fe.lib.mtb_mlp_set_host_allreduce(self.h, self._host_cb, world), "mlp_set_host_allreduce")
 
     def load_batch(self, x_ptr: int, y_ptr: int, batch: int):
         self.fe._check(self.fe.lib.mtb_mlp_load_batch(self.h, x_ptr, y_ptr, batch), "mlp_load_batch")

@@ -30,6 +30,7 @@
 #ifndef MTB_CPU_ONLY
 #include "cuda_backend.hpp"
 #include "ops_ext.hpp"
+#include "tensor/backend/cpu/cpu_buffer.hpp"
 #include "tensor/execution/environment.hpp"
 #include "tensor/graph/value.hpp"
 #include "tensor/storage/materialization.hpp"
@@ -216,6 +217,7 @@ struct MlpTrainer {
     mt::nn::AdamW::State state;
     std::vector<mt::nn::ParameterId> order;  // layer order: weight, bias, ...
     void *comm = nullptr;
+    int (*host_allreduce)(void *, std::size_t) = nullptr;
     int world = 1;
     std::optional<mt::Tensor> x_resident;
     std::optional<mt::Tensor> y_resident;
@@ -242,13 +244,17 @@ struct MlpTrainer {
         return read_loss ? mt::item<float>(loss) : 0.0F;
     }
 
+    // Data-parallel gradient exchange: the loss and all gradients are
+    // materialised in one evaluation, each gradient's dense storage region is
+    // summed over the ranks in place and scaled by 1/world.  On a CUDA device the
+    // sum is an NCCL all-reduce on the device stream; on the CPU device it is the
+    // host callback (used to run the same path with CPU process groups).
     void allreduce(mt::nn::ParameterGradients &grads, const mt::Tensor &loss) {
 #ifdef MTB_CPU_ONLY
         (void)grads;
         (void)loss;
-        throw std::invalid_argument{"data parallelism needs the CUDA build"};
+        throw std::invalid_argument{"data parallelism needs the backend build"};
 #else
-        // materialise loss and gradients (one evaluation), then sum them in place
         std::vector<mt::Tensor> roots{loss};
         for (const auto &id : order) roots.push_back(grads.at(id));
         std::vector<mt::Tensor> leaves = mt::leafify(roots);
@@ -256,31 +262,45 @@ struct MlpTrainer {
         std::vector<std::size_t> counts;
         for (std::size_t i = 0; i < order.size(); ++i) {
             mt::Tensor g = leaves[i + 1];
-            const auto &value = mt::detail::TensorAccess::value(g);
-            const auto *m = value->materialization();
-            // the region of a permuted dense layout is [offset, offset + numel)
-            const auto &layout = m->layout();
-            std::int64_t span = 1;
-            for (std::size_t d = 0; d < g.rank(); ++d)
-                span += (g.shape()[d] - 1) * std::abs(layout.stride(d));
-            if (span != static_cast<std::int64_t>(g.numel())) {
-                g = mt::leafify(mt::contiguous(g));
+            {
+                // the region of a permuted dense layout is [lowest offset, + numel)
+                const auto &layout = mt::detail::TensorAccess::value(g)->materialization()->layout();
+                std::int64_t span = 1;
+                for (std::size_t d = 0; d < g.rank(); ++d) span += (g.shape()[d] - 1) * std::abs(layout.stride(d));
+                if (span != static_cast<std::int64_t>(g.numel())) g = mt::leafify(mt::contiguous(g));
             }
-            const auto &v2 = mt::detail::TensorAccess::value(g);
-            const auto *m2 = v2->materialization();
-            auto *buf = dynamic_cast<mt::detail::cuda::CudaBuffer *>(m2->buffer_ref().get());
-            std::int64_t lo = m2->layout().offset();
+            const auto *m = mt::detail::TensorAccess::value(g)->materialization();
+            std::int64_t lo = m->layout().offset();
             for (std::size_t d = 0; d < g.rank(); ++d)
-                if (m2->layout().stride(d) < 0) lo += (g.shape()[d] - 1) * m2->layout().stride(d);
-            buffers.push_back(static_cast<float *>(buf->data()) + lo);
+                if (m->layout().stride(d) < 0) lo += (g.shape()[d] - 1) * m->layout().stride(d);
+            std::byte *base = nullptr;
+            if (auto *cb = dynamic_cast<mt::detail::cuda::CudaBuffer *>(m->buffer_ref().get())) {
+                base = static_cast<std::byte *>(cb->data());
+            } else if (auto *hb = dynamic_cast<mt::detail::cpu::CpuBuffer *>(m->buffer_ref().get())) {
+                base = hb->data();
+            } else {
+                throw std::logic_error{"gradient storage of an unknown buffer type"};
+            }
+            buffers.push_back(reinterpret_cast<float *>(base) + lo);
             counts.push_back(g.numel());
             grads.at(order[i]) = g;
         }
-        auto &rt = dynamic_cast<mt::detail::cuda::CudaRuntime &>(
-            mt::detail::environment().runtime_for(device));
-        mt::detail::cuda::check(mtc_comm_allreduce_f32(comm, buffers.data(), counts.data(),
-                                                       static_cast<int32_t>(buffers.size()), 1.0F / world, rt.stream()),
-                                "gradient all-reduce");
+        if (device.type() == mt::DeviceType::Cuda) {
+            if (comm == nullptr) throw std::logic_error{"no NCCL communicator attached"};
+            auto &rt = dynamic_cast<mt::detail::cuda::CudaRuntime &>(mt::detail::environment().runtime_for(device));
+            mt::detail::cuda::check(mtc_comm_allreduce_f32(comm, buffers.data(), counts.data(),
+                                                           static_cast<int32_t>(buffers.size()), 1.0F / world,
+                                                           rt.stream()),
+                                    "gradient all-reduce");
+        } else {
+            if (host_allreduce == nullptr) throw std::logic_error{"no host all-reduce attached"};
+            const float scale = 1.0F / static_cast<float>(world);
+            for (std::size_t i = 0; i < buffers.size(); ++i) {
+                if (host_allreduce(buffers[i], counts[i]) != 0) throw std::runtime_error{"host all-reduce failed"};
+                float *p = static_cast<float *>(buffers[i]);
+                for (std::size_t j = 0; j < counts[i]; ++j) p[j] *= scale;
+            }
+        }
 #endif
     }
 };
@@ -305,6 +325,14 @@ int mtb_mlp_set_comm(void *handle, void *comm, int32_t world) {
     return guarded([&] {
         auto *t = static_cast<MlpTrainer *>(handle);
         t->comm = comm;
+        t->world = world;
+    });
+}
+
+int mtb_mlp_set_host_allreduce(void *handle, int (*sum_in_place)(void *, size_t), int32_t world) {
+    return guarded([&] {
+        auto *t = static_cast<MlpTrainer *>(handle);
+        t->host_allreduce = sum_in_place;
         t->world = world;
     });
 }

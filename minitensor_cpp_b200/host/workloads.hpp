@@ -31,6 +31,9 @@ void mtb_mlp_destroy(void *handle);
 // Attach a data-parallel communicator (from mtc_comm_init) of `world` ranks:
 // gradients are summed over ranks and scaled by 1/world before the update.
 int mtb_mlp_set_comm(void *handle, void *comm, int32_t world);
+// CPU-device data parallelism: `sum_in_place(buffer, count)` must sum the float
+// buffer over all ranks in place (0 = ok); gradients are then scaled by 1/world.
+int mtb_mlp_set_host_allreduce(void *handle, int (*sum_in_place)(void *, size_t), int32_t world);
 // Upload one batch (host memory; copied to the device) that mtb_mlp_step_resident reuses.
 int mtb_mlp_load_batch(void *handle, const float *x, const int64_t *labels, int64_t batch);
 // One training step on the resident batch; *loss receives the step's loss when read_loss != 0.
