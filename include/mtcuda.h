@@ -229,6 +229,20 @@ enum {
  * batch dimensions and arbitrary strides.  Float32 in, float32 accumulate. */
 int mtc_matmul(const mtc_desc *lhs, const mtc_desc *rhs, const mtc_desc *out, int32_t algo, void *stream);
 
+/* The MTC_GEMM_3XTF32 matmul for callers that cannot allocate device memory:
+ * code whose memory is owned by another framework's allocator, or a latency
+ * path that must never wait on an allocation.  No reference counterpart (the
+ * reference allocates only through DeviceRuntime::allocate).  Nothing is
+ * allocated: the split hi/lo operands (2*batch*(M+N)*round_up(K,4) floats) go
+ * to one fixed 32 MiB device array, so larger problems are rejected with
+ * MTC_ERR_INVALID_ARGUMENT, and problems too small for the tensor-core path with
+ * MTC_ERR_UNSUPPORTED.  The array exists on every GPU that loads the library,
+ * until the process exits.  The first call on a device looks up its device
+ * address (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race, so
+ * serialise them (one stream, or events between streams). */
+int mtc_matmul_3xtf32_static(const mtc_desc *lhs, const mtc_desc *rhs, const mtc_desc *out, void *stream);
+
 /* --------------------------------------------------------- creation (A14) -- */
 
 /* out[...] = value; `value` points at 4 bytes (Float32) or 8 bytes (Int64)

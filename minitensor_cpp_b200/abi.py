@@ -170,6 +170,7 @@ def _declare(L):
         "mtc_reduce": ([c_i32, P(Desc), P(c_i64), c_i32, P(Desc), c_vp], c_int),
         "mtc_log_softmax": ([P(Desc), c_i64, P(Desc), c_vp], c_int),
         "mtc_matmul": ([P(Desc), P(Desc), P(Desc), c_i32, c_vp], c_int),
+        "mtc_matmul_3xtf32_static": ([P(Desc), P(Desc), P(Desc), c_vp], c_int),
         "mtc_fill": ([P(Desc), c_vp, c_vp], c_int),
         "mtc_uniform": ([P(Desc), c_f, c_f, ctypes.c_uint64, ctypes.c_uint64, c_vp], c_int),
         "mtc_normal": ([P(Desc), c_f, c_f, ctypes.c_uint64, ctypes.c_uint64, c_vp], c_int),

@@ -251,3 +251,20 @@ extern "C" int mtc_matmul(const mtc_desc *lhs, const mtc_desc *rhs, const mtc_de
     if (mark != nullptr) profile_end(mark, s, 2.0 * double(p.M) * double(p.N) * double(p.K) * double(p.batch));
     return rc;
 }
+
+extern "C" int mtc_matmul_3xtf32_static(const mtc_desc *lhs, const mtc_desc *rhs, const mtc_desc *out, void *stream) {
+    clear_error();
+    MTC_TRY(validate(lhs, "lhs"));
+    MTC_TRY(validate(rhs, "rhs"));
+    MTC_TRY(validate(out, "output"));
+    if (lhs->dtype != MTC_FLOAT32 || rhs->dtype != MTC_FLOAT32 || out->dtype != MTC_FLOAT32)
+        return fail(MTC_ERR_LOGIC, "matmul requires Float32");
+    GemmProblem p;
+    MTC_TRY(build_problem(*lhs, *rhs, *out, p));
+    if (numel_of(*out) == 0) return MTC_OK;
+    if (p.K == 0) {
+        const float zero = 0.0f;
+        return mtc_fill(out, &zero, stream);
+    }
+    return gemm_3xtf32_static(p, static_cast<cudaStream_t>(stream));
+}

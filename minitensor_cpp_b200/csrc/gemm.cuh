@@ -28,5 +28,8 @@ int gemm_3xtf32(const GemmProblem &p, cudaStream_t stream);
 // SIMT path (any strides, any sizes).  exact: the CPU reference's rounding and
 // order (float product, then float sum, k ascending); otherwise one FFMA per k.
 int gemm_simt(const GemmProblem &p, cudaStream_t stream, bool exact);
+// The tensor-core path with its split operands in a fixed static device array
+// (no allocation); rejects problems whose workspace exceeds that array.
+int gemm_3xtf32_static(const GemmProblem &p, cudaStream_t stream);
 
 }  // namespace mtc

@@ -524,4 +524,98 @@ int gemm_3xtf32(const GemmProblem &p, cudaStream_t stream) {
     return rc;
 }
 
+// ----------------------------------------------------- allocation-free variant --
+// The same tensor-core GEMM for callers that must not allocate device memory
+// (for example code running under another framework's memory manager, or a
+// path that must not risk an allocation): the split operands live in this
+// fixed array instead of a pool allocation.  Every GPU that loads the library
+// holds it until the process exits.  All calls share it and each call
+// overwrites the part it uses, so calls that overlap on the GPU (different
+// streams, or different host threads) race; nothing in it needs to start zeroed
+// because the pack kernels write every element the GEMM reads.
+
+constexpr size_t kStaticWorkspaceFloats = size_t(8) << 20;  // 32 MiB
+static __device__ __align__(256) float g_static_workspace[kStaticWorkspaceFloats];
+
+namespace {
+std::mutex g_static_mutex;
+float *g_static_ptr[64] = {};
+
+// Device address of g_static_workspace on the current device; looked up once per
+// device (the host-side name is only a stand-in, never a device address).
+int static_workspace(float **out) {
+    int dev = 0;
+    MTC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(MTC_ERR_RUNTIME, "device index %d outside the supported range", dev);
+    std::lock_guard<std::mutex> lock(g_static_mutex);
+    if (g_static_ptr[dev] == nullptr) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_workspace);
+        if (e != cudaSuccess || p == nullptr)
+            return fail(MTC_ERR_RUNTIME, "cudaGetSymbolAddress of the static workspace failed: %s",
+                        cudaGetErrorString(e));
+        g_static_ptr[dev] = static_cast<float *>(p);
+    }
+    *out = g_static_ptr[dev];
+    return MTC_OK;
+}
+}  // namespace
+
+int gemm_3xtf32_static(const GemmProblem &p, cudaStream_t stream) {
+    if (p.M < 64 || p.N < 64 || p.K < 16) return fail(MTC_ERR_UNSUPPORTED, "problem too small for the tensor-core path");
+    if (p.batch > 65535 || (p.M + 31) / 32 > 65535 || (p.N + 31) / 32 > 65535)
+        return fail(MTC_ERR_UNSUPPORTED, "problem too large for the tensor-core launch shape");
+    const int64_t Kp = (p.K + 3) / 4 * 4;
+    const double need = 2.0 * double(p.batch) * (double(p.M) + double(p.N)) * double(Kp);
+    if (need > double(kStaticWorkspaceFloats))
+        return fail(MTC_ERR_INVALID_ARGUMENT,
+                    "allocation-free GEMM needs 2*batch*(M+N)*round_up(K,4) = %.0f floats of workspace; the static "
+                    "workspace holds %zu (32 MiB)",
+                    need, kStaticWorkspaceFloats);
+    float *ws = nullptr;
+    MTC_TRY(static_workspace(&ws));
+    const size_t a_elems = static_cast<size_t>(p.batch * p.M * Kp);
+    const size_t b_elems = static_cast<size_t>(p.batch * p.N * Kp);
+    float *ahi = ws;
+    float *alo = ahi + a_elems;
+    float *bhi = alo + a_elems;
+    float *blo = bhi + b_elems;
+    MTC_TRY(pack(p.A, p.a_off, p.a_rs, p.a_cs, p.M, p.K, Kp, p, p.a_bs, ahi, alo, stream));
+    MTC_TRY(pack(p.B, p.b_off, p.b_cs, p.b_rs, p.N, p.K, Kp, p, p.b_bs, bhi, blo, stream));
+    CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+    MTC_TRY(make_map(m_ahi, ahi, Kp, p.M, p.batch, TC_BM));
+    MTC_TRY(make_map(m_alo, alo, Kp, p.M, p.batch, TC_BM));
+    MTC_TRY(make_map(m_bhi, bhi, Kp, p.N, p.batch, TC_BN));
+    MTC_TRY(make_map(m_blo, blo, Kp, p.N, p.batch, TC_BN));
+    TcArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.M = p.M;
+    a.N = p.N;
+    a.Kp = Kp;
+    a.batch = p.batch;
+    a.tiles_m = static_cast<int>((p.M + TC_BM - 1) / TC_BM);
+    a.tiles_n = static_cast<int>((p.N + TC_BN - 1) / TC_BN);
+    a.total_tiles = static_cast<int64_t>(a.tiles_m) * a.tiles_n * p.batch;
+    a.C = p.C;
+    a.c_off = p.c_off;
+    a.c_rs = p.c_rs;
+    a.c_cs = p.c_cs;
+    a.batch_rank = p.batch_rank;
+    for (int d = 0; d < p.batch_rank; ++d) {
+        a.batch_shape[d] = p.batch_shape[d];
+        a.c_bs[d] = p.c_bs[d];
+    }
+    bool vec = p.c_cs == 1 && (p.c_rs % 4) == 0 && (p.c_off % 4) == 0 && (reinterpret_cast<uintptr_t>(p.C) % 16) == 0;
+    for (int d = 0; d < p.batch_rank && vec; ++d) vec = (p.c_bs[d] % 4) == 0;
+    a.vec_store = vec ? 1 : 0;
+    a.err = device_error_word();
+    MTC_CUDA_TRY(cudaFuncSetAttribute(k_gemm_3xtf32, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_BYTES));
+    int dev = 0, sms = 0;
+    MTC_CUDA_TRY(cudaGetDevice(&dev));
+    MTC_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int64_t grid = a.total_tiles < sms ? a.total_tiles : sms;
+    k_gemm_3xtf32<<<static_cast<unsigned>(grid), TC_THREADS, TC_SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, a);
+    return check_launch("3xTF32 GEMM (static workspace)");
+}
+
 }  // namespace mtc
