@@ -224,10 +224,19 @@ def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
     row = torch.rand(1, n, device="cuda", generator=g) * 2 - 1
     col = torch.rand(n, 1, device="cuda", generator=g) * 2 - 1
     Y = torch.empty(n, n, device="cuda")
+    E = torch.empty(n, 1, device="cuda")
+    # the evaluator's two clusters: exp(-col) over [n,1], then relu(A*B + row) * e over [n,n]
+    prog_e = [(abi.NEGATE, 1, 0, 0, 0.0), (abi.EXP, 2, 1, 0, 0.0)]
     prog = [(abi.MULTIPLY, 4, 0, 1, 0.0), (abi.ADD, 5, 4, 2, 0.0), (abi.RELU, 6, 5, 0, 0.0),
-            (abi.NEGATE, 7, 3, 0, 0.0), (abi.EXP, 8, 7, 0, 0.0), (abi.MULTIPLY, 9, 6, 8, 0.0)]
-    ins = [abi.View.of(A), abi.View.of(Bs.t()), abi.View.of(row), abi.View.of(col)]
-    ms = _time_ms(lambda: abi.fused(prog, ins, [9], [abi.View.of(Y)]))
+            (abi.MULTIPLY, 7, 6, 3, 0.0)]
+    ins = [abi.View.of(A), abi.View.of(Bs.t()), abi.View.of(row), abi.View.of(E)]
+    vcol, vE, vYc = abi.View.of(col), abi.View.of(E), abi.View.of(Y)
+
+    def chain():
+        abi.fused(prog_e, [vcol], [2], [vE])
+        abi.fused(prog, ins, [7], [vYc])
+
+    ms = _time_ms(chain)
     out["chain_fused_GBps"] = gbs(12 * n * n, ms)
     vY = abi.View.of(Y)
     o = torch.empty(n, device="cuda")
@@ -252,6 +261,14 @@ def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
             ms = _time_ms(lambda: abi.matmul(abi.View.of(a), bv, abi.View.of(c)), iters=3)
             out[f"gemm_{m}{tag}_TFLOPs"] = 2 * m ** 3 / (ms * 1e-3) / 1e12
     out["gemm_8192_frac_of_3xtf32"] = out["gemm_8192_TFLOPs"] / peak3
+    # the same 8192^3 GEMM with the other kernel variants / shared-memory rings
+    for variant in ("32x2", "pair16x6", "pair32x3"):
+        os.environ["MTC_TC_PIPELINE"] = variant
+        try:
+            ms = _time_ms(lambda: abi.matmul(abi.View.of(a), abi.View.of(b), abi.View.of(c)), iters=3)
+        finally:
+            del os.environ["MTC_TC_PIPELINE"]
+        out[f"gemm_8192_{variant}_TFLOPs"] = 2 * 8192 ** 3 / (ms * 1e-3) / 1e12
     a = torch.randn(64, 1024, 1024, device="cuda")
     b = torch.randn(64, 1024, 1024, device="cuda")
     c = torch.empty(64, 1024, 1024, device="cuda")

@@ -33,7 +33,7 @@ SUM, LOGSUMEXP, MAX, ARGMAX = 0x0301, 0x0302, 0x0380, 0x0381
 UNARY_OPS = (ABS, SIGN, NEGATE, EXP, LOG, SQRT, TANH, SIGMOID, RELU)
 BINARY_OPS = (ADD, SUBTRACT, MULTIPLY, DIVIDE, LOGADDEXP)
 
-GEMM_AUTO, GEMM_SIMT, GEMM_3XTF32 = 0, 1, 2
+GEMM_AUTO, GEMM_SIMT, GEMM_3XTF32, GEMM_SIMT_FFMA = 0, 1, 2, 3
 
 LIB_DIR = Path(__file__).resolve().parent / "lib"
 

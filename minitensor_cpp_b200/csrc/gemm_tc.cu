@@ -9,8 +9,10 @@
 // Pipeline (one persistent CTA per SM, 192 threads):
 //   pack kernel  : A -> Ahi/Alo [batch][M][Kp], B -> Bhi/Blo [batch][N][Kp],
 //                  both K-major (transposing strided views through shared memory).
-//   warp 0       : TMA producer, 128x32 (A) and 256x32 (B) fp32 boxes with the
-//                  128-byte swizzle, into a 2-stage ring of 96 KB stages.
+//   warp 0       : TMA producer, 128xBK (A) and 256xBK (B) fp32 boxes into a ring
+//                  of shared-memory stages: BK=16 with the 64-byte swizzle in 4
+//                  stages of 48 KB (default), or BK=32 with the 128-byte swizzle
+//                  in 2 stages of 96 KB (MTC_TC_PIPELINE=32x2).
 //   warp 1       : allocates 512 TMEM columns (two 128x256 fp32 accumulators);
 //                  one thread issues tcgen05.mma.kind::tf32 (M=128, N=256, K=8),
 //                  3 per k-step, and tcgen05.commit releases stages / accumulators.
@@ -20,6 +22,7 @@
 // device error word and leaves its loops (no hang).
 #include <cuda.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -34,13 +37,27 @@ namespace {
 
 constexpr int TC_BM = 128;
 constexpr int TC_BN = 256;
-constexpr int TC_BK = 32;  // fp32 elements = 128 bytes = one swizzle row
-constexpr int TC_STAGES = 2;
-constexpr int TC_A_BYTES = TC_BM * TC_BK * 4;                 // 16 KB
-constexpr int TC_B_BYTES = TC_BN * TC_BK * 4;                 // 32 KB
-constexpr int TC_STAGE_BYTES = 2 * TC_A_BYTES + 2 * TC_B_BYTES;  // 96 KB
-constexpr int TC_SMEM_BYTES = TC_STAGES * TC_STAGE_BYTES + 1024 + 256;
 constexpr int TC_THREADS = 192;
+
+// Pipeline shape: BK fp32 elements along K per stage (one swizzle row of BK*4
+// bytes), STAGES stages in the ring.
+template <int BK_, int STAGES_>
+struct TcPipe {
+    static constexpr int BK = BK_;
+    static constexpr int STAGES = STAGES_;
+    static constexpr int A_BYTES = TC_BM * BK * 4;
+    static constexpr int B_BYTES = TC_BN * BK * 4;
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+    // smem descriptor layout code (tcgen05): 2 = 128-byte swizzle, 4 = 64-byte swizzle
+    static constexpr uint64_t LAYOUT = BK == 32 ? 2ull : 4ull;
+    // byte distance between 8-row core-matrix groups: 8 rows x one swizzle row
+    static constexpr uint64_t SBO = 8ull * BK * 4;
+    static_assert(BK == 16 || BK == 32, "BK is one 64- or 128-byte swizzle row");
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+};
+using PipeDeep = TcPipe<16, 4>;     // 4 x 48 KB
+using PipeWide = TcPipe<32, 2>;     // 2 x 96 KB
 constexpr uint32_t TC_TMEM_COLS = 512;
 constexpr long long kWaitLimit = 20000000;  // bounded spins per wait
 constexpr int kErrTimeout = MTC_ERR_RUNTIME;
@@ -106,10 +123,12 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
-__device__ __forceinline__ uint64_t smem_desc_sw128(const void *tile) {
+// Shared-memory matrix descriptor: K-major, swizzled rows of BK*4 bytes, 8-row
+// groups SBO bytes apart, descriptor version 1 (bit 46).
+template <class P>
+__device__ __forceinline__ uint64_t smem_desc(const void *tile) {
     const uint64_t addr = smem_u32(tile);
-    return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | ((1024ull >> 4) << 32) | (1ull << 46) | (2ull << 61);
+    return ((addr & 0x3FFFFull) >> 4) | (1ull << 16) | ((P::SBO >> 4) << 32) | (1ull << 46) | (P::LAYOUT << 61);
 }
 
 // Instruction descriptor: D=F32, A=B=TF32, both K-major, M=128, N=TC_BN.
@@ -164,6 +183,7 @@ __device__ __forceinline__ void tile_coords(const TcArgs &a, int64_t t, int &tm,
     tn = static_cast<int>(in_group / gsize);
 }
 
+template <class P>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     k_gemm_3xtf32(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
                   const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
@@ -171,6 +191,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem =
         reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int TC_STAGES = P::STAGES;
+    constexpr int TC_BK = P::BK;
+    constexpr int TC_A_BYTES = P::A_BYTES;
+    constexpr int TC_B_BYTES = P::B_BYTES;
+    constexpr int TC_STAGE_BYTES = P::STAGE_BYTES;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + TC_STAGES * TC_STAGE_BYTES);
     uint64_t *full = bars;                       // [TC_STAGES]
     uint64_t *empty = bars + TC_STAGES;          // [TC_STAGES]
@@ -263,10 +288,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                     tc_fence_after();
                     unsigned char *st = smem + s * TC_STAGE_BYTES;
-                    const uint64_t a_hi = smem_desc_sw128(st);
-                    const uint64_t a_lo = smem_desc_sw128(st + TC_A_BYTES);
-                    const uint64_t b_hi = smem_desc_sw128(st + 2 * TC_A_BYTES);
-                    const uint64_t b_lo = smem_desc_sw128(st + 2 * TC_A_BYTES + TC_B_BYTES);
+                    const uint64_t a_hi = smem_desc<P>(st);
+                    const uint64_t a_lo = smem_desc<P>(st + TC_A_BYTES);
+                    const uint64_t b_hi = smem_desc<P>(st + 2 * TC_A_BYTES);
+                    const uint64_t b_lo = smem_desc<P>(st + 2 * TC_A_BYTES + TC_B_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < TC_BK / 8; ++kk) {
                         const uint64_t adv = static_cast<uint64_t>(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
@@ -342,6 +367,295 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TC_TMEM_COLS));
+    }
+}
+
+// ------------------------------------------------------- CTA-pair kernel --
+// The same 3xTF32 product with tcgen05.mma.cta_group::2: a cluster of two CTAs
+// on two SMs computes one 256x256 tile.  Each CTA stages its own 128 rows of A
+// and its own 128 columns of B, so every SM moves half the B bytes of the
+// single-CTA kernel per MMA; the leader CTA (rank 0) issues M=256, N=256 MMAs
+// that read both CTAs' shared memory and write each CTA's 128 accumulator rows
+// into that CTA's TMEM.
+//   both CTAs, warp 0 : TMA producer into the own ring, completion counted on
+//                       the leader's full barrier (.cta_group::2 loads)
+//   leader, warp 1    : MMA issuer; tcgen05.commit arrives on the empty /
+//                       accumulator-full barriers of both CTAs (CTA mask 0b11)
+//   both, warp 1      : allocates / frees TMEM together (cta_group::2)
+//   both, warps 2..5  : epilogue of the own 128 rows; one lane per warp
+//                       arrives on the leader's accumulator-empty barrier
+
+template <int BK_, int STAGES_>
+struct PairPipe {
+    static constexpr int BK = BK_;
+    static constexpr int STAGES = STAGES_;
+    static constexpr int A_BYTES = 128 * BK * 4;  // this CTA's 128 rows of A
+    static constexpr int B_BYTES = 128 * BK * 4;  // this CTA's 128 columns of B
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr uint64_t LAYOUT = BK == 32 ? 2ull : 4ull;
+    static constexpr uint64_t SBO = 8ull * BK * 4;
+    static_assert(BK == 16 || BK == 32, "BK is one 64- or 128-byte swizzle row");
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory per CTA");
+};
+using PairDeep = PairPipe<16, 6>;  // 6 x 32 KB
+using PairWide = PairPipe<32, 3>;  // 3 x 64 KB
+
+// D=F32, A=B=TF32, both K-major, M=256 (two CTAs), N=256.
+constexpr uint32_t kPairInstrDesc = (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(256 >> 3) << 17) |
+                                    (uint32_t(256 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t peer_addr(const void *p, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+    return out;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(void *dst, const CUtensorMap *map, uint32_t leader_bar, int x, int y,
+                                                 int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(kPairInstrDesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive once on the barrier at this offset in both CTAs of the pair when the
+// issuing thread's prior MMAs complete.
+__device__ __forceinline__ void umma_commit_both(uint64_t *bar) {
+    const uint16_t mask = 0x3;
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(smem_u32(bar)), "h"(mask)
+                 : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_pair_local(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void pair_tile_coords(const TcArgs &a, int64_t t, int &tm, int &tn, int &tb) {
+    tile_coords(a, t, tm, tn, tb);  // tiles_m / tiles_n count 256x256 pair tiles
+}
+
+template <class P>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
+    k_gemm_3xtf32_pair(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
+                       const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
+                       const TcArgs args) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // the same aligned offset in both CTAs (same dynamic size, same static layout)
+    unsigned char *smem =
+        reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int S = P::STAGES;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * P::STAGE_BYTES);
+    uint64_t *full = bars;               // [S]  leader's: both CTAs' TMA bytes
+    uint64_t *empty = bars + S;          // [S]  each CTA's: stage consumed by the MMAs
+    uint64_t *acc_full = bars + 2 * S;   // [2]  each CTA's: accumulator ready
+    uint64_t *acc_empty = acc_full + 2;  // [2]  leader's: both epilogues done
+    uint64_t *drain = acc_empty + 2;     // [1]  leader's: all MMAs complete
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int64_t cluster = blockIdx.x / 2;
+    const int64_t clusters = gridDim.x / 2;
+    const int64_t kblocks = (args.Kp + P::BK - 1) / P::BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 8);  // 4 epilogue warps x 2 CTAs
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TC_TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int64_t it = 0;
+            bool ok = true;
+            for (int64_t t = cluster; t < args.total_tiles && ok; t += clusters) {
+                int tm, tn, tb;
+                pair_tile_coords(args, t, tm, tn, tb);
+                const int a_row = tm * 256 + static_cast<int>(rank) * 128;
+                const int b_row = tn * 256 + static_cast<int>(rank) * 128;
+                for (int64_t kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = static_cast<int>(it % S);
+                    const uint32_t round = static_cast<uint32_t>(it / S);
+                    if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    unsigned char *st = smem + s * P::STAGE_BYTES;
+                    if (leader) mbar_expect_tx(&full[s], 2 * P::STAGE_BYTES);
+                    const uint32_t fb = peer_addr(&full[s], 0);
+                    const int kx = static_cast<int>(kb * P::BK);
+                    tma_load_3d_pair(st, &tm_ahi, fb, kx, a_row, tb);
+                    tma_load_3d_pair(st + P::A_BYTES, &tm_alo, fb, kx, a_row, tb);
+                    tma_load_3d_pair(st + 2 * P::A_BYTES, &tm_bhi, fb, kx, b_row, tb);
+                    tma_load_3d_pair(st + 2 * P::A_BYTES + P::B_BYTES, &tm_blo, fb, kx, b_row, tb);
+                }
+            }
+            if (!ok) atomicCAS(args.err, 0ull, static_cast<unsigned long long>(kErrTimeout));
+            if (leader) {  // every stage issued by the pair has landed before the cluster exits
+                for (int64_t d = it > S ? it - S : 0; d < it; ++d) {
+                    const int s = static_cast<int>(d % S);
+                    const uint32_t round = static_cast<uint32_t>(d / S);
+                    for (long long i = 0; i < kWaitLimit && !mbar_try_wait(&full[s], round & 1u); ++i) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            int64_t it = 0;
+            int64_t local = 0;
+            bool ok = true;
+            for (int64_t t = cluster; t < args.total_tiles && ok; t += clusters, ++local) {
+                const int b = static_cast<int>(local & 1);
+                const uint32_t use = static_cast<uint32_t>(local >> 1);
+                if (!mbar_wait(&acc_empty[b], (use & 1u) ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * TC_BN);
+                for (int64_t kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = static_cast<int>(it % S);
+                    const uint32_t round = static_cast<uint32_t>(it / S);
+                    if (!mbar_wait(&full[s], round & 1u, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    unsigned char *st = smem + s * P::STAGE_BYTES;
+                    const uint64_t a_hi = smem_desc<P>(st);
+                    const uint64_t a_lo = smem_desc<P>(st + P::A_BYTES);
+                    const uint64_t b_hi = smem_desc<P>(st + 2 * P::A_BYTES);
+                    const uint64_t b_lo = smem_desc<P>(st + 2 * P::A_BYTES + P::B_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < P::BK / 8; ++kk) {
+                        const uint64_t adv = static_cast<uint64_t>(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
+                        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+                        umma_tf32_pair(d_tmem, a_hi + adv, b_hi + adv, acc);
+                        umma_tf32_pair(d_tmem, a_hi + adv, b_lo + adv, 1u);
+                        umma_tf32_pair(d_tmem, a_lo + adv, b_hi + adv, 1u);
+                    }
+                    umma_commit_both(&empty[s]);
+                }
+                if (!ok) break;
+                umma_commit_both(&acc_full[b]);
+            }
+            if (!ok) atomicCAS(args.err, 0ull, static_cast<unsigned long long>(kErrTimeout));
+            // drain: all MMAs of the pair complete before either CTA frees TMEM
+            umma_commit_pair_local(drain);
+            for (long long i = 0; i < kWaitLimit && !mbar_try_wait(drain, 0u); ++i) {
+            }
+        }
+    } else {
+        const int quadrant = warp % 4;
+        const int row_in_tile = static_cast<int>(rank) * 128 + quadrant * 32 + lane;
+        const uint32_t acc_empty_leader0 = peer_addr(&acc_empty[0], 0);
+        const uint32_t acc_empty_leader1 = peer_addr(&acc_empty[1], 0);
+        int64_t local = 0;
+        for (int64_t t = cluster; t < args.total_tiles; t += clusters, ++local) {
+            const int b = static_cast<int>(local & 1);
+            const uint32_t use = static_cast<uint32_t>(local >> 1);
+            if (!mbar_wait(&acc_full[b], use & 1u, abort_flag)) {
+                atomicCAS(args.err, 0ull, static_cast<unsigned long long>(kErrTimeout));
+                break;
+            }
+            tc_fence_after();
+            int tm, tn, tb;
+            pair_tile_coords(args, t, tm, tn, tb);
+            int64_t co = args.c_off;
+            {
+                int64_t rem = tb;
+                for (int d = args.batch_rank - 1; d >= 0; --d) {
+                    const int64_t c = rem % args.batch_shape[d];
+                    rem /= args.batch_shape[d];
+                    co += c * args.c_bs[d];
+                }
+            }
+            const int64_t m = static_cast<int64_t>(tm) * 256 + row_in_tile;
+            const int64_t n0 = static_cast<int64_t>(tn) * 256;
+            const uint32_t taddr_row = tmem_base + (static_cast<uint32_t>(quadrant * 32) << 16) +
+                                       static_cast<uint32_t>(b * TC_BN);
+#pragma unroll 1
+            for (int c = 0; c < 256 / 32; ++c) {
+                float v[32];
+                tmem_ld32(taddr_row + static_cast<uint32_t>(c * 32), v);
+                if (m < args.M) {
+                    const int64_t nb = n0 + c * 32;
+                    float *dst = args.C + co + m * args.c_rs;
+                    if (args.vec_store && nb + 32 <= args.N) {
+                        float4 *d4 = reinterpret_cast<float4 *>(dst + nb);
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (nb + j < args.N) dst[(nb + j) * args.c_cs] = v[j];
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(b == 0 ? acc_empty_leader0 : acc_empty_leader1);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // the leader's MMAs into this CTA's TMEM have drained
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TC_TMEM_COLS));
     }
 }
 
@@ -425,17 +739,19 @@ PFN_EncodeTiled encode_fn() {
     return fn;
 }
 
+template <class P>
 int make_map(CUtensorMap &map, float *base, int64_t Kp, int64_t rows, int64_t batch, uint32_t box_rows) {
     PFN_EncodeTiled enc = encode_fn();
     if (enc == nullptr) return fail(MTC_ERR_RUNTIME, "cuTensorMapEncodeTiled is unavailable");
     const cuuint64_t dims[3] = {static_cast<cuuint64_t>(Kp), static_cast<cuuint64_t>(rows),
                                 static_cast<cuuint64_t>(batch)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(Kp) * 4, static_cast<cuuint64_t>(rows * Kp) * 4};
-    const cuuint32_t box[3] = {static_cast<cuuint32_t>(TC_BK), box_rows, 1};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(P::BK), box_rows, 1};
     const cuuint32_t elem[3] = {1, 1, 1};
+    const CUtensorMapSwizzle swz = P::BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, elem,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MTC_ERR_RUNTIME, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
     return MTC_OK;
 }
@@ -465,6 +781,125 @@ int pack(const float *src, int64_t off, int64_t sr, int64_t sk, int64_t rows, in
     return check_launch("3xTF32 split pack");
 }
 
+// Tensor maps over the packed operands and the persistent GEMM launch with
+// pipeline shape P (allocates nothing).
+template <class P>
+int launch_tc(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float *bhi, float *blo, cudaStream_t stream) {
+    CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+    MTC_TRY(make_map<P>(m_ahi, ahi, Kp, p.M, p.batch, TC_BM));
+    MTC_TRY(make_map<P>(m_alo, alo, Kp, p.M, p.batch, TC_BM));
+    MTC_TRY(make_map<P>(m_bhi, bhi, Kp, p.N, p.batch, TC_BN));
+    MTC_TRY(make_map<P>(m_blo, blo, Kp, p.N, p.batch, TC_BN));
+    TcArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.M = p.M;
+    a.N = p.N;
+    a.Kp = Kp;
+    a.batch = p.batch;
+    a.tiles_m = static_cast<int>((p.M + TC_BM - 1) / TC_BM);
+    a.tiles_n = static_cast<int>((p.N + TC_BN - 1) / TC_BN);
+    a.total_tiles = static_cast<int64_t>(a.tiles_m) * a.tiles_n * p.batch;
+    a.C = p.C;
+    a.c_off = p.c_off;
+    a.c_rs = p.c_rs;
+    a.c_cs = p.c_cs;
+    a.batch_rank = p.batch_rank;
+    for (int d = 0; d < p.batch_rank; ++d) {
+        a.batch_shape[d] = p.batch_shape[d];
+        a.c_bs[d] = p.c_bs[d];
+    }
+    bool vec = p.c_cs == 1 && (p.c_rs % 4) == 0 && (p.c_off % 4) == 0 && (reinterpret_cast<uintptr_t>(p.C) % 16) == 0;
+    for (int d = 0; d < p.batch_rank && vec; ++d) vec = (p.c_bs[d] % 4) == 0;
+    a.vec_store = vec ? 1 : 0;
+    a.err = device_error_word();
+    MTC_CUDA_TRY(cudaFuncSetAttribute(k_gemm_3xtf32<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, P::SMEM_BYTES));
+    int dev = 0, sms = 0;
+    MTC_CUDA_TRY(cudaGetDevice(&dev));
+    MTC_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int64_t grid = a.total_tiles < sms ? a.total_tiles : sms;
+    k_gemm_3xtf32<P><<<static_cast<unsigned>(grid), TC_THREADS, P::SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo,
+                                                                                        a);
+    return check_launch("3xTF32 GEMM");
+}
+
+// Clusters of the CTA-pair kernel that fit on the device at once (cached per device).
+template <class P>
+int pair_clusters(int *out) {
+    static std::mutex mu;
+    static int cached[64] = {};
+    int dev = 0;
+    MTC_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(MTC_ERR_RUNTIME, "device index %d outside the supported range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (cached[dev] == 0) {
+        MTC_CUDA_TRY(cudaFuncSetAttribute(k_gemm_3xtf32_pair<P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          P::SMEM_BYTES));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2, 1, 1);
+        cfg.blockDim = dim3(TC_THREADS, 1, 1);
+        cfg.dynamicSmemBytes = P::SMEM_BYTES;
+        int n = 0;
+        MTC_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, k_gemm_3xtf32_pair<P>, &cfg));
+        if (n <= 0) return fail(MTC_ERR_UNSUPPORTED, "no CTA pair of the tensor-core GEMM fits on this device");
+        cached[dev] = n;
+    }
+    *out = cached[dev];
+    return MTC_OK;
+}
+
+// The CTA-pair kernel: 256x256 tiles, each CTA stages 128 rows of A and 128 of B.
+template <class P>
+int launch_pair(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float *bhi, float *blo,
+                cudaStream_t stream) {
+    CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+    MTC_TRY(make_map<P>(m_ahi, ahi, Kp, p.M, p.batch, 128));
+    MTC_TRY(make_map<P>(m_alo, alo, Kp, p.M, p.batch, 128));
+    MTC_TRY(make_map<P>(m_bhi, bhi, Kp, p.N, p.batch, 128));
+    MTC_TRY(make_map<P>(m_blo, blo, Kp, p.N, p.batch, 128));
+    TcArgs a;
+    std::memset(&a, 0, sizeof(a));
+    a.M = p.M;
+    a.N = p.N;
+    a.Kp = Kp;
+    a.batch = p.batch;
+    a.tiles_m = static_cast<int>((p.M + 255) / 256);
+    a.tiles_n = static_cast<int>((p.N + 255) / 256);
+    a.total_tiles = static_cast<int64_t>(a.tiles_m) * a.tiles_n * p.batch;
+    a.C = p.C;
+    a.c_off = p.c_off;
+    a.c_rs = p.c_rs;
+    a.c_cs = p.c_cs;
+    a.batch_rank = p.batch_rank;
+    for (int d = 0; d < p.batch_rank; ++d) {
+        a.batch_shape[d] = p.batch_shape[d];
+        a.c_bs[d] = p.c_bs[d];
+    }
+    bool vec = p.c_cs == 1 && (p.c_rs % 4) == 0 && (p.c_off % 4) == 0 && (reinterpret_cast<uintptr_t>(p.C) % 16) == 0;
+    for (int d = 0; d < p.batch_rank && vec; ++d) vec = (p.c_bs[d] % 4) == 0;
+    a.vec_store = vec ? 1 : 0;
+    a.err = device_error_word();
+    int max_clusters = 0;
+    MTC_TRY(pair_clusters<P>(&max_clusters));
+    const int64_t clusters = a.total_tiles < max_clusters ? a.total_tiles : max_clusters;
+    k_gemm_3xtf32_pair<P><<<static_cast<unsigned>(2 * clusters), TC_THREADS, P::SMEM_BYTES, stream>>>(
+        m_ahi, m_alo, m_bhi, m_blo, a);
+    return check_launch("3xTF32 GEMM (CTA pair)");
+}
+
+// MTC_TC_PIPELINE picks the kernel and ring: "16x4" (default) and "32x2" run
+// the single-CTA kernel with 4 x 48 KB or 2 x 96 KB stages, "pair16x6" and
+// "pair32x3" the CTA-pair kernel with 6 x 32 KB or 3 x 64 KB stages.
+int launch_tc_selected(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float *bhi, float *blo,
+                       cudaStream_t stream) {
+    const char *sel = std::getenv("MTC_TC_PIPELINE");
+    if (sel != nullptr) {
+        if (std::strcmp(sel, "32x2") == 0) return launch_tc<PipeWide>(p, Kp, ahi, alo, bhi, blo, stream);
+        if (std::strcmp(sel, "pair16x6") == 0) return launch_pair<PairDeep>(p, Kp, ahi, alo, bhi, blo, stream);
+        if (std::strcmp(sel, "pair32x3") == 0) return launch_pair<PairWide>(p, Kp, ahi, alo, bhi, blo, stream);
+    }
+    return launch_tc<PipeDeep>(p, Kp, ahi, alo, bhi, blo, stream);
+}
+
 }  // namespace
 
 int gemm_3xtf32(const GemmProblem &p, cudaStream_t stream) {
@@ -485,41 +920,7 @@ int gemm_3xtf32(const GemmProblem &p, cudaStream_t stream) {
     int rc = pack(p.A, p.a_off, p.a_rs, p.a_cs, p.M, p.K, Kp, p, p.a_bs, ahi, alo, stream);
     // B[k][n] packed as B'[n][k]: rows advance along n (b_cs), k along b_rs
     if (rc == MTC_OK) rc = pack(p.B, p.b_off, p.b_cs, p.b_rs, p.N, p.K, Kp, p, p.b_bs, bhi, blo, stream);
-    CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
-    if (rc == MTC_OK) rc = make_map(m_ahi, ahi, Kp, p.M, p.batch, TC_BM);
-    if (rc == MTC_OK) rc = make_map(m_alo, alo, Kp, p.M, p.batch, TC_BM);
-    if (rc == MTC_OK) rc = make_map(m_bhi, bhi, Kp, p.N, p.batch, TC_BN);
-    if (rc == MTC_OK) rc = make_map(m_blo, blo, Kp, p.N, p.batch, TC_BN);
-    if (rc == MTC_OK) {
-        TcArgs a;
-        std::memset(&a, 0, sizeof(a));
-        a.M = p.M;
-        a.N = p.N;
-        a.Kp = Kp;
-        a.batch = p.batch;
-        a.tiles_m = static_cast<int>((p.M + TC_BM - 1) / TC_BM);
-        a.tiles_n = static_cast<int>((p.N + TC_BN - 1) / TC_BN);
-        a.total_tiles = static_cast<int64_t>(a.tiles_m) * a.tiles_n * p.batch;
-        a.C = p.C;
-        a.c_off = p.c_off;
-        a.c_rs = p.c_rs;
-        a.c_cs = p.c_cs;
-        a.batch_rank = p.batch_rank;
-        for (int d = 0; d < p.batch_rank; ++d) {
-            a.batch_shape[d] = p.batch_shape[d];
-            a.c_bs[d] = p.c_bs[d];
-        }
-        bool vec = p.c_cs == 1 && (p.c_rs % 4) == 0 && (p.c_off % 4) == 0 &&
-                   (reinterpret_cast<uintptr_t>(p.C) % 16) == 0;
-        for (int d = 0; d < p.batch_rank && vec; ++d) vec = (p.c_bs[d] % 4) == 0;
-        a.vec_store = vec ? 1 : 0;
-        a.err = device_error_word();
-        MTC_CUDA_TRY(cudaFuncSetAttribute(k_gemm_3xtf32, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_BYTES));
-        const int sms = sm_count(current_device());
-        const int64_t grid = a.total_tiles < sms ? a.total_tiles : sms;
-        k_gemm_3xtf32<<<static_cast<unsigned>(grid), TC_THREADS, TC_SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, a);
-        rc = check_launch("3xTF32 GEMM");
-    }
+    if (rc == MTC_OK) rc = launch_tc_selected(p, Kp, ahi, alo, bhi, blo, stream);
     scratch_free(scratch, stream);
     return rc;
 }
@@ -582,40 +983,7 @@ int gemm_3xtf32_static(const GemmProblem &p, cudaStream_t stream) {
     float *blo = bhi + b_elems;
     MTC_TRY(pack(p.A, p.a_off, p.a_rs, p.a_cs, p.M, p.K, Kp, p, p.a_bs, ahi, alo, stream));
     MTC_TRY(pack(p.B, p.b_off, p.b_cs, p.b_rs, p.N, p.K, Kp, p, p.b_bs, bhi, blo, stream));
-    CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
-    MTC_TRY(make_map(m_ahi, ahi, Kp, p.M, p.batch, TC_BM));
-    MTC_TRY(make_map(m_alo, alo, Kp, p.M, p.batch, TC_BM));
-    MTC_TRY(make_map(m_bhi, bhi, Kp, p.N, p.batch, TC_BN));
-    MTC_TRY(make_map(m_blo, blo, Kp, p.N, p.batch, TC_BN));
-    TcArgs a;
-    std::memset(&a, 0, sizeof(a));
-    a.M = p.M;
-    a.N = p.N;
-    a.Kp = Kp;
-    a.batch = p.batch;
-    a.tiles_m = static_cast<int>((p.M + TC_BM - 1) / TC_BM);
-    a.tiles_n = static_cast<int>((p.N + TC_BN - 1) / TC_BN);
-    a.total_tiles = static_cast<int64_t>(a.tiles_m) * a.tiles_n * p.batch;
-    a.C = p.C;
-    a.c_off = p.c_off;
-    a.c_rs = p.c_rs;
-    a.c_cs = p.c_cs;
-    a.batch_rank = p.batch_rank;
-    for (int d = 0; d < p.batch_rank; ++d) {
-        a.batch_shape[d] = p.batch_shape[d];
-        a.c_bs[d] = p.c_bs[d];
-    }
-    bool vec = p.c_cs == 1 && (p.c_rs % 4) == 0 && (p.c_off % 4) == 0 && (reinterpret_cast<uintptr_t>(p.C) % 16) == 0;
-    for (int d = 0; d < p.batch_rank && vec; ++d) vec = (p.c_bs[d] % 4) == 0;
-    a.vec_store = vec ? 1 : 0;
-    a.err = device_error_word();
-    MTC_CUDA_TRY(cudaFuncSetAttribute(k_gemm_3xtf32, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_BYTES));
-    int dev = 0, sms = 0;
-    MTC_CUDA_TRY(cudaGetDevice(&dev));
-    MTC_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const int64_t grid = a.total_tiles < sms ? a.total_tiles : sms;
-    k_gemm_3xtf32<<<static_cast<unsigned>(grid), TC_THREADS, TC_SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, a);
-    return check_launch("3xTF32 GEMM (static workspace)");
+    return launch_tc_selected(p, Kp, ahi, alo, bhi, blo, stream);
 }
 
 }  // namespace mtc

@@ -1,0 +1,140 @@
+"""Single-kernel cases of the backend, for profiling and timing one kernel alone.
+
+    python -m minitensor_cpp_b200.kernel_cases gemm --m 8192 --n 8192 --k 8192 [--bt] [--batch B]
+    python -m minitensor_cpp_b200.kernel_cases chain --n 8192
+    python -m minitensor_cpp_b200.kernel_cases reduce --n 8192 --op sum --axis 0
+    python -m minitensor_cpp_b200.kernel_cases log_softmax --n 8192
+    python -m minitensor_cpp_b200.kernel_cases gather --rows 16777216 --cols 64
+
+Each case allocates its operands on cuda:0 with torch (device memory only),
+calls the C ABI `--reps` times on the backend's stream, synchronises, checks
+the device error word and prints one line with the mean time per call measured
+with CUDA events.  Under a profiler, select the launch with `-k` and `-s`.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+
+from . import abi
+
+
+def _events_ms(fn, reps: int, stream) -> float:
+    import torch
+
+    fn()  # first call: NVRTC / tensor-map set-up, not timed
+    torch.cuda.synchronize()
+    # `stream` is the current torch stream's handle, so events on it bracket the calls
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        fn()
+    stop.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(stop) / reps
+
+
+def case_gemm(a, torch, stream):
+    algo = {"auto": abi.GEMM_AUTO, "simt": abi.GEMM_SIMT, "3xtf32": abi.GEMM_3XTF32,
+            "simt_ffma": abi.GEMM_SIMT_FFMA}[a.algo]
+    g = torch.Generator(device="cuda").manual_seed(a.seed)
+    lead = (a.batch,) if a.batch > 1 else ()
+    A = torch.randn(*lead, a.m, a.k, device="cuda", generator=g)
+    B = torch.randn(*lead, a.n, a.k, device="cuda", generator=g).transpose(-1, -2) if a.bt else \
+        torch.randn(*lead, a.k, a.n, device="cuda", generator=g)
+    C = torch.empty(*lead, a.m, a.n, device="cuda")
+    va, vb, vc = abi.View.of(A), abi.View.of(B), abi.View.of(C)
+    ms = _events_ms(lambda: abi.matmul(va, vb, vc, algo, stream), a.reps, stream)
+    flop = 2.0 * a.batch * a.m * a.n * a.k
+    return {"ms": ms, "tflops": flop / ms / 1e9}
+
+
+def case_chain(a, torch, stream):
+    """relu(A*B + row) * e with B a transposed view and e = exp(-col) precomputed [n,1]."""
+    n = a.n
+    g = torch.Generator(device="cuda").manual_seed(a.seed)
+    u = lambda *s: torch.rand(*s, device="cuda", generator=g) * 2 - 1
+    A, Bs, row, col = u(n, n), u(n, n), u(1, n), u(n, 1)
+    E = torch.empty(n, 1, device="cuda")
+    Y = torch.empty(n, n, device="cuda")
+    abi.fused([(abi.NEGATE, 1, 0, 0, 0.0), (abi.EXP, 2, 1, 0, 0.0)], [abi.View.of(col)], [2], [abi.View.of(E)],
+              stream)
+    prog = [(abi.MULTIPLY, 4, 0, 1, 0.0), (abi.ADD, 5, 4, 2, 0.0), (abi.RELU, 6, 5, 0, 0.0),
+            (abi.MULTIPLY, 7, 6, 3, 0.0)]
+    ins = [abi.View.of(A), abi.View.of(Bs.t()), abi.View.of(row), abi.View.of(E)]
+    vy = abi.View.of(Y)
+    ms = _events_ms(lambda: abi.fused(prog, ins, [7], [vy], stream), a.reps, stream)
+    return {"ms": ms, "gbs": 4.0 * (3 * n * n + 2 * n) / ms / 1e6}
+
+
+def case_reduce(a, torch, stream):
+    op = {"sum": abi.SUM, "max": abi.MAX, "argmax": abi.ARGMAX, "lse": abi.LSE}[a.op]
+    g = torch.Generator(device="cuda").manual_seed(a.seed)
+    X = torch.rand(a.n, a.m or a.n, device="cuda", generator=g) * 2 - 1
+    out_len = X.shape[1 - a.axis]
+    dtype = torch.int64 if a.op == "argmax" else torch.float32
+    O = torch.empty(out_len, device="cuda", dtype=dtype)
+    vx, vo = abi.View.of(X), abi.View.of(O)
+    ms = _events_ms(lambda: abi.reduce(op, vx, [a.axis], vo, stream), a.reps, stream)
+    return {"ms": ms, "gbs": X.numel() * 4.0 / ms / 1e6}
+
+
+def case_log_softmax(a, torch, stream):
+    g = torch.Generator(device="cuda").manual_seed(a.seed)
+    X = torch.rand(a.n, a.m or a.n, device="cuda", generator=g) * 2 - 1
+    Y = torch.empty_like(X)
+    vx, vy = abi.View.of(X), abi.View.of(Y)
+    ms = _events_ms(lambda: abi.log_softmax(vx, 1, vy, stream), a.reps, stream)
+    return {"ms": ms, "gbs": X.numel() * 8.0 / ms / 1e6}
+
+
+def case_gather(a, torch, stream):
+    g = torch.Generator(device="cuda").manual_seed(a.seed)
+    T = torch.randn(a.rows, a.cols, device="cuda", generator=g)
+    idx = torch.randint(0, a.rows, (a.rows,), device="cuda", generator=g, dtype=torch.int64)
+    O = torch.empty(a.rows, a.cols, device="cuda")
+    # row gather: the index column broadcast over the row width (stride 0)
+    vt, vi, vo = abi.View.of(T), abi.View(idx, (a.rows, a.cols), (1, 0), 0), abi.View.of(O)
+    ms = _events_ms(lambda: abi.gather(vt, vi, 0, vo, stream), a.reps, stream)
+    return {"ms": ms, "gbs": (2.0 * a.rows * a.cols * 4 + a.rows * 8) / ms / 1e6}
+
+
+CASES = {"gemm": case_gemm, "chain": case_chain, "reduce": case_reduce, "log_softmax": case_log_softmax,
+         "gather": case_gather}
+
+
+def main(argv=None) -> int:
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("case", choices=sorted(CASES))
+    p.add_argument("--m", type=int, default=0)
+    p.add_argument("--n", type=int, default=8192)
+    p.add_argument("--k", type=int, default=8192)
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--bt", action="store_true", help="B is the transposed view of an [n, k] tensor")
+    p.add_argument("--algo", default="3xtf32")
+    p.add_argument("--op", default="sum")
+    p.add_argument("--axis", type=int, default=0)
+    p.add_argument("--rows", type=int, default=1 << 24)
+    p.add_argument("--cols", type=int, default=64)
+    p.add_argument("--reps", type=int, default=3)
+    p.add_argument("--seed", type=int, default=0)
+    a = p.parse_args(argv)
+    if a.case == "gemm" and a.m == 0:
+        a.m = a.n
+    import torch
+
+    if not torch.cuda.is_available():
+        print("kernel_cases: no CUDA device", file=sys.stderr)
+        return 2
+    torch.cuda.set_device(0)
+    abi.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    res = CASES[a.case](a, torch, stream)
+    abi.check_device_errors(0, stream)
+    print(json.dumps({"case": a.case, **{k: v for k, v in vars(a).items() if k != "case"}, **res}))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,6 +1,7 @@
 """Parity of the tcgen05 3xTF32 tensor-core GEMM (forced, no SIMT fallback)
 against the float32 oracle: |C - C_ref| <= 1e-5 * sqrt(K) * (|A| |B|)_ij, the
-normwise per-element form of the 1e-5*sqrt(K) relative bound."""
+normwise per-element form of the 1e-5*sqrt(K) relative bound.  Every case runs
+with each kernel variant and shared-memory ring."""
 import numpy as np
 import pytest
 
@@ -11,6 +12,15 @@ from oracle import mt_oracle as mo
 pytestmark = pytest.mark.gpu
 
 F = np.float32
+
+
+@pytest.fixture(autouse=True, params=["16x4", "32x2", "pair16x6", "pair32x3"])
+def pipeline(request, monkeypatch):
+    """Every kernel and ring: the single-CTA kernel with 4 stages of BK=16 (64-byte
+    swizzle) or 2 of BK=32 (128-byte swizzle), and the CTA-pair kernel with 6
+    stages of BK=16 or 3 of BK=32."""
+    monkeypatch.setenv("MTC_TC_PIPELINE", request.param)
+    return request.param
 
 
 def _run(a_st, a_shape, a_strides, b_st, b_shape, b_strides, out_offset=0, algo=abi.GEMM_3XTF32):
