@@ -190,32 +190,38 @@ def _worker(args):
 
 # ------------------------------------------------------------ micro (N=1) --
 
-def _time_ms(fn, iters=5, warm=2, stream=None) -> float:
+def _time_ms(fn, reps=10, groups=3, warm=2) -> float:
+    """Per-call device time of `fn` (a prepared ABI call): `reps` calls back to
+    back between two CUDA events on the current stream, best of `groups`."""
     import torch
 
     for _ in range(warm):
         fn()
     torch.cuda.synchronize()
     best = float("inf")
-    for _ in range(iters):
+    for _ in range(groups):
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record(stream)
-        fn()
-        e.record(stream)
+        s.record()
+        for _ in range(reps):
+            fn()
+        e.record()
         torch.cuda.synchronize()
-        best = min(best, s.elapsed_time(e))
+        best = min(best, s.elapsed_time(e) / reps)
     return best
 
 
 def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
     """The elementwise/reduction, GEMM and indexing benchmarks, kernel-level
-    through the C ABI on cuda:0 (best of 5, inputs larger than L2)."""
+    through the C ABI on cuda:0.  Each figure is the per-call time of prepared
+    calls issued back to back (best of 3 groups); every operand set is larger
+    than the 126 MB L2."""
     import torch
 
     from minitensor_cpp_b200 import abi
 
     out = {}
     gbs = lambda nbytes, ms: nbytes / (ms * 1e-3) / 1e9
+    V = abi.View.of
     # -- broadcast/strided chain relu(A*B^T + row)*exp(-col) and reductions on 8192^2
     n = 8192
     g = torch.Generator(device="cuda").manual_seed(SEED)
@@ -229,24 +235,22 @@ def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
     prog_e = [(abi.NEGATE, 1, 0, 0, 0.0), (abi.EXP, 2, 1, 0, 0.0)]
     prog = [(abi.MULTIPLY, 4, 0, 1, 0.0), (abi.ADD, 5, 4, 2, 0.0), (abi.RELU, 6, 5, 0, 0.0),
             (abi.MULTIPLY, 7, 6, 3, 0.0)]
-    ins = [abi.View.of(A), abi.View.of(Bs.t()), abi.View.of(row), abi.View.of(E)]
-    vcol, vE, vYc = abi.View.of(col), abi.View.of(E), abi.View.of(Y)
+    call_e = abi.fused(prog_e, [V(col)], [2], [V(E)], prepare=True)
+    call_y = abi.fused(prog, [V(A), V(Bs.t()), V(row), V(E)], [7], [V(Y)], prepare=True)
 
     def chain():
-        abi.fused(prog_e, [vcol], [2], [vE])
-        abi.fused(prog, ins, [7], [vYc])
+        call_e()
+        call_y()
 
-    ms = _time_ms(chain)
-    out["chain_fused_GBps"] = gbs(12 * n * n, ms)
-    vY = abi.View.of(Y)
+    out["chain_fused_GBps"] = gbs(12 * n * n, _time_ms(chain))
     o = torch.empty(n, device="cuda")
     oi = torch.empty(n, device="cuda", dtype=torch.int64)
     for ax in (0, 1):
         for name, op, dst in (("sum", abi.SUM, o), ("max", abi.MAX, o), ("argmax", abi.ARGMAX, oi)):
-            ms = _time_ms(lambda: abi.reduce(op, vY, [ax], abi.View.of(dst)))
+            ms = _time_ms(abi.reduce(op, V(Y), [ax], V(dst), prepare=True))
             out[f"{name}_axis{ax}_GBps"] = gbs(4 * n * n, ms)
     Z = torch.empty(n, n, device="cuda")
-    ms = _time_ms(lambda: abi.log_softmax(vY, 1, abi.View.of(Z)))
+    ms = _time_ms(abi.log_softmax(V(Y), 1, V(Z), prepare=True))
     out["log_softmax_axis1_GBps"] = gbs(8 * n * n, ms)
     hb = [v for k, v in out.items() if k.endswith("GBps")]
     out["elementwise_reduce_min_frac_of_hbm"] = min(hb) / hbm_gbs
@@ -257,27 +261,27 @@ def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
         a = torch.randn(m, m, device="cuda")
         b = torch.randn(m, m, device="cuda")
         c = torch.empty(m, m, device="cuda")
-        for tag, bv in (("", abi.View.of(b)), ("_bT", abi.View.of(b.t()))):
-            ms = _time_ms(lambda: abi.matmul(abi.View.of(a), bv, abi.View.of(c)), iters=3)
+        for tag, bv in (("", V(b)), ("_bT", V(b.t()))):
+            ms = _time_ms(abi.matmul(V(a), bv, V(c), prepare=True), reps=3)
             out[f"gemm_{m}{tag}_TFLOPs"] = 2 * m ** 3 / (ms * 1e-3) / 1e12
     out["gemm_8192_frac_of_3xtf32"] = out["gemm_8192_TFLOPs"] / peak3
     # the same 8192^3 GEMM with the other kernel variants / shared-memory rings
     for variant in ("32x2", "pair16x6", "pair32x3"):
         os.environ["MTC_TC_PIPELINE"] = variant
         try:
-            ms = _time_ms(lambda: abi.matmul(abi.View.of(a), abi.View.of(b), abi.View.of(c)), iters=3)
+            ms = _time_ms(abi.matmul(V(a), V(b), V(c), prepare=True), reps=3)
         finally:
             del os.environ["MTC_TC_PIPELINE"]
         out[f"gemm_8192_{variant}_TFLOPs"] = 2 * 8192 ** 3 / (ms * 1e-3) / 1e12
     a = torch.randn(64, 1024, 1024, device="cuda")
     b = torch.randn(64, 1024, 1024, device="cuda")
     c = torch.empty(64, 1024, 1024, device="cuda")
-    ms = _time_ms(lambda: abi.matmul(abi.View.of(a), abi.View.of(b), abi.View.of(c)), iters=3)
+    ms = _time_ms(abi.matmul(V(a), V(b), V(c), prepare=True), reps=3)
     out["gemm_batched_64x1024_TFLOPs"] = 2 * 64 * 1024 ** 3 / (ms * 1e-3) / 1e12
     a = torch.randn(65536, 1024, device="cuda")
     b = torch.randn(1024, 8192, device="cuda")
     c = torch.empty(65536, 8192, device="cuda")
-    ms = _time_ms(lambda: abi.matmul(abi.View.of(a), abi.View.of(b), abi.View.of(c)), iters=3)
+    ms = _time_ms(abi.matmul(V(a), V(b), V(c), prepare=True), reps=3)
     out["gemm_skinny_65536x1024x8192_TFLOPs"] = 2 * 65536 * 1024 * 8192 / (ms * 1e-3) / 1e12
     del a, b, c
     # -- Int64 gather / scatter-add of 2^24 rows of 64 floats, concat 4 x [4096, 8192]
@@ -286,16 +290,16 @@ def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
     idx = torch.randint(0, rows, (rows, 1), device="cuda", dtype=torch.int64, generator=g)
     idx_b = abi.View(idx.view(-1), (rows, width), (1, 0), 0)  # broadcast_to([rows, width])
     res = torch.empty(rows, width, device="cuda")
-    ms = _time_ms(lambda: abi.gather(abi.View.of(table), idx_b, 0, abi.View.of(res)), iters=3)
+    ms = _time_ms(abi.gather(V(table), idx_b, 0, V(res), prepare=True), reps=3)
     out["gather_rows_GBps"] = gbs(rows * 520, ms)
     upd = torch.floor(torch.rand(rows, width, device="cuda", generator=g) * 16 - 8)
-    ms = _time_ms(lambda: abi.gather_scatter_add(abi.View.of(upd), idx_b, 0, abi.View.of(res)), iters=3)
+    ms = _time_ms(abi.gather_scatter_add(V(upd), idx_b, 0, V(res), prepare=True), reps=3)
     out["scatter_add_rows_GBps"] = gbs(rows * 520, ms)
     del table, idx, res, upd
     parts = [torch.randn(4096, 8192, device="cuda") for _ in range(4)]
     for axis, shape in ((0, (16384, 8192)), (1, (4096, 32768))):
         dst = torch.empty(shape, device="cuda")
-        ms = _time_ms(lambda: abi.concat([abi.View.of(p) for p in parts], axis, abi.View.of(dst)), iters=3)
+        ms = _time_ms(abi.concat([V(p) for p in parts], axis, V(dst), prepare=True), reps=3)
         out[f"concat_axis{axis}_GBps"] = gbs(2 * 4 * 4096 * 8192 * 4, ms)
     del parts
     torch.cuda.empty_cache()

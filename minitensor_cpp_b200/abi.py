@@ -220,18 +220,31 @@ def _stream(stream):
 
 
 # ------------------------------------------------------------------ wrappers --
+# Every kernel wrapper takes `prepare=True` to return a zero-argument callable
+# with its ctypes arguments converted once: repeated calls then cost one ctypes
+# dispatch, so back-to-back launches keep the GPU busy in timing loops.
 
-def unary(op: int, x: View, out: View, stream=None) -> None:
-    check(lib().mtc_unary(op, ctypes.byref(x.desc()), ctypes.byref(out.desc()), _stream(stream)), "unary")
+def _run(name: str, args: tuple, what: str, prepare: bool):
+    fn = getattr(lib(), name)
+    if prepare:
+        def call() -> None:
+            check(fn(*args), what)
+        return call
+    check(fn(*args), what)
+    return None
 
 
-def binary(op: int, a: View, b: View, out: View, stream=None) -> None:
-    check(lib().mtc_binary(op, ctypes.byref(a.desc()), ctypes.byref(b.desc()), ctypes.byref(out.desc()),
-                           _stream(stream)), "binary")
+def unary(op: int, x: View, out: View, stream=None, prepare: bool = False):
+    return _run("mtc_unary", (op, ctypes.byref(x.desc()), ctypes.byref(out.desc()), _stream(stream)), "unary", prepare)
+
+
+def binary(op: int, a: View, b: View, out: View, stream=None, prepare: bool = False):
+    return _run("mtc_binary", (op, ctypes.byref(a.desc()), ctypes.byref(b.desc()), ctypes.byref(out.desc()),
+                               _stream(stream)), "binary", prepare)
 
 
 def fused(program: Sequence[tuple], inputs: Sequence[View], out_regs: Sequence[int], outputs: Sequence[View],
-          stream=None) -> None:
+          stream=None, prepare: bool = False):
     """program: (op, dst, a, b, imm) tuples."""
     n = len(program)
     instrs = (Instr * max(n, 1))()
@@ -240,47 +253,48 @@ def fused(program: Sequence[tuple], inputs: Sequence[View], out_regs: Sequence[i
     ins = (Desc * max(len(inputs), 1))(*[v.desc() for v in inputs])
     outs = (Desc * len(outputs))(*[v.desc() for v in outputs])
     regs = (ctypes.c_int32 * len(out_regs))(*out_regs)
-    check(lib().mtc_fused(instrs, n, ins, len(inputs), regs, outs, len(outputs), _stream(stream)), "fused")
+    return _run("mtc_fused", (instrs, n, ins, len(inputs), regs, outs, len(outputs), _stream(stream)), "fused",
+                prepare)
 
 
-def copy(src: View, dst: View, stream=None) -> None:
-    check(lib().mtc_copy(ctypes.byref(src.desc()), ctypes.byref(dst.desc()), _stream(stream)), "copy")
+def copy(src: View, dst: View, stream=None, prepare: bool = False):
+    return _run("mtc_copy", (ctypes.byref(src.desc()), ctypes.byref(dst.desc()), _stream(stream)), "copy", prepare)
 
 
-def concat(inputs: Sequence[View], axis: int, out: View, stream=None) -> None:
+def concat(inputs: Sequence[View], axis: int, out: View, stream=None, prepare: bool = False):
     arr = (Desc * len(inputs))(*[v.desc() for v in inputs])
-    check(lib().mtc_concat(arr, len(inputs), axis, ctypes.byref(out.desc()), _stream(stream)), "concat")
+    return _run("mtc_concat", (arr, len(inputs), axis, ctypes.byref(out.desc()), _stream(stream)), "concat", prepare)
 
 
-def index_scatter(x: View, dst_view: View, out: View, stream=None) -> None:
-    check(lib().mtc_index_scatter(ctypes.byref(x.desc()), ctypes.byref(dst_view.desc()), ctypes.byref(out.desc()),
-                                  _stream(stream)), "index_scatter")
+def index_scatter(x: View, dst_view: View, out: View, stream=None, prepare: bool = False):
+    return _run("mtc_index_scatter", (ctypes.byref(x.desc()), ctypes.byref(dst_view.desc()), ctypes.byref(out.desc()),
+                                      _stream(stream)), "index_scatter", prepare)
 
 
-def gather(src: View, idx: View, axis: int, out: View, stream=None) -> None:
-    check(lib().mtc_gather(ctypes.byref(src.desc()), ctypes.byref(idx.desc()), axis, ctypes.byref(out.desc()),
-                           _stream(stream)), "gather")
+def gather(src: View, idx: View, axis: int, out: View, stream=None, prepare: bool = False):
+    return _run("mtc_gather", (ctypes.byref(src.desc()), ctypes.byref(idx.desc()), axis, ctypes.byref(out.desc()),
+                               _stream(stream)), "gather", prepare)
 
 
-def gather_scatter_add(upd: View, idx: View, axis: int, out: View, stream=None) -> None:
-    check(lib().mtc_gather_scatter_add(ctypes.byref(upd.desc()), ctypes.byref(idx.desc()), axis,
-                                       ctypes.byref(out.desc()), _stream(stream)), "gather_scatter_add")
+def gather_scatter_add(upd: View, idx: View, axis: int, out: View, stream=None, prepare: bool = False):
+    return _run("mtc_gather_scatter_add", (ctypes.byref(upd.desc()), ctypes.byref(idx.desc()), axis,
+                                           ctypes.byref(out.desc()), _stream(stream)), "gather_scatter_add", prepare)
 
 
-def reduce(op: int, x: View, axes: Sequence[int], out: View, stream=None) -> None:
+def reduce(op: int, x: View, axes: Sequence[int], out: View, stream=None, prepare: bool = False):
     ax = (ctypes.c_int64 * max(len(axes), 1))(*axes)
-    check(lib().mtc_reduce(op, ctypes.byref(x.desc()), ax, len(axes), ctypes.byref(out.desc()), _stream(stream)),
-          "reduce")
+    return _run("mtc_reduce", (op, ctypes.byref(x.desc()), ax, len(axes), ctypes.byref(out.desc()), _stream(stream)),
+                "reduce", prepare)
 
 
-def log_softmax(x: View, axis: int, out: View, stream=None) -> None:
-    check(lib().mtc_log_softmax(ctypes.byref(x.desc()), axis, ctypes.byref(out.desc()), _stream(stream)),
-          "log_softmax")
+def log_softmax(x: View, axis: int, out: View, stream=None, prepare: bool = False):
+    return _run("mtc_log_softmax", (ctypes.byref(x.desc()), axis, ctypes.byref(out.desc()), _stream(stream)),
+                "log_softmax", prepare)
 
 
-def matmul(a: View, b: View, out: View, algo: int = GEMM_AUTO, stream=None) -> None:
-    check(lib().mtc_matmul(ctypes.byref(a.desc()), ctypes.byref(b.desc()), ctypes.byref(out.desc()), algo,
-                           _stream(stream)), "matmul")
+def matmul(a: View, b: View, out: View, algo: int = GEMM_AUTO, stream=None, prepare: bool = False):
+    return _run("mtc_matmul", (ctypes.byref(a.desc()), ctypes.byref(b.desc()), ctypes.byref(out.desc()), algo,
+                               _stream(stream)), "matmul", prepare)
 
 
 def fill(out: View, value, stream=None) -> None:

@@ -141,7 +141,27 @@ int plan_elementwise(const mtc_desc *inputs, int n_in, const mtc_desc *outputs, 
         if (out_rows && nt > 0 && batch <= 65535 && tiles_y <= 65535) {
             a.transposed = mask;
             a.batch_rank = static_cast<unsigned>(r - 2);
-            plan.variant = nt == 1 ? EwVariant::Tiled1 : EwVariant::Tiled2;
+            // 128-bit variant: every operand read or written as float4 along its contiguous axis
+            auto aligned = [](const float *p, int64_t off) { return (reinterpret_cast<uintptr_t>(p + off) % 16) == 0; };
+            bool v4 = s.shape[r - 1] % 4 == 0;
+            for (int j = 0; j < n_out && v4; ++j) {
+                v4 = aligned(a.out[j], a.out_off[j]);
+                for (int d = 0; d < r - 1 && v4; ++d) v4 = s.stride[j][d] % 4 == 0;
+            }
+            for (int k = 0; k < n_in && v4; ++k) {
+                const int64_t *st = s.stride[n_out + k];
+                if (mask & (1u << k)) {
+                    v4 = s.shape[r - 2] % 4 == 0 && aligned(a.in[k], a.in_off[k]) && st[r - 1] % 4 == 0;
+                    for (int d = 0; d < r - 2 && v4; ++d) v4 = st[d] % 4 == 0;
+                } else if (st[r - 1] == 1) {
+                    v4 = aligned(a.in[k], a.in_off[k]);
+                    for (int d = 0; d < r - 1 && v4; ++d) v4 = st[d] % 4 == 0;
+                } else {
+                    v4 = st[r - 1] == 0;
+                }
+            }
+            if (v4) plan.variant = nt == 1 ? EwVariant::Tiled4x1 : EwVariant::Tiled4x2;
+            else plan.variant = nt == 1 ? EwVariant::Tiled1 : EwVariant::Tiled2;
             plan.block = dim3(MTC_EW_TILE_THREADS);
             plan.grid = dim3(static_cast<unsigned>((s.shape[r - 1] + MTC_EW_TILE - 1) / MTC_EW_TILE),
                              static_cast<unsigned>(tiles_y), static_cast<unsigned>(batch));
@@ -186,6 +206,16 @@ int launch(const EwPlan &p, cudaStream_t stream) {
             mtc_ew_tiled<Op, 2><<<p.grid, p.block, 0, stream>>>(p.args);
         } else {
             mtc_ew_tiled<Op, 1><<<p.grid, p.block, 0, stream>>>(p.args);
+        }
+        break;
+    case EwVariant::Tiled4x1:
+        mtc_ew_tiled4<Op, 1><<<p.grid, p.block, 0, stream>>>(p.args);
+        break;
+    case EwVariant::Tiled4x2:
+        if constexpr (Op::kIn >= 2) {
+            mtc_ew_tiled4<Op, 2><<<p.grid, p.block, 0, stream>>>(p.args);
+        } else {
+            mtc_ew_tiled4<Op, 1><<<p.grid, p.block, 0, stream>>>(p.args);
         }
         break;
     }

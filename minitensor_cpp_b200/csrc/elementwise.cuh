@@ -7,7 +7,7 @@
 
 namespace mtc {
 
-enum class EwVariant { Empty, Flat4, Flat1, Strided, Tiled1, Tiled2, Rows4, Rows1 };
+enum class EwVariant { Empty, Flat4, Flat1, Strided, Tiled1, Tiled2, Rows4, Rows1, Tiled4x1, Tiled4x2 };
 
 struct EwPlan {
     MtcEwArgs args;

@@ -381,4 +381,121 @@ __global__ void __launch_bounds__(MTC_EW_TILE_THREADS) mtc_ew_tiled(const MtcEwA
     }
 }
 
+// Tiled, 128-bit: the same tile walk with float4 traffic.  Requirements (checked
+// by the planner): column count a multiple of 4; outputs and row-contiguous
+// inputs 16-byte aligned along their rows; column-broadcast inputs (stride 0
+// along the row) read as one scalar per row; transposed inputs 16-byte aligned
+// along their contiguous axis (the tile's rows) with a row count that is a
+// multiple of 4.  A transposed input is staged in shared memory in the tile's
+// row-major order with the 16-byte chunks of each row XOR-swizzled by
+// (row / 4) % 8: the scalar stores of the staging pass and the float4 reads of
+// the compute pass are then at most 2-way bank conflicted.
+// grid = (ceil(cols/64), ceil(rows/64), batch); a thread owns 4 columns of 4 rows.
+
+template <class Op, int NT>
+__global__ void __launch_bounds__(MTC_EW_TILE_THREADS) mtc_ew_tiled4(const MtcEwArgs a) {
+    constexpr int NIN = Op::kIn;
+    constexpr int NOUT = Op::kOut;
+    constexpr int T = MTC_EW_TILE;
+    __shared__ __align__(16) float stage[NT > 0 ? NT : 1][T][T];
+    const Op op;
+    const int r = a.rank;
+    const unsigned int rows = a.shape[r - 2];
+    const unsigned int cols = a.shape[r - 1];
+    const unsigned int r0 = blockIdx.y * T;
+    const unsigned int c0 = blockIdx.x * T;
+
+    long long ib[NIN > 0 ? NIN : 1];
+    long long ob[NOUT];
+#pragma unroll
+    for (int k = 0; k < NIN; ++k) ib[k] = a.in_off[k];
+#pragma unroll
+    for (int j = 0; j < NOUT; ++j) ob[j] = a.out_off[j];
+    unsigned int rem = blockIdx.z;
+    for (int d = static_cast<int>(a.batch_rank) - 1; d >= 0; --d) {
+        const unsigned int c = rem % a.shape[d];
+        rem /= a.shape[d];
+#pragma unroll
+        for (int k = 0; k < NIN; ++k) ib[k] += static_cast<long long>(c) * a.in_str[k][d];
+#pragma unroll
+        for (int j = 0; j < NOUT; ++j) ob[j] += static_cast<long long>(c) * a.out_str[j][d];
+    }
+
+    const int q = threadIdx.x % 16;  // 16-byte chunk of a 64-wide tile row
+    const int g = threadIdx.x / 16;  // 0..15
+
+    if (NT > 0) {
+        // staging: a thread loads rows 4q..4q+3 of tile columns g, g+16, g+32, g+48
+        int slot = 0;
+#pragma unroll
+        for (int k = 0; k < NIN; ++k) {
+            if (a.transposed & (1u << k)) {
+                const long long cs = a.in_str[k][r - 1];
+                const float *src = a.in[k] + ib[k] + (r0 + 4u * q);
+                const bool row_in = r0 + 4u * q < rows;
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                    const unsigned int lc = g + 16 * p;
+                    if (row_in && c0 + lc < cols) {
+                        const float4 v = __ldg(reinterpret_cast<const float4 *>(src + static_cast<long long>(c0 + lc) * cs));
+                        float *dst = &stage[slot][4 * q][(((lc >> 2) ^ (q & 7)) << 2) | (lc & 3)];
+                        dst[0] = v.x;
+                        dst[T] = v.y;
+                        dst[2 * T] = v.z;
+                        dst[3 * T] = v.w;
+                    }
+                }
+                ++slot;
+            }
+        }
+        __syncthreads();
+    }
+
+    const unsigned int cc = c0 + 4u * q;
+    if (cc >= cols) return;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const unsigned int lr = g + 16 * p;
+        if (r0 + lr >= rows) break;
+        const long long row = r0 + lr;
+        float x[NIN > 0 ? NIN : 1][4];
+        int slot = 0;
+#pragma unroll
+        for (int k = 0; k < NIN; ++k) {
+            if (NT > 0 && (a.transposed & (1u << k))) {
+                const float4 v = *reinterpret_cast<const float4 *>(&stage[slot][lr][(q ^ ((lr >> 2) & 7)) << 2]);
+                x[k][0] = v.x;
+                x[k][1] = v.y;
+                x[k][2] = v.z;
+                x[k][3] = v.w;
+                ++slot;
+            } else if (a.in_str[k][r - 1] == 0) {
+                const float v = __ldg(a.in[k] + ib[k] + row * a.in_str[k][r - 2]);
+                x[k][0] = x[k][1] = x[k][2] = x[k][3] = v;
+            } else {
+                const float4 v = __ldg(reinterpret_cast<const float4 *>(a.in[k] + ib[k] + row * a.in_str[k][r - 2] + cc));
+                x[k][0] = v.x;
+                x[k][1] = v.y;
+                x[k][2] = v.z;
+                x[k][3] = v.w;
+            }
+        }
+        float y[NOUT][4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float xi[NIN > 0 ? NIN : 1];
+            float yi[NOUT];
+#pragma unroll
+            for (int k = 0; k < NIN; ++k) xi[k] = x[k][i];
+            op(xi, yi, a.imm);
+#pragma unroll
+            for (int j = 0; j < NOUT; ++j) y[j][i] = yi[j];
+        }
+#pragma unroll
+        for (int j = 0; j < NOUT; ++j)
+            *reinterpret_cast<float4 *>(a.out[j] + ob[j] + row * a.out_str[j][r - 2] + cc) =
+                make_float4(y[j][0], y[j][1], y[j][2], y[j][3]);
+    }
+}
+
 #endif  // MTC_EW_KERNELS_CUH

@@ -60,11 +60,12 @@ Driver &driver() {
     return d;
 }
 
-constexpr int kVariants = 7;  // flat4, flat1, strided, tiled1, tiled2, rows4, rows1
+constexpr int kVariants = 9;  // flat4, flat1, strided, tiled1, tiled2, rows4, rows1, tiled4x1, tiled4x2
 const char *const kNameExpr[kVariants] = {"mtc_ew_flat<MtcFused, 4>", "mtc_ew_flat<MtcFused, 1>",
                                           "mtc_ew_strided<MtcFused>", "mtc_ew_tiled<MtcFused, 1>",
                                           "mtc_ew_tiled<MtcFused, 2>", "mtc_ew_rows<MtcFused, 4>",
-                                          "mtc_ew_rows<MtcFused, 1>"};
+                                          "mtc_ew_rows<MtcFused, 1>", "mtc_ew_tiled4<MtcFused, 1>",
+                                          "mtc_ew_tiled4<MtcFused, 2>"};
 
 struct CompiledProgram {
     CUmodule module = nullptr;
@@ -262,6 +263,8 @@ extern "C" int mtc_fused(const mtc_instr *program, int32_t n_instr, const mtc_de
     case EwVariant::Tiled2: v = 4; break;
     case EwVariant::Rows4: v = 5; break;
     case EwVariant::Rows1: v = 6; break;
+    case EwVariant::Tiled4x1: v = 7; break;
+    case EwVariant::Tiled4x2: v = 8; break;
     default: return MTC_OK;
     }
     std::string key = std::to_string(device) + ":" + std::to_string(v) + "\n" + src.substr(std::strlen(kTemplateSource));

@@ -328,6 +328,67 @@ __global__ void __launch_bounds__(256) k_per_output(const RedArgs a) {
     }
 }
 
+// Column reduction: the innermost kept axis is contiguous and one strided axis
+// is reduced (sum over axis 0 of a row-major matrix, or over the middle axis of
+// [B, R, C]).  A CTA owns 128 consecutive outputs - one float4 per lane, so a
+// warp load is one 512-byte row segment - of one batch index (blockIdx.z) and a
+// chunk of the reduced axis (blockIdx.y).  Its 8 warps take interleaved rows
+// with four float4 loads in flight per thread, then merge in warp order through
+// shared memory (a fixed order: results are deterministic).
+constexpr int kColWarps = 8;
+
+template <int OP>
+__global__ void __launch_bounds__(256) k_col_tile(const RedArgs a, long long ncols, long long batch_stride) {
+    __shared__ State part[kColWarps][128];
+    const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+    const long long col = static_cast<long long>(blockIdx.x) * 128 + lane * 4;
+    const long long per = (a.R + a.chunks - 1) / a.chunks;
+    const long long r0 = static_cast<long long>(blockIdx.y) * per;
+    const long long r1 = r0 + per < a.R ? r0 + per : a.R;
+    State s[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s[j] = Reducer<OP>::init();
+    if (col < ncols) {
+        const long long rs = a.rstr[0];
+        const float *base = a.in + a.in_off + static_cast<long long>(blockIdx.z) * batch_stride + col;
+        long long r = r0 + warp;
+        for (; r + 3 * kColWarps < r1; r += 4 * kColWarps) {
+            float4 q[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) q[u] = __ldg(reinterpret_cast<const float4 *>(base + (r + u * kColWarps) * rs));
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const long long e = r + u * kColWarps;
+                Reducer<OP>::add(s[0], q[u].x, e);
+                Reducer<OP>::add(s[1], q[u].y, e);
+                Reducer<OP>::add(s[2], q[u].z, e);
+                Reducer<OP>::add(s[3], q[u].w, e);
+            }
+        }
+        for (; r < r1; r += kColWarps) {
+            const float4 q = __ldg(reinterpret_cast<const float4 *>(base + r * rs));
+            Reducer<OP>::add(s[0], q.x, r);
+            Reducer<OP>::add(s[1], q.y, r);
+            Reducer<OP>::add(s[2], q.z, r);
+            Reducer<OP>::add(s[3], q.w, r);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) part[warp][lane * 4 + j] = s[j];
+    __syncthreads();
+    if (threadIdx.x < 128) {
+        State t = part[0][threadIdx.x];
+#pragma unroll
+        for (int w = 1; w < kColWarps; ++w) Reducer<OP>::merge(t, part[w][threadIdx.x]);
+        const long long c = static_cast<long long>(blockIdx.x) * 128 + threadIdx.x;
+        if (c < ncols) {
+            const long long o = static_cast<long long>(blockIdx.z) * ncols + c;
+            if (a.chunks == 1) store_result<OP>(a, o, t);
+            else a.partial[o * a.chunks + blockIdx.y] = t;
+        }
+    }
+}
+
 // Visits the reduced elements of one output in the reference's order (reduced
 // axes row-major, ReductionPlan, iteration/reduction.cpp:14-121).
 template <class F>
@@ -637,6 +698,40 @@ int run_reduction(RedPlan &p, cudaStream_t stream) {
             k_row_block<OP><<<static_cast<unsigned>(blocks), 512, 0, stream>>>(a);
         }
         return check_launch("row reduction");
+    }
+    // column kernel: contiguous innermost kept axis, one reduced axis, float4 aligned
+    if (a.rrank == 1 && (a.krank == 1 || a.krank == 2) && a.kstr[a.krank - 1] == 1) {
+        const long long ncols = a.kshape[a.krank - 1];
+        const long long nbatch = a.krank == 2 ? a.kshape[0] : 1;
+        const long long bstride = a.krank == 2 ? a.kstr[0] : 0;
+        const bool v4 = ncols % 4 == 0 && a.rstr[0] % 4 == 0 && bstride % 4 == 0 &&
+                        (reinterpret_cast<uintptr_t>(a.in + a.in_off) % 16) == 0;
+        if (v4 && nbatch <= 65535) {
+            const long long gx = (ncols + 127) / 128;
+            const long long want = static_cast<long long>(sms) * 8;  // 8 CTAs of 256 threads per SM
+            long long chunks = (want + gx * nbatch - 1) / (gx * nbatch);
+            const long long max_chunks = (a.R + 63) / 64;  // at least 64 rows per chunk
+            if (chunks > max_chunks) chunks = max_chunks;
+            if (chunks > 65535) chunks = 65535;
+            if (chunks < 1) chunks = 1;
+            a.chunks = static_cast<int>(chunks);
+            void *scratch = nullptr;
+            if (chunks > 1) {
+                MTC_TRY(scratch_alloc(static_cast<size_t>(a.nout * chunks) * sizeof(State), stream, &scratch));
+                a.partial = static_cast<State *>(scratch);
+            }
+            const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(chunks), static_cast<unsigned>(nbatch));
+            k_col_tile<OP><<<grid, 256, 0, stream>>>(a, ncols, bstride);
+            int rc = check_launch("column reduction");
+            if (rc == MTC_OK && chunks > 1) {
+                long long fb = (a.nout + 255) / 256;
+                if (fb > static_cast<long long>(sms) * 8) fb = static_cast<long long>(sms) * 8;
+                k_finalize<OP><<<static_cast<unsigned>(fb), 256, 0, stream>>>(a);
+                rc = check_launch("column reduction finalize");
+            }
+            scratch_free(scratch, stream);
+            return rc;
+        }
     }
     // per-output kernel: split the reduction so the grid fills the machine
     const long long target = static_cast<long long>(sms) * 2048;

@@ -7,9 +7,10 @@
     python -m minitensor_cpp_b200.kernel_cases gather --rows 16777216 --cols 64
 
 Each case allocates its operands on cuda:0 with torch (device memory only),
-calls the C ABI `--reps` times on the backend's stream, synchronises, checks
+calls the C ABI `--reps` times back to back (prepared calls) on the current stream, synchronises, checks
 the device error word and prints one line with the mean time per call measured
-with CUDA events.  Under a profiler, select the launch with `-k` and `-s`.
+with CUDA events, after --warm-s seconds of untimed calls.  Under a profiler,
+pass --warm-s 0 --reps 1: the launches are then the set-up call and one timed call.
 """
 from __future__ import annotations
 
@@ -20,11 +21,20 @@ import sys
 from . import abi
 
 
+WARM_S = 0.3
+
+
 def _events_ms(fn, reps: int, stream) -> float:
     import torch
 
+    import time
+
     fn()  # first call: NVRTC / tensor-map set-up, not timed
     torch.cuda.synchronize()
+    t0 = time.perf_counter()  # then WARM_S seconds of calls so the SM clock has left idle
+    while time.perf_counter() - t0 < WARM_S:
+        fn()
+        torch.cuda.synchronize()
     # `stream` is the current torch stream's handle, so events on it bracket the calls
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
@@ -45,7 +55,7 @@ def case_gemm(a, torch, stream):
         torch.randn(*lead, a.k, a.n, device="cuda", generator=g)
     C = torch.empty(*lead, a.m, a.n, device="cuda")
     va, vb, vc = abi.View.of(A), abi.View.of(B), abi.View.of(C)
-    ms = _events_ms(lambda: abi.matmul(va, vb, vc, algo, stream), a.reps, stream)
+    ms = _events_ms(abi.matmul(va, vb, vc, algo, stream, prepare=True), a.reps, stream)
     flop = 2.0 * a.batch * a.m * a.n * a.k
     return {"ms": ms, "tflops": flop / ms / 1e9}
 
@@ -64,7 +74,7 @@ def case_chain(a, torch, stream):
             (abi.MULTIPLY, 7, 6, 3, 0.0)]
     ins = [abi.View.of(A), abi.View.of(Bs.t()), abi.View.of(row), abi.View.of(E)]
     vy = abi.View.of(Y)
-    ms = _events_ms(lambda: abi.fused(prog, ins, [7], [vy], stream), a.reps, stream)
+    ms = _events_ms(abi.fused(prog, ins, [7], [vy], stream, prepare=True), a.reps, stream)
     return {"ms": ms, "gbs": 4.0 * (3 * n * n + 2 * n) / ms / 1e6}
 
 
@@ -76,7 +86,7 @@ def case_reduce(a, torch, stream):
     dtype = torch.int64 if a.op == "argmax" else torch.float32
     O = torch.empty(out_len, device="cuda", dtype=dtype)
     vx, vo = abi.View.of(X), abi.View.of(O)
-    ms = _events_ms(lambda: abi.reduce(op, vx, [a.axis], vo, stream), a.reps, stream)
+    ms = _events_ms(abi.reduce(op, vx, [a.axis], vo, stream, prepare=True), a.reps, stream)
     return {"ms": ms, "gbs": X.numel() * 4.0 / ms / 1e6}
 
 
@@ -85,7 +95,7 @@ def case_log_softmax(a, torch, stream):
     X = torch.rand(a.n, a.m or a.n, device="cuda", generator=g) * 2 - 1
     Y = torch.empty_like(X)
     vx, vy = abi.View.of(X), abi.View.of(Y)
-    ms = _events_ms(lambda: abi.log_softmax(vx, 1, vy, stream), a.reps, stream)
+    ms = _events_ms(abi.log_softmax(vx, 1, vy, stream, prepare=True), a.reps, stream)
     return {"ms": ms, "gbs": X.numel() * 8.0 / ms / 1e6}
 
 
@@ -96,7 +106,7 @@ def case_gather(a, torch, stream):
     O = torch.empty(a.rows, a.cols, device="cuda")
     # row gather: the index column broadcast over the row width (stride 0)
     vt, vi, vo = abi.View.of(T), abi.View(idx, (a.rows, a.cols), (1, 0), 0), abi.View.of(O)
-    ms = _events_ms(lambda: abi.gather(vt, vi, 0, vo, stream), a.reps, stream)
+    ms = _events_ms(abi.gather(vt, vi, 0, vo, stream, prepare=True), a.reps, stream)
     return {"ms": ms, "gbs": (2.0 * a.rows * a.cols * 4 + a.rows * 8) / ms / 1e6}
 
 
@@ -119,7 +129,10 @@ def main(argv=None) -> int:
     p.add_argument("--cols", type=int, default=64)
     p.add_argument("--reps", type=int, default=3)
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--warm-s", type=float, default=0.3, help="untimed calls before timing (0 under a profiler)")
     a = p.parse_args(argv)
+    global WARM_S
+    WARM_S = a.warm_s
     if a.case == "gemm" and a.m == 0:
         a.m = a.n
     import torch

@@ -213,6 +213,38 @@ def test_fused_chain_equals_unfused_chain(cuda):
     assert_ulp(host(out), y.storage, 2, "fused chain")
 
 
+@pytest.mark.parametrize("offset", [0, 4, 1])
+def test_fused_tiled_transposes_batched_two_outputs(cuda, offset):
+    """Two transposed inputs, a contiguous one and a column broadcast in a batched
+    space with partial 64x64 tiles; two outputs.  Offsets 0 and 4 keep every
+    operand 16-byte aligned (the float4 tile kernel), offset 1 does not (the
+    scalar tile kernel).  Only +, * and relu: bit-exact against numpy."""
+    rng = np.random.default_rng(21)
+    b, n, m = 3, 100, 132
+    st = lambda: rng.uniform(-1, 1, b * n * m + offset).astype(F)
+    P, Q, R = st(), st(), st()
+    colv = rng.uniform(-1, 1, b * n).astype(F)
+    tr = [b * n * m, 1, n]  # element (i, r, c) at i*n*m + c*n + r
+    Pt = hv(P, [b, n, m], tr, offset)
+    Qt = hv(Q, [b, n, m], tr, offset)
+    Rc = hv(R, [b, n, m], None, offset)
+    Cb = hv(colv, [b, n, 1])
+    pv = mo.view(P, [b, n, m], tr, offset)
+    qv = mo.view(Q, [b, n, m], tr, offset)
+    rv = mo.view(R, [b, n, m], abi.contiguous_strides([b, n, m]), offset)
+    cv = colv.reshape(b, n, 1)
+    e0 = mo.unary(mo.RELU, (pv * qv + rv).astype(F)) * cv
+    e1 = (pv + cv) * rv
+    prog = [(abi.MULTIPLY, 4, 0, 1, 0.0), (abi.ADD, 5, 4, 2, 0.0), (abi.RELU, 6, 5, 0, 0.0),
+            (abi.MULTIPLY, 7, 6, 3, 0.0), (abi.ADD, 8, 0, 3, 0.0), (abi.MULTIPLY, 9, 8, 2, 0.0)]
+    outs = [gpu(out_like([b, n, m], offset=offset)) for _ in range(2)]
+    abi.fused(prog, [gpu(Pt), gpu(Qt), gpu(Rc), gpu(Cb)], [7, 9], outs)
+    for o, e, name in zip(outs, (e0, e1), ("relu(p*q + r) * c", "(p + c) * r")):
+        got = host(o)
+        assert (got[:offset] == -7.0).all(), "wrote before the output offset"
+        assert_bits(got[offset:], e.astype(F).reshape(-1), name)
+
+
 def test_fused_multi_output_adamw_program(cuda):
     """AdamW's update graph as one fused program with three outputs (p', m', v')."""
     rng = np.random.default_rng(11)
@@ -298,6 +330,40 @@ def test_max_argmax_vs_oracle(cuda):
             oi = gpu(out_like(kept, dtype=np.int64, fill=-1))
             abi.reduce(abi.ARGMAX, gpu(layout), [axis], oi)
             assert_bits(host(oi), mo.reduce_argmax(x, axis), f"argmax axis {axis}")
+
+
+@pytest.mark.parametrize("op", [abi.SUM, abi.LOGSUMEXP, abi.MAX, abi.ARGMAX])
+def test_column_reductions_beyond_the_exact_regime(cuda, op):
+    """Reductions of a strided axis with a contiguous kept axis, large enough to
+    leave the small exact path: [6000, 516] over axis 0 (a partial 128-column
+    group, chunked) and [3, 2000, 388] over axis 1 (batched).  NaN, an all -inf
+    row and a tie are planted for max/argmax."""
+    rng = np.random.default_rng(17)
+    a = rng.standard_normal((6000, 516)).astype(F)
+    b = rng.standard_normal((3, 2000, 388)).astype(F)
+    if op in (abi.MAX, abi.ARGMAX):
+        a[4000, 7] = np.nan
+        a[17, :] = -np.inf
+        a[100, 9] = a[5000, 9] = 60.0  # tie: the first index wins
+        b[1, 1500, 3] = np.nan
+        b[2, 10, 5] = b[2, 1999, 5] = 70.0
+    for x, axis in ((a, 0), (b, 1)):
+        kept = [e for d, e in enumerate(x.shape) if d != axis]
+        view = hv(x, x.shape)
+        if op == abi.ARGMAX:
+            oi = gpu(out_like(kept, dtype=np.int64, fill=-1))
+            abi.reduce(op, gpu(view), [axis], oi)
+            assert_bits(host(oi), mo.reduce_argmax(x, axis).reshape(-1), f"argmax {x.shape} axis {axis}")
+            continue
+        out = gpu(out_like(kept))
+        abi.reduce(op, gpu(view), [axis], out)
+        if op == abi.MAX:
+            assert_bits(host(out), mo.reduce_max(x, [axis]).reshape(-1), f"max {x.shape} axis {axis}")
+            continue
+        ref = out_like(kept)
+        rk.reduce(op, view, [axis], False, ref)
+        scale = mo.reduce_sum(np.abs(x), [axis]).reshape(-1) if op == abi.SUM else None
+        assert_rel_sqrtk(host(out), ref.storage, x.shape[axis], scale, f"op {op:#x} {x.shape} axis {axis}")
 
 
 def test_log_softmax_vs_oracle(cuda):
