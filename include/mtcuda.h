@@ -128,10 +128,13 @@ int mtc_set_device(int device);
 
 /* Per-device work stream created on first use (non-blocking w.r.t. the legacy stream). */
 int mtc_device_stream(int device, void **stream);
-/* Stream-ordered allocation of `bytes` on `device`; *ptr = NULL for 0 bytes
- * (the reference hands out a valid empty buffer, runtime_test.cpp:85-94). */
+/* Stream-ordered allocation of `bytes` on `device` from the backend's caching
+ * allocator (cached blocks are reused in stream order; cudaMalloc only when
+ * nothing fits); *ptr = NULL for 0 bytes (the reference hands out a valid
+ * empty buffer, runtime_test.cpp:85-94). */
 int mtc_alloc(int device, size_t bytes, void *stream, void **ptr);
-/* Stream-ordered release of a block from mtc_alloc. */
+/* Stream-ordered release of a block from mtc_alloc: reusable at once by later
+ * work on `stream`, by other streams once `stream` has passed this point. */
 int mtc_free(int device, void *ptr, void *stream);
 /* Host -> device copy, ordered on `stream`; `src` must stay valid until the
  * stream reaches the copy (pageable sources are staged by the driver before return). */
@@ -140,9 +143,9 @@ int mtc_copy_from_host(int device, void *dst, const void *src, size_t bytes, voi
 int mtc_copy_to_host(int device, void *dst, const void *src, size_t bytes, void *stream);
 /* Wait for all work queued on `stream`. */
 int mtc_stream_synchronize(void *stream);
-/* Bytes reserved by / in use in the device pool. */
+/* Bytes held from the driver by / handed out from the caching allocator. */
 int mtc_pool_stats(int device, uint64_t *reserved_bytes, uint64_t *used_bytes);
-/* Return cached-but-unused pool memory to the driver. */
+/* Return cached-but-unused blocks to the driver (synchronises the device). */
 int mtc_pool_trim(int device);
 
 /* Device-side error word: synchronises `stream`, then returns MTC_ERR_OUT_OF_RANGE

@@ -118,6 +118,16 @@ int sm_count(int device);
 int current_device();
 
 // Stream-ordered scratch allocation for kernels that need workspace.
+// MTB_TRACE set: host calls of the library that take 5 ms or more are reported
+// on stderr with a label (allocation, packing, launch), to find host stalls.
+bool host_trace();
+struct HostSpan {
+    const char *label;
+    double t0;
+    explicit HostSpan(const char *l);
+    ~HostSpan();
+};
+
 int scratch_alloc(size_t bytes, cudaStream_t stream, void **ptr);
 void scratch_free(void *ptr, cudaStream_t stream);
 

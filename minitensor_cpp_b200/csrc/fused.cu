@@ -13,6 +13,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -274,7 +275,11 @@ extern "C" int mtc_fused(const mtc_instr *program, int32_t n_instr, const mtc_de
         auto it = g_cache.find(key);
         if (it == g_cache.end()) {
             auto fresh = std::make_unique<CompiledProgram>();
+            const auto t0 = std::chrono::steady_clock::now();
             MTC_TRY(compile(src, v, *fresh));
+            if (std::getenv("MTB_TRACE") != nullptr)
+                std::fprintf(stderr, "mtc fused program: variant %d compiled or loaded in %.1f ms\n", v,
+                             std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count());
             it = g_cache.emplace(key, std::move(fresh)).first;
         }
         cp = it->second.get();

@@ -912,16 +912,29 @@ int gemm_3xtf32(const GemmProblem &p, cudaStream_t stream) {
     const size_t a_elems = static_cast<size_t>(p.batch * p.M * Kp);
     const size_t b_elems = static_cast<size_t>(p.batch * p.N * Kp);
     void *scratch = nullptr;
-    MTC_TRY(scratch_alloc((2 * a_elems + 2 * b_elems) * sizeof(float) + 1024, stream, &scratch));
+    {
+        HostSpan span("3xTF32 workspace allocation");
+        MTC_TRY(scratch_alloc((2 * a_elems + 2 * b_elems) * sizeof(float) + 1024, stream, &scratch));
+    }
     float *ahi = static_cast<float *>(scratch);
     float *alo = ahi + a_elems;
     float *bhi = alo + a_elems;
     float *blo = bhi + b_elems;
-    int rc = pack(p.A, p.a_off, p.a_rs, p.a_cs, p.M, p.K, Kp, p, p.a_bs, ahi, alo, stream);
-    // B[k][n] packed as B'[n][k]: rows advance along n (b_cs), k along b_rs
-    if (rc == MTC_OK) rc = pack(p.B, p.b_off, p.b_cs, p.b_rs, p.N, p.K, Kp, p, p.b_bs, bhi, blo, stream);
-    if (rc == MTC_OK) rc = launch_tc_selected(p, Kp, ahi, alo, bhi, blo, stream);
-    scratch_free(scratch, stream);
+    int rc;
+    {
+        HostSpan span("3xTF32 operand packs");
+        rc = pack(p.A, p.a_off, p.a_rs, p.a_cs, p.M, p.K, Kp, p, p.a_bs, ahi, alo, stream);
+        // B[k][n] packed as B'[n][k]: rows advance along n (b_cs), k along b_rs
+        if (rc == MTC_OK) rc = pack(p.B, p.b_off, p.b_cs, p.b_rs, p.N, p.K, Kp, p, p.b_bs, bhi, blo, stream);
+    }
+    {
+        HostSpan span("3xTF32 tensor maps and launch");
+        if (rc == MTC_OK) rc = launch_tc_selected(p, Kp, ahi, alo, bhi, blo, stream);
+    }
+    {
+        HostSpan span("3xTF32 workspace release");
+        scratch_free(scratch, stream);
+    }
     return rc;
 }
 

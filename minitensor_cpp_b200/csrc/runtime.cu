@@ -5,7 +5,14 @@
 
 #include <algorithm>
 #include <atomic>
+#include <chrono>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <map>
+#include <memory>
+#include <unordered_map>
+#include <string>
 #include <mutex>
 #include <vector>
 
@@ -24,6 +31,168 @@ struct DeviceState {
 
 std::mutex g_mutex;
 std::vector<DeviceState> g_devices;
+
+// ------------------------------------------------------ caching allocator --
+// Device memory for graph buffers and kernel workspaces.  The evaluator
+// allocates one buffer per materialised node and the GEMM one workspace per
+// call, gigabytes per training step, so blocks are cached and reused in stream
+// order instead of going to the driver: a block freed on stream S is handed to
+// the next request on S at once (everything that used it is queued before
+// anything that will), and a block freed on another stream becomes reusable by
+// every stream when an event recorded at the free has completed.  Requests of
+// 1 MiB or less are rounded to 512 bytes, larger ones to 2 MiB; the best fit
+// whose size is within 1/8 (at least 2 MiB) of the request is reused whole.
+// cudaMalloc is called only when nothing fits; when it fails, the unused cached
+// blocks are released (after a device synchronisation) and it is retried once.
+
+struct Block {
+    void *ptr = nullptr;
+    size_t size = 0;
+    cudaStream_t stream = nullptr;  // stream of the last owner
+};
+
+struct PendingFree {
+    Block block;
+    cudaEvent_t done = nullptr;
+};
+
+struct DevicePool {
+    std::mutex mu;
+    // free blocks reusable by one stream (stream order) or, key nullptr, by any stream
+    std::vector<std::pair<cudaStream_t, std::multimap<size_t, Block>>> free_lists;
+    std::vector<PendingFree> pending;
+    std::unordered_map<void *, Block> live;
+    std::vector<cudaEvent_t> spare_events;
+    uint64_t reserved = 0;
+    uint64_t cached = 0;
+
+    std::multimap<size_t, Block> &list_for(cudaStream_t s) {
+        for (auto &fl : free_lists)
+            if (fl.first == s) return fl.second;
+        free_lists.emplace_back(s, std::multimap<size_t, Block>{});
+        return free_lists.back().second;
+    }
+};
+
+std::mutex g_pool_mutex;
+std::vector<std::unique_ptr<DevicePool>> g_pools;
+
+DevicePool &pool_of(int device) {
+    std::lock_guard<std::mutex> lock(g_pool_mutex);
+    if (static_cast<int>(g_pools.size()) <= device) g_pools.resize(device + 1);
+    if (!g_pools[device]) g_pools[device] = std::make_unique<DevicePool>();
+    return *g_pools[device];
+}
+
+size_t round_request(size_t bytes) {
+    constexpr size_t kSmall = size_t(1) << 20, kLarge = size_t(2) << 20;
+    if (bytes <= kSmall) return (bytes + 511) & ~size_t(511);
+    return (bytes + kLarge - 1) / kLarge * kLarge;
+}
+
+bool take_fit(std::multimap<size_t, Block> &fl, size_t want, Block &out) {
+    auto it = fl.lower_bound(want);
+    if (it == fl.end()) return false;
+    const size_t slack = std::max(want / 8, size_t(2) << 20);
+    if (it->first > want + slack) return false;
+    out = it->second;
+    fl.erase(it);
+    return true;
+}
+
+// Moves blocks whose cross-stream free has completed to the any-stream list.
+void collect_pending(DevicePool &pool) {
+    for (size_t i = 0; i < pool.pending.size();) {
+        PendingFree &pf = pool.pending[i];
+        if (cudaEventQuery(pf.done) == cudaSuccess) {
+            Block b = pf.block;
+            b.stream = nullptr;
+            pool.list_for(nullptr).emplace(b.size, b);
+            pool.spare_events.push_back(pf.done);
+            pool.pending[i] = pool.pending.back();
+            pool.pending.pop_back();
+        } else {
+            cudaGetLastError();  // cudaErrorNotReady is not an error here
+            ++i;
+        }
+    }
+}
+
+// Returns every cached (unused) block to the driver; the caller holds pool.mu.
+int release_cached(DevicePool &pool) {
+    MTC_CUDA_TRY(cudaDeviceSynchronize());
+    collect_pending(pool);
+    for (auto &fl : pool.free_lists) {
+        for (auto &kv : fl.second) {
+            cudaFree(kv.second.ptr);
+            pool.reserved -= kv.second.size;
+            pool.cached -= kv.second.size;
+        }
+        fl.second.clear();
+    }
+    return MTC_OK;
+}
+
+int pool_alloc(int device, size_t bytes, cudaStream_t stream, void **ptr) {
+    *ptr = nullptr;
+    if (bytes == 0) return MTC_OK;
+    DevicePool &pool = pool_of(device);
+    const size_t want = round_request(bytes);
+    std::lock_guard<std::mutex> lock(pool.mu);
+    if (!pool.pending.empty()) collect_pending(pool);
+    Block b;
+    bool hit = take_fit(pool.list_for(stream), want, b);
+    if (!hit) hit = take_fit(pool.list_for(nullptr), want, b);
+    if (hit) {
+        pool.cached -= b.size;
+    } else {
+        void *p = nullptr;
+        cudaError_t e = cudaMalloc(&p, want);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            MTC_TRY(release_cached(pool));
+            e = cudaMalloc(&p, want);
+        }
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return fail(MTC_ERR_RUNTIME, "device %d: allocation of %zu bytes failed: %s", device, bytes,
+                        cudaGetErrorString(e));
+        }
+        b.ptr = p;
+        b.size = want;
+        pool.reserved += want;
+    }
+    b.stream = stream;
+    pool.live.emplace(b.ptr, b);
+    *ptr = b.ptr;
+    return MTC_OK;
+}
+
+int pool_free(int device, void *ptr, cudaStream_t stream) {
+    if (ptr == nullptr) return MTC_OK;
+    DevicePool &pool = pool_of(device);
+    std::lock_guard<std::mutex> lock(pool.mu);
+    auto it = pool.live.find(ptr);
+    if (it == pool.live.end()) return fail(MTC_ERR_INVALID_ARGUMENT, "device %d: %p is not a live block", device, ptr);
+    Block b = it->second;
+    pool.live.erase(it);
+    pool.cached += b.size;
+    if (stream == b.stream) {
+        pool.list_for(stream).emplace(b.size, b);
+        return MTC_OK;
+    }
+    // freed on another stream: reusable once that stream has passed this point
+    cudaEvent_t ev = nullptr;
+    if (!pool.spare_events.empty()) {
+        ev = pool.spare_events.back();
+        pool.spare_events.pop_back();
+    } else {
+        MTC_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    }
+    MTC_CUDA_TRY(cudaEventRecord(ev, stream));
+    pool.pending.push_back(PendingFree{b, ev});
+    return MTC_OK;
+}
 
 int ensure_device(int device, DeviceState **out) {
     int count = 0;
@@ -44,13 +213,6 @@ int ensure_device(int device, DeviceState **out) {
         MTC_CUDA_TRY(cudaSetDevice(device));
         MTC_CUDA_TRY(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking));
         MTC_CUDA_TRY(cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, device));
-        // Keep freed blocks cached in the default pool: the evaluator allocates
-        // one buffer per graph node, so returning memory to the driver on every
-        // synchronisation would make each step pay cudaMalloc again.
-        cudaMemPool_t pool;
-        MTC_CUDA_TRY(cudaDeviceGetDefaultMemPool(&pool, device));
-        uint64_t threshold = UINT64_MAX;
-        MTC_CUDA_TRY(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold));
         MTC_CUDA_TRY(cudaSetDevice(prev));
         st.ready = true;
     }
@@ -167,15 +329,33 @@ int sm_count(int device) {
     return st->sms;
 }
 
+bool host_trace() {
+    static const bool on = std::getenv("MTB_TRACE") != nullptr;
+    return on;
+}
+
+static double now_ms() {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+HostSpan::HostSpan(const char *l) : label{l}, t0{host_trace() ? now_ms() : 0.0} {}
+
+HostSpan::~HostSpan() {
+    if (!host_trace()) return;
+    const double ms = now_ms() - t0;
+    if (ms >= 5.0) std::fprintf(stderr, "mtc slow host call: %s %.1f ms\n", label, ms);
+}
+
 int scratch_alloc(size_t bytes, cudaStream_t stream, void **ptr) {
-    *ptr = nullptr;
-    if (bytes == 0) return MTC_OK;
-    MTC_CUDA_TRY(cudaMallocAsync(ptr, bytes, stream));
-    return MTC_OK;
+    int device = 0;
+    MTC_CUDA_TRY(cudaGetDevice(&device));
+    return pool_alloc(device, bytes, stream, ptr);
 }
 
 void scratch_free(void *ptr, cudaStream_t stream) {
-    if (ptr) cudaFreeAsync(ptr, stream);
+    if (ptr == nullptr) return;
+    int device = 0;
+    if (cudaGetDevice(&device) == cudaSuccess) (void)pool_free(device, ptr, stream);
 }
 
 int validate(const mtc_desc *d, const char *name) {
@@ -343,24 +523,16 @@ int mtc_alloc(int device, size_t bytes, void *stream, void **ptr) {
     MTC_TRY(ensure_device(device, &st));
     DeviceGuard guard(device);
     MTC_TRY(guard.rc);
-    // 256-byte granularity keeps every buffer aligned for 128-bit and TMA access.
-    const size_t rounded = (bytes + 255) & ~static_cast<size_t>(255);
-    cudaError_t e = cudaMallocAsync(ptr, rounded, static_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess) {
-        cudaGetLastError();
-        *ptr = nullptr;
-        return fail(MTC_ERR_RUNTIME, "device %d: allocation of %zu bytes failed: %s", device, bytes,
-                    cudaGetErrorString(e));
-    }
-    return MTC_OK;
+    // cudaMalloc blocks are 512-byte aligned: every buffer suits 128-bit and TMA access
+    HostSpan span("buffer allocation");
+    return pool_alloc(device, bytes, static_cast<cudaStream_t>(stream), ptr);
 }
 
 int mtc_free(int device, void *ptr, void *stream) {
     if (ptr == nullptr) return MTC_OK;
     DeviceGuard guard(device);
     MTC_TRY(guard.rc);
-    MTC_CUDA_TRY(cudaFreeAsync(ptr, static_cast<cudaStream_t>(stream)));
-    return MTC_OK;
+    return pool_free(device, ptr, static_cast<cudaStream_t>(stream));
 }
 
 int mtc_copy_from_host(int device, void *dst, const void *src, size_t bytes, void *stream) {
@@ -387,21 +559,21 @@ int mtc_stream_synchronize(void *stream) {
 }
 
 int mtc_pool_stats(int device, uint64_t *reserved_bytes, uint64_t *used_bytes) {
-    cudaMemPool_t pool;
-    MTC_CUDA_TRY(cudaDeviceGetDefaultMemPool(&pool, device));
-    MTC_CUDA_TRY(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemCurrent, reserved_bytes));
-    MTC_CUDA_TRY(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemCurrent, used_bytes));
+    clear_error();
+    if (device < 0) return fail(MTC_ERR_INVALID_ARGUMENT, "negative device index");
+    DevicePool &pool = pool_of(device);
+    std::lock_guard<std::mutex> lock(pool.mu);
+    if (reserved_bytes) *reserved_bytes = pool.reserved;
+    if (used_bytes) *used_bytes = pool.reserved - pool.cached;
     return MTC_OK;
 }
 
 int mtc_pool_trim(int device) {
     DeviceGuard guard(device);
     MTC_TRY(guard.rc);
-    MTC_CUDA_TRY(cudaDeviceSynchronize());
-    cudaMemPool_t pool;
-    MTC_CUDA_TRY(cudaDeviceGetDefaultMemPool(&pool, device));
-    MTC_CUDA_TRY(cudaMemPoolTrimTo(pool, 0));
-    return MTC_OK;
+    DevicePool &pool = pool_of(device);
+    std::lock_guard<std::mutex> lock(pool.mu);
+    return release_cached(pool);
 }
 
 }  // extern "C"

@@ -96,9 +96,10 @@ class Frontend:
         return out, red[:m], red[m:m + n], red[m + n:]
 
     def stats(self) -> dict:
-        buf = (ctypes.c_uint64 * 6)()
+        buf = (ctypes.c_uint64 * 9)()
         self.lib.mtb_evaluator_stats(buf)
-        keys = ("kernel_steps", "fused_launches", "fused_nodes", "folded_constants", "view_steps", "evaluations")
+        keys = ("kernel_steps", "fused_launches", "fused_nodes", "folded_constants", "view_steps", "evaluations",
+                "plan_ns", "execute_ns", "check_ns")
         return dict(zip(keys, list(buf)))
 
     def reset_stats(self):

@@ -94,6 +94,9 @@ struct EvaluatorStats {
     std::uint64_t folded_constants = 0;
     std::uint64_t view_steps = 0;
     std::uint64_t evaluations = 0;
+    std::uint64_t plan_ns = 0;     // host time planning and clustering
+    std::uint64_t execute_ns = 0;  // host time issuing kernels (allocation and launch calls)
+    std::uint64_t check_ns = 0;    // host time in the deferred index-error check (a stream synchronisation)
 };
 EvaluatorStats &evaluator_stats();
 

@@ -19,6 +19,8 @@
 //  - the cluster runs as one mtc_fused launch at the position of its last node.
 // Values internal to a cluster stay unmaterialised and are recomputed from
 // their producers if a later evaluation asks for them.
+#include <chrono>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <optional>
@@ -180,6 +182,8 @@ class FusedEvaluator {
         : runtimes_{runtimes}, kernels_{kernels} {}
 
     bool run(std::span<const ValueRef> roots) {
+        using clock = std::chrono::steady_clock;
+        const auto t0 = clock::now();
         Planner planner(runtimes_, kernels_);
         bool has_cuda = false;
         plan_ = planner.build(roots, has_cuda);
@@ -207,7 +211,12 @@ class FusedEvaluator {
             if (external > 0) s.materialize = true;
         }
         if (evaluator_options().fusion) form_clusters();
+        const auto t1 = clock::now();
         execute();
+        const auto t2 = clock::now();
+        auto &st = evaluator_stats();
+        st.plan_ns += static_cast<std::uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(t1 - t0).count());
+        st.execute_ns += static_cast<std::uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(t2 - t1).count());
         return true;
     }
 
@@ -271,17 +280,21 @@ class FusedEvaluator {
     void execute() {
         bool index_kernels = false;
         DeviceRuntime *index_runtime = nullptr;
+        static const bool trace = std::getenv("MTB_TRACE") != nullptr;
         for (int i = 0; i < static_cast<int>(plan_.size()); ++i) {
             Step &s = plan_[i];
             if (s.folded) {
                 ++evaluator_stats().folded_constants;
                 continue;
             }
+            const auto t0 = std::chrono::steady_clock::now();
             if (s.cluster >= 0) {
                 if (clusters_[s.cluster].root == i) launch_cluster(clusters_[s.cluster]);
+                if (trace) report_slow(t0, "fused cluster", s);
                 continue;
             }
             execute_kernel_step(s);
+            if (trace) report_slow(t0, "kernel", s);
             const std::uint32_t id = s.node->primitive().id().value();
             if (s.on_cuda && (id == kGatherId || id == kScatterAddId)) {
                 index_kernels = true;
@@ -291,10 +304,22 @@ class FusedEvaluator {
         if (index_kernels && evaluator_options().check_index_errors && index_runtime != nullptr) {
             auto &rt = dynamic_cast<CudaRuntime &>(*index_runtime);
             int64_t detail = 0;
+            const auto c0 = std::chrono::steady_clock::now();
             const int rc = mtc_check_device_errors(rt.index(), rt.stream(), &detail);
+            evaluator_stats().check_ns += static_cast<std::uint64_t>(
+                std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - c0).count());
             if (rc == MTC_ERR_OUT_OF_RANGE) throw std::out_of_range{"gather index is out of range"};
             check(rc, "device error check");
         }
+    }
+
+    // MTB_TRACE: host calls of 20 ms or more (allocation, compilation or a
+    // blocked launch) are reported with the primitive that made them.
+    static void report_slow(std::chrono::steady_clock::time_point t0, const char *what, const Step &s) {
+        const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+        if (ms >= 20.0)
+            std::fprintf(stderr, "mtb slow host call: %s, primitive 0x%04x, %.1f ms\n", what,
+                         static_cast<unsigned>(s.node->primitive().id().value()), ms);
     }
 
     // Members in plan order; registers: external inputs first, then one per

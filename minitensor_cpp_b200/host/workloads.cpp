@@ -3,6 +3,8 @@
 
 #include <chrono>
 #include <cmath>
+#include <cstdio>
+#include <cstdlib>
 #include <limits>
 #include <memory>
 #include <optional>
@@ -209,6 +211,28 @@ int mtb_spiral_train(int device, int steps, int points, int hidden, uint64_t see
 
 namespace {
 
+// MTB_TRACE=1: one line per training step on stderr with the host time of each
+// phase (graph construction, gradient exchange, evaluations), for telling a
+// host-bound step from a device-bound one.
+struct StepTrace {
+    using clock = std::chrono::steady_clock;
+    bool on = std::getenv("MTB_TRACE") != nullptr;
+    clock::time_point last = clock::now();
+    std::string line;
+    void mark(const char *phase) {
+        if (!on) return;
+        const auto now = clock::now();
+        char buf[96];
+        std::snprintf(buf, sizeof(buf), "%s%s %.1f ms", line.empty() ? "" : ", ", phase,
+                      std::chrono::duration<double, std::milli>(now - last).count());
+        line += buf;
+        last = now;
+    }
+    ~StepTrace() {
+        if (on) std::fprintf(stderr, "mtb step: %s\n", line.c_str());
+    }
+};
+
 struct MlpTrainer {
     mt::Device device;
     DenseMlp model;
@@ -233,15 +257,23 @@ struct MlpTrainer {
     }
 
     float step(const mt::Tensor &x, const mt::Tensor &y, bool read_loss) {
+        StepTrace trace;
         const mt::Tensor logits = mt::nn::forward(model, params, x);
         const mt::Tensor loss = mt::nn::categorical_cross_entropy_with_logits(logits, y);
         auto grads = mt::nn::parameter_gradients(loss, params);
+        trace.mark("graph");
         if (world > 1) allreduce(grads, loss);
+        trace.mark("allreduce");
         auto [next_params, next_state] = optimizer.step(std::move(params), std::move(state), grads);
         grads.clear();
+        trace.mark("optimizer graph");
         params = mt::nn::leafify_parameter_values(std::move(next_params));
+        trace.mark("evaluate parameters");
         state = mt::nn::leafify_optimizer_state(std::move(next_state));
-        return read_loss ? mt::item<float>(loss) : 0.0F;
+        trace.mark("evaluate state");
+        const float value = read_loss ? mt::item<float>(loss) : 0.0F;
+        trace.mark("loss");
+        return value;
     }
 
     // Data-parallel gradient exchange: the loss and all gradients are
@@ -449,17 +481,20 @@ int mtb_chain(int device, int64_t n, int64_t m, const float *a, const float *b_s
     });
 }
 
-void mtb_evaluator_stats(uint64_t *out6) {
+void mtb_evaluator_stats(uint64_t *out9) {
 #ifndef MTB_CPU_ONLY
     const auto &s = mt::detail::cuda::evaluator_stats();
-    out6[0] = s.kernel_steps;
-    out6[1] = s.fused_launches;
-    out6[2] = s.fused_nodes;
-    out6[3] = s.folded_constants;
-    out6[4] = s.view_steps;
-    out6[5] = s.evaluations;
+    out9[0] = s.kernel_steps;
+    out9[1] = s.fused_launches;
+    out9[2] = s.fused_nodes;
+    out9[3] = s.folded_constants;
+    out9[4] = s.view_steps;
+    out9[5] = s.evaluations;
+    out9[6] = s.plan_ns;
+    out9[7] = s.execute_ns;
+    out9[8] = s.check_ns;
 #else
-    for (int i = 0; i < 6; ++i) out6[i] = 0;
+    for (int i = 0; i < 9; ++i) out9[i] = 0;
 #endif
 }
 

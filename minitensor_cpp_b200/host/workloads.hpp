@@ -59,8 +59,9 @@ int mtb_chain(int device, int64_t n, int64_t m, const float *a, const float *b_s
               const float *col, float *out, float *reductions);
 
 // Counters of the fusing evaluator (zeros in the CPU-only build):
-// kernel_steps, fused_launches, fused_nodes, folded_constants, view_steps, evaluations.
-void mtb_evaluator_stats(uint64_t *out6);
+// kernel_steps, fused_launches, fused_nodes, folded_constants, view_steps, evaluations,
+// and host nanoseconds spent planning, issuing kernels and in the index-error check.
+void mtb_evaluator_stats(uint64_t *out9);
 void mtb_evaluator_reset_stats(void);
 // 1 when the library has the CUDA backend, 0 for the CPU-only build.
 int mtb_has_cuda(void);

@@ -79,7 +79,7 @@ def case_chain(a, torch, stream):
 
 
 def case_reduce(a, torch, stream):
-    op = {"sum": abi.SUM, "max": abi.MAX, "argmax": abi.ARGMAX, "lse": abi.LSE}[a.op]
+    op = {"sum": abi.SUM, "max": abi.MAX, "argmax": abi.ARGMAX, "lse": abi.LOGSUMEXP}[a.op]
     g = torch.Generator(device="cuda").manual_seed(a.seed)
     X = torch.rand(a.n, a.m or a.n, device="cuda", generator=g) * 2 - 1
     out_len = X.shape[1 - a.axis]

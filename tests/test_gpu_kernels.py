@@ -224,7 +224,7 @@ def test_fused_tiled_transposes_batched_two_outputs(cuda, offset):
     st = lambda: rng.uniform(-1, 1, b * n * m + offset).astype(F)
     P, Q, R = st(), st(), st()
     colv = rng.uniform(-1, 1, b * n).astype(F)
-    tr = [b * n * m, 1, n]  # element (i, r, c) at i*n*m + c*n + r
+    tr = [n * m, 1, n]  # element (i, r, c) at i*n*m + c*n + r
     Pt = hv(P, [b, n, m], tr, offset)
     Qt = hv(Q, [b, n, m], tr, offset)
     Rc = hv(R, [b, n, m], None, offset)
