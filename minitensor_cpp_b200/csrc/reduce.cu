@@ -44,13 +44,18 @@ struct Reducer<MTC_OP_SUM> {
     __device__ static float result(const State &s) { return s.a; }
 };
 
+// Maximum that returns NaN when either operand is NaN (one instruction).
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
+}
+
 template <>
 struct Reducer<MTC_OP_MAX> {
     // NaN propagates; an empty reduction gives -inf.
     __device__ static State init() { return State{-INFINITY, 0.0f, kEmpty, 0, 0}; }
-    __device__ static void add(State &s, float x, long long) {
-        if (s.a == s.a && (x != x || x > s.a)) s.a = x;
-    }
+    __device__ static void add(State &s, float x, long long) { s.a = max_nan(s.a, x); }
     __device__ static void merge(State &s, const State &o) { add(s, o.a, 0); }
     __device__ static float result(const State &s) { return s.a; }
 };
@@ -78,6 +83,15 @@ struct Reducer<MTC_OP_ARGMAX> {
         if (take) s = o;
     }
     __device__ static long long result(const State &s) { return s.i == kEmpty ? 0 : s.i; }
+    // The update of a thread that walks its elements in increasing index order
+    // from a state seeded with (-inf, first index): x replaces the best when it
+    // is larger or NaN, unless the best is already NaN (the first NaN wins).
+    __device__ static void add_seeded(State &s, float x, long long idx) {
+        if (!(x <= s.a) && s.a == s.a) {
+            s.a = x;
+            s.i = idx;
+        }
+    }
 };
 
 template <>
@@ -120,6 +134,22 @@ struct Reducer<MTC_OP_LOGSUMEXP> {
         return s.a + logf(s.b);
     }
 };
+
+// Element update for a thread that visits its elements in increasing index
+// order and has at least one: ARGMAX uses the seeded form (state seeded with
+// the first index), every other op its ordinary add.
+template <int OP>
+__device__ __forceinline__ State seeded_init(long long first) {
+    State s = Reducer<OP>::init();
+    if constexpr (OP == MTC_OP_ARGMAX) s.i = first;
+    return s;
+}
+
+template <int OP>
+__device__ __forceinline__ void add_in_order(State &s, float x, long long idx) {
+    if constexpr (OP == MTC_OP_ARGMAX) Reducer<OP>::add_seeded(s, x, idx);
+    else Reducer<OP>::add(s, x, idx);
+}
 
 __device__ __forceinline__ State shfl_down(const State &s, int delta) {
     State o;
@@ -196,26 +226,27 @@ __device__ __forceinline__ State accumulate_row(const RedArgs &a, long long base
         const float4 *p = reinterpret_cast<const float4 *>(a.in + base);
         const long long nv = R / 4;
         long long v = lane;
-        // four independent 128-bit loads in flight per thread, consumed in index order
-        for (; v + 3LL * lanes < nv; v += 4LL * lanes) {
-            float4 q[4];
+        if (v < nv) s = seeded_init<OP>(4 * v);
+        // eight independent 128-bit loads in flight per thread, consumed in index order
+        for (; v + 7LL * lanes < nv; v += 8LL * lanes) {
+            float4 q[8];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) q[u] = __ldg(p + v + u * lanes);
+            for (int u = 0; u < 8; ++u) q[u] = __ldg(p + v + u * lanes);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < 8; ++u) {
                 const long long e = 4 * (v + u * lanes);
-                Reducer<OP>::add(s, q[u].x, e);
-                Reducer<OP>::add(s, q[u].y, e + 1);
-                Reducer<OP>::add(s, q[u].z, e + 2);
-                Reducer<OP>::add(s, q[u].w, e + 3);
+                add_in_order<OP>(s, q[u].x, e);
+                add_in_order<OP>(s, q[u].y, e + 1);
+                add_in_order<OP>(s, q[u].z, e + 2);
+                add_in_order<OP>(s, q[u].w, e + 3);
             }
         }
         for (; v < nv; v += lanes) {
             const float4 q = __ldg(p + v);
-            Reducer<OP>::add(s, q.x, 4 * v);
-            Reducer<OP>::add(s, q.y, 4 * v + 1);
-            Reducer<OP>::add(s, q.z, 4 * v + 2);
-            Reducer<OP>::add(s, q.w, 4 * v + 3);
+            add_in_order<OP>(s, q.x, 4 * v);
+            add_in_order<OP>(s, q.y, 4 * v + 1);
+            add_in_order<OP>(s, q.z, 4 * v + 2);
+            add_in_order<OP>(s, q.w, 4 * v + 3);
         }
     } else {
         const long long st = a.rrun_stride;
@@ -346,31 +377,33 @@ __global__ void __launch_bounds__(256) k_col_tile(const RedArgs a, long long nco
     const long long r0 = static_cast<long long>(blockIdx.y) * per;
     const long long r1 = r0 + per < a.R ? r0 + per : a.R;
     State s[4];
+    const long long first = r0 + warp;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) s[j] = Reducer<OP>::init();
+    for (int j = 0; j < 4; ++j) s[j] = first < r1 ? seeded_init<OP>(first) : Reducer<OP>::init();
     if (col < ncols) {
         const long long rs = a.rstr[0];
         const float *base = a.in + a.in_off + static_cast<long long>(blockIdx.z) * batch_stride + col;
-        long long r = r0 + warp;
-        for (; r + 3 * kColWarps < r1; r += 4 * kColWarps) {
-            float4 q[4];
+        long long r = first;
+        // eight rows (eight 128-bit loads) in flight per thread
+        for (; r + 7 * kColWarps < r1; r += 8 * kColWarps) {
+            float4 q[8];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) q[u] = __ldg(reinterpret_cast<const float4 *>(base + (r + u * kColWarps) * rs));
+            for (int u = 0; u < 8; ++u) q[u] = __ldg(reinterpret_cast<const float4 *>(base + (r + u * kColWarps) * rs));
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < 8; ++u) {
                 const long long e = r + u * kColWarps;
-                Reducer<OP>::add(s[0], q[u].x, e);
-                Reducer<OP>::add(s[1], q[u].y, e);
-                Reducer<OP>::add(s[2], q[u].z, e);
-                Reducer<OP>::add(s[3], q[u].w, e);
+                add_in_order<OP>(s[0], q[u].x, e);
+                add_in_order<OP>(s[1], q[u].y, e);
+                add_in_order<OP>(s[2], q[u].z, e);
+                add_in_order<OP>(s[3], q[u].w, e);
             }
         }
         for (; r < r1; r += kColWarps) {
             const float4 q = __ldg(reinterpret_cast<const float4 *>(base + r * rs));
-            Reducer<OP>::add(s[0], q.x, r);
-            Reducer<OP>::add(s[1], q.y, r);
-            Reducer<OP>::add(s[2], q.z, r);
-            Reducer<OP>::add(s[3], q.w, r);
+            add_in_order<OP>(s[0], q.x, r);
+            add_in_order<OP>(s[1], q.y, r);
+            add_in_order<OP>(s[2], q.z, r);
+            add_in_order<OP>(s[3], q.w, r);
         }
     }
 #pragma unroll
