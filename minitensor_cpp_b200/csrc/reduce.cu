@@ -16,6 +16,9 @@
 #include <cfloat>
 #include <cmath>
 #include <cstring>
+#include <mutex>
+#include <utility>
+#include <vector>
 
 #include "common.cuh"
 
@@ -369,7 +372,8 @@ __global__ void __launch_bounds__(256) k_per_output(const RedArgs a) {
 constexpr int kColWarps = 8;
 
 template <int OP>
-__global__ void __launch_bounds__(256) k_col_tile(const RedArgs a, long long ncols, long long batch_stride) {
+__global__ void __launch_bounds__(256) k_col_tile(const RedArgs a, long long ncols, long long batch_stride,
+                                                  unsigned int *arrivals) {
     __shared__ State part[kColWarps][128];
     const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
     const long long col = static_cast<long long>(blockIdx.x) * 128 + lane * 4;
@@ -409,17 +413,76 @@ __global__ void __launch_bounds__(256) k_col_tile(const RedArgs a, long long nco
 #pragma unroll
     for (int j = 0; j < 4; ++j) part[warp][lane * 4 + j] = s[j];
     __syncthreads();
+    const long long c = static_cast<long long>(blockIdx.x) * 128 + threadIdx.x;
+    const long long o = static_cast<long long>(blockIdx.z) * ncols + c;
     if (threadIdx.x < 128) {
         State t = part[0][threadIdx.x];
 #pragma unroll
         for (int w = 1; w < kColWarps; ++w) Reducer<OP>::merge(t, part[w][threadIdx.x]);
-        const long long c = static_cast<long long>(blockIdx.x) * 128 + threadIdx.x;
         if (c < ncols) {
-            const long long o = static_cast<long long>(blockIdx.z) * ncols + c;
             if (a.chunks == 1) store_result<OP>(a, o, t);
-            else a.partial[o * a.chunks + blockIdx.y] = t;
+            else a.partial[static_cast<long long>(blockIdx.y) * a.nout + o] = t;  // chunk-major
         }
     }
+    if (a.chunks == 1) return;
+    // the last CTA of this column group to finish merges the chunk partials in
+    // chunk order and re-arms the group's arrival counter for the next launch
+    __shared__ unsigned int last;
+    __threadfence();
+    __syncthreads();
+    const unsigned int group = blockIdx.z * gridDim.x + blockIdx.x;
+    if (threadIdx.x == 0) last = atomicAdd(&arrivals[group], 1u) == static_cast<unsigned int>(a.chunks) - 1u;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (threadIdx.x < 128 && c < ncols) {
+        // one coalesced row of partials per chunk; four chunks' loads in flight
+        auto load = [&](int k) {
+            const State *q = a.partial + static_cast<long long>(k) * a.nout + o;
+            State r;
+            r.a = __ldcg(&q->a);
+            r.b = __ldcg(&q->b);
+            r.i = __ldcg(&q->i);
+            r.flags = __ldcg(&q->flags);
+            r.pad = 0;
+            return r;
+        };
+        State t = load(0);
+        int k = 1;
+        for (; k + 3 < a.chunks; k += 4) {
+            const State q0 = load(k), q1 = load(k + 1), q2 = load(k + 2), q3 = load(k + 3);
+            Reducer<OP>::merge(t, q0);
+            Reducer<OP>::merge(t, q1);
+            Reducer<OP>::merge(t, q2);
+            Reducer<OP>::merge(t, q3);
+        }
+        for (; k < a.chunks; ++k) Reducer<OP>::merge(t, load(k));
+        store_result<OP>(a, o, t);
+    }
+    if (threadIdx.x == 0) arrivals[group] = 0u;
+}
+
+// Arrival counters of the column kernel, one array per (device, stream): zeroed
+// once on the stream that uses them, then re-armed by the kernel itself.
+constexpr unsigned int kColGroups = 1u << 16;
+std::mutex g_arrivals_mutex;
+std::vector<std::pair<std::pair<int, cudaStream_t>, unsigned int *>> g_arrivals;
+
+int col_arrivals(cudaStream_t stream, unsigned int **out) {
+    int dev = 0;
+    MTC_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(g_arrivals_mutex);
+    for (auto &e : g_arrivals)
+        if (e.first.first == dev && e.first.second == stream) {
+            *out = e.second;
+            return MTC_OK;
+        }
+    void *p = nullptr;
+    MTC_CUDA_TRY(cudaMalloc(&p, kColGroups * sizeof(unsigned int)));
+    MTC_CUDA_TRY(cudaMemsetAsync(p, 0, kColGroups * sizeof(unsigned int), stream));
+    g_arrivals.push_back({{dev, stream}, static_cast<unsigned int *>(p)});
+    *out = static_cast<unsigned int *>(p);
+    return MTC_OK;
 }
 
 // Visits the reduced elements of one output in the reference's order (reduced
@@ -531,63 +594,43 @@ __global__ void __launch_bounds__(512) k_log_softmax_rows(const RedArgs a) {
 template <int NV4>
 __global__ void __launch_bounds__(256) k_lse_resident(const RedArgs a) {
     __shared__ float red_f[8];
-    __shared__ int red_i[8];
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const long long nv = a.R / 4;
     for (long long o = blockIdx.x; o < a.nout; o += gridDim.x) {
         const long long base = kept_offset(a, static_cast<unsigned int>(o));
         const float4 *p = reinterpret_cast<const float4 *>(a.in + base);
         float4 v[NV4];
-        float mx = -INFINITY;
-        int flags = 0;  // bit0 NaN, bit1 +inf
 #pragma unroll
         for (int i = 0; i < NV4; ++i) {
             const long long idx = threadIdx.x + 256LL * i;
             v[i] = idx < nv ? __ldg(p + idx) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
         }
+        // NaN-propagating maximum: NaN anywhere -> NaN, +inf -> +inf, all -inf -> -inf
+        float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < NV4; ++i) {
-            const float e[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+        for (int i = 0; i < NV4; ++i)
+            mx = max_nan(max_nan(mx, v[i].x), max_nan(max_nan(v[i].y, v[i].z), v[i].w));
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                if (e[j] != e[j]) flags |= 1;
-                else {
-                    if (e[j] == INFINITY) flags |= 2;
-                    mx = fmaxf(mx, e[j]);
-                }
-            }
-        }
-#pragma unroll
-        for (int d = 16; d >= 1; d >>= 1) {
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, d));
-            flags |= __shfl_xor_sync(0xffffffffu, flags, d);
-        }
-        if (lane == 0) {
-            red_f[warp] = mx;
-            red_i[warp] = flags;
-        }
+        for (int d = 16; d >= 1; d >>= 1) mx = max_nan(mx, __shfl_xor_sync(0xffffffffu, mx, d));
+        if (lane == 0) red_f[warp] = mx;
         __syncthreads();
         mx = red_f[0];
-        flags = red_i[0];
 #pragma unroll
-        for (int w = 1; w < 8; ++w) {
-            mx = fmaxf(mx, red_f[w]);
-            flags |= red_i[w];
-        }
+        for (int w = 1; w < 8; ++w) mx = max_nan(mx, red_f[w]);
         __syncthreads();
         float lse;
-        if (flags & 1) {
-            lse = NAN;
-        } else if (isinf(mx)) {
-            lse = mx;
+        if (mx != mx || isinf(mx)) {
+            lse = mx;  // NaN, +inf (a +inf element), or -inf (every element -inf)
         } else {
+            // x - max <= 0: the hardware exponential's relative error (~2^-21) is far
+            // inside the 1e-5*sqrt(K) reduction bound
             float s = 0.0f;
 #pragma unroll
             for (int i = 0; i < NV4; ++i) {
-                s += expf(__fsub_rn(v[i].x, mx));
-                s += expf(__fsub_rn(v[i].y, mx));
-                s += expf(__fsub_rn(v[i].z, mx));
-                s += expf(__fsub_rn(v[i].w, mx));
+                s += __expf(__fsub_rn(v[i].x, mx));
+                s += __expf(__fsub_rn(v[i].y, mx));
+                s += __expf(__fsub_rn(v[i].z, mx));
+                s += __expf(__fsub_rn(v[i].w, mx));
             }
 #pragma unroll
             for (int d = 16; d >= 1; d >>= 1) s += __shfl_xor_sync(0xffffffffu, s, d);
@@ -739,7 +782,7 @@ int run_reduction(RedPlan &p, cudaStream_t stream) {
         const long long bstride = a.krank == 2 ? a.kstr[0] : 0;
         const bool v4 = ncols % 4 == 0 && a.rstr[0] % 4 == 0 && bstride % 4 == 0 &&
                         (reinterpret_cast<uintptr_t>(a.in + a.in_off) % 16) == 0;
-        if (v4 && nbatch <= 65535) {
+        if (v4 && nbatch <= 65535 && ((ncols + 127) / 128) * nbatch <= kColGroups) {
             const long long gx = (ncols + 127) / 128;
             const long long want = static_cast<long long>(sms) * 8;  // 8 CTAs of 256 threads per SM
             long long chunks = (want + gx * nbatch - 1) / (gx * nbatch);
@@ -753,15 +796,11 @@ int run_reduction(RedPlan &p, cudaStream_t stream) {
                 MTC_TRY(scratch_alloc(static_cast<size_t>(a.nout * chunks) * sizeof(State), stream, &scratch));
                 a.partial = static_cast<State *>(scratch);
             }
+            unsigned int *arrivals = nullptr;
+            if (chunks > 1) MTC_TRY(col_arrivals(stream, &arrivals));
             const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(chunks), static_cast<unsigned>(nbatch));
-            k_col_tile<OP><<<grid, 256, 0, stream>>>(a, ncols, bstride);
-            int rc = check_launch("column reduction");
-            if (rc == MTC_OK && chunks > 1) {
-                long long fb = (a.nout + 255) / 256;
-                if (fb > static_cast<long long>(sms) * 8) fb = static_cast<long long>(sms) * 8;
-                k_finalize<OP><<<static_cast<unsigned>(fb), 256, 0, stream>>>(a);
-                rc = check_launch("column reduction finalize");
-            }
+            k_col_tile<OP><<<grid, 256, 0, stream>>>(a, ncols, bstride, arrivals);
+            const int rc = check_launch("column reduction");
             scratch_free(scratch, stream);
             return rc;
         }

@@ -337,7 +337,8 @@ def test_column_reductions_beyond_the_exact_regime(cuda, op):
     """Reductions of a strided axis with a contiguous kept axis, large enough to
     leave the small exact path: [6000, 516] over axis 0 (a partial 128-column
     group, chunked) and [3, 2000, 388] over axis 1 (batched).  NaN, an all -inf
-    row and a tie are planted for max/argmax."""
+    row and a tie are planted for max/argmax.  A second call must give the same
+    bits (deterministic merge order; the last-CTA merge counters re-arm)."""
     rng = np.random.default_rng(17)
     a = rng.standard_normal((6000, 516)).astype(F)
     b = rng.standard_normal((3, 2000, 388)).astype(F)
@@ -356,7 +357,11 @@ def test_column_reductions_beyond_the_exact_regime(cuda, op):
             assert_bits(host(oi), mo.reduce_argmax(x, axis).reshape(-1), f"argmax {x.shape} axis {axis}")
             continue
         out = gpu(out_like(kept))
-        abi.reduce(op, gpu(view), [axis], out)
+        xv = gpu(view)
+        abi.reduce(op, xv, [axis], out)
+        again = gpu(out_like(kept))
+        abi.reduce(op, xv, [axis], again)  # the chunk-merge counters re-arm: same bits again
+        assert_bits(host(again), host(out), f"repeat {x.shape} axis {axis}")
         if op == abi.MAX:
             assert_bits(host(out), mo.reduce_max(x, [axis]).reshape(-1), f"max {x.shape} axis {axis}")
             continue
