@@ -723,6 +723,95 @@ __global__ void __launch_bounds__(256) k_split_pack(const PackArgs a) {
     }
 }
 
+__device__ __forceinline__ long long pack_batch_offset(const PackArgs &a, long long b) {
+    long long base = a.off;
+    long long rem = b;
+    for (int d = a.batch_rank - 1; d >= 0; --d) {
+        const long long c = rem % a.batch_shape[d];
+        rem /= a.batch_shape[d];
+        base += c * a.bs[d];
+    }
+    return base;
+}
+
+__device__ __forceinline__ void split4(const float4 v, float4 &h, float4 &l) {
+    split_tf32(v.x, h.x, l.x);
+    split_tf32(v.y, h.y, l.y);
+    split_tf32(v.z, h.z, l.z);
+    split_tf32(v.w, h.w, l.w);
+}
+
+// K-contiguous source (k stride 1, K a multiple of 4, rows 16-byte aligned):
+// one CTA per (batch, row), float4 along K, four loads in flight per thread.
+__global__ void __launch_bounds__(256) k_split_rows4(const PackArgs a) {
+    const long long row = blockIdx.x;  // b * rows + r
+    const long long b = row / a.rows;
+    const long long r = row - b * a.rows;
+    const float4 *src = reinterpret_cast<const float4 *>(a.src + pack_batch_offset(a, b) + r * a.sr);
+    float4 *hi = reinterpret_cast<float4 *>(a.hi + row * a.Kp);
+    float4 *lo = reinterpret_cast<float4 *>(a.lo + row * a.Kp);
+    const int n4 = static_cast<int>(a.K / 4);
+    int c = threadIdx.x;
+    for (; c + 768 < n4; c += 1024) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = __ldg(src + c + 256 * u);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            float4 h, l;
+            split4(v[u], h, l);
+            hi[c + 256 * u] = h;
+            lo[c + 256 * u] = l;
+        }
+    }
+    for (; c < n4; c += 256) {
+        float4 h, l;
+        split4(__ldg(src + c), h, l);
+        hi[c] = h;
+        lo[c] = l;
+    }
+}
+
+// Row-contiguous source (the transpose of a K-major operand: row stride 1,
+// rows a multiple of 4, 16-byte aligned columns): a 64 x 64 tile is read with
+// float4 loads along the rows, staged in shared memory row-major with the
+// 16-byte chunks of each row XOR-swizzled by (row / 4) % 8, and written with
+// float4 stores along K.  Columns K..Kp-1 are written as zeros.
+__global__ void __launch_bounds__(256) k_split_tile4(const PackArgs a) {
+    __shared__ __align__(16) float stage[64][64];
+    const long long r0 = static_cast<long long>(blockIdx.y) * 64;
+    const long long k0 = static_cast<long long>(blockIdx.x) * 64;
+    const long long b = blockIdx.z;
+    const float *src = a.src + pack_batch_offset(a, b);
+    const int q = threadIdx.x % 16, g = threadIdx.x / 16;
+    const bool row_in = r0 + 4 * q < a.rows;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const int lc = g + 16 * p;
+        const long long k = k0 + lc;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (row_in && k < a.K) v = __ldg(reinterpret_cast<const float4 *>(src + k * a.sk + r0 + 4 * q));
+        float *dst = &stage[4 * q][(((lc >> 2) ^ (q & 7)) << 2) | (lc & 3)];
+        dst[0] = v.x;
+        dst[64] = v.y;
+        dst[128] = v.z;
+        dst[192] = v.w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const int lr = g + 16 * p;
+        const long long r = r0 + lr;
+        if (r >= a.rows || k0 + 4 * q >= a.Kp) continue;
+        const float4 v = *reinterpret_cast<const float4 *>(&stage[lr][(q ^ ((lr >> 2) & 7)) << 2]);
+        float4 h, l;
+        split4(v, h, l);
+        const long long o = (b * a.rows + r) * a.Kp + k0 + 4 * q;
+        *reinterpret_cast<float4 *>(a.hi + o) = h;
+        *reinterpret_cast<float4 *>(a.lo + o) = l;
+    }
+}
+
 using PFN_EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                      const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                      CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -775,6 +864,18 @@ int pack(const float *src, int64_t off, int64_t sr, int64_t sk, int64_t rows, in
     a.hi = hi;
     a.lo = lo;
     a.k_contiguous = (sk == 1 || sr != 1) ? 1 : 0;
+    bool aligned = (reinterpret_cast<uintptr_t>(src + off) % 16) == 0;
+    for (int d = 0; d < p.batch_rank && aligned; ++d) aligned = bs[d] % 4 == 0;
+    if (aligned && sk == 1 && K % 4 == 0 && sr % 4 == 0 && p.batch * rows < (int64_t{1} << 31)) {
+        k_split_rows4<<<static_cast<unsigned>(p.batch * rows), 256, 0, stream>>>(a);
+        return check_launch("3xTF32 split pack (rows)");
+    }
+    if (aligned && sr == 1 && rows % 4 == 0 && sk % 4 == 0 && (rows + 63) / 64 <= 65535) {
+        const dim3 grid(static_cast<unsigned>((Kp + 63) / 64), static_cast<unsigned>((rows + 63) / 64),
+                        static_cast<unsigned>(p.batch));
+        k_split_tile4<<<grid, 256, 0, stream>>>(a);
+        return check_launch("3xTF32 split pack (transpose)");
+    }
     dim3 grid(static_cast<unsigned>((Kp + 31) / 32), static_cast<unsigned>((rows + 31) / 32),
               static_cast<unsigned>(p.batch));
     k_split_pack<<<grid, 256, 0, stream>>>(a);

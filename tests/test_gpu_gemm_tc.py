@@ -74,6 +74,18 @@ def test_batched_with_broadcast(cuda):
     _run(a, [3, 2, 130, 70], [2 * 130 * 70, 130 * 70, 70, 1], b, [2, 70, 260], [70 * 260, 260, 1])
 
 
+def test_batched_aligned_operands_take_the_vector_packs(cuda):
+    """K, M and N multiples of 4 and 16-byte aligned views: the float4 split packs
+    (K-contiguous rows, and the 64x64 swizzled transpose) with a K tail inside a
+    64-wide tile, partial row tiles and a batch axis, for both operand layouts."""
+    rng = np.random.default_rng(8)
+    bt, M, N, K = 3, 132, 200, 100
+    a = rng.standard_normal(bt * M * K).astype(F)
+    b = rng.standard_normal(bt * K * N).astype(F)
+    _run(a, [bt, M, K], [M * K, K, 1], b, [bt, K, N], [K * N, N, 1])         # rows pack for A, transpose for B
+    _run(a, [bt, M, K], [M * K, 1, M], b, [bt, K, N], [K * N, 1, K])         # transpose for A, rows pack for B
+
+
 def test_large_values_and_specials_stay_finite(cuda):
     rng = np.random.default_rng(5)
     M, N, K = 128, 256, 64
