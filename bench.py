@@ -252,6 +252,16 @@ def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
     Z = torch.empty(n, n, device="cuda")
     ms = _time_ms(abi.log_softmax(V(Y), 1, V(Z), prepare=True))
     out["log_softmax_axis1_GBps"] = gbs(8 * n * n, ms)
+    # the fused AdamW update of all 150.8 M parameters: p, g, m, v read; p', m', v' written
+    from minitensor_cpp_b200.kernel_cases import adamw_program
+
+    npar = sum(a * b + b for a, b in zip(WIDTHS[:-1], WIDTHS[1:]))
+    st = [torch.randn(npar, device="cuda", generator=g) for _ in range(3)] + [torch.rand(npar, device="cuda")]
+    res = [torch.empty(npar, device="cuda") for _ in range(3)]
+    prog_a, regs_a = adamw_program()
+    ms = _time_ms(abi.fused(prog_a, [V(t) for t in st], regs_a, [V(t) for t in res], prepare=True))
+    out["adamw_fused_update_GBps"] = gbs(28 * npar, ms)
+    del st, res
     hb = [v for k, v in out.items() if k.endswith("GBps")]
     out["elementwise_reduce_min_frac_of_hbm"] = min(hb) / hbm_gbs
     del A, Bs, Y, Z

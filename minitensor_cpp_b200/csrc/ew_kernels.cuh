@@ -122,9 +122,7 @@ __global__ void __launch_bounds__(256) mtc_ew_flat(const MtcEwArgs a) {
     const Op op;
     const long long nvec = a.numel / VEC;
     const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-    for (long long v = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += stride) {
-        float x[VEC][NIN > 0 ? NIN : 1];
-        float y[VEC][NOUT];
+    auto load = [&](long long v, float (&x)[VEC][NIN > 0 ? NIN : 1]) {
 #pragma unroll
         for (int k = 0; k < NIN; ++k) {
             if (a.in_str[k][0] == 0) {
@@ -142,6 +140,9 @@ __global__ void __launch_bounds__(256) mtc_ew_flat(const MtcEwArgs a) {
                 for (int l = 0; l < VEC; ++l) x[l][k] = __ldg(a.in[k] + a.in_off[k] + v * VEC + l);
             }
         }
+    };
+    auto compute_store = [&](long long v, float (&x)[VEC][NIN > 0 ? NIN : 1]) {
+        float y[VEC][NOUT];
 #pragma unroll
         for (int l = 0; l < VEC; ++l) op(x[l], y[l], a.imm);
 #pragma unroll
@@ -158,6 +159,16 @@ __global__ void __launch_bounds__(256) mtc_ew_flat(const MtcEwArgs a) {
                 for (int l = 0; l < VEC; ++l) a.out[j][a.out_off[j] + v * VEC + l] = y[l][j];
             }
         }
+    };
+    // two grid-stride units per iteration: both units' loads are in flight together
+    for (long long v = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; v < nvec; v += 2 * stride) {
+        float x0[VEC][NIN > 0 ? NIN : 1];
+        float x1[VEC][NIN > 0 ? NIN : 1];
+        const long long v1 = v + stride;
+        load(v, x0);
+        if (v1 < nvec) load(v1, x1);
+        compute_store(v, x0);
+        if (v1 < nvec) compute_store(v1, x1);
     }
     // scalar tail (numel not a multiple of VEC)
     const long long tail = nvec * VEC;

@@ -5,6 +5,7 @@
     python -m minitensor_cpp_b200.kernel_cases reduce --n 8192 --op sum --axis 0
     python -m minitensor_cpp_b200.kernel_cases log_softmax --n 8192
     python -m minitensor_cpp_b200.kernel_cases gather --rows 16777216 --cols 64
+    python -m minitensor_cpp_b200.kernel_cases adamw --numel 150823912
 
 Each case allocates its operands on cuda:0 with torch (device memory only),
 calls the C ABI `--reps` times back to back (prepared calls) on the current stream, synchronises, checks
@@ -110,8 +111,34 @@ def case_gather(a, torch, stream):
     return {"ms": ms, "gbs": (2.0 * a.rows * a.cols * 4 + a.rows * 8) / ms / 1e6}
 
 
+def adamw_program(lr=1e-3, b1=0.9, b2=0.999, eps=1e-8, c1=0.1, c2=0.001):
+    """AdamW's per-parameter update as one fused program: registers 0..3 are
+    p, g, m, v; outputs p', m', v' (the evaluator builds the same cluster)."""
+    C, M, A, D, S = abi.CONST, abi.MULTIPLY, abi.ADD, abi.DIVIDE, abi.SUBTRACT
+    prog = [(C, 4, 0, 0, b1), (M, 5, 4, 2, 0.0), (C, 6, 0, 0, 1 - b1), (M, 7, 6, 1, 0.0), (A, 8, 5, 7, 0.0),
+            (C, 9, 0, 0, b2), (M, 10, 9, 3, 0.0), (C, 11, 0, 0, 1 - b2), (M, 12, 11, 1, 0.0), (M, 13, 12, 1, 0.0),
+            (A, 14, 10, 13, 0.0), (C, 15, 0, 0, c1), (D, 16, 8, 15, 0.0), (C, 17, 0, 0, c2), (D, 18, 14, 17, 0.0),
+            (C, 21, 0, 0, lr), (M, 22, 21, 16, 0.0), (abi.SQRT, 23, 18, 0, 0.0), (C, 24, 0, 0, eps),
+            (A, 25, 23, 24, 0.0), (D, 26, 22, 25, 0.0), (S, 27, 0, 26, 0.0)]
+    return prog, [27, 8, 14]
+
+
+def case_adamw(a, torch, stream):
+    """The fused AdamW update over --numel parameters: 4 reads + 3 writes per element."""
+    n = a.numel
+    g = torch.Generator(device="cuda").manual_seed(a.seed)
+    p, gr, m = (torch.randn(n, device="cuda", generator=g) for _ in range(3))
+    v = torch.rand(n, device="cuda", generator=g)
+    outs = [torch.empty(n, device="cuda") for _ in range(3)]
+    prog, regs = adamw_program()
+    call = abi.fused(prog, [abi.View.of(t) for t in (p, gr, m, v)], regs, [abi.View.of(t) for t in outs], stream,
+                     prepare=True)
+    ms = _events_ms(call, a.reps, stream)
+    return {"ms": ms, "gbs": 28.0 * n / ms / 1e6}
+
+
 CASES = {"gemm": case_gemm, "chain": case_chain, "reduce": case_reduce, "log_softmax": case_log_softmax,
-         "gather": case_gather}
+         "gather": case_gather, "adamw": case_adamw}
 
 
 def main(argv=None) -> int:
@@ -128,6 +155,7 @@ def main(argv=None) -> int:
     p.add_argument("--rows", type=int, default=1 << 24)
     p.add_argument("--cols", type=int, default=64)
     p.add_argument("--reps", type=int, default=3)
+    p.add_argument("--numel", type=int, default=150823912, help="adamw: parameter count")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--warm-s", type=float, default=0.3, help="untimed calls before timing (0 under a profiler)")
     a = p.parse_args(argv)
