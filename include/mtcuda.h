@@ -281,6 +281,14 @@ int mtc_comm_init(int device, int rank, int n_ranks, const void *id, size_t id_b
 /* In-place sum all-reduce of `n` float32 buffers, then scale by `scale`, all on `stream`. */
 int mtc_comm_allreduce_f32(void *comm, void *const *buffers, const size_t *counts, int32_t n, float scale,
                            void *stream);
+/* The same reduction queued on the communicator's own stream behind the work
+ * already queued on `stream` (the gradients), so it overlaps later work on
+ * `stream`.  The buffers must not be touched by other streams until
+ * mtc_comm_wait.  No reference counterpart (the reference has no collective). */
+int mtc_comm_allreduce_f32_async(void *comm, void *const *buffers, const size_t *counts, int32_t n, float scale,
+                                 void *stream);
+/* Makes `stream` wait for every reduction queued by mtc_comm_allreduce_f32_async. */
+int mtc_comm_wait(void *comm, void *stream);
 int mtc_comm_destroy(void *comm);
 
 #ifdef __cplusplus

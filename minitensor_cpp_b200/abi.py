@@ -180,6 +180,8 @@ def _declare(L):
         "mtc_comm_unique_id": ([c_vp, c_sz], c_int),
         "mtc_comm_init": ([c_int, c_int, c_int, c_vp, c_sz, P(c_vp)], c_int),
         "mtc_comm_allreduce_f32": ([c_vp, P(c_vp), P(c_sz), c_i32, c_f, c_vp], c_int),
+        "mtc_comm_allreduce_f32_async": ([c_vp, P(c_vp), P(c_sz), c_i32, c_f, c_vp], c_int),
+        "mtc_comm_wait": ([c_vp, c_vp], c_int),
         "mtc_comm_destroy": ([c_vp], c_int),
     }
     for name, (args, res) in sig.items():
@@ -193,7 +195,7 @@ EXPORTED = (
     "mtc_free", "mtc_copy_from_host", "mtc_copy_to_host", "mtc_stream_synchronize", "mtc_pool_stats", "mtc_pool_trim",
     "mtc_check_device_errors", "mtc_unary", "mtc_binary", "mtc_fused", "mtc_copy", "mtc_concat", "mtc_index_scatter",
     "mtc_gather", "mtc_gather_scatter_add", "mtc_reduce", "mtc_log_softmax", "mtc_matmul", "mtc_fill", "mtc_uniform",
-    "mtc_normal", "mtc_launch_count", "mtc_profile_enable", "mtc_profile_gemm", "mtc_comm_unique_id", "mtc_comm_init", "mtc_comm_allreduce_f32", "mtc_comm_destroy",
+    "mtc_normal", "mtc_launch_count", "mtc_profile_enable", "mtc_profile_gemm", "mtc_comm_unique_id", "mtc_comm_init", "mtc_comm_allreduce_f32", "mtc_comm_allreduce_f32_async", "mtc_comm_wait", "mtc_comm_destroy",
 )
 
 

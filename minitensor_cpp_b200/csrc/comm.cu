@@ -57,6 +57,9 @@ struct Comm {
     int device = 0;
     int rank = 0;
     int n_ranks = 1;
+    cudaStream_t side = nullptr;  // the communicator's own stream (asynchronous reductions)
+    cudaEvent_t ready = nullptr;  // recorded on the caller's stream: the gradients are queued
+    cudaEvent_t done = nullptr;   // recorded on `side` after the latest reduction
 };
 
 __global__ void k_scale(float *p, long long n, float s) {
@@ -70,6 +73,32 @@ __global__ void k_scale(float *p, long long n, float s) {
         ncclResult_t r__ = (expr);                                                              \
         if (r__ != ncclSuccess) return fail(MTC_ERR_RUNTIME, "%s failed: %s", #expr, nccl().error_string(r__)); \
     } while (0)
+
+// Grouped in-place sum of the buffers over the ranks on stream `s`, then x scale.
+int allreduce_on(Comm *c, void *const *buffers, const size_t *counts, int32_t n, float scale, cudaStream_t s) {
+    MTC_NCCL_TRY(nccl().group_start());
+    for (int i = 0; i < n; ++i) {
+        if (counts[i] == 0) continue;
+        ncclResult_t r = nccl().all_reduce(buffers[i], buffers[i], counts[i], ncclFloat32, ncclSum, c->comm, s);
+        if (r != ncclSuccess) {
+            nccl().group_end();
+            return fail(MTC_ERR_RUNTIME, "ncclAllReduce failed: %s", nccl().error_string(r));
+        }
+    }
+    MTC_NCCL_TRY(nccl().group_end());
+    if (scale != 1.0f) {
+        const int sms = sm_count(c->device);
+        for (int i = 0; i < n; ++i) {
+            if (counts[i] == 0) continue;
+            long long blocks = (static_cast<long long>(counts[i]) + 255) / 256;
+            if (blocks > sms * 4) blocks = sms * 4;
+            k_scale<<<static_cast<unsigned>(blocks), 256, 0, s>>>(static_cast<float *>(buffers[i]),
+                                                                   static_cast<long long>(counts[i]), scale);
+        }
+        MTC_TRY(check_launch("gradient scale"));
+    }
+    return MTC_OK;
+}
 
 }  // namespace
 }  // namespace mtc
@@ -116,34 +145,48 @@ int mtc_comm_allreduce_f32(void *comm, void *const *buffers, const size_t *count
     if (c == nullptr || (n > 0 && (buffers == nullptr || counts == nullptr)))
         return fail(MTC_ERR_INVALID_ARGUMENT, "bad all-reduce arguments");
     MTC_TRY(need_nccl());
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    MTC_NCCL_TRY(nccl().group_start());
-    for (int i = 0; i < n; ++i) {
-        if (counts[i] == 0) continue;
-        ncclResult_t r = nccl().all_reduce(buffers[i], buffers[i], counts[i], ncclFloat32, ncclSum, c->comm, s);
-        if (r != ncclSuccess) {
-            nccl().group_end();
-            return fail(MTC_ERR_RUNTIME, "ncclAllReduce failed: %s", nccl().error_string(r));
-        }
+    return allreduce_on(c, buffers, counts, n, scale, static_cast<cudaStream_t>(stream));
+}
+
+int mtc_comm_allreduce_f32_async(void *comm, void *const *buffers, const size_t *counts, int32_t n, float scale,
+                                 void *stream) {
+    clear_error();
+    Comm *c = static_cast<Comm *>(comm);
+    if (c == nullptr || (n > 0 && (buffers == nullptr || counts == nullptr)))
+        return fail(MTC_ERR_INVALID_ARGUMENT, "bad all-reduce arguments");
+    MTC_TRY(need_nccl());
+    if (c->side == nullptr) {
+        MTC_CUDA_TRY(cudaSetDevice(c->device));
+        MTC_CUDA_TRY(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
+        MTC_CUDA_TRY(cudaEventCreateWithFlags(&c->ready, cudaEventDisableTiming));
+        MTC_CUDA_TRY(cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming));
     }
-    MTC_NCCL_TRY(nccl().group_end());
-    if (scale != 1.0f) {
-        const int sms = sm_count(c->device);
-        for (int i = 0; i < n; ++i) {
-            if (counts[i] == 0) continue;
-            long long blocks = (static_cast<long long>(counts[i]) + 255) / 256;
-            if (blocks > sms * 4) blocks = sms * 4;
-            k_scale<<<static_cast<unsigned>(blocks), 256, 0, s>>>(static_cast<float *>(buffers[i]),
-                                                                   static_cast<long long>(counts[i]), scale);
-        }
-        MTC_TRY(check_launch("gradient scale"));
-    }
+    MTC_CUDA_TRY(cudaEventRecord(c->ready, static_cast<cudaStream_t>(stream)));
+    MTC_CUDA_TRY(cudaStreamWaitEvent(c->side, c->ready, 0));
+    MTC_TRY(allreduce_on(c, buffers, counts, n, scale, c->side));
+    MTC_CUDA_TRY(cudaEventRecord(c->done, c->side));
     return MTC_OK;
 }
+
+int mtc_comm_wait(void *comm, void *stream) {
+    clear_error();
+    Comm *c = static_cast<Comm *>(comm);
+    if (c == nullptr) return fail(MTC_ERR_INVALID_ARGUMENT, "null communicator");
+    if (c->done == nullptr) return MTC_OK;  // nothing was queued asynchronously
+    MTC_CUDA_TRY(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), c->done, 0));
+    return MTC_OK;
+}
+
 
 int mtc_comm_destroy(void *comm) {
     Comm *c = static_cast<Comm *>(comm);
     if (c == nullptr) return MTC_OK;
+    if (c->side != nullptr) {
+        cudaStreamSynchronize(c->side);
+        cudaEventDestroy(c->ready);
+        cudaEventDestroy(c->done);
+        cudaStreamDestroy(c->side);
+    }
     if (c->comm && nccl().ok) nccl().comm_destroy(c->comm);
     delete c;
     return MTC_OK;

@@ -240,6 +240,7 @@ struct MlpTrainer {
     mt::nn::AdamW optimizer;
     mt::nn::AdamW::State state;
     std::vector<mt::nn::ParameterId> order;  // layer order: weight, bias, ...
+    std::vector<std::vector<mt::nn::ParameterId>> layers;  // the same ids grouped per layer
     void *comm = nullptr;
     int (*host_allreduce)(void *, std::size_t) = nullptr;
     int world = 1;
@@ -251,8 +252,13 @@ struct MlpTrainer {
           params{mt::nn::initialize(model, mt::RandomKey{seed}, mt::TensorOptions{mt::DType::Float32, dev})},
           optimizer{lr, 0.0F}, state{optimizer.initialize(params)} {
         for (const auto &layer : params.tree().layers()) {
+            layers.emplace_back();
             order.push_back(layer.weight());
-            if (layer.bias()) order.push_back(*layer.bias());
+            layers.back().push_back(layer.weight());
+            if (layer.bias()) {
+                order.push_back(*layer.bias());
+                layers.back().push_back(*layer.bias());
+            }
         }
     }
 
@@ -276,65 +282,89 @@ struct MlpTrainer {
         return value;
     }
 
-    // Data-parallel gradient exchange: the loss and all gradients are
-    // materialised in one evaluation, each gradient's dense storage region is
-    // summed over the ranks in place and scaled by 1/world.  On a CUDA device the
-    // sum is an NCCL all-reduce on the device stream; on the CPU device it is the
-    // host callback (used to run the same path with CPU process groups).
+    // Data-parallel gradient exchange.  Each gradient's dense storage region is
+    // summed over the ranks in place and scaled by 1/world, then the unchanged
+    // AdamW step runs.
+    //  - CUDA device: layers are evaluated last to first, one evaluation per
+    //    layer (the first also materialises the loss).  As soon as a layer's
+    //    gradients are queued, their NCCL all-reduce is queued on the
+    //    communicator's own stream behind them, so it runs while the next
+    //    layer's backward GEMMs run on the device stream; the device stream
+    //    waits for every reduction before the optimizer.
+    //  - CPU device: one evaluation, then the host callback per gradient (used to
+    //    run the same path with CPU process groups).
     void allreduce(mt::nn::ParameterGradients &grads, const mt::Tensor &loss) {
 #ifdef MTB_CPU_ONLY
         (void)grads;
         (void)loss;
         throw std::invalid_argument{"data parallelism needs the backend build"};
 #else
-        std::vector<mt::Tensor> roots{loss};
-        for (const auto &id : order) roots.push_back(grads.at(id));
-        std::vector<mt::Tensor> leaves = mt::leafify(roots);
-        std::vector<void *> buffers;
-        std::vector<std::size_t> counts;
-        for (std::size_t i = 0; i < order.size(); ++i) {
-            mt::Tensor g = leaves[i + 1];
-            {
-                // the region of a permuted dense layout is [lowest offset, + numel)
-                const auto &layout = mt::detail::TensorAccess::value(g)->materialization()->layout();
-                std::int64_t span = 1;
-                for (std::size_t d = 0; d < g.rank(); ++d) span += (g.shape()[d] - 1) * std::abs(layout.stride(d));
-                if (span != static_cast<std::int64_t>(g.numel())) g = mt::leafify(mt::contiguous(g));
-            }
-            const auto *m = mt::detail::TensorAccess::value(g)->materialization();
-            std::int64_t lo = m->layout().offset();
-            for (std::size_t d = 0; d < g.rank(); ++d)
-                if (m->layout().stride(d) < 0) lo += (g.shape()[d] - 1) * m->layout().stride(d);
-            std::byte *base = nullptr;
-            if (auto *cb = dynamic_cast<mt::detail::cuda::CudaBuffer *>(m->buffer_ref().get())) {
-                base = static_cast<std::byte *>(cb->data());
-            } else if (auto *hb = dynamic_cast<mt::detail::cpu::CpuBuffer *>(m->buffer_ref().get())) {
-                base = hb->data();
-            } else {
-                throw std::logic_error{"gradient storage of an unknown buffer type"};
-            }
-            buffers.push_back(reinterpret_cast<float *>(base) + lo);
-            counts.push_back(g.numel());
-            grads.at(order[i]) = g;
-        }
         if (device.type() == mt::DeviceType::Cuda) {
             if (comm == nullptr) throw std::logic_error{"no NCCL communicator attached"};
             auto &rt = dynamic_cast<mt::detail::cuda::CudaRuntime &>(mt::detail::environment().runtime_for(device));
-            mt::detail::cuda::check(mtc_comm_allreduce_f32(comm, buffers.data(), counts.data(),
-                                                           static_cast<int32_t>(buffers.size()), 1.0F / world,
-                                                           rt.stream()),
-                                    "gradient all-reduce");
-        } else {
-            if (host_allreduce == nullptr) throw std::logic_error{"no host all-reduce attached"};
-            const float scale = 1.0F / static_cast<float>(world);
-            for (std::size_t i = 0; i < buffers.size(); ++i) {
-                if (host_allreduce(buffers[i], counts[i]) != 0) throw std::runtime_error{"host all-reduce failed"};
-                float *p = static_cast<float *>(buffers[i]);
-                for (std::size_t j = 0; j < counts[i]; ++j) p[j] *= scale;
+            for (std::size_t l = layers.size(); l-- > 0;) {
+                std::vector<mt::Tensor> roots;
+                if (l + 1 == layers.size()) roots.push_back(loss);
+                for (const auto &id : layers[l]) roots.push_back(grads.at(id));
+                std::vector<mt::Tensor> leaves = mt::leafify(roots);
+                const std::size_t skip = l + 1 == layers.size() ? 1 : 0;
+                std::vector<void *> buffers;
+                std::vector<std::size_t> counts;
+                for (std::size_t i = 0; i < layers[l].size(); ++i) {
+                    mt::Tensor g = leaves[i + skip];
+                    buffers.push_back(dense_region(g));
+                    counts.push_back(g.numel());
+                    grads.at(layers[l][i]) = g;
+                }
+                mt::detail::cuda::check(mtc_comm_allreduce_f32_async(comm, buffers.data(), counts.data(),
+                                                                     static_cast<int32_t>(buffers.size()),
+                                                                     1.0F / world, rt.stream()),
+                                        "gradient all-reduce");
             }
+            mt::detail::cuda::check(mtc_comm_wait(comm, rt.stream()), "gradient all-reduce wait");
+            return;
+        }
+        std::vector<mt::Tensor> roots{loss};
+        for (const auto &id : order) roots.push_back(grads.at(id));
+        std::vector<mt::Tensor> leaves = mt::leafify(roots);
+        if (host_allreduce == nullptr) throw std::logic_error{"no host all-reduce attached"};
+        const float scale = 1.0F / static_cast<float>(world);
+        for (std::size_t i = 0; i < order.size(); ++i) {
+            mt::Tensor g = leaves[i + 1];
+            float *p = static_cast<float *>(dense_region(g));
+            grads.at(order[i]) = g;
+            if (host_allreduce(p, g.numel()) != 0) throw std::runtime_error{"host all-reduce failed"};
+            for (std::size_t j = 0; j < g.numel(); ++j) p[j] *= scale;
         }
 #endif
     }
+
+#ifndef MTB_CPU_ONLY
+    // Start of the dense storage region of a materialised gradient; a gradient
+    // whose layout does not cover exactly numel elements is made contiguous first
+    // (the region of a permuted dense layout is [lowest offset, + numel)).
+    static void *dense_region(mt::Tensor &g) {
+        {
+            const auto &layout = mt::detail::TensorAccess::value(g)->materialization()->layout();
+            std::int64_t span = 1;
+            for (std::size_t d = 0; d < g.rank(); ++d) span += (g.shape()[d] - 1) * std::abs(layout.stride(d));
+            if (span != static_cast<std::int64_t>(g.numel())) g = mt::leafify(mt::contiguous(g));
+        }
+        const auto *m = mt::detail::TensorAccess::value(g)->materialization();
+        std::int64_t lo = m->layout().offset();
+        for (std::size_t d = 0; d < g.rank(); ++d)
+            if (m->layout().stride(d) < 0) lo += (g.shape()[d] - 1) * m->layout().stride(d);
+        std::byte *base = nullptr;
+        if (auto *cb = dynamic_cast<mt::detail::cuda::CudaBuffer *>(m->buffer_ref().get())) {
+            base = static_cast<std::byte *>(cb->data());
+        } else if (auto *hb = dynamic_cast<mt::detail::cpu::CpuBuffer *>(m->buffer_ref().get())) {
+            base = hb->data();
+        } else {
+            throw std::logic_error{"gradient storage of an unknown buffer type"};
+        }
+        return reinterpret_cast<float *>(base) + lo;
+    }
+#endif
 };
 
 }  // namespace
