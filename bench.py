@@ -267,13 +267,18 @@ def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
     del A, Bs, Y, Z
     # -- GEMM sweep (3xTF32 tensor cores)
     peak3 = tf32_tflops / 3.0
-    for m in (2048, 4096, 8192):
+    for m in (1024, 2048, 4096, 16384, 8192):
         a = torch.randn(m, m, device="cuda")
         b = torch.randn(m, m, device="cuda")
         c = torch.empty(m, m, device="cuda")
         for tag, bv in (("", V(b)), ("_bT", V(b.t()))):
-            ms = _time_ms(abi.matmul(V(a), bv, V(c), prepare=True), reps=3)
+            ms = _time_ms(abi.matmul(V(a), bv, V(c), abi.GEMM_3XTF32, prepare=True), reps=3)
             out[f"gemm_{m}{tag}_TFLOPs"] = 2 * m ** 3 / (ms * 1e-3) / 1e12
+        if m == 4096:
+            # the SIMT kernels: exact (the CPU's k-ascending rounding) and FFMA
+            for tag, algo in (("exact", abi.GEMM_SIMT), ("ffma", abi.GEMM_SIMT_FFMA)):
+                ms = _time_ms(abi.matmul(V(a), V(b), V(c), algo, prepare=True), reps=3)
+                out[f"gemm_simt_{tag}_4096_TFLOPs"] = 2 * m ** 3 / (ms * 1e-3) / 1e12
     out["gemm_8192_frac_of_3xtf32"] = out["gemm_8192_TFLOPs"] / peak3
     # the same 8192^3 GEMM with the other kernel variants / shared-memory rings
     for variant in ("32x2", "pair16x6", "pair32x3"):
@@ -313,7 +318,51 @@ def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
         out[f"concat_axis{axis}_GBps"] = gbs(2 * 4 * 4096 * 8192 * 4, ms)
     del parts
     torch.cuda.empty_cache()
+    # -- spiral MLP (300 points, 2-64-64-3, Adam), full batch, through MiniTensor's API
+    from minitensor_cpp_b200.frontend import Frontend
+
+    fe = Frontend()
+    fe.spiral_train(0, 20, loss_every=0)  # warm-up: NVRTC programs and allocator blocks
+    n0 = abi.launch_count()
+    steps = 500
+    _, secs = fe.spiral_train(0, steps, loss_every=0)
+    out["spiral_train_samples_per_s"] = 300 * steps / secs
+    out["spiral_launches_per_step"] = (abi.launch_count() - n0) / steps
+    # -- the broadcast chain and its reductions end to end through the API: host
+    #    arrays in, Y and sum(axis 0), sum(axis 1), logsumexp(axis 1) back to the host
+    out["chain_api_e2e_s"] = _chain_api_seconds(fe, 0)
     return {k: round(v, 3) for k, v in out.items()}
+
+
+def _chain_inputs(n: int = 8192):
+    import numpy as np
+
+    rng = np.random.default_rng(SEED)
+    f = lambda *shape: rng.uniform(-1, 1, shape).astype(np.float32)
+    return f(n, n), f(n, n), f(1, n), f(n, 1)
+
+
+def _chain_api_seconds(fe, device: int) -> float:
+    """relu(A * B^T + row) * exp(-col) on 8192^2 and its sum/sum/logsumexp
+    reductions through the workload API, host arrays in and results out."""
+    a, b, row, col = _chain_inputs()
+    fe.chain(device, a[:64, :64], b[:64, :64], row[:, :64], col[:64], reductions=True)  # warm-up
+    t0 = time.perf_counter()
+    fe.chain(device, a, b, row, col, reductions=True)
+    return time.perf_counter() - t0
+
+
+def cpu_micro() -> dict:
+    """The other benchmark configurations on the reference CPU backend (oracle/_ref,
+    one core): the spiral MLP and the chain with its reductions."""
+    from minitensor_cpp_b200.frontend import Frontend
+    from oracle import refkernels
+
+    ref = Frontend(refkernels.LIB_PATH)
+    steps = 100
+    _, secs = ref.spiral_train(-1, steps, loss_every=0)
+    return {"spiral_train_samples_per_s": round(300 * steps / secs, 1),
+            "chain_api_e2e_s": round(_chain_api_seconds(ref, -1), 3), "cores": 1}
 
 
 # ----------------------------------------------------------------- our arm --
@@ -449,6 +498,8 @@ def run_ours(args) -> None:
         cpu = {"value": s["samples"] / s["seconds"], "unit": "samples/s", "cores": 1, "kind": "reference",
                "sample": f"1 training step at batch {args.cpu_batch} (same model, Adam) on the reference CPU "
                          f"backend, {s['seconds']:.1f} s"}
+        if not args.skip_micro:
+            cpu["micro"] = cpu_micro()
     line = {
         "metric": METRIC,
         "value": value,
