@@ -168,6 +168,18 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+// x = hi + lo with hi = x truncated to TF32 (low 13 mantissa bits cleared) and
+// lo = x - hi exact in float32; non-finite values keep hi = x, lo = 0.
+__device__ __forceinline__ void split_tf32(float x, float &hi, float &lo) {
+    if (!isfinite(x)) {
+        hi = x;
+        lo = 0.0f;
+        return;
+    }
+    hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+    lo = __fsub_rn(x, hi);
+}
+
 __device__ __forceinline__ void tile_coords(const TcArgs &a, int64_t t, int &tm, int &tn, int &tb) {
     const int64_t per_batch = static_cast<int64_t>(a.tiles_m) * a.tiles_n;
     tb = static_cast<int>(t / per_batch);
@@ -183,11 +195,17 @@ __device__ __forceinline__ void tile_coords(const TcArgs &a, int64_t t, int &tm,
     tn = static_cast<int>(in_group / gsize);
 }
 
-template <class P>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+// DIRECT bit 0 / bit 1: operand A / B is loaded raw (fp32, K-major) from its own
+// tensor into the "hi" slot, and four converter warps write lo = x - trunc(x)
+// into the "lo" slot in shared memory.  The tensor core reads a TF32 operand
+// from the upper 19 bits of each 32-bit word, so the raw value acts as hi.
+template <class P, int DIRECT>
+__global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
     k_gemm_3xtf32(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
                   const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
                   const TcArgs args) {
+    constexpr bool AD = (DIRECT & 1) != 0;
+    constexpr bool BD = (DIRECT & 2) != 0;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem =
         reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -202,8 +220,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint64_t *acc_full = bars + 2 * TC_STAGES;   // [2]
     uint64_t *acc_empty = acc_full + 2;          // [2]
     uint64_t *drain = acc_empty + 2;             // [1] completion of the MMA issuer's work
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t *conv = drain + 1;                  // [TC_STAGES] lo slots written (DIRECT)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(conv + TC_STAGES);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    // bytes the TMA delivers per stage: raw operands fill one slot, packed ones two
+    constexpr uint32_t kStageTx = (AD ? TC_A_BYTES : 2 * TC_A_BYTES) + (BD ? TC_B_BYTES : 2 * TC_B_BYTES);
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
@@ -213,6 +234,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (int s = 0; s < TC_STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
+            mbar_init(&conv[s], 128);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
@@ -248,12 +270,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         break;
                     }
                     unsigned char *st = smem + s * TC_STAGE_BYTES;
-                    mbar_expect_tx(&full[s], TC_STAGE_BYTES);
+                    mbar_expect_tx(&full[s], kStageTx);
                     const int kx = static_cast<int>(kb * TC_BK);
                     tma_load_3d(st, &tm_ahi, &full[s], kx, tm * TC_BM, tb);
-                    tma_load_3d(st + TC_A_BYTES, &tm_alo, &full[s], kx, tm * TC_BM, tb);
+                    if (!AD) tma_load_3d(st + TC_A_BYTES, &tm_alo, &full[s], kx, tm * TC_BM, tb);
                     tma_load_3d(st + 2 * TC_A_BYTES, &tm_bhi, &full[s], kx, tn * TC_BN, tb);
-                    tma_load_3d(st + 2 * TC_A_BYTES + TC_B_BYTES, &tm_blo, &full[s], kx, tn * TC_BN, tb);
+                    if (!BD) tma_load_3d(st + 2 * TC_A_BYTES + TC_B_BYTES, &tm_blo, &full[s], kx, tn * TC_BN, tb);
                 }
             }
             if (!ok) atomicCAS(args.err, 0ull, static_cast<unsigned long long>(kErrTimeout));
@@ -282,7 +304,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 for (int64_t kb = 0; kb < kblocks; ++kb, ++it) {
                     const int s = static_cast<int>(it % TC_STAGES);
                     const uint32_t round = static_cast<uint32_t>(it / TC_STAGES);
-                    if (!mbar_wait(&full[s], round & 1u, abort_flag)) {
+                    // with raw operands the converters' barrier completes after the TMA's
+                    if (!mbar_wait(DIRECT ? &conv[s] : &full[s], round & 1u, abort_flag)) {
                         ok = false;
                         break;
                     }
@@ -311,7 +334,44 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (long long i = 0; i < kWaitLimit && !mbar_try_wait(drain, 0u); ++i) {
             }
         }
-    } else {
+    } else if (DIRECT && warp >= 6) {
+        // converters: lo = x - trunc(x) of every raw operand tile, position for
+        // position (the swizzled layout of the hi slot is reused as is)
+        const int ct = threadIdx.x - TC_THREADS;  // 0..127
+        int64_t it = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
+            for (int64_t kb = 0; kb < kblocks; ++kb, ++it) {
+                const int s = static_cast<int>(it % TC_STAGES);
+                const uint32_t round = static_cast<uint32_t>(it / TC_STAGES);
+                if (!mbar_wait(&full[s], round & 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                unsigned char *st = smem + s * TC_STAGE_BYTES;
+                auto convert = [&](const unsigned char *raw, unsigned char *lo, int bytes) {
+                    const float4 *src = reinterpret_cast<const float4 *>(raw);
+                    float4 *dst = reinterpret_cast<float4 *>(lo);
+#pragma unroll 4
+                    for (int i = ct; i < bytes / 16; i += 128) {
+                        const float4 v = src[i];
+                        float4 h, l;
+                        split_tf32(v.x, h.x, l.x);
+                        split_tf32(v.y, h.y, l.y);
+                        split_tf32(v.z, h.z, l.z);
+                        split_tf32(v.w, h.w, l.w);
+                        dst[i] = l;
+                    }
+                };
+                if (AD) convert(st, st + TC_A_BYTES, TC_A_BYTES);
+                if (BD) convert(st + 2 * TC_A_BYTES, st + 2 * TC_A_BYTES + TC_B_BYTES, TC_B_BYTES);
+                // make the generic-proxy stores visible to the tensor core before arriving
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(&conv[s]);
+            }
+        }
+        if (!ok) atomicCAS(args.err, 0ull, static_cast<unsigned long long>(kErrTimeout));
+    } else if (warp >= 2 && warp < 6) {
         // epilogue: warps 2..5 cover TMEM lane quadrants (warp % 4)
         const int quadrant = warp % 4;
         const int row_in_tile = quadrant * 32 + lane;
@@ -676,16 +736,6 @@ struct PackArgs {
     int k_contiguous;
 };
 
-__device__ __forceinline__ void split_tf32(float x, float &hi, float &lo) {
-    if (!isfinite(x)) {
-        hi = x;
-        lo = 0.0f;
-        return;
-    }
-    hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
-    lo = __fsub_rn(x, hi);
-}
-
 __global__ void __launch_bounds__(256) k_split_pack(const PackArgs a) {
     __shared__ float tile[32][33];
     const int64_t r0 = static_cast<int64_t>(blockIdx.y) * 32;
@@ -828,21 +878,78 @@ PFN_EncodeTiled encode_fn() {
     return fn;
 }
 
+// One GEMM operand as its tensor maps see it: `rows` K-major rows of `kdim`
+// elements, `pitch` elements apart, batches `bstride` elements apart.  Packed
+// operands have split hi / lo arrays; a raw (direct) operand is the caller's own
+// tensor, whose lo the kernel computes in shared memory.
+struct TcOperand {
+    const float *hi = nullptr;
+    const float *lo = nullptr;
+    int64_t kdim = 0;
+    int64_t pitch = 0;
+    int64_t bstride = 0;
+    bool direct = false;
+};
+
+TcOperand packed_operand(const float *hi, const float *lo, int64_t Kp, int64_t rows) {
+    TcOperand o;
+    o.hi = hi;
+    o.lo = lo;
+    o.kdim = Kp;
+    o.pitch = Kp;
+    o.bstride = rows * Kp;
+    return o;
+}
+
+// A strided operand can be read raw when K is its contiguous axis and its rows and
+// batches start on 16-byte boundaries (TMA global-address and stride rules).
+bool direct_operand(const float *base, int64_t off, int64_t row_stride, int64_t k_stride, int64_t rows,
+                    const GemmProblem &p, const int64_t *bs, TcOperand &o) {
+    // rows at least K apart and batches at least a whole matrix apart (no overlap)
+    if (k_stride != 1 || row_stride < p.K || (row_stride * 4) % 16 != 0) return false;
+    if ((reinterpret_cast<uintptr_t>(base + off) % 16) != 0) return false;
+    int64_t bstride = rows * row_stride;
+    if (p.batch_rank > 1) return false;
+    if (p.batch_rank == 1) {
+        if (bs[0] < rows * row_stride || (bs[0] * 4) % 16 != 0) return false;
+        bstride = bs[0];
+    }
+    o.hi = base + off;
+    o.lo = nullptr;
+    o.kdim = p.K;
+    o.pitch = row_stride;
+    o.bstride = bstride;
+    o.direct = true;
+    return true;
+}
+
 template <class P>
-int make_map(CUtensorMap &map, float *base, int64_t Kp, int64_t rows, int64_t batch, uint32_t box_rows) {
+int make_map(CUtensorMap &map, const float *base, int64_t kdim, int64_t rows, int64_t batch, int64_t pitch,
+             int64_t bstride, uint32_t box_rows) {
     PFN_EncodeTiled enc = encode_fn();
     if (enc == nullptr) return fail(MTC_ERR_RUNTIME, "cuTensorMapEncodeTiled is unavailable");
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(Kp), static_cast<cuuint64_t>(rows),
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kdim), static_cast<cuuint64_t>(rows),
                                 static_cast<cuuint64_t>(batch)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(Kp) * 4, static_cast<cuuint64_t>(rows * Kp) * 4};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(pitch) * 4, static_cast<cuuint64_t>(bstride) * 4};
     const cuuint32_t box[3] = {static_cast<cuuint32_t>(P::BK), box_rows, 1};
     const cuuint32_t elem[3] = {1, 1, 1};
     const CUtensorMapSwizzle swz = P::BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-    const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, base, dims, strides, box, elem,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(base), dims, strides, box,
+                           elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MTC_ERR_RUNTIME, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
     return MTC_OK;
+}
+
+template <class P>
+int operand_maps(const TcOperand &o, int64_t rows, int64_t batch, uint32_t box_rows, CUtensorMap &hi,
+                 CUtensorMap &lo) {
+    MTC_TRY(make_map<P>(hi, o.hi, o.kdim, rows, batch, o.pitch, o.bstride, box_rows));
+    if (o.direct) {
+        lo = hi;  // never loaded: the kernel writes lo itself
+        return MTC_OK;
+    }
+    return make_map<P>(lo, o.lo, o.kdim, rows, batch, o.pitch, o.bstride, box_rows);
 }
 
 int pack(const float *src, int64_t off, int64_t sr, int64_t sk, int64_t rows, int64_t K, int64_t Kp,
@@ -884,13 +991,28 @@ int pack(const float *src, int64_t off, int64_t sr, int64_t sk, int64_t rows, in
 
 // Tensor maps over the packed operands and the persistent GEMM launch with
 // pipeline shape P (allocates nothing).
+template <class P, int DIRECT>
+int launch_tc_variant(const CUtensorMap &m_ahi, const CUtensorMap &m_alo, const CUtensorMap &m_bhi,
+                      const CUtensorMap &m_blo, const TcArgs &a, cudaStream_t stream) {
+    constexpr int threads = DIRECT ? TC_THREADS + 128 : TC_THREADS;
+    MTC_CUDA_TRY(cudaFuncSetAttribute(k_gemm_3xtf32<P, DIRECT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      P::SMEM_BYTES));
+    int dev = 0, sms = 0;
+    MTC_CUDA_TRY(cudaGetDevice(&dev));
+    MTC_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int64_t grid = a.total_tiles < sms ? a.total_tiles : sms;
+    k_gemm_3xtf32<P, DIRECT><<<static_cast<unsigned>(grid), threads, P::SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi,
+                                                                                             m_blo, a);
+    return check_launch("3xTF32 GEMM");
+}
+
+// Tensor maps over the two operands and the persistent GEMM launch with
+// pipeline shape P (allocates nothing).
 template <class P>
-int launch_tc(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float *bhi, float *blo, cudaStream_t stream) {
+int launch_tc(const GemmProblem &p, int64_t Kp, const TcOperand &A, const TcOperand &B, cudaStream_t stream) {
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
-    MTC_TRY(make_map<P>(m_ahi, ahi, Kp, p.M, p.batch, TC_BM));
-    MTC_TRY(make_map<P>(m_alo, alo, Kp, p.M, p.batch, TC_BM));
-    MTC_TRY(make_map<P>(m_bhi, bhi, Kp, p.N, p.batch, TC_BN));
-    MTC_TRY(make_map<P>(m_blo, blo, Kp, p.N, p.batch, TC_BN));
+    MTC_TRY(operand_maps<P>(A, p.M, p.batch, TC_BM, m_ahi, m_alo));
+    MTC_TRY(operand_maps<P>(B, p.N, p.batch, TC_BN, m_bhi, m_blo));
     TcArgs a;
     std::memset(&a, 0, sizeof(a));
     a.M = p.M;
@@ -913,14 +1035,12 @@ int launch_tc(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float *b
     for (int d = 0; d < p.batch_rank && vec; ++d) vec = (p.c_bs[d] % 4) == 0;
     a.vec_store = vec ? 1 : 0;
     a.err = device_error_word();
-    MTC_CUDA_TRY(cudaFuncSetAttribute(k_gemm_3xtf32<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, P::SMEM_BYTES));
-    int dev = 0, sms = 0;
-    MTC_CUDA_TRY(cudaGetDevice(&dev));
-    MTC_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const int64_t grid = a.total_tiles < sms ? a.total_tiles : sms;
-    k_gemm_3xtf32<P><<<static_cast<unsigned>(grid), TC_THREADS, P::SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo,
-                                                                                        a);
-    return check_launch("3xTF32 GEMM");
+    switch ((A.direct ? 1 : 0) | (B.direct ? 2 : 0)) {
+    case 0: return launch_tc_variant<P, 0>(m_ahi, m_alo, m_bhi, m_blo, a, stream);
+    case 1: return launch_tc_variant<P, 1>(m_ahi, m_alo, m_bhi, m_blo, a, stream);
+    case 2: return launch_tc_variant<P, 2>(m_ahi, m_alo, m_bhi, m_blo, a, stream);
+    default: return launch_tc_variant<P, 3>(m_ahi, m_alo, m_bhi, m_blo, a, stream);
+    }
 }
 
 // Clusters of the CTA-pair kernel that fit on the device at once (cached per device).
@@ -953,10 +1073,8 @@ template <class P>
 int launch_pair(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float *bhi, float *blo,
                 cudaStream_t stream) {
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
-    MTC_TRY(make_map<P>(m_ahi, ahi, Kp, p.M, p.batch, 128));
-    MTC_TRY(make_map<P>(m_alo, alo, Kp, p.M, p.batch, 128));
-    MTC_TRY(make_map<P>(m_bhi, bhi, Kp, p.N, p.batch, 128));
-    MTC_TRY(make_map<P>(m_blo, blo, Kp, p.N, p.batch, 128));
+    MTC_TRY(operand_maps<P>(packed_operand(ahi, alo, Kp, p.M), p.M, p.batch, 128, m_ahi, m_alo));
+    MTC_TRY(operand_maps<P>(packed_operand(bhi, blo, Kp, p.N), p.N, p.batch, 128, m_bhi, m_blo));
     TcArgs a;
     std::memset(&a, 0, sizeof(a));
     a.M = p.M;
@@ -989,16 +1107,65 @@ int launch_pair(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float 
 
 // MTC_TC_PIPELINE picks the kernel and ring: "16x4" (default) and "32x2" run
 // the single-CTA kernel with 4 x 48 KB or 2 x 96 KB stages, "pair16x6" and
-// "pair32x3" the CTA-pair kernel with 6 x 32 KB or 3 x 64 KB stages.
-int launch_tc_selected(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float *bhi, float *blo,
-                       cudaStream_t stream) {
+// "pair32x3" the CTA-pair kernel with 6 x 32 KB or 3 x 64 KB stages.  The
+// single-CTA kernel reads a K-contiguous A raw (no split pack for it);
+// MTC_TC_DIRECT selects the raw operands explicitly ("0", "a", "b", "ab").
+enum class TcKernel { Deep, Wide, PairDeep, PairWide };
+
+TcKernel selected_kernel() {
     const char *sel = std::getenv("MTC_TC_PIPELINE");
     if (sel != nullptr) {
-        if (std::strcmp(sel, "32x2") == 0) return launch_tc<PipeWide>(p, Kp, ahi, alo, bhi, blo, stream);
-        if (std::strcmp(sel, "pair16x6") == 0) return launch_pair<PairDeep>(p, Kp, ahi, alo, bhi, blo, stream);
-        if (std::strcmp(sel, "pair32x3") == 0) return launch_pair<PairWide>(p, Kp, ahi, alo, bhi, blo, stream);
+        if (std::strcmp(sel, "32x2") == 0) return TcKernel::Wide;
+        if (std::strcmp(sel, "pair16x6") == 0) return TcKernel::PairDeep;
+        if (std::strcmp(sel, "pair32x3") == 0) return TcKernel::PairWide;
     }
-    return launch_tc<PipeDeep>(p, Kp, ahi, alo, bhi, blo, stream);
+    return TcKernel::Deep;
+}
+
+// Which operands may be read raw: MTC_TC_DIRECT = "0" (none), "a", "b", "ab";
+// unset: the default policy of choose_direct.
+int direct_mask(TcKernel k) {
+    if (k == TcKernel::PairDeep || k == TcKernel::PairWide) return 0;
+    const char *d = std::getenv("MTC_TC_DIRECT");
+    if (d == nullptr) return -1;
+    return (std::strchr(d, 'a') ? 1 : 0) | (std::strchr(d, 'b') ? 2 : 0);
+}
+
+// Packs the operands that cannot be read raw into `ws` (2 * batch * rows * Kp
+// floats each), then launches the selected kernel.
+int run_tc(const GemmProblem &p, int64_t Kp, TcKernel k, bool a_direct, bool b_direct, const TcOperand &a_raw,
+           const TcOperand &b_raw, float *ws, cudaStream_t stream) {
+    const size_t a_elems = a_direct ? 0 : static_cast<size_t>(p.batch * p.M * Kp);
+    const size_t b_elems = b_direct ? 0 : static_cast<size_t>(p.batch * p.N * Kp);
+    float *ahi = ws, *alo = ws + a_elems, *bhi = alo + a_elems, *blo = bhi + b_elems;
+    {
+        HostSpan span("3xTF32 operand packs");
+        if (!a_direct) MTC_TRY(pack(p.A, p.a_off, p.a_rs, p.a_cs, p.M, p.K, Kp, p, p.a_bs, ahi, alo, stream));
+        // B[k][n] packed as B'[n][k]: rows advance along n (b_cs), k along b_rs
+        if (!b_direct) MTC_TRY(pack(p.B, p.b_off, p.b_cs, p.b_rs, p.N, p.K, Kp, p, p.b_bs, bhi, blo, stream));
+    }
+    HostSpan span("3xTF32 tensor maps and launch");
+    const TcOperand A = a_direct ? a_raw : packed_operand(ahi, alo, Kp, p.M);
+    const TcOperand B = b_direct ? b_raw : packed_operand(bhi, blo, Kp, p.N);
+    switch (k) {
+    case TcKernel::Wide: return launch_tc<PipeWide>(p, Kp, A, B, stream);
+    case TcKernel::PairDeep: return launch_pair<PairDeep>(p, Kp, ahi, alo, bhi, blo, stream);
+    case TcKernel::PairWide: return launch_pair<PairWide>(p, Kp, ahi, alo, bhi, blo, stream);
+    default: return launch_tc<PipeDeep>(p, Kp, A, B, stream);
+    }
+}
+
+// Decides which operands are read raw: A is K-contiguous when its column stride
+// is 1; B (packed as B'[n][k]) when its row stride is 1.
+void choose_direct(const GemmProblem &p, TcKernel k, bool &ad, bool &bd, TcOperand &a_raw, TcOperand &b_raw) {
+    ad = bd = false;
+    const int mask = direct_mask(k);
+    if (mask == 0) return;
+    // Default: A only.  Converting a raw 256-row B tile per stage costs the MMA
+    // issuer more than its split pack saves (measured on B200: a raw B made the
+    // 65536x8192x8192 GEMM 21 % slower, a raw A made it 1 % faster).
+    ad = (mask < 0 || (mask & 1)) && direct_operand(p.A, p.a_off, p.a_rs, p.a_cs, p.M, p, p.a_bs, a_raw);
+    bd = (mask > 0 && (mask & 2)) && direct_operand(p.B, p.b_off, p.b_cs, p.b_rs, p.N, p, p.b_bs, b_raw);
 }
 
 }  // namespace
@@ -1010,28 +1177,18 @@ int gemm_3xtf32(const GemmProblem &p, cudaStream_t stream) {
     const int64_t Kp = (p.K + 3) / 4 * 4;  // 16-byte row pitch for the tensor maps
     if (Kp >= (int64_t{1} << 31) || p.M >= (int64_t{1} << 31) || p.N >= (int64_t{1} << 31))
         return fail(MTC_ERR_UNSUPPORTED, "extent beyond the tensor-map range");
-    const size_t a_elems = static_cast<size_t>(p.batch * p.M * Kp);
-    const size_t b_elems = static_cast<size_t>(p.batch * p.N * Kp);
+    const TcKernel k = selected_kernel();
+    bool ad, bd;
+    TcOperand a_raw, b_raw;
+    choose_direct(p, k, ad, bd, a_raw, b_raw);
+    const size_t a_elems = ad ? 0 : static_cast<size_t>(p.batch * p.M * Kp);
+    const size_t b_elems = bd ? 0 : static_cast<size_t>(p.batch * p.N * Kp);
     void *scratch = nullptr;
-    {
+    if (a_elems + b_elems > 0) {
         HostSpan span("3xTF32 workspace allocation");
         MTC_TRY(scratch_alloc((2 * a_elems + 2 * b_elems) * sizeof(float) + 1024, stream, &scratch));
     }
-    float *ahi = static_cast<float *>(scratch);
-    float *alo = ahi + a_elems;
-    float *bhi = alo + a_elems;
-    float *blo = bhi + b_elems;
-    int rc;
-    {
-        HostSpan span("3xTF32 operand packs");
-        rc = pack(p.A, p.a_off, p.a_rs, p.a_cs, p.M, p.K, Kp, p, p.a_bs, ahi, alo, stream);
-        // B[k][n] packed as B'[n][k]: rows advance along n (b_cs), k along b_rs
-        if (rc == MTC_OK) rc = pack(p.B, p.b_off, p.b_cs, p.b_rs, p.N, p.K, Kp, p, p.b_bs, bhi, blo, stream);
-    }
-    {
-        HostSpan span("3xTF32 tensor maps and launch");
-        if (rc == MTC_OK) rc = launch_tc_selected(p, Kp, ahi, alo, bhi, blo, stream);
-    }
+    const int rc = run_tc(p, Kp, k, ad, bd, a_raw, b_raw, static_cast<float *>(scratch), stream);
     {
         HostSpan span("3xTF32 workspace release");
         scratch_free(scratch, stream);
@@ -1089,15 +1246,11 @@ int gemm_3xtf32_static(const GemmProblem &p, cudaStream_t stream) {
                     need, kStaticWorkspaceFloats);
     float *ws = nullptr;
     MTC_TRY(static_workspace(&ws));
-    const size_t a_elems = static_cast<size_t>(p.batch * p.M * Kp);
-    const size_t b_elems = static_cast<size_t>(p.batch * p.N * Kp);
-    float *ahi = ws;
-    float *alo = ahi + a_elems;
-    float *bhi = alo + a_elems;
-    float *blo = bhi + b_elems;
-    MTC_TRY(pack(p.A, p.a_off, p.a_rs, p.a_cs, p.M, p.K, Kp, p, p.a_bs, ahi, alo, stream));
-    MTC_TRY(pack(p.B, p.b_off, p.b_cs, p.b_rs, p.N, p.K, Kp, p, p.b_bs, bhi, blo, stream));
-    return launch_tc_selected(p, Kp, ahi, alo, bhi, blo, stream);
+    const TcKernel k = selected_kernel();
+    bool ad, bd;
+    TcOperand a_raw, b_raw;
+    choose_direct(p, k, ad, bd, a_raw, b_raw);
+    return run_tc(p, Kp, k, ad, bd, a_raw, b_raw, ws, stream);
 }
 
 }  // namespace mtc

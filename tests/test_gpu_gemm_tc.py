@@ -14,13 +14,19 @@ pytestmark = pytest.mark.gpu
 F = np.float32
 
 
-@pytest.fixture(autouse=True, params=["16x4", "32x2", "pair16x6", "pair32x3"])
+@pytest.fixture(autouse=True, params=["16x4", "16x4-0", "16x4-ab", "32x2", "pair16x6", "pair32x3"])
 def pipeline(request, monkeypatch):
     """Every kernel and ring: the single-CTA kernel with 4 stages of BK=16 (64-byte
-    swizzle) or 2 of BK=32 (128-byte swizzle), and the CTA-pair kernel with 6
-    stages of BK=16 or 3 of BK=32."""
-    monkeypatch.setenv("MTC_TC_PIPELINE", request.param)
-    return request.param
+    swizzle) or 2 of BK=32 (128-byte swizzle), reading a K-contiguous A raw (lo
+    computed in shared memory; the default), splitting every operand first
+    ("-0"), or reading both K-contiguous operands raw ("-ab"); and the CTA-pair
+    kernel with 6 stages of BK=16 or 3 of BK=32."""
+    name = request.param
+    pipe, _, direct = name.partition("-")
+    monkeypatch.setenv("MTC_TC_PIPELINE", pipe)
+    if direct:
+        monkeypatch.setenv("MTC_TC_DIRECT", direct)
+    return name
 
 
 def _run(a_st, a_shape, a_strides, b_st, b_shape, b_strides, out_offset=0, algo=abi.GEMM_3XTF32):
@@ -84,6 +90,29 @@ def test_batched_aligned_operands_take_the_vector_packs(cuda):
     b = rng.standard_normal(bt * K * N).astype(F)
     _run(a, [bt, M, K], [M * K, K, 1], b, [bt, K, N], [K * N, N, 1])         # rows pack for A, transpose for B
     _run(a, [bt, M, K], [M * K, 1, M], b, [bt, K, N], [K * N, 1, K])         # transpose for A, rows pack for B
+
+
+def test_padded_row_pitch_and_offset_views(cuda):
+    """K-contiguous operands whose rows are further apart than K (a column slice of
+    a wider matrix) and start at an element offset: still 16-byte aligned, so
+    they are read raw; an unaligned offset falls back to the split pack."""
+    rng = np.random.default_rng(9)
+    M, N, K, pad = 200, 260, 96, 12
+    a = rng.standard_normal(M * (K + pad) + 8).astype(F)
+    b = rng.standard_normal(N * (K + pad) + 8).astype(F)
+    for off in (0, 4, 1):
+        import torch
+
+        av = mo.view(a, [M, K], [K + pad, 1], off)
+        bv = mo.view(b, [K, N], [1, K + pad], off)
+        exp = mo.matmul(av, bv)
+        A = abi.View(torch.from_numpy(a).cuda(), (M, K), (K + pad, 1), off)
+        B = abi.View(torch.from_numpy(b).cuda(), (K, N), (1, K + pad), off)
+        C = abi.View(torch.empty(M * N, device="cuda"), (M, N), (N, 1), 0)
+        abi.matmul(A, B, C, abi.GEMM_3XTF32)
+        torch.cuda.synchronize()
+        assert_rel_sqrtk(C.tensor().cpu().numpy().reshape(-1), exp.reshape(-1), K,
+                         mo.matmul(np.abs(av), np.abs(bv)).reshape(-1), f"padded rows, offset {off}")
 
 
 def test_large_values_and_specials_stay_finite(cuda):
