@@ -152,6 +152,16 @@ int mtc_pool_trim(int device);
  * (and the offending index in *detail) if a gather/scatter kernel met an index
  * outside its axis since the last check, MTC_OK otherwise; the word is cleared. */
 int mtc_check_device_errors(int device, void *stream, int64_t *detail);
+/* Asynchronous form of the same check, for evaluators that must not
+ * synchronise: mtc_watch_device_errors queues a copy of the error word to
+ * pinned host memory on `stream` behind the work queued so far;
+ * mtc_poll_device_errors returns MTC_ERR_OUT_OF_RANGE (index in *detail) when
+ * the latest such copy, once it has arrived (wait = 0) or after waiting for it
+ * (wait = 1), shows an error, and clears the word.  No reference counterpart:
+ * the reference's CPU loop throws out_of_range inline (copy/loops.hpp:206-209);
+ * here the throw comes at the next evaluation or device-to-host read. */
+int mtc_watch_device_errors(int device, void *stream);
+int mtc_poll_device_errors(int device, int wait, int64_t *detail);
 
 /* --------------------------------------------------- elementwise (A4, A5) -- */
 

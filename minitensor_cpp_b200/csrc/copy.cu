@@ -3,6 +3,7 @@
 // Reference: src/tensor/backend/cpu/kernels/copy/loops.hpp:22-303 and
 // creation/loops.hpp:21-37.
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -541,6 +542,85 @@ int mtc_check_device_errors(int device, void *stream, int64_t *detail) {
     }
     if (prev != device) cudaSetDevice(prev);
     return rc;
+}
+
+// Asynchronous form: a snapshot of the error word is copied to pinned host
+// memory on `stream` behind the work queued so far, and an event marks its
+// arrival.  mtc_poll_device_errors reads the latest snapshot once its event has
+// completed (or waits for it), so a caller can check for index errors without
+// synchronising every evaluation.
+namespace {
+struct ErrorSnapshot {
+    unsigned long long *host = nullptr;  // pinned [2]
+    cudaEvent_t ready = nullptr;
+    bool pending = false;
+};
+std::mutex g_snap_mutex;
+ErrorSnapshot g_snaps[64];
+}  // namespace
+
+int mtc_watch_device_errors(int device, void *stream) {
+    clear_error();
+    if (device < 0 || device >= 64) return fail(MTC_ERR_INVALID_ARGUMENT, "device index %d out of range", device);
+    int prev = 0;
+    MTC_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != device) MTC_CUDA_TRY(cudaSetDevice(device));
+    std::lock_guard<std::mutex> lock(g_snap_mutex);
+    ErrorSnapshot &sn = g_snaps[device];
+    int rc = MTC_OK;
+    if (sn.host == nullptr) {
+        if (cudaHostAlloc(reinterpret_cast<void **>(&sn.host), 2 * sizeof(unsigned long long), cudaHostAllocDefault) !=
+                cudaSuccess ||
+            cudaEventCreateWithFlags(&sn.ready, cudaEventDisableTiming) != cudaSuccess) {
+            rc = fail(MTC_ERR_RUNTIME, "error-word snapshot set-up failed: %s", cudaGetErrorString(cudaGetLastError()));
+        }
+    }
+    if (rc == MTC_OK) {
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (cudaMemcpyFromSymbolAsync(sn.host, g_device_error, 2 * sizeof(unsigned long long), 0,
+                                      cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+            cudaEventRecord(sn.ready, s) != cudaSuccess) {
+            rc = fail(MTC_ERR_RUNTIME, "error-word snapshot failed: %s", cudaGetErrorString(cudaGetLastError()));
+        } else {
+            sn.pending = true;
+        }
+    }
+    if (prev != device) cudaSetDevice(prev);
+    return rc;
+}
+
+int mtc_poll_device_errors(int device, int wait, int64_t *detail) {
+    clear_error();
+    if (device < 0 || device >= 64) return fail(MTC_ERR_INVALID_ARGUMENT, "device index %d out of range", device);
+    unsigned long long word[2] = {0, 0};
+    {
+        std::lock_guard<std::mutex> lock(g_snap_mutex);
+        ErrorSnapshot &sn = g_snaps[device];
+        if (!sn.pending) return MTC_OK;
+        const cudaError_t q = wait ? cudaEventSynchronize(sn.ready) : cudaEventQuery(sn.ready);
+        if (q == cudaErrorNotReady) {
+            cudaGetLastError();
+            return MTC_OK;  // not known yet
+        }
+        if (q != cudaSuccess) return fail(MTC_ERR_RUNTIME, "error-word snapshot: %s", cudaGetErrorString(q));
+        word[0] = sn.host[0];
+        word[1] = sn.host[1];
+        sn.pending = false;
+    }
+    if (word[0] == 0) return MTC_OK;
+    // an error was recorded: clear the word (synchronously; this is the error path)
+    int prev = 0;
+    MTC_CUDA_TRY(cudaGetDevice(&prev));
+    if (prev != device) MTC_CUDA_TRY(cudaSetDevice(device));
+    MTC_CUDA_TRY(cudaDeviceSynchronize());
+    const unsigned long long zero[2] = {0, 0};
+    MTC_CUDA_TRY(cudaMemcpyToSymbol(g_device_error, zero, sizeof(zero)));
+    if (prev != device) cudaSetDevice(prev);
+    if (detail) *detail = static_cast<int64_t>(word[1]);
+    if (word[0] == MTC_ERR_OUT_OF_RANGE)
+        return fail(MTC_ERR_OUT_OF_RANGE, "an index kernel met index %lld outside its axis",
+                    static_cast<long long>(word[1]));
+    return fail(static_cast<int>(word[0]), "a device kernel gave up waiting (error %llu)", word[0]);
 }
 
 }  // extern "C"

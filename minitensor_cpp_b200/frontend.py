@@ -53,6 +53,7 @@ class Frontend:
             "mtb_mlp_materialize": ([vp], ctypes.c_int),
             "mtb_mlp_stream": ([vp], vp),
             "mtb_chain": ([ctypes.c_int, i64, i64, P(f32), P(f32), P(f32), P(f32), P(f32), P(f32)], ctypes.c_int),
+            "mtb_gather_rows": ([ctypes.c_int, i64, i64, P(f32), i64, P(i64), P(f32)], ctypes.c_int),
             "mtb_evaluator_stats": ([P(u64)], None),
             "mtb_evaluator_reset_stats": ([], None),
         }
@@ -94,6 +95,17 @@ class Frontend:
         if red is None:
             return out
         return out, red[:m], red[m:m + n], red[m + n:]
+
+    def gather_rows(self, device: int, table: np.ndarray, index: np.ndarray) -> np.ndarray:
+        """table[index, :] through MiniTensor's gather (IndexError for an index out of range)."""
+        t = np.ascontiguousarray(table, dtype=np.float32)
+        i = np.ascontiguousarray(index, dtype=np.int64)
+        out = np.empty((i.size, t.shape[1]), dtype=np.float32)
+        P = ctypes.POINTER
+        self._check(self.lib.mtb_gather_rows(device, t.shape[0], t.shape[1], t.ctypes.data_as(P(ctypes.c_float)),
+                                             i.size, i.ctypes.data_as(P(ctypes.c_int64)),
+                                             out.ctypes.data_as(P(ctypes.c_float))), "gather_rows")
+        return out
 
     def stats(self) -> dict:
         buf = (ctypes.c_uint64 * 9)()

@@ -100,4 +100,9 @@ struct EvaluatorStats {
 };
 EvaluatorStats &evaluator_stats();
 
+// Throws std::out_of_range when an index kernel on `device` recorded an index
+// outside its axis (a snapshot of the device error word queued after an
+// evaluation); wait = true waits for the latest snapshot first.
+void raise_device_errors(int device, bool wait);
+
 }  // namespace minitensor::detail::cuda

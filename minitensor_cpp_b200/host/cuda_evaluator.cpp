@@ -188,6 +188,12 @@ class FusedEvaluator {
         bool has_cuda = false;
         plan_ = planner.build(roots, has_cuda);
         if (!has_cuda) return false;
+        // an index error of an earlier evaluation whose snapshot has arrived
+        for (const Step &s : plan_) {
+            if (!s.on_cuda) continue;
+            raise_device_errors(static_cast<int>(s.output->spec().device.index()), false);
+            break;
+        }
         index_cache_ = planner.index();
         ++evaluator_stats().evaluations;
         const auto &index = index_cache_;
@@ -302,14 +308,14 @@ class FusedEvaluator {
             }
         }
         if (index_kernels && evaluator_options().check_index_errors && index_runtime != nullptr) {
+            // queue a snapshot of the device error word; it is examined at the next
+            // evaluation on this device or the next device-to-host read, so the
+            // host does not wait for the GPU here
             auto &rt = dynamic_cast<CudaRuntime &>(*index_runtime);
-            int64_t detail = 0;
             const auto c0 = std::chrono::steady_clock::now();
-            const int rc = mtc_check_device_errors(rt.index(), rt.stream(), &detail);
+            check(mtc_watch_device_errors(rt.index(), rt.stream()), "device error check");
             evaluator_stats().check_ns += static_cast<std::uint64_t>(
                 std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - c0).count());
-            if (rc == MTC_ERR_OUT_OF_RANGE) throw std::out_of_range{"gather index is out of range"};
-            check(rc, "device error check");
         }
     }
 

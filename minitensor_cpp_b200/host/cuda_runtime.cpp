@@ -89,6 +89,15 @@ void CudaRuntime::copy_to_host(std::span<std::byte> destination, const Buffer &s
                            static_cast<const std::byte *>(buffer->data()) + source_offset_bytes, destination.size(),
                            stream()),
           "device-to-host copy");
+    // the copy synchronised the stream: every queued error-word snapshot has arrived
+    raise_device_errors(static_cast<int>(index()), true);
+}
+
+void raise_device_errors(int device, bool wait) {
+    int64_t detail = 0;
+    const int rc = mtc_poll_device_errors(device, wait ? 1 : 0, &detail);
+    if (rc == MTC_ERR_OUT_OF_RANGE) throw std::out_of_range{"gather index is out of range"};
+    check(rc, "device error check");
 }
 
 }  // namespace minitensor::detail::cuda

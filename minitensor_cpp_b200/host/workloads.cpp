@@ -511,6 +511,20 @@ int mtb_chain(int device, int64_t n, int64_t m, const float *a, const float *b_s
     });
 }
 
+int mtb_gather_rows(int device, int64_t rows, int64_t cols, const float *table, int64_t n, const int64_t *index,
+                    float *out) {
+    return guarded([&] {
+        const mt::Device dev = device_of(device);
+        const mt::Tensor t = mt::from_data(std::span<const float>(table, static_cast<std::size_t>(rows * cols)),
+                                           mt::Shape{rows, cols}, dev);
+        const mt::Tensor i = mt::from_data(std::span<const std::int64_t>(index, static_cast<std::size_t>(n)),
+                                           mt::Shape{n, 1}, dev);
+        const mt::Tensor g = mt::gather(t, 0, mt::broadcast_to(i, mt::Shape{n, cols}));
+        const std::vector<float> v = mt::to_vector(g);
+        std::copy(v.begin(), v.end(), out);
+    });
+}
+
 void mtb_evaluator_stats(uint64_t *out9) {
 #ifndef MTB_CPU_ONLY
     const auto &s = mt::detail::cuda::evaluator_stats();

@@ -58,6 +58,12 @@ void *mtb_mlp_stream(void *handle);
 int mtb_chain(int device, int64_t n, int64_t m, const float *a, const float *b_storage, const float *row,
               const float *col, float *out, float *reductions);
 
+// Row gather through the public API: out[r, :] = table[index[r], :] for n rows
+// (gather along axis 0 with the index column broadcast over the row width).  An
+// index outside [0, rows) raises out_of_range (MTC_ERR_OUT_OF_RANGE).
+int mtb_gather_rows(int device, int64_t rows, int64_t cols, const float *table, int64_t n, const int64_t *index,
+                    float *out);
+
 // Counters of the fusing evaluator (zeros in the CPU-only build):
 // kernel_steps, fused_launches, fused_nodes, folded_constants, view_steps, evaluations,
 // and host nanoseconds spent planning, issuing kernels and in the index-error check.

@@ -54,3 +54,17 @@ def test_cuda_device_without_gpu_raises_runtime_error(fe):
         pytest.skip("a GPU is visible")
     with pytest.raises(RuntimeError, match="no runtime is registered"):
         fe.spiral_train(0, 1)
+
+
+def test_gather_rows_and_index_error_on_the_cpu_device():
+    """The row-gather workload on the CPU device of both libraries: same rows, and
+    an index outside the table raises IndexError (copy/loops.hpp:206-209)."""
+    from minitensor_cpp_b200.frontend import Frontend
+    from oracle import refkernels as rk
+
+    table = np.arange(60, dtype=np.float32).reshape(15, 4)
+    idx = np.array([14, 0, 7, 7], dtype=np.int64)
+    for fe in (Frontend(), Frontend(rk.LIB_PATH)):
+        np.testing.assert_array_equal(fe.gather_rows(-1, table, idx), table[idx])
+        with pytest.raises(IndexError):
+            fe.gather_rows(-1, table, np.array([15], dtype=np.int64))

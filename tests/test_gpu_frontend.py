@@ -96,3 +96,19 @@ def test_mlp_training_steps_match_reference(fe, ref):
     assert abs(lh - lc) <= 1e-4 * abs(lc), (lh, lc)
     g.close()
     c.close()
+
+
+def test_gather_index_error_through_the_api(fe, ref):
+    """An index outside the table raises IndexError through MiniTensor's API on the
+    GPU as on the reference CPU backend (on the GPU at the read that follows the
+    evaluation), and the next evaluation on the device is unaffected."""
+    rng = np.random.default_rng(31)
+    table = rng.standard_normal((1000, 64)).astype(F)
+    bad = np.array([3, 999, 1000, 7], dtype=np.int64)
+    good = rng.integers(0, 1000, 4096).astype(np.int64)
+    for lib in (ref, fe):
+        dev = -1 if lib is ref else 0
+        with pytest.raises(IndexError):
+            lib.gather_rows(dev, table, bad)
+        out = lib.gather_rows(dev, table, good)
+        np.testing.assert_array_equal(out, table[good])
