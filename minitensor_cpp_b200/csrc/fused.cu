@@ -75,6 +75,7 @@ struct CompiledProgram {
 
 std::mutex g_cache_mutex;
 std::unordered_map<std::string, std::unique_ptr<CompiledProgram>> g_cache;  // key: device + source
+std::unordered_map<std::string, CompiledProgram *> g_bin_cache;               // key: program structure bytes
 
 bool is_unary(int op) {
     return (op >= MTC_OP_ABS && op <= MTC_OP_SIGMOID) || op == MTC_OP_RELU;
@@ -133,7 +134,7 @@ int generate(const mtc_instr *program, int n_instr, int n_in, const int32_t *out
         snprintf(line, sizeof(line), "        y[%d] = r%d;\n", j, out_regs[j]);
         body += line;
     }
-    src = kTemplateSource;
+    src.clear();  // the program-specific part only: kTemplateSource precedes it when compiled
     snprintf(line, sizeof(line),
              "\nstruct MtcFused {\n    static constexpr int kIn = %d;\n    static constexpr int kOut = %d;\n", n_in,
              n_out);
@@ -183,8 +184,11 @@ void write_file(const std::string &path, const std::string &data) {
     else std::remove(tmp.c_str());
 }
 
-// Compiles one kernel variant of a program (NVRTC, sm_100a) or loads it from the disk cache.
-int compile(const std::string &src, int variant, CompiledProgram &out) {
+// Compiles one kernel variant of a program (NVRTC, sm_100a) or loads it from the
+// disk cache.  `program` is the generated MtcFused definition; the kernel
+// templates precede it in the compiled source.
+int compile(const std::string &program, int variant, CompiledProgram &out) {
+    const std::string src = std::string(kTemplateSource) + program;
     const std::string full = src + "\n// variant " + kNameExpr[variant] + "\n";
     const std::string dir = cache_dir();
     char name[32];
@@ -249,10 +253,8 @@ extern "C" int mtc_fused(const mtc_instr *program, int32_t n_instr, const mtc_de
     MTC_TRY(plan_elementwise(inputs, n_inputs, outputs, n_outputs, plan));
     if (plan.variant == EwVariant::Empty) return MTC_OK;
 
-    std::string src;
-    MTC_TRY(generate(program, n_instr, n_inputs, out_regs, n_outputs, src));
     int n_imm = 0;
-    for (int i = 0; i < n_instr; ++i)
+    for (int i = 0; i < n_instr && n_imm < MTC_EW_MAX_IMM; ++i)
         if (program[i].op == MTC_OP_CONST) plan.args.imm[n_imm++] = program[i].imm;
     const int device = current_device();
     int v = 0;
@@ -268,9 +270,33 @@ extern "C" int mtc_fused(const mtc_instr *program, int32_t n_instr, const mtc_de
     case EwVariant::Tiled4x2: v = 8; break;
     default: return MTC_OK;
     }
-    std::string key = std::to_string(device) + ":" + std::to_string(v) + "\n" + src.substr(std::strlen(kTemplateSource));
+    // First level: the program's structure as bytes (device, variant, operand
+    // counts, output registers, and op / registers of every instruction; the
+    // constants are launch arguments).  A hit skips source generation entirely.
+    std::string bin;
+    {
+        const int32_t head[4] = {device, v, n_inputs, n_outputs};
+        bin.append(reinterpret_cast<const char *>(head), sizeof(head));
+        bin.append(reinterpret_cast<const char *>(out_regs), sizeof(int32_t) * static_cast<size_t>(n_outputs));
+        for (int i = 0; i < n_instr; ++i) {
+            const int32_t w[2] = {program[i].op, (int32_t(uint16_t(program[i].dst)) << 16) | uint16_t(program[i].a)};
+            const int16_t b = program[i].b;
+            bin.append(reinterpret_cast<const char *>(w), sizeof(w));
+            bin.append(reinterpret_cast<const char *>(&b), sizeof(b));
+        }
+    }
     CompiledProgram *cp = nullptr;
     {
+        std::lock_guard<std::mutex> lock(g_cache_mutex);
+        auto hit = g_bin_cache.find(bin);
+        if (hit != g_bin_cache.end()) cp = hit->second;
+    }
+    if (cp == nullptr) {
+        // Second level: the generated source text (validates the program), then
+        // NVRTC or the disk cache on a miss.
+        std::string src;
+        MTC_TRY(generate(program, n_instr, n_inputs, out_regs, n_outputs, src));
+        std::string key = std::to_string(device) + ":" + std::to_string(v) + "\n" + src;
         std::lock_guard<std::mutex> lock(g_cache_mutex);
         auto it = g_cache.find(key);
         if (it == g_cache.end()) {
@@ -283,6 +309,7 @@ extern "C" int mtc_fused(const mtc_instr *program, int32_t n_instr, const mtc_de
             it = g_cache.emplace(key, std::move(fresh)).first;
         }
         cp = it->second.get();
+        g_bin_cache.emplace(std::move(bin), cp);
     }
     if (cp->fn == nullptr) return fail(MTC_ERR_LOGIC, "fused variant %d was not compiled", v);
     void *params[] = {&plan.args};
