@@ -74,7 +74,21 @@ struct TcArgs {
     int64_t c_bs[kMaxBatchRank];
     int vec_store;  // C rows contiguous and 16-byte aligned: float4 stores
     unsigned long long *err;
+    // split-K: work unit u = tile u / splits, K blocks [(u % splits) * kb_per_split, +kb_per_split);
+    // with splits > 1 each unit writes its partial tile to ws[split][batch][M][N]
+    int splits;
+    int64_t kb_per_split;
+    float *ws;
 };
+
+// Tile and K-block range of work unit u.
+__device__ __forceinline__ void unit_range(const TcArgs &a, int64_t u, int64_t kblocks, int64_t &t, int &split,
+                                           int64_t &kb0, int64_t &kb1) {
+    t = u / a.splits;
+    split = static_cast<int>(u - t * a.splits);
+    kb0 = static_cast<int64_t>(split) * a.kb_per_split;
+    kb1 = kb0 + a.kb_per_split < kblocks ? kb0 + a.kb_per_split : kblocks;
+}
 
 // ------------------------------------------------------------ PTX helpers --
 
@@ -259,10 +273,13 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
         if (lane == 0) {
             int64_t it = 0;
             bool ok = true;
-            for (int64_t t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
+            for (int64_t u = blockIdx.x; u < args.total_tiles * args.splits && ok; u += gridDim.x) {
+                int64_t t, kb0, kb1;
+                int split;
+                unit_range(args, u, kblocks, t, split, kb0, kb1);
                 int tm, tn, tb;
                 tile_coords(args, t, tm, tn, tb);
-                for (int64_t kb = 0; kb < kblocks; ++kb, ++it) {
+                for (int64_t kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = static_cast<int>(it % TC_STAGES);
                     const uint32_t round = static_cast<uint32_t>(it / TC_STAGES);
                     if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, abort_flag)) {
@@ -292,7 +309,10 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
             int64_t it = 0;
             int64_t local = 0;
             bool ok = true;
-            for (int64_t t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x, ++local) {
+            for (int64_t u = blockIdx.x; u < args.total_tiles * args.splits && ok; u += gridDim.x, ++local) {
+                int64_t t, kb0, kb1;
+                int split;
+                unit_range(args, u, kblocks, t, split, kb0, kb1);
                 const int b = static_cast<int>(local & 1);
                 const uint32_t use = static_cast<uint32_t>(local >> 1);
                 if (!mbar_wait(&acc_empty[b], (use & 1u) ^ 1u, abort_flag)) {
@@ -301,7 +321,7 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * TC_BN);
-                for (int64_t kb = 0; kb < kblocks; ++kb, ++it) {
+                for (int64_t kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = static_cast<int>(it % TC_STAGES);
                     const uint32_t round = static_cast<uint32_t>(it / TC_STAGES);
                     // with raw operands the converters' barrier completes after the TMA's
@@ -318,7 +338,7 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
 #pragma unroll
                     for (int kk = 0; kk < TC_BK / 8; ++kk) {
                         const uint64_t adv = static_cast<uint64_t>(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
-                        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+                        const uint32_t acc = (kb > kb0 || kk > 0) ? 1u : 0u;
                         umma_tf32(d_tmem, a_hi + adv, b_hi + adv, acc);
                         umma_tf32(d_tmem, a_hi + adv, b_lo + adv, 1u);
                         umma_tf32(d_tmem, a_lo + adv, b_hi + adv, 1u);
@@ -340,8 +360,11 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
         const int ct = threadIdx.x - TC_THREADS;  // 0..127
         int64_t it = 0;
         bool ok = true;
-        for (int64_t t = blockIdx.x; t < args.total_tiles && ok; t += gridDim.x) {
-            for (int64_t kb = 0; kb < kblocks; ++kb, ++it) {
+        for (int64_t u = blockIdx.x; u < args.total_tiles * args.splits && ok; u += gridDim.x) {
+            int64_t t, kb0, kb1;
+            int split;
+            unit_range(args, u, kblocks, t, split, kb0, kb1);
+            for (int64_t kb = kb0; kb < kb1; ++kb, ++it) {
                 const int s = static_cast<int>(it % TC_STAGES);
                 const uint32_t round = static_cast<uint32_t>(it / TC_STAGES);
                 if (!mbar_wait(&full[s], round & 1u, abort_flag)) {
@@ -376,7 +399,10 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
         const int quadrant = warp % 4;
         const int row_in_tile = quadrant * 32 + lane;
         int64_t local = 0;
-        for (int64_t t = blockIdx.x; t < args.total_tiles; t += gridDim.x, ++local) {
+        for (int64_t u = blockIdx.x; u < args.total_tiles * args.splits; u += gridDim.x, ++local) {
+            int64_t t, kb0, kb1;
+            int split;
+            unit_range(args, u, kblocks, t, split, kb0, kb1);
             const int b = static_cast<int>(local & 1);
             const uint32_t use = static_cast<uint32_t>(local >> 1);
             if (!mbar_wait(&acc_full[b], use & 1u, abort_flag)) {
@@ -386,8 +412,17 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
             tc_fence_after();
             int tm, tn, tb;
             tile_coords(args, t, tm, tn, tb);
-            int64_t co = args.c_off;
-            {
+            // destination: C, or with split-K this split's partial tile in ws
+            float *out = args.C;
+            int64_t co = args.c_off, c_rs = args.c_rs, c_cs = args.c_cs;
+            bool vec = args.vec_store != 0;
+            if (args.splits > 1) {
+                out = args.ws;
+                co = (static_cast<int64_t>(split) * args.batch + tb) * args.M * args.N;
+                c_rs = args.N;
+                c_cs = 1;
+                vec = (args.N % 4) == 0;
+            } else {
                 int64_t rem = tb;
                 for (int d = args.batch_rank - 1; d >= 0; --d) {
                     const int64_t c = rem % args.batch_shape[d];
@@ -405,15 +440,15 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
                 tmem_ld32(taddr_row + static_cast<uint32_t>(c * 32), v);
                 if (m < args.M) {
                     const int64_t nb = n0 + c * 32;
-                    float *dst = args.C + co + m * args.c_rs;
-                    if (args.vec_store && nb + 32 <= args.N) {
+                    float *dst = out + co + m * c_rs;
+                    if (vec && nb + 32 <= args.N) {
                         float4 *d4 = reinterpret_cast<float4 *>(dst + nb);
 #pragma unroll
                         for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
                     } else {
 #pragma unroll
                         for (int j = 0; j < 32; ++j)
-                            if (nb + j < args.N) dst[(nb + j) * args.c_cs] = v[j];
+                            if (nb + j < args.N) dst[(nb + j) * c_cs] = v[j];
                     }
                 }
             }
@@ -427,6 +462,29 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TC_TMEM_COLS));
+    }
+}
+
+// Split-K reduction: C = ws[0] + ws[1] + ... in split order (deterministic),
+// written through C's strides; one thread per output element.
+__global__ void __launch_bounds__(256) k_splitk_reduce(const TcArgs a) {
+    const int64_t total = a.batch * a.M * a.N;
+    const int64_t plane = a.batch * a.M * a.N;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float acc = a.ws[i];
+        for (int s = 1; s < a.splits; ++s) acc = __fadd_rn(acc, a.ws[s * plane + i]);
+        const int64_t n = i % a.N;
+        const int64_t rest = i / a.N;
+        const int64_t m = rest % a.M;
+        int64_t rem = rest / a.M;
+        int64_t co = a.c_off;
+        for (int d = a.batch_rank - 1; d >= 0; --d) {
+            const int64_t c = rem % a.batch_shape[d];
+            rem /= a.batch_shape[d];
+            co += c * a.c_bs[d];
+        }
+        a.C[co + m * a.c_rs + n * a.c_cs] = acc;
     }
 }
 
@@ -1000,7 +1058,8 @@ int launch_tc_variant(const CUtensorMap &m_ahi, const CUtensorMap &m_alo, const 
     int dev = 0, sms = 0;
     MTC_CUDA_TRY(cudaGetDevice(&dev));
     MTC_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    const int64_t grid = a.total_tiles < sms ? a.total_tiles : sms;
+    const int64_t units = a.total_tiles * a.splits;
+    const int64_t grid = units < sms ? units : sms;
     k_gemm_3xtf32<P, DIRECT><<<static_cast<unsigned>(grid), threads, P::SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi,
                                                                                              m_blo, a);
     return check_launch("3xTF32 GEMM");
@@ -1009,7 +1068,8 @@ int launch_tc_variant(const CUtensorMap &m_ahi, const CUtensorMap &m_alo, const 
 // Tensor maps over the two operands and the persistent GEMM launch with
 // pipeline shape P (allocates nothing).
 template <class P>
-int launch_tc(const GemmProblem &p, int64_t Kp, const TcOperand &A, const TcOperand &B, cudaStream_t stream) {
+int launch_tc(const GemmProblem &p, int64_t Kp, const TcOperand &A, const TcOperand &B, cudaStream_t stream,
+              int splits = 1, float *split_ws = nullptr) {
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
     MTC_TRY(operand_maps<P>(A, p.M, p.batch, TC_BM, m_ahi, m_alo));
     MTC_TRY(operand_maps<P>(B, p.N, p.batch, TC_BN, m_bhi, m_blo));
@@ -1035,12 +1095,27 @@ int launch_tc(const GemmProblem &p, int64_t Kp, const TcOperand &A, const TcOper
     for (int d = 0; d < p.batch_rank && vec; ++d) vec = (p.c_bs[d] % 4) == 0;
     a.vec_store = vec ? 1 : 0;
     a.err = device_error_word();
-    switch ((A.direct ? 1 : 0) | (B.direct ? 2 : 0)) {
-    case 0: return launch_tc_variant<P, 0>(m_ahi, m_alo, m_bhi, m_blo, a, stream);
-    case 1: return launch_tc_variant<P, 1>(m_ahi, m_alo, m_bhi, m_blo, a, stream);
-    case 2: return launch_tc_variant<P, 2>(m_ahi, m_alo, m_bhi, m_blo, a, stream);
-    default: return launch_tc_variant<P, 3>(m_ahi, m_alo, m_bhi, m_blo, a, stream);
+    const int64_t kblocks = (Kp + P::BK - 1) / P::BK;
+    a.splits = 1;
+    a.kb_per_split = kblocks;
+    if (splits > 1 && split_ws != nullptr) {
+        a.kb_per_split = (kblocks + splits - 1) / splits;
+        a.splits = static_cast<int>((kblocks + a.kb_per_split - 1) / a.kb_per_split);
+        a.ws = split_ws;
     }
+    int rc;
+    switch ((A.direct ? 1 : 0) | (B.direct ? 2 : 0)) {
+    case 0: rc = launch_tc_variant<P, 0>(m_ahi, m_alo, m_bhi, m_blo, a, stream); break;
+    case 1: rc = launch_tc_variant<P, 1>(m_ahi, m_alo, m_bhi, m_blo, a, stream); break;
+    case 2: rc = launch_tc_variant<P, 2>(m_ahi, m_alo, m_bhi, m_blo, a, stream); break;
+    default: rc = launch_tc_variant<P, 3>(m_ahi, m_alo, m_bhi, m_blo, a, stream); break;
+    }
+    if (rc != MTC_OK || a.splits == 1) return rc;
+    const int64_t total = a.batch * a.M * a.N;
+    int64_t blocks = (total + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    k_splitk_reduce<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a);
+    return check_launch("3xTF32 split-K reduction");
 }
 
 // Clusters of the CTA-pair kernel that fit on the device at once (cached per device).
@@ -1134,7 +1209,7 @@ int direct_mask(TcKernel k) {
 // Packs the operands that cannot be read raw into `ws` (2 * batch * rows * Kp
 // floats each), then launches the selected kernel.
 int run_tc(const GemmProblem &p, int64_t Kp, TcKernel k, bool a_direct, bool b_direct, const TcOperand &a_raw,
-           const TcOperand &b_raw, float *ws, cudaStream_t stream) {
+           const TcOperand &b_raw, float *ws, cudaStream_t stream, int splits = 1, float *split_ws = nullptr) {
     const size_t a_elems = a_direct ? 0 : static_cast<size_t>(p.batch * p.M * Kp);
     const size_t b_elems = b_direct ? 0 : static_cast<size_t>(p.batch * p.N * Kp);
     float *ahi = ws, *alo = ws + a_elems, *bhi = alo + a_elems, *blo = bhi + b_elems;
@@ -1148,10 +1223,10 @@ int run_tc(const GemmProblem &p, int64_t Kp, TcKernel k, bool a_direct, bool b_d
     const TcOperand A = a_direct ? a_raw : packed_operand(ahi, alo, Kp, p.M);
     const TcOperand B = b_direct ? b_raw : packed_operand(bhi, blo, Kp, p.N);
     switch (k) {
-    case TcKernel::Wide: return launch_tc<PipeWide>(p, Kp, A, B, stream);
+    case TcKernel::Wide: return launch_tc<PipeWide>(p, Kp, A, B, stream, splits, split_ws);
     case TcKernel::PairDeep: return launch_pair<PairDeep>(p, Kp, ahi, alo, bhi, blo, stream);
     case TcKernel::PairWide: return launch_pair<PairWide>(p, Kp, ahi, alo, bhi, blo, stream);
-    default: return launch_tc<PipeDeep>(p, Kp, A, B, stream);
+    default: return launch_tc<PipeDeep>(p, Kp, A, B, stream, splits, split_ws);
     }
 }
 
@@ -1183,12 +1258,31 @@ int gemm_3xtf32(const GemmProblem &p, cudaStream_t stream) {
     choose_direct(p, k, ad, bd, a_raw, b_raw);
     const size_t a_elems = ad ? 0 : static_cast<size_t>(p.batch * p.M * Kp);
     const size_t b_elems = bd ? 0 : static_cast<size_t>(p.batch * p.N * Kp);
-    void *scratch = nullptr;
-    if (a_elems + b_elems > 0) {
-        HostSpan span("3xTF32 workspace allocation");
-        MTC_TRY(scratch_alloc((2 * a_elems + 2 * b_elems) * sizeof(float) + 1024, stream, &scratch));
+    // split-K when the output tiles fill less than half of the GPU and K is long:
+    // each split of at least 8 K blocks writes a partial tile, summed in order
+    int splits = 1;
+    if (k == TcKernel::Deep || k == TcKernel::Wide) {
+        int dev = 0, sms = 0;
+        MTC_CUDA_TRY(cudaGetDevice(&dev));
+        MTC_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        const int64_t tiles = ((p.M + TC_BM - 1) / TC_BM) * ((p.N + TC_BN - 1) / TC_BN) * p.batch;
+        const int64_t kblocks = (Kp + (k == TcKernel::Deep ? PipeDeep::BK : PipeWide::BK) - 1) /
+                                (k == TcKernel::Deep ? PipeDeep::BK : PipeWide::BK);
+        if (2 * tiles <= sms && kblocks >= 16) {
+            int64_t sp = sms / tiles;
+            if (sp > kblocks / 8) sp = kblocks / 8;
+            if (sp > 8) sp = 8;
+            splits = sp > 1 ? static_cast<int>(sp) : 1;
+        }
     }
-    const int rc = run_tc(p, Kp, k, ad, bd, a_raw, b_raw, static_cast<float *>(scratch), stream);
+    const size_t split_elems = splits > 1 ? static_cast<size_t>(splits) * p.batch * p.M * p.N : 0;
+    void *scratch = nullptr;
+    if (a_elems + b_elems + split_elems > 0) {
+        HostSpan span("3xTF32 workspace allocation");
+        MTC_TRY(scratch_alloc((2 * a_elems + 2 * b_elems + split_elems) * sizeof(float) + 1024, stream, &scratch));
+    }
+    float *split_ws = splits > 1 ? static_cast<float *>(scratch) + 2 * a_elems + 2 * b_elems : nullptr;
+    const int rc = run_tc(p, Kp, k, ad, bd, a_raw, b_raw, static_cast<float *>(scratch), stream, splits, split_ws);
     {
         HostSpan span("3xTF32 workspace release");
         scratch_free(scratch, stream);

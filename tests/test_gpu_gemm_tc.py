@@ -115,6 +115,17 @@ def test_padded_row_pitch_and_offset_views(cuda):
                          mo.matmul(np.abs(av), np.abs(bv)).reshape(-1), f"padded rows, offset {off}")
 
 
+def test_split_k_when_tiles_do_not_fill_the_gpu(cuda):
+    """Few output tiles and a long K: the single-CTA kernel splits K (partial tiles
+    summed in split order), batched, with ragged edges and an output offset."""
+    rng = np.random.default_rng(13)
+    bt, M, N, K = 2, 200, 300, 1000
+    a = rng.standard_normal(bt * M * K).astype(F)
+    b = rng.standard_normal(bt * K * N).astype(F)
+    _run(a, [bt, M, K], [M * K, K, 1], b, [bt, K, N], [K * N, N, 1], out_offset=5)
+    _run(a[: M * K], [M, K], [K, 1], b[: K * N], [K, N], [1, K])  # one tile column, transposed B
+
+
 def test_large_values_and_specials_stay_finite(cuda):
     rng = np.random.default_rng(5)
     M, N, K = 128, 256, 64
