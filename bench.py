@@ -354,15 +354,44 @@ def _chain_api_seconds(fe, device: int) -> float:
 
 def cpu_micro() -> dict:
     """The other benchmark configurations on the reference CPU backend (oracle/_ref,
-    one core): the spiral MLP and the chain with its reductions."""
+    one core): the spiral MLP, the chain with its reductions, a 1024^3 GEMM, a
+    2^20-row sample of the row gather, and the axis-0 concat."""
     from minitensor_cpp_b200.frontend import Frontend
     from oracle import refkernels
+
+    import numpy as np
 
     ref = Frontend(refkernels.LIB_PATH)
     steps = 100
     _, secs = ref.spiral_train(-1, steps, loss_every=0)
-    return {"spiral_train_samples_per_s": round(300 * steps / secs, 1),
-            "chain_api_e2e_s": round(_chain_api_seconds(ref, -1), 3), "cores": 1}
+    out = {"spiral_train_samples_per_s": round(300 * steps / secs, 1),
+           "chain_api_e2e_s": round(_chain_api_seconds(ref, -1), 3), "cores": 1}
+    hv = refkernels.HostView
+    rng = np.random.default_rng(SEED)
+    # GEMM 1024^3 (contiguous operands) on the reference's CPU kernel
+    n = 1024
+    a = hv.of(rng.standard_normal((n, n)).astype(np.float32))
+    b = hv.of(rng.standard_normal((n, n)).astype(np.float32))
+    c = hv.of(np.zeros((n, n), np.float32))
+    t0 = time.perf_counter()
+    refkernels.matmul(a, b, c)
+    out["gemm_1024_GFLOPs"] = round(2 * n ** 3 / (time.perf_counter() - t0) / 1e9, 2)
+    # row gather of 2^20 rows of 64 floats (a sample of the 2^24-row benchmark)
+    rows, width = 1 << 20, 64
+    table = hv.of(rng.standard_normal((rows, width)).astype(np.float32))
+    idx = rng.integers(0, rows, rows).astype(np.int64)
+    idx_b = hv(idx, (rows, width), (1, 0), 0)
+    res = hv.of(np.zeros((rows, width), np.float32))
+    t0 = time.perf_counter()
+    refkernels.gather(table, idx_b, 0, res)
+    out["gather_rows_GBps"] = round(rows * 520 / (time.perf_counter() - t0) / 1e9, 3)
+    # concat of four [4096, 8192] tensors along axis 0
+    parts = [hv.of(rng.standard_normal((4096, 8192)).astype(np.float32)) for _ in range(4)]
+    dst = hv.of(np.zeros((16384, 8192), np.float32))
+    t0 = time.perf_counter()
+    refkernels.concat(parts, 0, dst)
+    out["concat_axis0_GBps"] = round(2 * 4 * 4096 * 8192 * 4 / (time.perf_counter() - t0) / 1e9, 3)
+    return out
 
 
 # ----------------------------------------------------------------- our arm --
