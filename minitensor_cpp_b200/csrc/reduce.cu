@@ -370,52 +370,72 @@ __global__ void __launch_bounds__(256) k_per_output(const RedArgs a) {
 // with four float4 loads in flight per thread, then merge in warp order through
 // shared memory (a fixed order: results are deterministic).
 constexpr int kColWarps = 8;
+#ifndef MTC_COL_ROWS_IN_FLIGHT
+#define MTC_COL_ROWS_IN_FLIGHT 8
+#endif
+constexpr int kColRows = MTC_COL_ROWS_IN_FLIGHT;  // rows (vector loads) in flight per thread
+#ifndef MTC_COL_ARGMAX_VEC
+#define MTC_COL_ARGMAX_VEC 2
+#endif
 
-template <int OP>
+template <int OP, int VEC>
 __global__ void __launch_bounds__(256) k_col_tile(const RedArgs a, long long ncols, long long batch_stride,
                                                   unsigned int *arrivals) {
-    __shared__ State part[kColWarps][128];
+    constexpr int CW = 32 * VEC;  // outputs per CTA
+    __shared__ State part[kColWarps][CW];
     const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
-    const long long col = static_cast<long long>(blockIdx.x) * 128 + lane * 4;
+    const long long col = static_cast<long long>(blockIdx.x) * CW + lane * VEC;
     const long long per = (a.R + a.chunks - 1) / a.chunks;
     const long long r0 = static_cast<long long>(blockIdx.y) * per;
     const long long r1 = r0 + per < a.R ? r0 + per : a.R;
-    State s[4];
+    State s[VEC];
     const long long first = r0 + warp;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) s[j] = first < r1 ? seeded_init<OP>(first) : Reducer<OP>::init();
+    for (int j = 0; j < VEC; ++j) s[j] = first < r1 ? seeded_init<OP>(first) : Reducer<OP>::init();
+    auto load = [&](const float *p, float (&q)[VEC]) {
+        if constexpr (VEC == 4) {
+            const float4 t = __ldg(reinterpret_cast<const float4 *>(p));
+            q[0] = t.x;
+            q[1] = t.y;
+            q[2] = t.z;
+            q[3] = t.w;
+        } else if constexpr (VEC == 2) {
+            const float2 t = __ldg(reinterpret_cast<const float2 *>(p));
+            q[0] = t.x;
+            q[1] = t.y;
+        } else {
+            q[0] = __ldg(p);
+        }
+    };
     if (col < ncols) {
         const long long rs = a.rstr[0];
         const float *base = a.in + a.in_off + static_cast<long long>(blockIdx.z) * batch_stride + col;
         long long r = first;
-        // eight rows (eight 128-bit loads) in flight per thread
-        for (; r + 7 * kColWarps < r1; r += 8 * kColWarps) {
-            float4 q[8];
+        // kColRows rows (vector loads) in flight per thread
+        for (; r + (kColRows - 1) * kColWarps < r1; r += kColRows * kColWarps) {
+            float q[kColRows][VEC];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) q[u] = __ldg(reinterpret_cast<const float4 *>(base + (r + u * kColWarps) * rs));
+            for (int u = 0; u < kColRows; ++u) load(base + (r + u * kColWarps) * rs, q[u]);
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < kColRows; ++u) {
                 const long long e = r + u * kColWarps;
-                add_in_order<OP>(s[0], q[u].x, e);
-                add_in_order<OP>(s[1], q[u].y, e);
-                add_in_order<OP>(s[2], q[u].z, e);
-                add_in_order<OP>(s[3], q[u].w, e);
+#pragma unroll
+                for (int j = 0; j < VEC; ++j) add_in_order<OP>(s[j], q[u][j], e);
             }
         }
         for (; r < r1; r += kColWarps) {
-            const float4 q = __ldg(reinterpret_cast<const float4 *>(base + r * rs));
-            add_in_order<OP>(s[0], q.x, r);
-            add_in_order<OP>(s[1], q.y, r);
-            add_in_order<OP>(s[2], q.z, r);
-            add_in_order<OP>(s[3], q.w, r);
+            float q[VEC];
+            load(base + r * rs, q);
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) add_in_order<OP>(s[j], q[j], r);
         }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) part[warp][lane * 4 + j] = s[j];
+    for (int j = 0; j < VEC; ++j) part[warp][lane * VEC + j] = s[j];
     __syncthreads();
-    const long long c = static_cast<long long>(blockIdx.x) * 128 + threadIdx.x;
+    const long long c = static_cast<long long>(blockIdx.x) * CW + threadIdx.x;
     const long long o = static_cast<long long>(blockIdx.z) * ncols + c;
-    if (threadIdx.x < 128) {
+    if (threadIdx.x < CW) {
         State t = part[0][threadIdx.x];
 #pragma unroll
         for (int w = 1; w < kColWarps; ++w) Reducer<OP>::merge(t, part[w][threadIdx.x]);
@@ -435,7 +455,7 @@ __global__ void __launch_bounds__(256) k_col_tile(const RedArgs a, long long nco
     __syncthreads();
     if (!last) return;
     __threadfence();
-    if (threadIdx.x < 128 && c < ncols) {
+    if (threadIdx.x < CW && c < ncols) {
         // one coalesced row of partials per chunk; four chunks' loads in flight
         auto load = [&](int k) {
             const State *q = a.partial + static_cast<long long>(k) * a.nout + o;
@@ -782,8 +802,10 @@ int run_reduction(RedPlan &p, cudaStream_t stream) {
         const long long bstride = a.krank == 2 ? a.kstr[0] : 0;
         const bool v4 = ncols % 4 == 0 && a.rstr[0] % 4 == 0 && bstride % 4 == 0 &&
                         (reinterpret_cast<uintptr_t>(a.in + a.in_off) % 16) == 0;
-        if (v4 && nbatch <= 65535 && ((ncols + 127) / 128) * nbatch <= kColGroups) {
-            const long long gx = (ncols + 127) / 128;
+        // argmax: 2 outputs per lane (fewer registers per thread, twice the CTAs)
+        constexpr int vec = OP == MTC_OP_ARGMAX ? MTC_COL_ARGMAX_VEC : 4;
+        if (v4 && nbatch <= 65535 && ((ncols + 32 * vec - 1) / (32 * vec)) * nbatch <= kColGroups) {
+            const long long gx = (ncols + 32 * vec - 1) / (32 * vec);
             const long long want = static_cast<long long>(sms) * 8;  // 8 CTAs of 256 threads per SM
             long long chunks = (want + gx * nbatch - 1) / (gx * nbatch);
             const long long max_chunks = (a.R + 63) / 64;  // at least 64 rows per chunk
@@ -799,7 +821,7 @@ int run_reduction(RedPlan &p, cudaStream_t stream) {
             unsigned int *arrivals = nullptr;
             if (chunks > 1) MTC_TRY(col_arrivals(stream, &arrivals));
             const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(chunks), static_cast<unsigned>(nbatch));
-            k_col_tile<OP><<<grid, 256, 0, stream>>>(a, ncols, bstride, arrivals);
+            k_col_tile<OP, vec><<<grid, 256, 0, stream>>>(a, ncols, bstride, arrivals);
             const int rc = check_launch("column reduction");
             scratch_free(scratch, stream);
             return rc;
