@@ -146,8 +146,55 @@ __global__ void __launch_bounds__(256, 2) k_gemm_simt(const SimtArgs args) {
 
 }  // namespace
 
+// Small problems in the CPU's exact order: one thread per output element, the
+// k loop ascending with __fmul_rn then __fadd_rn as the reference's loop, and
+// sixteen (A, B) pairs loaded ahead of the dependent adds.  Latency, not
+// bandwidth, bounds these sizes, so spreading outputs over threads wins.
+__global__ void __launch_bounds__(128) k_gemm_small_exact(const GemmProblem p) {
+    const long long total = p.batch * p.M * p.N;
+    for (long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; t < total;
+         t += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long n = t % p.N;
+        const long long rest = t / p.N;
+        const long long m = rest % p.M;
+        long long rem = rest / p.M;
+        long long ao = p.a_off, bo = p.b_off, co = p.c_off;
+        for (int d = p.batch_rank - 1; d >= 0; --d) {
+            const long long c = rem % p.batch_shape[d];
+            rem /= p.batch_shape[d];
+            ao += c * p.a_bs[d];
+            bo += c * p.b_bs[d];
+            co += c * p.c_bs[d];
+        }
+        const float *a = p.A + ao + m * p.a_rs;
+        const float *b = p.B + bo + n * p.b_cs;
+        float acc = 0.0f;
+        long long k = 0;
+        for (; k + 16 <= p.K; k += 16) {
+            float x[16], y[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                x[u] = __ldg(a + (k + u) * p.a_cs);
+                y[u] = __ldg(b + (k + u) * p.b_rs);
+            }
+#pragma unroll
+            for (int u = 0; u < 16; ++u) acc = __fadd_rn(acc, __fmul_rn(x[u], y[u]));
+        }
+        for (; k < p.K; ++k) acc = __fadd_rn(acc, __fmul_rn(__ldg(a + k * p.a_cs), __ldg(b + k * p.b_rs)));
+        p.C[co + m * p.c_rs + n * p.c_cs] = acc;
+    }
+}
+
 int gemm_simt(const GemmProblem &p, cudaStream_t stream, bool exact) {
     if (p.M == 0 || p.N == 0 || p.batch == 0) return MTC_OK;
+    const double work = double(p.batch) * double(p.M) * double(p.N) * double(p.K);
+    if (exact && work <= double(1 << 22)) {
+        const long long total = p.batch * p.M * p.N;
+        long long blocks = (total + 127) / 128;
+        if (blocks > 148 * 16) blocks = 148 * 16;
+        k_gemm_small_exact<<<static_cast<unsigned>(blocks), 128, 0, stream>>>(p);
+        return check_launch("small exact GEMM");
+    }
     SimtArgs args;
     args.p = p;
     args.a_kmajor = (p.a_cs == 1 || p.a_rs != 1) ? 1 : 0;

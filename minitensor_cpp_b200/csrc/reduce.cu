@@ -509,6 +509,21 @@ int col_arrivals(cudaStream_t stream, unsigned int **out) {
 // axes row-major, ReductionPlan, iteration/reduction.cpp:14-121).
 template <class F>
 __device__ __forceinline__ void walk_reduced(const RedArgs &a, long long base, F &&f) {
+    if (a.rrank == 1) {
+        // one reduced axis: sixteen loads in flight, consumed strictly in order
+        const long long st = a.rstr[0];
+        const float *p = a.in + base;
+        long long r = 0;
+        for (; r + 16 <= a.R; r += 16, p += 16 * st) {
+            float v[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[u] = __ldg(p + u * st);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) f(v[u], r + u);
+        }
+        for (; r < a.R; ++r, p += st) f(__ldg(p), r);
+        return;
+    }
     unsigned int coord[MTC_MAX_RANK];
     for (int d = 0; d < a.rrank; ++d) coord[d] = 0;
     long long off = base;
