@@ -162,6 +162,13 @@ int mtc_check_device_errors(int device, void *stream, int64_t *detail);
  * here the throw comes at the next evaluation or device-to-host read. */
 int mtc_watch_device_errors(int device, void *stream);
 int mtc_poll_device_errors(int device, int wait, int64_t *detail);
+/* Failure-path self-test: a one-thread kernel waits on a shared-memory barrier
+ * that nothing completes, gives up after `spins` polls (1 .. 2^24) exactly like
+ * the GEMM's bounded waits, and records MTC_ERR_RUNTIME in the device error
+ * word; mtc_check_device_errors then reports it and clears the word.  Tests the
+ * give-up path of a bounded wait without a fault or a hang.  No reference
+ * counterpart. */
+int mtc_selftest_bounded_wait(int64_t spins, void *stream);
 
 /* --------------------------------------------------- elementwise (A4, A5) -- */
 

@@ -161,6 +161,7 @@ def _declare(L):
         "mtc_check_device_errors": ([c_int, c_vp, P(c_i64)], c_int),
         "mtc_watch_device_errors": ([c_int, c_vp], c_int),
         "mtc_poll_device_errors": ([c_int, c_int, P(ctypes.c_int64)], c_int),
+        "mtc_selftest_bounded_wait": ([c_i64, c_vp], c_int),
         "mtc_unary": ([c_i32, P(Desc), P(Desc), c_vp], c_int),
         "mtc_binary": ([c_i32, P(Desc), P(Desc), P(Desc), c_vp], c_int),
         "mtc_fused": ([P(Instr), c_i32, P(Desc), c_i32, P(c_i32), P(Desc), c_i32, c_vp], c_int),
@@ -195,7 +196,7 @@ def _declare(L):
 EXPORTED = (
     "mtc_last_error", "mtc_version", "mtc_device_count", "mtc_device_sm_count", "mtc_set_device", "mtc_device_stream", "mtc_alloc",
     "mtc_free", "mtc_copy_from_host", "mtc_copy_to_host", "mtc_stream_synchronize", "mtc_pool_stats", "mtc_pool_trim",
-    "mtc_check_device_errors", "mtc_watch_device_errors", "mtc_poll_device_errors", "mtc_unary", "mtc_binary", "mtc_fused", "mtc_copy", "mtc_concat", "mtc_index_scatter",
+    "mtc_check_device_errors", "mtc_watch_device_errors", "mtc_poll_device_errors", "mtc_selftest_bounded_wait", "mtc_unary", "mtc_binary", "mtc_fused", "mtc_copy", "mtc_concat", "mtc_index_scatter",
     "mtc_gather", "mtc_gather_scatter_add", "mtc_reduce", "mtc_log_softmax", "mtc_matmul", "mtc_fill", "mtc_uniform",
     "mtc_normal", "mtc_launch_count", "mtc_profile_enable", "mtc_profile_gemm", "mtc_comm_unique_id", "mtc_comm_init", "mtc_comm_allreduce_f32", "mtc_comm_allreduce_f32_async", "mtc_comm_wait", "mtc_comm_destroy",
 )

@@ -777,6 +777,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     }
 }
 
+// Failure-path self-test: one thread waits on an mbarrier that nothing ever
+// arrives at, with the same bounded try-wait loop as the GEMM's roles, then
+// records the timeout in the device error word and returns.  It exercises the
+// give-up path of a bounded wait without faulting or hanging the GPU.
+__global__ void k_wait_selftest(long long spins, unsigned long long *err) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    bool done = false;
+    for (long long i = 0; i < spins && !done; ++i) done = mbar_try_wait(&bar, 0u);
+    if (!done) atomicCAS(err, 0ull, static_cast<unsigned long long>(kErrTimeout));
+    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(&bar)) : "memory");
+}
+
 // ------------------------------------------------------------- split pack --
 // dst_hi/dst_lo: [batch][rows][Kp] row-major.  Source element (batch, r, k) at
 // off + batch offsets + r*sr + k*sk.  A 32x32 tile goes through shared memory so
@@ -1348,3 +1363,11 @@ int gemm_3xtf32_static(const GemmProblem &p, cudaStream_t stream) {
 }
 
 }  // namespace mtc
+
+extern "C" int mtc_selftest_bounded_wait(int64_t spins, void *stream) {
+    mtc::clear_error();
+    if (spins < 1 || spins > (int64_t{1} << 24))
+        return mtc::fail(MTC_ERR_INVALID_ARGUMENT, "spin limit %lld outside [1, 2^24]", static_cast<long long>(spins));
+    mtc::k_wait_selftest<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(spins, mtc::device_error_word());
+    return mtc::check_launch("bounded-wait self-test");
+}

@@ -98,3 +98,59 @@ def test_two_rank_gloo_training_matches_single_process(tmp_path):
     assert diff.max() <= STEPS * 2 * LR + 1e-6
     assert np.mean(diff > 1e-5) < 0.02, float(np.mean(diff > 1e-5))
     single.close()
+
+
+def _rank_fails_main(rank, world, port, out_path):
+    """Rank 1 leaves before the gradient exchange; rank 0 must see the exchange
+    fail (an exception from its step, within the process-group timeout) rather
+    than hang."""
+    import sys
+    from datetime import timedelta
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import torch
+    import torch.distributed as dist
+
+    from minitensor_cpp_b200.frontend import Frontend, MlpTrainer
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    if rank == 1:
+        os._exit(3)  # the failure: this rank is gone before any collective
+    fe = Frontend()
+    tr = MlpTrainer(fe, -1, WIDTHS[0], WIDTHS[1], 1, WIDTHS[-1], seed=5, lr=LR)
+
+    def sum_in_place(arr):
+        t = torch.from_numpy(arr)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+
+    tr.set_host_allreduce(sum_in_place, world)
+    x, y = _data()
+    tr.load_batch(x.ctypes.data, y.ctypes.data, BATCH // world)
+    try:
+        tr.step_resident(read_loss=True)
+        outcome = "completed"
+    except RuntimeError as e:
+        outcome = f"failed: {e}"
+    with open(out_path, "w") as f:
+        f.write(outcome)
+    os._exit(0)
+
+
+def test_a_rank_that_leaves_makes_the_exchange_fail_not_hang(tmp_path):
+    import torch.multiprocessing as mp
+
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    out = tmp_path / "rank0.txt"
+    procs = [ctx.Process(target=_rank_fails_main, args=(r, 2, port, str(out))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode is not None for p in procs), "a rank hung"
+    assert procs[1].exitcode == 3
+    assert procs[0].exitcode == 0
+    text = out.read_text()
+    assert text.startswith("failed:") and "all-reduce" in text, text
