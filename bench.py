@@ -322,12 +322,23 @@ def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
     from minitensor_cpp_b200.frontend import Frontend
 
     fe = Frontend()
-    fe.spiral_train(0, 20, loss_every=0)  # warm-up: NVRTC programs and allocator blocks
-    n0 = abi.launch_count()
     steps = 500
+    # eager: every step re-planned and its kernels launched one by one
+    graphs = fe.set_graphs(False)
+    fe.spiral_train(0, 20, loss_every=0)  # warm-up: NVRTC programs and allocator blocks
     _, secs = fe.spiral_train(0, steps, loss_every=0)
+    out["spiral_eager_samples_per_s"] = 300 * steps / secs
+    # default: the repeated step plan is recorded once and replayed as a CUDA graph
+    fe.set_graphs(True)
+    fe.spiral_train(0, 20, loss_every=0)
+    n0 = abi.launch_count()
+    fe.reset_stats()
+    _, secs = fe.spiral_train(0, steps, loss_every=0)
+    st = fe.stats()
+    fe.set_graphs(graphs)
     out["spiral_train_samples_per_s"] = 300 * steps / secs
     out["spiral_launches_per_step"] = (abi.launch_count() - n0) / steps
+    out["spiral_replayed_steps_frac"] = st["graph_replays"] / max(st["evaluations"], 1)
     # -- the broadcast chain and its reductions end to end through the API: host
     #    arrays in, Y and sum(axis 0), sum(axis 1), logsumexp(axis 1) back to the host
     out["chain_api_e2e_s"] = _chain_api_seconds(fe, 0)

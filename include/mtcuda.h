@@ -122,9 +122,9 @@ int mtc_set_device(int device);
 
 /* ------------------------------------------------------ DeviceRuntime (A2) --
  * Replaces CpuRuntime/CpuBuffer (src/tensor/backend/cpu/cpu_runtime.cpp:31-87,
- * cpu_buffer.cpp:13-32).  Memory comes from a per-device stream-ordered pool
- * (cudaMallocAsync with an unbounded release threshold), so freed blocks are
- * reused by later work on the same stream without a device synchronisation. */
+ * cpu_buffer.cpp:13-32).  Memory comes from a per-device caching allocator whose
+ * blocks are reused in stream order, so freed blocks serve later work on the
+ * same stream without a device synchronisation. */
 
 /* Per-device work stream created on first use (non-blocking w.r.t. the legacy stream). */
 int mtc_device_stream(int device, void **stream);
@@ -145,7 +145,8 @@ int mtc_copy_to_host(int device, void *dst, const void *src, size_t bytes, void 
 int mtc_stream_synchronize(void *stream);
 /* Bytes held from the driver by / handed out from the caching allocator. */
 int mtc_pool_stats(int device, uint64_t *reserved_bytes, uint64_t *used_bytes);
-/* Return cached-but-unused blocks to the driver (synchronises the device). */
+/* Return cached-but-unused blocks to the driver (synchronises the device).
+ * Blocks protected for recorded graphs (mtc_pool_protect) stay. */
 int mtc_pool_trim(int device);
 
 /* Device-side error word: synchronises `stream`, then returns MTC_ERR_OUT_OF_RANGE
@@ -275,6 +276,46 @@ int mtc_fill(const mtc_desc *out, const void *value, void *stream);
  * uses double Box-Muller like the CPU and matches it to float32 rounding. */
 int mtc_uniform(const mtc_desc *out, float low, float high, uint64_t key0, uint64_t key1, void *stream);
 int mtc_normal(const mtc_desc *out, float mean, float std_dev, uint64_t key0, uint64_t key1, void *stream);
+
+/* ------------------------------------------------------ graph replay (plan cache) --
+ * The evaluator of a repeated plan (a training step) records the plan's launches
+ * once with stream capture and replays them as one CUDA graph.  The reference
+ * re-plans and re-dispatches every node on every evaluation
+ * (src/tensor/execution/evaluator.cpp:196-206); the README lists reusable
+ * compiled graphs as future work (README.md:35). */
+
+typedef struct mtc_graph mtc_graph;
+
+/* Starts recording the calling thread's launches on `stream` (relaxed stream
+ * capture: nothing runs until mtc_graph_launch).  While recording, blocks that
+ * mtc_free / the kernels' workspaces release on `device` stay allocated and
+ * belong to the graph, because its replays use them again. */
+int mtc_capture_begin(int device, void *stream);
+/* Ends the recording.  keep != 0: instantiates it into *graph (MTC_OK), which
+ * owns the retained blocks.  keep == 0 (or a failed capture): discards it,
+ * returns the retained blocks to the pool and sets *graph = NULL. */
+int mtc_capture_end(int keep, mtc_graph **graph);
+/* Number of mtc_fused calls recorded so far by the calling thread's capture. */
+int mtc_capture_fused_count(int32_t *count);
+/* Runs the recorded launches on the stream they were recorded on. */
+int mtc_graph_launch(mtc_graph *graph);
+/* Replaces the constants (MTC_OP_CONST immediates, in program order) of the
+ * `index`-th recorded mtc_fused launch for the following replays. */
+int mtc_graph_set_constants(mtc_graph *graph, int32_t index, const float *imm, int32_t n_imm);
+/* Kernels one replay launches (counted by mtc_launch_count at each replay). */
+int mtc_graph_launches(const mtc_graph *graph, uint64_t *count);
+/* Frees the graph; its retained blocks return to the pool in stream order. */
+int mtc_graph_destroy(mtc_graph *graph);
+/* Takes the cached free block that starts at `ptr` (a block an earlier
+ * mtc_alloc returned and mtc_free released) for `bytes` on `stream`, as
+ * mtc_alloc would.  MTC_OK when it was free, reusable on `stream` and large
+ * enough; MTC_ERR_UNSUPPORTED (nothing changes) otherwise. */
+int mtc_pool_take(int device, void *ptr, size_t bytes, void *stream);
+/* Adds `delta` to the protection count of the pool block at `ptr`.  While the
+ * count is positive the block, once released, is kept for mtc_pool_take
+ * (the replays of the graphs that use it) instead of being handed to other
+ * requests; at zero it becomes an ordinary cached block again. */
+int mtc_pool_protect(int device, void *ptr, int32_t delta);
 
 /* ------------------------------------------------------------ instrumentation -- */
 

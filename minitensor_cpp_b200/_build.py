@@ -33,7 +33,7 @@ NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
 
-CU_SOURCES = ["runtime.cu", "elementwise.cu", "fused.cu", "copy.cu", "random.cu", "reduce.cu", "gemm.cu",
+CU_SOURCES = ["runtime.cu", "graph.cu", "elementwise.cu", "fused.cu", "copy.cu", "random.cu", "reduce.cu", "gemm.cu",
               "gemm_tc.cu", "comm.cu"]
 
 

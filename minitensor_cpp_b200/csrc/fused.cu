@@ -24,6 +24,7 @@
 #include <vector>
 
 #include "elementwise.cuh"
+#include "graph.cuh"
 
 namespace mtc {
 namespace {
@@ -249,9 +250,15 @@ extern "C" int mtc_fused(const mtc_instr *program, int32_t n_instr, const mtc_de
         return fail(MTC_ERR_INVALID_ARGUMENT, "fused operand counts %d/%d out of range", n_inputs, n_outputs);
     if ((n_instr > 0 && program == nullptr) || out_regs == nullptr)
         return fail(MTC_ERR_INVALID_ARGUMENT, "null fused program");
+    Capture *capture = active_capture();
+    if (capture != nullptr && static_cast<cudaStream_t>(stream) != capture->stream)
+        return fail(MTC_ERR_INVALID_ARGUMENT, "fused launch on a stream other than the recorded one");
     EwPlan plan;
     MTC_TRY(plan_elementwise(inputs, n_inputs, outputs, n_outputs, plan));
-    if (plan.variant == EwVariant::Empty) return MTC_OK;
+    if (plan.variant == EwVariant::Empty) {
+        if (capture != nullptr) capture->fused.emplace_back();  // launches nothing
+        return MTC_OK;
+    }
 
     int n_imm = 0;
     for (int i = 0; i < n_instr && n_imm < MTC_EW_MAX_IMM; ++i)
@@ -268,7 +275,9 @@ extern "C" int mtc_fused(const mtc_instr *program, int32_t n_instr, const mtc_de
     case EwVariant::Rows1: v = 6; break;
     case EwVariant::Tiled4x1: v = 7; break;
     case EwVariant::Tiled4x2: v = 8; break;
-    default: return MTC_OK;
+    default:
+        if (capture != nullptr) capture->fused.emplace_back();
+        return MTC_OK;
     }
     // First level: the program's structure as bytes (device, variant, operand
     // counts, output registers, and op / registers of every instruction; the
@@ -317,5 +326,21 @@ extern "C" int mtc_fused(const mtc_instr *program, int32_t n_instr, const mtc_de
                                  plan.block.z, 0, static_cast<CUstream>(stream), params, nullptr);
     if (r != CUDA_SUCCESS) return fail(MTC_ERR_RUNTIME, "launch of fused kernel failed (CUresult %d)", static_cast<int>(r));
     count_launch();
+    if (capture != nullptr) {
+        // remember the kernel node, so replays can receive other constants
+        cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+        const cudaGraphNode_t *deps = nullptr;
+        size_t n_deps = 0;
+        if (cudaStreamGetCaptureInfo(capture->stream, &status, nullptr, nullptr, &deps, &n_deps) != cudaSuccess ||
+            status != cudaStreamCaptureStatusActive || n_deps != 1)
+            return fail(MTC_ERR_RUNTIME, "the recorded fused kernel node cannot be identified");
+        FusedNode f;
+        f.node = deps[0];
+        f.fn = cp->fn;
+        f.grid = plan.grid;
+        f.block = plan.block;
+        f.args = plan.args;
+        capture->fused.push_back(f);
+    }
     return MTC_OK;
 }

@@ -17,6 +17,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "graph.cuh"
 
 namespace mtc {
 
@@ -57,20 +58,37 @@ struct PendingFree {
 };
 
 struct DevicePool {
+    using FreeList = std::multimap<size_t, Block>;
     std::mutex mu;
     // free blocks reusable by one stream (stream order) or, key nullptr, by any stream
-    std::vector<std::pair<cudaStream_t, std::multimap<size_t, Block>>> free_lists;
+    std::vector<std::pair<cudaStream_t, std::unique_ptr<FreeList>>> free_lists;
+    // every free block by address, for taking one back by address (graph replay)
+    std::unordered_map<void *, std::pair<FreeList *, FreeList::iterator>> free_at;
     std::vector<PendingFree> pending;
     std::unordered_map<void *, Block> live;
+    // blocks recorded graphs use (reference counts): when free they are parked
+    // in `parked`, where only a take by address (a replay) finds them
+    std::unordered_map<void *, int> protect;
+    FreeList parked;
     std::vector<cudaEvent_t> spare_events;
     uint64_t reserved = 0;
     uint64_t cached = 0;
 
-    std::multimap<size_t, Block> &list_for(cudaStream_t s) {
+    FreeList &list_for(cudaStream_t s) {
         for (auto &fl : free_lists)
-            if (fl.first == s) return fl.second;
-        free_lists.emplace_back(s, std::multimap<size_t, Block>{});
-        return free_lists.back().second;
+            if (fl.first == s) return *fl.second;
+        free_lists.emplace_back(s, std::make_unique<FreeList>());
+        return *free_lists.back().second;
+    }
+
+    void put_free(cudaStream_t s, const Block &b) {
+        FreeList &fl = protect.count(b.ptr) ? parked : list_for(s);
+        free_at[b.ptr] = {&fl, fl.emplace(b.size, b)};
+    }
+
+    void erase_free(FreeList &fl, FreeList::iterator it) {
+        free_at.erase(it->second.ptr);
+        fl.erase(it);
     }
 };
 
@@ -90,13 +108,14 @@ size_t round_request(size_t bytes) {
     return (bytes + kLarge - 1) / kLarge * kLarge;
 }
 
-bool take_fit(std::multimap<size_t, Block> &fl, size_t want, Block &out) {
+bool take_fit(DevicePool &pool, cudaStream_t s, size_t want, Block &out) {
+    DevicePool::FreeList &fl = pool.list_for(s);
     auto it = fl.lower_bound(want);
     if (it == fl.end()) return false;
     const size_t slack = std::max(want / 8, size_t(2) << 20);
     if (it->first > want + slack) return false;
     out = it->second;
-    fl.erase(it);
+    pool.erase_free(fl, it);
     return true;
 }
 
@@ -107,7 +126,7 @@ void collect_pending(DevicePool &pool) {
         if (cudaEventQuery(pf.done) == cudaSuccess) {
             Block b = pf.block;
             b.stream = nullptr;
-            pool.list_for(nullptr).emplace(b.size, b);
+            pool.put_free(nullptr, b);
             pool.spare_events.push_back(pf.done);
             pool.pending[i] = pool.pending.back();
             pool.pending.pop_back();
@@ -123,13 +142,16 @@ int release_cached(DevicePool &pool) {
     MTC_CUDA_TRY(cudaDeviceSynchronize());
     collect_pending(pool);
     for (auto &fl : pool.free_lists) {
-        for (auto &kv : fl.second) {
+        for (auto &kv : *fl.second) {
             cudaFree(kv.second.ptr);
             pool.reserved -= kv.second.size;
             pool.cached -= kv.second.size;
         }
-        fl.second.clear();
+        fl.second->clear();
     }
+    // parked blocks stay: recorded graphs replay into them
+    pool.free_at.clear();
+    for (auto it = pool.parked.begin(); it != pool.parked.end(); ++it) pool.free_at[it->second.ptr] = {&pool.parked, it};
     return MTC_OK;
 }
 
@@ -141,8 +163,8 @@ int pool_alloc(int device, size_t bytes, cudaStream_t stream, void **ptr) {
     std::lock_guard<std::mutex> lock(pool.mu);
     if (!pool.pending.empty()) collect_pending(pool);
     Block b;
-    bool hit = take_fit(pool.list_for(stream), want, b);
-    if (!hit) hit = take_fit(pool.list_for(nullptr), want, b);
+    bool hit = take_fit(pool, stream, want, b);
+    if (!hit) hit = take_fit(pool, nullptr, want, b);
     if (hit) {
         pool.cached -= b.size;
     } else {
@@ -170,27 +192,58 @@ int pool_alloc(int device, size_t bytes, cudaStream_t stream, void **ptr) {
 
 int pool_free(int device, void *ptr, cudaStream_t stream) {
     if (ptr == nullptr) return MTC_OK;
-    DevicePool &pool = pool_of(device);
-    std::lock_guard<std::mutex> lock(pool.mu);
-    auto it = pool.live.find(ptr);
-    if (it == pool.live.end()) return fail(MTC_ERR_INVALID_ARGUMENT, "device %d: %p is not a live block", device, ptr);
-    Block b = it->second;
-    pool.live.erase(it);
-    pool.cached += b.size;
-    if (stream == b.stream) {
-        pool.list_for(stream).emplace(b.size, b);
+    if (Capture *c = active_capture(); c != nullptr && c->device == device) {
+        // recording: the graph's replays use this block again, so it stays
+        // allocated until the graph is destroyed
+        DevicePool &pool = pool_of(device);
+        std::lock_guard<std::mutex> lock(pool.mu);
+        if (pool.live.count(ptr) == 0)
+            return fail(MTC_ERR_INVALID_ARGUMENT, "device %d: %p is not a live block", device, ptr);
+        c->retained.push_back(ptr);
         return MTC_OK;
     }
-    // freed on another stream: reusable once that stream has passed this point
-    cudaEvent_t ev = nullptr;
-    if (!pool.spare_events.empty()) {
-        ev = pool.spare_events.back();
-        pool.spare_events.pop_back();
-    } else {
-        MTC_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    return release_block(device, ptr, stream);
+}
+
+// Takes the free block at `ptr` back for a request of `bytes` on `stream`.
+// Changes the protection count of the block at `ptr`; a block whose count
+// drops to zero while parked returns to its stream's free list.
+int pool_protect(int device, void *ptr, int delta) {
+    DevicePool &pool = pool_of(device);
+    std::lock_guard<std::mutex> lock(pool.mu);
+    const bool known = pool.live.count(ptr) || pool.free_at.count(ptr);
+    if (!known) return fail(MTC_ERR_INVALID_ARGUMENT, "device %d: %p is not a block of the pool", device, ptr);
+    int &n = pool.protect[ptr];
+    n += delta;
+    if (n > 0) return MTC_OK;
+    pool.protect.erase(ptr);
+    auto f = pool.free_at.find(ptr);
+    if (f != pool.free_at.end() && f->second.first == &pool.parked) {
+        const Block b = f->second.second->second;
+        pool.erase_free(pool.parked, f->second.second);
+        pool.put_free(b.stream, b);
     }
-    MTC_CUDA_TRY(cudaEventRecord(ev, stream));
-    pool.pending.push_back(PendingFree{b, ev});
+    return MTC_OK;
+}
+
+int pool_take(int device, void *ptr, size_t bytes, cudaStream_t stream) {
+    DevicePool &pool = pool_of(device);
+    const size_t want = round_request(bytes);
+    std::lock_guard<std::mutex> lock(pool.mu);
+    if (!pool.pending.empty()) collect_pending(pool);
+    auto f = pool.free_at.find(ptr);
+    if (f == pool.free_at.end()) return fail(MTC_ERR_UNSUPPORTED, "device %d: %p is not a free block", device, ptr);
+    DevicePool::FreeList *fl = f->second.first;
+    auto it = f->second.second;
+    const bool usable = fl == &pool.list_for(stream) || fl == &pool.list_for(nullptr) ||
+                        (fl == &pool.parked && (it->second.stream == stream || it->second.stream == nullptr));
+    if (!usable) return fail(MTC_ERR_UNSUPPORTED, "device %d: %p was released on another stream", device, ptr);
+    Block b = it->second;
+    if (b.size < want) return fail(MTC_ERR_UNSUPPORTED, "device %d: the block at %p is too small", device, ptr);
+    pool.erase_free(*fl, it);
+    pool.cached -= b.size;
+    b.stream = stream;
+    pool.live.emplace(b.ptr, b);
     return MTC_OK;
 }
 
@@ -237,6 +290,39 @@ struct DeviceGuard {
 };
 }  // namespace
 
+int release_block(int device, void *ptr, cudaStream_t stream) {
+    if (ptr == nullptr) return MTC_OK;
+    DevicePool &pool = pool_of(device);
+    std::lock_guard<std::mutex> lock(pool.mu);
+    auto it = pool.live.find(ptr);
+    if (it == pool.live.end()) return fail(MTC_ERR_INVALID_ARGUMENT, "device %d: %p is not a live block", device, ptr);
+    Block b = it->second;
+    pool.live.erase(it);
+    pool.cached += b.size;
+    if (stream == b.stream) {
+        pool.put_free(stream, b);
+        return MTC_OK;
+    }
+    // freed on another stream: reusable once that stream has passed this point
+    cudaEvent_t ev = nullptr;
+    if (!pool.spare_events.empty()) {
+        ev = pool.spare_events.back();
+        pool.spare_events.pop_back();
+    } else {
+        MTC_CUDA_TRY(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+    }
+    MTC_CUDA_TRY(cudaEventRecord(ev, stream));
+    pool.pending.push_back(PendingFree{b, ev});
+    return MTC_OK;
+}
+
+namespace {
+thread_local Capture *t_capture = nullptr;
+}  // namespace
+
+Capture *active_capture() { return t_capture; }
+void set_active_capture(Capture *c) { t_capture = c; }
+
 int fail(int code, const char *fmt, ...) {
     char buf[1024];
     va_list ap;
@@ -259,6 +345,10 @@ int check_launch(const char *what) {
 }
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+uint64_t launches_so_far() { return g_launches.load(std::memory_order_relaxed); }
+
+void count_launches(int64_t n) { g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed); }
 
 // ------------------------------------------------------------ GEMM profile --
 
@@ -566,6 +656,19 @@ int mtc_pool_stats(int device, uint64_t *reserved_bytes, uint64_t *used_bytes) {
     if (reserved_bytes) *reserved_bytes = pool.reserved;
     if (used_bytes) *used_bytes = pool.reserved - pool.cached;
     return MTC_OK;
+}
+
+int mtc_pool_take(int device, void *ptr, size_t bytes, void *stream) {
+    clear_error();
+    if (device < 0) return fail(MTC_ERR_INVALID_ARGUMENT, "negative device index");
+    if (ptr == nullptr || bytes == 0) return fail(MTC_ERR_INVALID_ARGUMENT, "nothing to take");
+    return pool_take(device, ptr, bytes, static_cast<cudaStream_t>(stream));
+}
+
+int mtc_pool_protect(int device, void *ptr, int32_t delta) {
+    clear_error();
+    if (device < 0 || ptr == nullptr) return fail(MTC_ERR_INVALID_ARGUMENT, "no block to protect");
+    return pool_protect(device, ptr, delta);
 }
 
 int mtc_pool_trim(int device) {

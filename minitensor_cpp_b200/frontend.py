@@ -56,6 +56,8 @@ class Frontend:
             "mtb_gather_rows": ([ctypes.c_int, i64, i64, P(f32), i64, P(i64), P(f32)], ctypes.c_int),
             "mtb_evaluator_stats": ([P(u64)], None),
             "mtb_evaluator_reset_stats": ([], None),
+            "mtb_graph_cache_clear": ([], None),
+            "mtb_set_graphs": ([ctypes.c_int], ctypes.c_int),
         }
         for name, (args, res) in sigs.items():
             fn = getattr(L, name)
@@ -108,14 +110,22 @@ class Frontend:
         return out
 
     def stats(self) -> dict:
-        buf = (ctypes.c_uint64 * 9)()
+        buf = (ctypes.c_uint64 * 12)()
         self.lib.mtb_evaluator_stats(buf)
         keys = ("kernel_steps", "fused_launches", "fused_nodes", "folded_constants", "view_steps", "evaluations",
-                "plan_ns", "execute_ns", "check_ns")
+                "plan_ns", "execute_ns", "check_ns", "graph_captures", "graph_replays", "graph_fallbacks")
         return dict(zip(keys, list(buf)))
 
     def reset_stats(self):
         self.lib.mtb_evaluator_reset_stats()
+
+    def set_graphs(self, on: bool) -> bool:
+        """Turns the replay of repeated evaluation plans on or off; returns the previous setting."""
+        return bool(self.lib.mtb_set_graphs(1 if on else 0))
+
+    def clear_graphs(self):
+        """Destroys every plan recorded for replay."""
+        self.lib.mtb_graph_cache_clear()
 
 
 class MlpTrainer:

@@ -50,6 +50,8 @@ class CudaRuntime final : public DeviceRuntime {
 
     [[nodiscard]] Device device() const noexcept override { return device_; }
     [[nodiscard]] BufferRef allocate(std::size_t size_bytes) override;
+    // A buffer over a block already taken from the allocator (mtc_pool_take).
+    [[nodiscard]] BufferRef adopt(void *data, std::size_t size_bytes);
     void copy_from_host(Buffer &destination, std::size_t destination_offset_bytes,
                         std::span<const std::byte> source) override;
     void copy_to_host(std::span<std::byte> destination, const Buffer &source, std::size_t source_offset_bytes) override;
@@ -79,10 +81,14 @@ void register_cuda_kernels(KernelRegistry &registry);
 // Returns false (and does nothing) when the graph has no CUDA work.
 bool evaluate_fused(const RuntimeRegistry &runtimes, const KernelRegistry &kernels, std::span<const ValueRef> roots);
 
-// Process-wide switches (environment MTB_FUSION=0 disables elementwise fusion).
+// Process-wide switches: environment MTB_FUSION=0 disables elementwise fusion,
+// MTB_GRAPHS=0 the replay of repeated plans, MTB_GRAPH_MAX_BYTES (default 64 MiB)
+// bounds the output bytes of a plan that is recorded for replay.
 struct EvaluatorOptions {
     bool fusion = true;
     bool check_index_errors = true;
+    bool graphs = true;
+    std::size_t graph_max_bytes = std::size_t(64) << 20;
 };
 EvaluatorOptions &evaluator_options();
 
@@ -96,9 +102,15 @@ struct EvaluatorStats {
     std::uint64_t evaluations = 0;
     std::uint64_t plan_ns = 0;     // host time planning and clustering
     std::uint64_t execute_ns = 0;  // host time issuing kernels (allocation and launch calls)
-    std::uint64_t check_ns = 0;    // host time in the deferred index-error check (a stream synchronisation)
+    std::uint64_t check_ns = 0;    // host time queueing the deferred index-error check
+    std::uint64_t graph_captures = 0;  // plans recorded for replay
+    std::uint64_t graph_replays = 0;   // evaluations run as one replay of a recorded plan
+    std::uint64_t graph_fallbacks = 0; // recorded plans whose output blocks were in use (run eagerly)
 };
 EvaluatorStats &evaluator_stats();
+
+// Destroys every recorded plan (their workspaces return to the allocator).
+void clear_graph_cache();
 
 // Throws std::out_of_range when an index kernel on `device` recorded an index
 // outside its axis (a snapshot of the device error word queued after an

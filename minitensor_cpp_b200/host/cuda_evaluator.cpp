@@ -20,11 +20,15 @@
 // Values internal to a cluster stay unmaterialised and are recomputed from
 // their producers if a later evaluation asks for them.
 #include <chrono>
+#include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
+#include <mutex>
 #include <optional>
 #include <stdexcept>
+#include <string>
 #include <unordered_map>
 #include <utility>
 #include <vector>
@@ -32,12 +36,22 @@
 #include <minitensor/host_scalar.hpp>
 
 #include "cuda_backend.hpp"
+#include "ops_ext.hpp"
 #include "tensor/core/tensor_spec.hpp"
 #include "tensor/dispatch/kernel_key.hpp"
 #include "tensor/graph/node.hpp"
 #include "tensor/graph/primitive.hpp"
 #include "tensor/graph/value.hpp"
 #include "tensor/primitives/creation/full.hpp"
+#include "tensor/primitives/creation/normal.hpp"
+#include "tensor/primitives/creation/uniform.hpp"
+#include "tensor/primitives/manipulation/basic_index.hpp"
+#include "tensor/primitives/manipulation/concatenate.hpp"
+#include "tensor/primitives/manipulation/gather.hpp"
+#include "tensor/primitives/manipulation/permute.hpp"
+#include "tensor/primitives/reduction/logsumexp.hpp"
+#include "tensor/primitives/reduction/sum.hpp"
+#include "tensor/random_key_access.hpp"
 #include "tensor/storage/dense_size.hpp"
 #include "tensor/storage/layout.hpp"
 #include "tensor/storage/materialization.hpp"
@@ -49,6 +63,8 @@ EvaluatorOptions &evaluator_options() {
         EvaluatorOptions o;
         if (const char *v = std::getenv("MTB_FUSION")) o.fusion = std::strcmp(v, "0") != 0;
         if (const char *v = std::getenv("MTB_INDEX_CHECKS")) o.check_index_errors = std::strcmp(v, "0") != 0;
+        if (const char *v = std::getenv("MTB_GRAPHS")) o.graphs = std::strcmp(v, "0") != 0;
+        if (const char *v = std::getenv("MTB_GRAPH_MAX_BYTES")) o.graph_max_bytes = std::strtoull(v, nullptr, 10);
         return o;
     }();
     return options;
@@ -144,36 +160,212 @@ class Planner {
     bool has_cuda_ = false;
 };
 
-void execute_kernel_step(const Step &step) {
-    Value &output = *step.output;
-    const Node &node = *step.node;
-    const Primitive &primitive = node.primitive();
-    const auto inputs = node.inputs();
-    std::vector<TensorView> views;
-    views.reserve(inputs.size());
-    for (const ValueRef &input : inputs) {
-        const Materialization *m = input->materialization();
-        if (m == nullptr) throw std::logic_error{"planned operation has unmaterialized input"};
-        if (inputs.size() == 1) {
-            auto shared = primitive.try_derive_shared_layout(input->spec(), m->layout(), output.spec());
-            if (shared) {
-                output.materialize(Materialization(m->buffer_ref(), std::move(*shared)));
-                ++evaluator_stats().view_steps;
-                return;
-            }
-        }
-        views.emplace_back(input->spec(), *m);
+// ------------------------------------------------------------- plan replay --
+//
+// A plan that repeats (a training step builds the same graph every step) is
+// recorded once with stream capture and then replayed as one CUDA graph.  The
+// key of a plan is its structure (every step's primitive, parameters, output
+// spec, fusion decisions and input references) together with the data
+// pointers and layouts of its leaf inputs.  A replay is sound because:
+//  - an equal key means the same launches on the same operands, except for the
+//    outputs and the constants folded into fused programs;
+//  - the outputs are the very blocks the recording wrote, taken back from the
+//    allocator (mtc_pool_take) before the replay; when one is still in use the
+//    evaluation runs eagerly instead;
+//  - folded constants (an optimizer's per-step coefficients) are compared with
+//    the recorded ones and patched into their kernel nodes before the replay.
+// When a plan is recorded while an earlier recording of the same structure
+// exists, and that recording's outputs are this plan's leaves (the parameters
+// of step t+1 are outputs of step t), the new outputs are placed in the blocks
+// the earlier recording read.  The two recordings then alternate: every later
+// step finds its leaves where one of them expects them.
+
+struct KeyWriter {
+    std::string bytes;
+    template <typename T>
+    void pod(const T &v) {
+        bytes.append(reinterpret_cast<const char *>(&v), sizeof(T));
     }
-    if (step.kernel == nullptr) throw std::logic_error{"primitive must either share storage or plan a kernel"};
-    const TensorSpec &spec = output.spec();
-    BufferRef buffer = step.runtime->allocate(dense_size_bytes(spec));
-    Materialization m(std::move(buffer), Layout::contiguous(spec.shape));
-    {
-        MutableTensorView out(spec, m);
-        (*step.kernel)(*step.runtime, primitive, views, out);
+    void shape(const Shape &s) {
+        pod(static_cast<std::uint32_t>(s.rank()));
+        for (Extent e : s.dimensions()) pod(static_cast<std::int64_t>(e));
     }
-    output.materialize(std::move(m));
-    if (step.on_cuda) ++evaluator_stats().kernel_steps;
+    void layout(const Layout &l) {
+        pod(static_cast<std::int64_t>(l.offset()));
+        pod(static_cast<std::uint32_t>(l.rank()));
+        for (auto st : l.strides()) pod(static_cast<std::int64_t>(st));
+    }
+    template <typename Seq>
+    void seq(const Seq &v) {
+        pod(static_cast<std::uint32_t>(v.size()));
+        for (const auto &x : v) pod(static_cast<std::int64_t>(x));
+    }
+};
+
+// Writes the parameters of `primitive` that shape its launches.  False for a
+// primitive this evaluator does not know: such plans are never recorded.
+bool write_parameters(const Primitive &primitive, std::uint32_t id, bool folded, KeyWriter &w) {
+    switch (id) {
+    case 0x0001: {  // Full; a folded value is a fused constant, patched at replay
+        if (folded) return true;
+        const HostScalar &v = dynamic_cast<const FullPrimitive &>(primitive).fill_value();
+        w.pod(static_cast<std::uint8_t>(v.dtype()));
+        if (v.dtype() == DType::Float32) w.pod(v.get<float>());
+        else w.pod(v.get<std::int64_t>());
+        return true;
+    }
+    case 0x0002: {
+        const auto &u = dynamic_cast<const UniformPrimitive &>(primitive);
+        const auto &k = RandomKeyAccess::words(u.key());
+        w.pod(u.low());
+        w.pod(u.high());
+        w.pod(k[0]);
+        w.pod(k[1]);
+        return true;
+    }
+    case 0x0003: {
+        const auto &n = dynamic_cast<const NormalPrimitive &>(primitive);
+        const auto &k = RandomKeyAccess::words(n.key());
+        w.pod(n.mean());
+        w.pod(n.std_dev());
+        w.pod(k[0]);
+        w.pod(k[1]);
+        return true;
+    }
+    case 0x0203: w.seq(dynamic_cast<const PermutePrimitive &>(primitive).permutation()); return true;
+    case 0x0205: w.pod(static_cast<std::uint64_t>(dynamic_cast<const ConcatenatePrimitive &>(primitive).axis())); return true;
+    case 0x0206: {  // the slice as a layout over a contiguous input
+        const auto &p = dynamic_cast<const BasicIndexPrimitive &>(primitive).parameters();
+        w.layout(p.derive_layout(Layout::contiguous(p.input_shape())));
+        return true;
+    }
+    case 0x0207: {
+        const auto &p = dynamic_cast<const BasicIndexScatterPrimitive &>(primitive).parameters();
+        w.layout(p.derive_layout(Layout::contiguous(p.input_shape())));
+        return true;
+    }
+    case 0x0208: w.pod(static_cast<std::uint64_t>(dynamic_cast<const GatherPrimitive &>(primitive).axis())); return true;
+    case 0x0209:
+        w.pod(static_cast<std::uint64_t>(dynamic_cast<const GatherScatterAddPrimitive &>(primitive).axis()));
+        return true;
+    case 0x0301: {
+        const auto &r = dynamic_cast<const SumPrimitive &>(primitive);
+        w.seq(r.axes());
+        w.pod(static_cast<std::uint8_t>(r.keep_dim()));
+        return true;
+    }
+    case 0x0302: {
+        const auto &r = dynamic_cast<const LogSumExpPrimitive &>(primitive);
+        w.seq(r.axes());
+        w.pod(static_cast<std::uint8_t>(r.keep_dim()));
+        return true;
+    }
+    case 0x0201:  // Contiguous, Reshape, BroadcastTo, Matmul: the specs say it all
+    case 0x0202:
+    case 0x0204:
+    case 0x0401: return true;
+    default:
+        if (is_unary_id(id) || is_binary_id(id)) return true;
+        return ext::write_primitive_key(primitive, w.bytes);
+    }
+}
+
+// One materialisation a recorded plan installs, in execution order.
+struct Install {
+    int step = -1;
+    bool view = false;
+    void *ptr = nullptr;  // buffer: the block the recording wrote
+    std::size_t bytes = 0;
+    std::optional<Layout> layout;  // view: the layout over its input's buffer
+};
+
+// The folded constants of one recorded fused launch.
+struct FusedConstants {
+    std::int32_t index = 0;     // position among the recording's mtc_fused calls
+    std::vector<int> steps;     // plan steps of the Full nodes, in program order
+    std::vector<float> values;  // what the kernel node holds now
+};
+
+// Bytes of blocks protected for recordings, over all of them (bounded by
+// kMaxProtectedBytes; guarded by the cache mutex).
+std::size_t g_protected_bytes = 0;
+constexpr std::size_t kMaxProtectedBytes = std::size_t(1) << 30;
+
+struct Recording {
+    int device = -1;
+    std::vector<const void *> leaves;
+    mtc_graph *graph = nullptr;
+    std::vector<Install> installs;
+    std::vector<FusedConstants> constants;
+    bool index_kernels = false;
+    EvaluatorStats work;  // evaluator counters of one evaluation of the plan
+    // Blocks this recording reads (leaves) or writes (outputs).  They are
+    // protected in the allocator: once released they wait for this recording's
+    // replays (and the next recording of the plan) instead of serving other
+    // requests, so the outputs are free whenever the plan comes back.
+    std::vector<void *> protected_blocks;
+    std::size_t protected_bytes = 0;
+    Recording() = default;
+    Recording(const Recording &) = delete;
+    Recording &operator=(const Recording &) = delete;
+    ~Recording() {
+        for (void *p : protected_blocks) (void)mtc_pool_protect(device, p, -1);
+        g_protected_bytes -= protected_bytes;
+        if (graph != nullptr) (void)mtc_graph_destroy(graph);
+    }
+    void protect(void *p, std::size_t bytes) {
+        if (p == nullptr || mtc_pool_protect(device, p, 1) != MTC_OK) return;
+        protected_blocks.push_back(p);
+        protected_bytes += bytes;
+        g_protected_bytes += bytes;
+    }
+};
+
+struct PlanHistory {
+    int seen = 0;
+    std::uint64_t captures = 0;
+    std::uint64_t replays = 0;
+    std::uint64_t fallbacks = 0;
+    bool disabled = false;
+    std::vector<std::unique_ptr<Recording>> recordings;
+};
+
+constexpr std::size_t kMaxRecordings = 4;  // per plan structure
+constexpr std::size_t kMaxPlans = 256;
+
+struct GraphCache {
+    std::mutex mu;
+    std::unordered_map<std::string, PlanHistory> plans;
+};
+
+GraphCache &graph_cache() {
+    // never destroyed: graphs must not be freed after the CUDA runtime at exit
+    static GraphCache *cache = new GraphCache;
+    return *cache;
+}
+
+void add_work(EvaluatorStats &to, const EvaluatorStats &w) {
+    to.kernel_steps += w.kernel_steps;
+    to.fused_launches += w.fused_launches;
+    to.fused_nodes += w.fused_nodes;
+    to.folded_constants += w.folded_constants;
+    to.view_steps += w.view_steps;
+}
+
+// MTB_TRACE: why a plan is not recorded or a recording failed.
+void trace_graph(const char *what, const char *detail) {
+    static const bool on = std::getenv("MTB_TRACE") != nullptr;
+    if (on) std::fprintf(stderr, "mtb plan replay: %s%s%s\n", what, detail[0] ? ": " : "", detail);
+}
+
+EvaluatorStats work_between(const EvaluatorStats &before, const EvaluatorStats &after) {
+    EvaluatorStats w;
+    w.kernel_steps = after.kernel_steps - before.kernel_steps;
+    w.fused_launches = after.fused_launches - before.fused_launches;
+    w.fused_nodes = after.fused_nodes - before.fused_nodes;
+    w.folded_constants = after.folded_constants - before.folded_constants;
+    w.view_steps = after.view_steps - before.view_steps;
+    return w;
 }
 
 class FusedEvaluator {
@@ -218,7 +410,7 @@ class FusedEvaluator {
         }
         if (evaluator_options().fusion) form_clusters();
         const auto t1 = clock::now();
-        execute();
+        if (!(evaluator_options().graphs && run_recorded())) execute();
         const auto t2 = clock::now();
         auto &st = evaluator_stats();
         st.plan_ns += static_cast<std::uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(t1 - t0).count());
@@ -283,9 +475,86 @@ class FusedEvaluator {
         return outputs <= MTC_MAX_FUSED_OUTPUTS && inputs - static_cast<int>(c.members.size()) <= MTC_MAX_FUSED_OPERANDS;
     }
 
+    // --------------------------------------------------------- eager steps --
+
+    // The materialisation of `v` as this evaluation sees it: while recording,
+    // outputs are held back until the recorded graph has run.
+    const Materialization *mat_of(const Value *v) const {
+        if (capturing_) {
+            const int pi = plan_index(v);
+            if (pi >= 0 && pending_[pi]) return &*pending_[pi];
+        }
+        return v->materialization();
+    }
+
+    void install(int pi, Materialization m, bool view) {
+        if (!capturing_) {
+            plan_[pi].output->materialize(std::move(m));
+            return;
+        }
+        m.validate(plan_[pi].output->spec());
+        Install rec;
+        rec.step = pi;
+        rec.view = view;
+        if (view) {
+            rec.layout = m.layout();
+        } else {
+            const auto *b = dynamic_cast<const CudaBuffer *>(m.buffer_ref().get());
+            if (b == nullptr) throw std::logic_error{"a recorded output is not a device buffer"};
+            rec.ptr = b->data();
+            rec.bytes = b->size_bytes();
+        }
+        installs_.push_back(std::move(rec));
+        pending_[pi].emplace(std::move(m));
+    }
+
+    BufferRef allocate_output(int pi, std::size_t bytes) {
+        if (capturing_ && !reserved_.empty()) {
+            auto r = reserved_.find(pi);
+            if (r != reserved_.end() && r->second->size_bytes() == bytes) {
+                BufferRef b = std::move(r->second);
+                reserved_.erase(r);
+                return b;
+            }
+        }
+        return plan_[pi].runtime->allocate(bytes);
+    }
+
+    void execute_step(int pi) {
+        Step &step = plan_[pi];
+        Value &output = *step.output;
+        const Node &node = *step.node;
+        const Primitive &primitive = node.primitive();
+        const auto inputs = node.inputs();
+        std::vector<TensorView> views;
+        views.reserve(inputs.size());
+        for (const ValueRef &input : inputs) {
+            const Materialization *m = mat_of(input.get());
+            if (m == nullptr) throw std::logic_error{"planned operation has unmaterialized input"};
+            if (inputs.size() == 1) {
+                auto shared = primitive.try_derive_shared_layout(input->spec(), m->layout(), output.spec());
+                if (shared) {
+                    install(pi, Materialization(m->buffer_ref(), std::move(*shared)), true);
+                    ++evaluator_stats().view_steps;
+                    return;
+                }
+            }
+            views.emplace_back(input->spec(), *m);
+        }
+        if (step.kernel == nullptr) throw std::logic_error{"primitive must either share storage or plan a kernel"};
+        const TensorSpec &spec = output.spec();
+        Materialization m(allocate_output(pi, dense_size_bytes(spec)), Layout::contiguous(spec.shape));
+        {
+            MutableTensorView out(spec, m);
+            (*step.kernel)(*step.runtime, primitive, views, out);
+        }
+        install(pi, std::move(m), false);
+        if (step.on_cuda) ++evaluator_stats().kernel_steps;
+    }
+
     void execute() {
-        bool index_kernels = false;
-        DeviceRuntime *index_runtime = nullptr;
+        index_kernels_ = false;
+        index_runtime_ = nullptr;
         static const bool trace = std::getenv("MTB_TRACE") != nullptr;
         for (int i = 0; i < static_cast<int>(plan_.size()); ++i) {
             Step &s = plan_[i];
@@ -299,24 +568,27 @@ class FusedEvaluator {
                 if (trace) report_slow(t0, "fused cluster", s);
                 continue;
             }
-            execute_kernel_step(s);
+            execute_step(i);
             if (trace) report_slow(t0, "kernel", s);
             const std::uint32_t id = s.node->primitive().id().value();
             if (s.on_cuda && (id == kGatherId || id == kScatterAddId)) {
-                index_kernels = true;
-                index_runtime = s.runtime;
+                index_kernels_ = true;
+                index_runtime_ = s.runtime;
             }
         }
-        if (index_kernels && evaluator_options().check_index_errors && index_runtime != nullptr) {
-            // queue a snapshot of the device error word; it is examined at the next
-            // evaluation on this device or the next device-to-host read, so the
-            // host does not wait for the GPU here
-            auto &rt = dynamic_cast<CudaRuntime &>(*index_runtime);
-            const auto c0 = std::chrono::steady_clock::now();
-            check(mtc_watch_device_errors(rt.index(), rt.stream()), "device error check");
-            evaluator_stats().check_ns += static_cast<std::uint64_t>(
-                std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - c0).count());
-        }
+        if (!capturing_) watch_index_errors();
+    }
+
+    // Queues a snapshot of the device error word after an evaluation that ran
+    // an index kernel; it is examined at the next evaluation on this device or
+    // the next device-to-host read, so the host does not wait for the GPU here.
+    void watch_index_errors() {
+        if (!index_kernels_ || !evaluator_options().check_index_errors || index_runtime_ == nullptr) return;
+        auto &rt = dynamic_cast<CudaRuntime &>(*index_runtime_);
+        const auto c0 = std::chrono::steady_clock::now();
+        check(mtc_watch_device_errors(rt.index(), rt.stream()), "device error check");
+        evaluator_stats().check_ns += static_cast<std::uint64_t>(
+            std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - c0).count());
     }
 
     // MTB_TRACE: host calls of 20 ms or more (allocation, compilation or a
@@ -336,6 +608,8 @@ class FusedEvaluator {
         std::vector<mtc_desc> inputs;
         std::vector<mtc_instr> program;
         std::vector<int> out_steps;
+        std::vector<int> const_steps;
+        std::vector<float> const_values;
         // external inputs
         for (int m : members) {
             for (const ValueRef &in : plan_[m].node->inputs()) {
@@ -344,7 +618,7 @@ class FusedEvaluator {
                 auto it = plan_index(v);
                 if (it >= 0 && plan_[it].cluster == plan_[m].cluster) continue;
                 if (it >= 0 && plan_[it].folded) continue;
-                const Materialization *mat = in->materialization();
+                const Materialization *mat = mat_of(v);
                 if (mat == nullptr) throw std::logic_error{"fused cluster has an unmaterialized input"};
                 reg.emplace(v, static_cast<int>(inputs.size()));
                 inputs.push_back(make_desc(TensorView(in->spec(), *mat)));
@@ -370,6 +644,8 @@ class FusedEvaluator {
                     ci.dst = static_cast<int16_t>(next);
                     ci.imm = full.fill_value().get<float>();
                     program.push_back(ci);
+                    const_steps.push_back(pi);
+                    const_values.push_back(ci.imm);
                     found = reg.emplace(v, next++).first;
                 }
                 operand[k] = found->second;
@@ -393,13 +669,14 @@ class FusedEvaluator {
         std::vector<int32_t> out_regs;
         for (int m : out_steps) {
             const TensorSpec &spec = plan_[m].output->spec();
-            BufferRef buffer = plan_[m].runtime->allocate(dense_size_bytes(spec));
-            mats.emplace_back(std::move(buffer), Layout::contiguous(spec.shape));
+            mats.emplace_back(allocate_output(m, dense_size_bytes(spec)), Layout::contiguous(spec.shape));
             out_regs.push_back(reg.at(plan_[m].output.get()));
         }
         for (std::size_t j = 0; j < out_steps.size(); ++j)
             outputs.push_back(make_desc(MutableTensorView(plan_[out_steps[j]].output->spec(), mats[j])));
         runtime->activate();
+        int32_t recorded_before = 0;
+        if (capturing_) check(mtc_capture_fused_count(&recorded_before), "recording");
         const int rc = mtc_fused(program.data(), static_cast<int32_t>(program.size()), inputs.data(),
                                  static_cast<int32_t>(inputs.size()), out_regs.data(), outputs.data(),
                                  static_cast<int32_t>(outputs.size()), runtime->stream());
@@ -409,18 +686,28 @@ class FusedEvaluator {
             return;
         }
         check(rc, "fused elementwise kernel");
-        for (std::size_t j = 0; j < out_steps.size(); ++j) plan_[out_steps[j]].output->materialize(std::move(mats[j]));
+        if (capturing_) {
+            int32_t recorded_after = 0;
+            check(mtc_capture_fused_count(&recorded_after), "recording");
+            if (recorded_after != recorded_before + 1) capture_unsafe_ = true;
+            else if (!const_steps.empty())
+                constants_.push_back(FusedConstants{recorded_before, std::move(const_steps), std::move(const_values)});
+        }
+        for (std::size_t j = 0; j < out_steps.size(); ++j) install(out_steps[j], std::move(mats[j]), false);
         ++evaluator_stats().fused_launches;
         evaluator_stats().fused_nodes += members.size();
     }
 
     void run_unfused(const std::vector<int> &members) {
+        // the folded constants become kernels with their values built in: a
+        // recording of them could not follow later values
+        if (capturing_) capture_unsafe_ = true;
         for (int m : members) {
             for (const ValueRef &in : plan_[m].node->inputs()) {
                 const int pi = plan_index(in.get());
-                if (pi >= 0 && plan_[pi].folded && in->materialization() == nullptr) execute_kernel_step(plan_[pi]);
+                if (pi >= 0 && plan_[pi].folded && mat_of(in.get()) == nullptr) execute_step(pi);
             }
-            execute_kernel_step(plan_[m]);
+            execute_step(m);
         }
     }
 
@@ -429,11 +716,260 @@ class FusedEvaluator {
         return it == index_cache_.end() ? -1 : it->second;
     }
 
+    // ---------------------------------------------------------- recording --
+
+    // The plan's key (structure bytes) and its leaves' data pointers; false
+    // when the plan is not recorded (host steps, several devices, an unknown
+    // primitive, outputs above MTB_GRAPH_MAX_BYTES).
+    bool plan_key(KeyWriter &w, std::vector<const void *> &leaves, CudaRuntime *&rt) {
+        leaf_values_.clear();
+        int device = -1;
+        std::size_t out_bytes = 0;
+        std::unordered_map<const Value *, int> leaf_slot;
+        w.bytes.reserve(plan_.size() * 64);
+        for (int i = 0; i < static_cast<int>(plan_.size()); ++i) {
+            const Step &s = plan_[i];
+            if (!s.on_cuda) return trace_graph("not recorded", "a step runs on the host"), false;
+            const TensorSpec &spec = s.output->spec();
+            const int dev = static_cast<int>(spec.device.index());
+            if (device < 0) device = dev;
+            else if (dev != device) return trace_graph("not recorded", "steps on several devices"), false;
+            if (rt == nullptr && s.runtime != nullptr) rt = dynamic_cast<CudaRuntime *>(s.runtime);
+            const Primitive &primitive = s.node->primitive();
+            const std::uint32_t id = primitive.id().value();
+            w.pod(id);
+            w.pod(static_cast<std::uint8_t>(spec.dtype));
+            w.shape(spec.shape);
+            w.pod(static_cast<std::uint8_t>((s.materialize ? 1 : 0) | (s.folded ? 2 : 0)));
+            w.pod(static_cast<std::int32_t>(s.cluster));
+            if (!write_parameters(primitive, id, s.folded, w)) {
+                trace_graph("not recorded, unknown primitive", std::string(primitive.name()).c_str());
+                return false;
+            }
+            const auto ins = s.node->inputs();
+            w.pod(static_cast<std::uint32_t>(ins.size()));
+            for (const ValueRef &in : ins) {
+                const int pi = plan_index(in.get());
+                if (pi >= 0) {
+                    w.pod(static_cast<std::int32_t>(pi));
+                    continue;
+                }
+                auto [slot, fresh] = leaf_slot.emplace(in.get(), static_cast<int>(leaves.size()));
+                if (fresh) {
+                    leaf_values_.push_back(in.get());
+                    const Materialization *m = in->materialization();
+                    const auto *b = m != nullptr ? dynamic_cast<const CudaBuffer *>(m->buffer_ref().get()) : nullptr;
+                    if (b == nullptr || static_cast<int>(b->device().index()) != device)
+                        return trace_graph("not recorded", "a leaf is not a buffer of the plan's device"), false;
+                    leaves.push_back(b->data());
+                    w.pod(std::int32_t{-1});  // a new leaf: its spec and layout
+                    w.pod(static_cast<std::uint8_t>(in->spec().dtype));
+                    w.shape(in->spec().shape);
+                    w.layout(m->layout());
+                }
+                w.pod(static_cast<std::int32_t>(-2 - slot->second));
+            }
+            if (s.materialize && s.kernel != nullptr) out_bytes += dense_size_bytes(spec);
+        }
+        if (rt == nullptr || device < 0) return trace_graph("not recorded", "no device runtime"), false;
+        if (out_bytes > evaluator_options().graph_max_bytes) return false;  // launch overhead does not matter
+        w.pod(device);
+        return true;
+    }
+
+    bool run_recorded() {
+        KeyWriter key;
+        std::vector<const void *> leaves;
+        CudaRuntime *rt = nullptr;
+        if (!plan_key(key, leaves, rt)) return false;
+        GraphCache &cache = graph_cache();
+        std::lock_guard<std::mutex> lock(cache.mu);
+        if (cache.plans.size() >= kMaxPlans && cache.plans.count(key.bytes) == 0) cache.plans.clear();
+        PlanHistory &h = cache.plans[key.bytes];
+        if (h.disabled) return false;
+        static const bool trace = std::getenv("MTB_TRACE") != nullptr;
+        char note[96];
+        for (auto &r : h.recordings) {
+            if (r->leaves != leaves) continue;
+            if (replay(*r, *rt)) {
+                ++h.replays;
+                ++evaluator_stats().graph_replays;
+                return true;
+            }
+            // an output block is still in use: this evaluation runs eagerly
+            ++h.fallbacks;
+            ++evaluator_stats().graph_fallbacks;
+            if (trace) {
+                std::snprintf(note, sizeof(note), "plan of %zu steps, %s", plan_.size(), mtc_last_error());
+                trace_graph("recorded outputs in use", note);
+            }
+            if (h.fallbacks > 16 && h.fallbacks > h.replays) h.disabled = true;
+            return false;
+        }
+        if (trace) {
+            std::snprintf(note, sizeof(note), "plan of %zu steps, %zu leaves, seen %d, %zu recordings", plan_.size(),
+                          leaves.size(), h.seen + 1, h.recordings.size());
+            trace_graph("no recording matches", note);
+        }
+        if (++h.seen < 2) return false;  // a plan seen once is not recorded
+        if (h.captures >= 4 * kMaxRecordings && h.replays < h.captures) {
+            h.disabled = true;  // the leaves never come back to recorded blocks
+            return false;
+        }
+        if (g_protected_bytes > kMaxProtectedBytes) {
+            trace_graph("not recorded", "recordings already protect the allowed memory");
+            return false;
+        }
+        return record(h, leaves, *rt);
+    }
+
+    bool record(PlanHistory &h, const std::vector<const void *> &leaves, CudaRuntime &rt) {
+        reserved_.clear();
+        if (!h.recordings.empty()) {
+            // outputs of the previous recording that are leaves here: the outputs
+            // of the same steps go to the blocks that recording read in their
+            // place.  They are taken now, before any intermediate of this
+            // evaluation can be given one of them.
+            const Recording &prev = *h.recordings.back();
+            std::unordered_map<const void *, const Install *> out_of;
+            for (const Install &in : prev.installs)
+                if (!in.view && in.ptr != nullptr) out_of.emplace(in.ptr, &in);
+            for (std::size_t i = 0; i < leaves.size() && i < prev.leaves.size(); ++i) {
+                auto f = out_of.find(leaves[i]);
+                if (f == out_of.end() || reserved_.count(f->second->step)) continue;
+                void *block = const_cast<void *>(prev.leaves[i]);
+                if (mtc_pool_take(rt.index(), block, f->second->bytes, rt.stream()) == MTC_OK)
+                    reserved_.emplace(f->second->step, rt.adopt(block, f->second->bytes));
+            }
+        }
+        const EvaluatorStats before = evaluator_stats();
+        auto restore = [&] {
+            EvaluatorStats &st = evaluator_stats();
+            st.kernel_steps = before.kernel_steps;
+            st.fused_launches = before.fused_launches;
+            st.fused_nodes = before.fused_nodes;
+            st.folded_constants = before.folded_constants;
+            st.view_steps = before.view_steps;
+        };
+        rt.activate();
+        if (mtc_capture_begin(rt.index(), rt.stream()) != MTC_OK) {
+            trace_graph("recording could not start", mtc_last_error());
+            h.disabled = true;
+            return false;
+        }
+        capturing_ = true;
+        capture_unsafe_ = false;
+        pending_.assign(plan_.size(), std::nullopt);
+        installs_.clear();
+        constants_.clear();
+        bool ok = true;
+        try {
+            execute();
+        } catch (const std::exception &e) {
+            trace_graph("recording failed", e.what());
+            ok = false;
+        }
+        capturing_ = false;
+        if (capture_unsafe_) trace_graph("not recorded", "constants run as kernels (no runtime compiler)");
+        ok = ok && !capture_unsafe_;
+        mtc_graph *graph = nullptr;
+        const int rc = mtc_capture_end(ok ? 1 : 0, &graph);
+        reserved_.clear();  // blocks reserved for outputs this plan did not write
+        auto rec = std::make_unique<Recording>();
+        rec->graph = graph;
+        if (ok && (rc != MTC_OK || graph == nullptr)) trace_graph("recording failed", mtc_last_error());
+        if (!ok || rc != MTC_OK || graph == nullptr || mtc_graph_launch(graph) != MTC_OK) {
+            // nothing ran: drop the held-back outputs; the caller evaluates eagerly
+            pending_.clear();
+            installs_.clear();
+            restore();
+            h.disabled = true;
+            return false;
+        }
+        for (const Install &in : installs_) plan_[in.step].output->materialize(std::move(*pending_[in.step]));
+        pending_.clear();
+        rec->device = rt.index();
+        for (const Install &in : installs_)
+            if (!in.view) rec->protect(in.ptr, in.bytes);
+        for (std::size_t i = 0; i < leaves.size(); ++i) {
+            // the leaf's whole buffer (a view may start at an offset)
+            const Value *v = leaf_values_[i];
+            const auto *b = dynamic_cast<const CudaBuffer *>(v->materialization()->buffer_ref().get());
+            rec->protect(const_cast<void *>(leaves[i]), b != nullptr ? b->size_bytes() : 0);
+        }
+        rec->leaves = leaves;
+        rec->installs = std::move(installs_);
+        rec->constants = std::move(constants_);
+        rec->index_kernels = index_kernels_;
+        rec->work = work_between(before, evaluator_stats());
+        watch_index_errors();
+        ++h.captures;
+        ++evaluator_stats().graph_captures;
+        if (h.recordings.size() >= kMaxRecordings) h.recordings.erase(h.recordings.begin());
+        h.recordings.push_back(std::move(rec));
+        return true;
+    }
+
+    bool replay(Recording &r, CudaRuntime &rt) {
+        const int device = rt.index();
+        void *stream = rt.stream();
+        std::vector<BufferRef> taken(r.installs.size());
+        for (std::size_t k = 0; k < r.installs.size(); ++k) {
+            const Install &in = r.installs[k];
+            if (in.view) continue;
+            // blocks taken so far go back to the pool with `taken` on failure
+            if (in.bytes != 0 && mtc_pool_take(device, in.ptr, in.bytes, stream) != MTC_OK) return false;
+            taken[k] = rt.adopt(in.ptr, in.bytes);
+        }
+        for (FusedConstants &fc : r.constants) {
+            bool changed = false;
+            for (std::size_t j = 0; j < fc.steps.size(); ++j) {
+                const float v =
+                    dynamic_cast<const FullPrimitive &>(plan_[fc.steps[j]].node->primitive()).fill_value().get<float>();
+                if (std::memcmp(&v, &fc.values[j], sizeof(float)) != 0) {
+                    fc.values[j] = v;
+                    changed = true;
+                }
+            }
+            if (changed)
+                check(mtc_graph_set_constants(r.graph, fc.index, fc.values.data(), static_cast<int32_t>(fc.values.size())),
+                      "recorded fused constants");
+        }
+        rt.activate();
+        check(mtc_graph_launch(r.graph), "recorded plan");
+        for (std::size_t k = 0; k < r.installs.size(); ++k) {
+            const Install &in = r.installs[k];
+            const Value &out = *plan_[in.step].output;
+            if (in.view) {
+                const Materialization *src = plan_[in.step].node->inputs()[0]->materialization();
+                if (src == nullptr) throw std::logic_error{"recorded view has an unmaterialized input"};
+                out.materialize(Materialization(src->buffer_ref(), *in.layout));
+            } else {
+                out.materialize(Materialization(std::move(taken[k]), Layout::contiguous(out.spec().shape)));
+            }
+        }
+        index_kernels_ = r.index_kernels;
+        index_runtime_ = &rt;
+        watch_index_errors();
+        add_work(evaluator_stats(), r.work);
+        return true;
+    }
+
     const RuntimeRegistry &runtimes_;
     const KernelRegistry &kernels_;
     std::vector<Step> plan_;
     std::vector<Cluster> clusters_;
     std::unordered_map<const Value *, int> index_cache_;
+    bool index_kernels_ = false;
+    DeviceRuntime *index_runtime_ = nullptr;
+    // recording state
+    bool capturing_ = false;
+    bool capture_unsafe_ = false;
+    std::vector<std::optional<Materialization>> pending_;
+    std::vector<Install> installs_;
+    std::vector<FusedConstants> constants_;
+    std::unordered_map<int, BufferRef> reserved_;  // plan step -> block its output goes to
+    std::vector<const Value *> leaf_values_;       // the plan's leaves, in key order
 };
 
 }  // namespace
@@ -441,6 +977,12 @@ class FusedEvaluator {
 bool evaluate_fused(const RuntimeRegistry &runtimes, const KernelRegistry &kernels, std::span<const ValueRef> roots) {
     FusedEvaluator evaluator(runtimes, kernels);
     return evaluator.run(roots);
+}
+
+void clear_graph_cache() {
+    GraphCache &cache = graph_cache();
+    std::lock_guard<std::mutex> lock(cache.mu);
+    cache.plans.clear();
 }
 
 }  // namespace minitensor::detail::cuda

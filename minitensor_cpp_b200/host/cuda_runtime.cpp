@@ -60,6 +60,10 @@ BufferRef CudaRuntime::allocate(std::size_t size_bytes) {
     return std::make_shared<CudaBuffer>(device_, ptr, size_bytes, s);
 }
 
+BufferRef CudaRuntime::adopt(void *data, std::size_t size_bytes) {
+    return std::make_shared<CudaBuffer>(device_, data, size_bytes, stream());
+}
+
 void CudaRuntime::copy_from_host(Buffer &destination, std::size_t destination_offset_bytes,
                                  std::span<const std::byte> source) {
     auto *buffer = dynamic_cast<CudaBuffer *>(&destination);

@@ -55,6 +55,7 @@ class MaxPrimitive final : public Primitive {
         return TensorSpec{reduction_shape(in.shape, axes_, keep_dim_), in.dtype, in.device};
     }
     [[nodiscard]] const std::vector<Shape::size_type> &axes() const noexcept { return axes_; }
+    [[nodiscard]] bool keep_dim() const noexcept { return keep_dim_; }
 
   private:
     std::vector<Shape::size_type> axes_;
@@ -79,6 +80,7 @@ class ArgMaxPrimitive final : public Primitive {
         return TensorSpec{reduction_shape(in.shape, ax, keep_dim_), DType::Int64, in.device};
     }
     [[nodiscard]] Shape::size_type axis() const noexcept { return axis_; }
+    [[nodiscard]] bool keep_dim() const noexcept { return keep_dim_; }
 
   private:
     Shape::size_type axis_;
@@ -242,6 +244,26 @@ void cuda_log_softmax(DeviceRuntime &rt, const Primitive &primitive, std::span<c
 }
 
 }  // namespace
+
+bool write_primitive_key(const Primitive &primitive, std::string &key) {
+    auto put = [&key](std::int64_t v) { key.append(reinterpret_cast<const char *>(&v), sizeof(v)); };
+    if (const auto *p = dynamic_cast<const MaxPrimitive *>(&primitive)) {
+        put(static_cast<std::int64_t>(p->axes().size()));
+        for (auto a : p->axes()) put(static_cast<std::int64_t>(a));
+        put(p->keep_dim() ? 1 : 0);
+        return true;
+    }
+    if (const auto *p = dynamic_cast<const ArgMaxPrimitive *>(&primitive)) {
+        put(static_cast<std::int64_t>(p->axis()));
+        put(p->keep_dim() ? 1 : 0);
+        return true;
+    }
+    if (const auto *p = dynamic_cast<const LogSoftmaxPrimitive *>(&primitive)) {
+        put(static_cast<std::int64_t>(p->axis()));
+        return true;
+    }
+    return false;
+}
 
 void register_extension_kernels(KernelRegistry &registry) {
     registry.register_kernel({MaxPrimitive::ID, DeviceType::Cpu}, cpu_max);

@@ -17,12 +17,14 @@
 
 #include <initializer_list>
 #include <span>
+#include <string>
 
 #include <minitensor/tensor.hpp>
 #include <minitensor/types.hpp>
 
 namespace minitensor::detail {
 class KernelRegistry;
+class Primitive;
 }
 
 namespace minitensor::b200 {
@@ -38,4 +40,7 @@ namespace minitensor::b200 {
 namespace minitensor::detail::ext {
 // CPU and CUDA kernels of the new primitives.
 void register_extension_kernels(KernelRegistry &registry);
+// Appends the parameters of a new primitive to a plan key (axes, keep_dim);
+// false when `primitive` is none of them.
+bool write_primitive_key(const Primitive &primitive, std::string &key);
 }  // namespace minitensor::detail::ext

@@ -525,20 +525,40 @@ int mtb_gather_rows(int device, int64_t rows, int64_t cols, const float *table, 
     });
 }
 
-void mtb_evaluator_stats(uint64_t *out9) {
+void mtb_evaluator_stats(uint64_t *out12) {
 #ifndef MTB_CPU_ONLY
     const auto &s = mt::detail::cuda::evaluator_stats();
-    out9[0] = s.kernel_steps;
-    out9[1] = s.fused_launches;
-    out9[2] = s.fused_nodes;
-    out9[3] = s.folded_constants;
-    out9[4] = s.view_steps;
-    out9[5] = s.evaluations;
-    out9[6] = s.plan_ns;
-    out9[7] = s.execute_ns;
-    out9[8] = s.check_ns;
+    out12[0] = s.kernel_steps;
+    out12[1] = s.fused_launches;
+    out12[2] = s.fused_nodes;
+    out12[3] = s.folded_constants;
+    out12[4] = s.view_steps;
+    out12[5] = s.evaluations;
+    out12[6] = s.plan_ns;
+    out12[7] = s.execute_ns;
+    out12[8] = s.check_ns;
+    out12[9] = s.graph_captures;
+    out12[10] = s.graph_replays;
+    out12[11] = s.graph_fallbacks;
 #else
-    for (int i = 0; i < 9; ++i) out9[i] = 0;
+    for (int i = 0; i < 12; ++i) out12[i] = 0;
+#endif
+}
+
+void mtb_graph_cache_clear(void) {
+#ifndef MTB_CPU_ONLY
+    mt::detail::cuda::clear_graph_cache();
+#endif
+}
+
+int mtb_set_graphs(int on) {
+#ifndef MTB_CPU_ONLY
+    const bool previous = mt::detail::cuda::evaluator_options().graphs;
+    mt::detail::cuda::evaluator_options().graphs = on != 0;
+    return previous ? 1 : 0;
+#else
+    (void)on;
+    return 0;
 #endif
 }
 

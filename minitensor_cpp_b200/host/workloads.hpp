@@ -67,8 +67,12 @@ int mtb_gather_rows(int device, int64_t rows, int64_t cols, const float *table, 
 // Counters of the fusing evaluator (zeros in the CPU-only build):
 // kernel_steps, fused_launches, fused_nodes, folded_constants, view_steps, evaluations,
 // and host nanoseconds spent planning, issuing kernels and in the index-error check.
-void mtb_evaluator_stats(uint64_t *out9);
+void mtb_evaluator_stats(uint64_t *out12);
 void mtb_evaluator_reset_stats(void);
+// Destroys every plan recorded for replay.
+void mtb_graph_cache_clear(void);
+// Turns the replay of repeated plans on or off; returns the previous setting.
+int mtb_set_graphs(int on);
 // 1 when the library has the CUDA backend, 0 for the CPU-only build.
 int mtb_has_cuda(void);
 
