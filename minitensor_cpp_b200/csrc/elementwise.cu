@@ -138,7 +138,11 @@ int plan_elementwise(const mtc_desc *inputs, int n_in, const mtc_desc *outputs, 
         int64_t batch = 1;
         for (int d = 0; d < r - 2; ++d) batch *= s.shape[d];
         const int64_t tiles_y = (s.shape[r - 2] + MTC_EW_TILE - 1) / MTC_EW_TILE;
-        if (out_rows && nt > 0 && batch <= 65535 && tiles_y <= 65535) {
+        const int64_t tiles_x = (s.shape[r - 1] + MTC_EW_TILE - 1) / MTC_EW_TILE;
+        // a handful of tiles leaves the GPU idle while each CTA walks its tile:
+        // below that the one-element-per-thread strided kernel has more in flight
+        const bool enough_tiles = tiles_x * tiles_y * batch >= 32;
+        if (out_rows && nt > 0 && enough_tiles && batch <= 65535 && tiles_y <= 65535) {
             a.transposed = mask;
             a.batch_rank = static_cast<unsigned>(r - 2);
             // 128-bit variant: every operand read or written as float4 along its contiguous axis
@@ -163,8 +167,7 @@ int plan_elementwise(const mtc_desc *inputs, int n_in, const mtc_desc *outputs, 
             if (v4) plan.variant = nt == 1 ? EwVariant::Tiled4x1 : EwVariant::Tiled4x2;
             else plan.variant = nt == 1 ? EwVariant::Tiled1 : EwVariant::Tiled2;
             plan.block = dim3(MTC_EW_TILE_THREADS);
-            plan.grid = dim3(static_cast<unsigned>((s.shape[r - 1] + MTC_EW_TILE - 1) / MTC_EW_TILE),
-                             static_cast<unsigned>(tiles_y), static_cast<unsigned>(batch));
+            plan.grid = dim3(static_cast<unsigned>(tiles_x), static_cast<unsigned>(tiles_y), static_cast<unsigned>(batch));
             return MTC_OK;
         }
     }

@@ -35,7 +35,12 @@ template <> __device__ __forceinline__ float mtc_unary<0x0103>(float x) { return
 template <> __device__ __forceinline__ float mtc_unary<0x0104>(float x) { return expf(x); }
 template <> __device__ __forceinline__ float mtc_unary<0x0105>(float x) { return logf(x); }
 template <> __device__ __forceinline__ float mtc_unary<0x0106>(float x) { return __fsqrt_rn(x); }
-template <> __device__ __forceinline__ float mtc_unary<0x0107>(float x) { return tanhf(x); }
+// tanh in double, rounded once: (nearly always) the correctly rounded float, so
+// the result stays within the host libm's own error of the CPU reference (the
+// float tanhf of either library alone can sit 3 ulp from the other's)
+template <> __device__ __forceinline__ float mtc_unary<0x0107>(float x) {
+    return __double2float_rn(tanh(static_cast<double>(x)));
+}
 template <> __device__ __forceinline__ float mtc_unary<0x0108>(float x) {
     // branch form of the CPU sigmoid (kernels.cpp:113-124)
     if (x >= 0.0f) {

@@ -185,9 +185,83 @@ __global__ void __launch_bounds__(128) k_gemm_small_exact(const GemmProblem p) {
     }
 }
 
+// Small problems with a long contraction: a 16x16 output tile per CTA, the A
+// and B panels of the tile staged in shared memory by all 256 threads at once
+// (coalesced along whichever axis has unit stride), then each thread runs its
+// output's k loop in the reference's order from shared memory.  The loads of a
+// panel are all in flight together, so the latency of memory is paid once per
+// chunk of kSmallKc k values instead of once per sixteen.
+constexpr int kSmallT = 16;     // output tile edge
+constexpr int kSmallPad = 17;   // shared row pitch: conflict-free stores along k
+constexpr int kSmallKc = 360;   // k values per staged chunk: 2 * 360 * 17 * 4 B = 48960 B
+
+__global__ void __launch_bounds__(256) k_gemm_small_staged(const GemmProblem p) {
+    __shared__ float As[kSmallKc * kSmallPad];  // As[k * pad + m]
+    __shared__ float Bs[kSmallKc * kSmallPad];  // Bs[k * pad + n]
+    const int t = threadIdx.x;
+    const int tm = t / kSmallT, tn = t % kSmallT;
+    const long long m0 = static_cast<long long>(blockIdx.y) * kSmallT;
+    const long long n0 = static_cast<long long>(blockIdx.x) * kSmallT;
+    long long ao = p.a_off, bo = p.b_off, co = p.c_off;
+    long long rem = blockIdx.z;
+    for (int d = p.batch_rank - 1; d >= 0; --d) {
+        const long long c = rem % p.batch_shape[d];
+        rem /= p.batch_shape[d];
+        ao += c * p.a_bs[d];
+        bo += c * p.b_bs[d];
+        co += c * p.c_bs[d];
+    }
+    const int mt = static_cast<int>(p.M - m0 < kSmallT ? p.M - m0 : kSmallT);
+    const int nt = static_cast<int>(p.N - n0 < kSmallT ? p.N - n0 : kSmallT);
+    const bool a_kfast = p.a_cs == 1 && p.a_rs != 1;  // A rows contiguous along k
+    const bool b_kfast = p.b_rs == 1 && p.b_cs != 1;  // B columns contiguous along k
+    float acc = 0.0f;
+    for (long long k0 = 0; k0 < p.K; k0 += kSmallKc) {
+        const int kn = static_cast<int>(p.K - k0 < kSmallKc ? p.K - k0 : kSmallKc);
+        const int na = mt * kn, nb = nt * kn;
+        for (int i = t; i < na; i += 256) {
+            const int m = a_kfast ? i / kn : i % mt;
+            const int k = a_kfast ? i % kn : i / mt;
+            As[k * kSmallPad + m] = __ldg(p.A + ao + (m0 + m) * p.a_rs + (k0 + k) * p.a_cs);
+        }
+        for (int i = t; i < nb; i += 256) {
+            const int n = b_kfast ? i / kn : i % nt;
+            const int k = b_kfast ? i % kn : i / nt;
+            Bs[k * kSmallPad + n] = __ldg(p.B + bo + (k0 + k) * p.b_rs + (n0 + n) * p.b_cs);
+        }
+        __syncthreads();
+        if (tm < mt && tn < nt) {
+            // the reference's rounding and order: float product, float sum, k ascending
+            int k = 0;
+            for (; k + 4 <= kn; k += 4) {
+                const float a0 = As[k * kSmallPad + tm], b0 = Bs[k * kSmallPad + tn];
+                const float a1 = As[(k + 1) * kSmallPad + tm], b1 = Bs[(k + 1) * kSmallPad + tn];
+                const float a2 = As[(k + 2) * kSmallPad + tm], b2 = Bs[(k + 2) * kSmallPad + tn];
+                const float a3 = As[(k + 3) * kSmallPad + tm], b3 = Bs[(k + 3) * kSmallPad + tn];
+                acc = __fadd_rn(acc, __fmul_rn(a0, b0));
+                acc = __fadd_rn(acc, __fmul_rn(a1, b1));
+                acc = __fadd_rn(acc, __fmul_rn(a2, b2));
+                acc = __fadd_rn(acc, __fmul_rn(a3, b3));
+            }
+            for (; k < kn; ++k) acc = __fadd_rn(acc, __fmul_rn(As[k * kSmallPad + tm], Bs[k * kSmallPad + tn]));
+        }
+        __syncthreads();
+    }
+    if (tm < mt && tn < nt) p.C[co + (m0 + tm) * p.c_rs + (n0 + tn) * p.c_cs] = acc;
+}
+
 int gemm_simt(const GemmProblem &p, cudaStream_t stream, bool exact) {
     if (p.M == 0 || p.N == 0 || p.batch == 0) return MTC_OK;
     const double work = double(p.batch) * double(p.M) * double(p.N) * double(p.K);
+    const long long tiles_m = (p.M + kSmallT - 1) / kSmallT, tiles_n = (p.N + kSmallT - 1) / kSmallT;
+    // staged tiles pay off when a tile holds a warp's worth of outputs and k is long
+    const bool staged_fits = (p.M < kSmallT ? p.M : kSmallT) * (p.N < kSmallT ? p.N : kSmallT) >= 32 &&
+                             p.K >= 32 && tiles_m <= 65535 && p.batch <= 65535;
+    if (exact && work <= double(1 << 22) && staged_fits) {
+        const dim3 grid(static_cast<unsigned>(tiles_n), static_cast<unsigned>(tiles_m), static_cast<unsigned>(p.batch));
+        k_gemm_small_staged<<<grid, 256, 0, stream>>>(p);
+        return check_launch("small staged exact GEMM");
+    }
     if (exact && work <= double(1 << 22)) {
         const long long total = p.batch * p.M * p.N;
         long long blocks = (total + 127) / 128;

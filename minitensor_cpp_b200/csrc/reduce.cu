@@ -582,6 +582,71 @@ __global__ void __launch_bounds__(128) k_exact_small(const RedArgs a) {
     }
 }
 
+// Offset of the reduced element with walk index r from its output's base (the
+// reduced axes row-major, the order walk_reduced visits them in).
+__device__ __forceinline__ long long reduced_offset(const RedArgs &a, long long r) {
+    long long off = 0;
+    for (int d = a.rrank - 1; d >= 0; --d) {
+        const long long c = r % a.rshape[d];
+        r /= a.rshape[d];
+        off += c * a.rstr[d];
+    }
+    return off;
+}
+
+constexpr int kStagedFloats = 12288;  // 48 KB of shared memory per CTA
+
+// Small reductions whose outputs each read many elements (bias gradients,
+// means): a CTA stages the inputs of up to G consecutive outputs in shared
+// memory with all of its threads, coalesced along the kept axis when that is
+// contiguous and along the reduced axis otherwise, so the loads are in flight
+// together.  Then one thread per output combines its elements from shared
+// memory in the reference's order, exactly as k_exact_small does from memory.
+template <int OP>
+__global__ void __launch_bounds__(256) k_exact_staged(const RedArgs a, int G) {
+    extern __shared__ float tile[];  // tile[r * gp + g]: conflict-free for both phases
+    const long long o0 = static_cast<long long>(blockIdx.x) * G;
+    const int gn = static_cast<int>(a.nout - o0 < G ? a.nout - o0 : G);
+    const int gp = G == 1 ? 1 : G + 1;
+    const long long R = a.R;
+    const bool kept_fast = a.krank > 0 && a.kstr[a.krank - 1] == 1 && gn > 1;
+    const long long total = static_cast<long long>(gn) * R;
+    for (long long i = threadIdx.x; i < total; i += blockDim.x) {
+        const long long g = kept_fast ? i % gn : i / R;
+        const long long r = kept_fast ? i / gn : i % R;
+        const long long off = kept_offset(a, static_cast<unsigned int>(o0 + g)) + reduced_offset(a, r);
+        tile[r * gp + g] = __ldg(a.in + off);
+    }
+    __syncthreads();
+    const int t = threadIdx.x;
+    if (t >= gn) return;
+    const long long o = o0 + t;
+    if constexpr (OP == MTC_OP_LOGSUMEXP) {
+        float mx = -INFINITY;
+        bool nan = false;
+        for (long long r = 0; r < R; ++r) {
+            const float x = tile[r * gp + t];
+            if (x != x) nan = true;
+            else mx = (mx < x) ? x : mx;  // std::max(mx, x)
+        }
+        float result;
+        if (nan) {
+            result = NAN;
+        } else if (isinf(mx)) {
+            result = mx;
+        } else {
+            float s = 0.0f;
+            for (long long r = 0; r < R; ++r) s = __fadd_rn(s, expf(__fsub_rn(tile[r * gp + t], mx)));
+            result = __fadd_rn(mx, logf(s));
+        }
+        static_cast<float *>(a.out)[a.out_off + o] = result;
+    } else {
+        State s = Reducer<OP>::init();
+        for (long long r = 0; r < R; ++r) Reducer<OP>::add(s, tile[r * gp + t], r);
+        store_result<OP>(a, o, s);
+    }
+}
+
 // Merges the chunk partials of every output in chunk order.
 template <int OP>
 __global__ void __launch_bounds__(256) k_finalize(const RedArgs a) {
@@ -788,6 +853,15 @@ int run_reduction(RedPlan &p, cudaStream_t stream) {
     const int sms = sm_count(current_device());
     if (a.R <= 8192 && a.nout * a.R <= (1LL << 21)) {
         // small: the reference's own order and rounding
+        if (a.R >= 32) {
+            // long walks: stage up to 32 outputs' elements per CTA in shared memory
+            const int G = a.R * 2 <= kStagedFloats ? static_cast<int>(std::min<long long>(32, kStagedFloats / a.R - 1)) : 1;
+            const int gp = G == 1 ? 1 : G + 1;
+            const long long blocks = (a.nout + G - 1) / G;
+            const size_t smem = static_cast<size_t>(a.R) * gp * sizeof(float);
+            k_exact_staged<OP><<<static_cast<unsigned>(blocks), 256, smem, stream>>>(a, G);
+            return check_launch("staged exact reduction");
+        }
         long long blocks = (a.nout + 127) / 128;
         if (blocks > static_cast<long long>(sms) * 16) blocks = static_cast<long long>(sms) * 16;
         k_exact_small<OP><<<static_cast<unsigned>(blocks < 1 ? 1 : blocks), 128, 0, stream>>>(a);

@@ -103,10 +103,12 @@ UNARY_ULP = {abi.ABS: 0, abi.SIGN: 0, abi.NEGATE: 0, abi.SQRT: 0, abi.EXP: 2, ab
 def _unary_layouts(rng, kind):
     base = rng.uniform(0.01, 20, 5000) if kind == "positive" else rng.uniform(-40, 40, 5000)
     st = np.concatenate([SPECIAL, base.astype(F)])
+    big = (rng.uniform(0.01, 20, 400 * 330) if kind == "positive" else rng.uniform(-40, 40, 400 * 330)).astype(F)
     return [
         hv(st, [st.size]),                                   # contiguous, 128-bit path
         hv(st, [50, 40], [40, 1], 3),                        # misaligned offset -> scalar flat path
-        hv(st, [40, 50], [1, 40], 0),                        # transposed view -> tiled path
+        hv(st, [40, 50], [1, 40], 0),                        # small transposed view -> strided path
+        hv(big, [400, 330], [1, 400], 0),                    # transposed view of 42 tiles -> tiled path
         hv(st, [20, 30], [-60, 2], 19 * 60),                 # negative + stride-2 -> generic strided path
     ]
 
@@ -163,12 +165,15 @@ def test_binary_vs_reference(cuda, op):
     b_st = rng.uniform(-50, 50, 200 * 301).astype(F)
     row = rng.uniform(-5, 5, 301).astype(F)
     col = rng.uniform(-5, 5, 200).astype(F)
+    big_a = rng.uniform(-50, 50, 300 * 401).astype(F)
+    big_b = rng.uniform(-50, 50, 300 * 401).astype(F)
     cases = [
         (hv(a_st, [200, 301]), hv(b_st, [200, 301])),                      # same shape, contiguous
         (hv(a_st, [200, 301]), hv(row, [1, 301])),                          # row broadcast
         (hv(a_st, [200, 301]), hv(col, [200, 1])),                          # column broadcast
-        (hv(a_st, [200, 301]), hv(b_st, [200, 301], [1, 200])),             # transposed rhs (tiled)
-        (hv(b_st, [200, 301], [1, 200]), hv(a_st, [200, 301], [1, 200])),   # both transposed
+        (hv(a_st, [200, 301]), hv(b_st, [200, 301], [1, 200])),             # transposed rhs, 20 tiles (strided)
+        (hv(big_a, [300, 401]), hv(big_b, [300, 401], [1, 300])),           # transposed rhs, 35 tiles (tiled)
+        (hv(big_b, [300, 401], [1, 300]), hv(big_a, [300, 401], [1, 300])), # both transposed (tiled)
         (hv(np.array([2.5], F), []), hv(a_st, [200, 301])),                 # scalar lhs
         (hv(a_st, [100, 301], [-602, 1], 199 * 301), hv(row, [301])),       # negative stride, rank-1 rhs
     ]
@@ -220,7 +225,7 @@ def test_fused_tiled_transposes_batched_two_outputs(cuda, offset):
     operand 16-byte aligned (the float4 tile kernel), offset 1 does not (the
     scalar tile kernel).  Only +, * and relu: bit-exact against numpy."""
     rng = np.random.default_rng(21)
-    b, n, m = 3, 100, 132
+    b, n, m = 3, 200, 260  # 4 x 5 tiles per batch entry, partial at both edges
     st = lambda: rng.uniform(-1, 1, b * n * m + offset).astype(F)
     P, Q, R = st(), st(), st()
     colv = rng.uniform(-1, 1, b * n).astype(F)
@@ -585,9 +590,18 @@ def test_descriptor_validation_rejects_out_of_bounds_views(cuda):
 def test_exact_simt_gemm_is_bit_identical_to_reference(cuda):
     """MTC_GEMM_SIMT rounds like the CPU (float product, float sum, k ascending)."""
     rng = np.random.default_rng(41)
-    for sa, sb, bt in (([33, 70], [70, 45], False), ([129, 257], [257, 131], True), ([7], [7, 3], False),
-                       ([2, 3, 17, 19], [19, 23], False)):
-        a = hv(rng.standard_normal(int(np.prod(sa))).astype(F), sa)
+    # (lhs shape, rhs shape, lhs transposed view, rhs transposed view); the small
+    # ones take the shared-memory staged kernel (K >= 32, a warp of outputs per
+    # tile), the spiral model's weight gradients among them (xT . G, K = 300)
+    cases = (([33, 70], [70, 45], False, False), ([129, 257], [257, 131], False, True), ([7], [7, 3], False, False),
+             ([2, 3, 17, 19], [19, 23], False, False), ([64, 300], [300, 64], True, False),
+             ([300, 64], [64, 64], False, True), ([2, 300], [300, 64], True, False), ([8, 1000], [1000, 8], False, True),
+             ([3, 40, 300], [300, 24], False, False))
+    for sa, sb, at, bt in cases:
+        if at:
+            a = hv(rng.standard_normal(int(np.prod(sa))).astype(F), sa, [1, sa[0]])
+        else:
+            a = hv(rng.standard_normal(int(np.prod(sa))).astype(F), sa)
         if bt:
             b = hv(rng.standard_normal(int(np.prod(sb))).astype(F), sb, [1, sb[0]])
         else:
@@ -602,11 +616,19 @@ def test_small_sums_are_bit_identical_to_reference(cuda):
     rng = np.random.default_rng(43)
     # reductions of at most 8192 elements per output and 2^21 in all take the
     # reference's sequential order (the spiral model's bias gradients and loss mean)
-    x = hv(rng.standard_normal(60 * 64).astype(F), [60, 64])
-    for axes in ([0], [1], [0, 1]):
+    cases = [(hv(rng.standard_normal(60 * 64).astype(F), [60, 64]), axes) for axes in ([0], [1], [0, 1])]
+    cases += [
+        (hv(rng.standard_normal(300 * 64).astype(F), [300, 64]), [0]),          # bias gradient, staged
+        (hv(rng.standard_normal(300 * 3).astype(F), [300, 3]), [0]),            # three long columns
+        (hv(rng.standard_normal(300).astype(F), [300]), [0]),                   # a loss mean's sum
+        (hv(rng.standard_normal(64 * 300).astype(F), [300, 64], [1, 300]), [0]),  # transposed storage
+        (hv(rng.standard_normal(6 * 50 * 8).astype(F), [6, 50, 8]), [0, 2]),     # two reduced axes
+        (hv(rng.standard_normal(300 * 10).astype(F), [300, 10]), [1]),          # short rows: per-thread kernel
+    ]
+    for x, axes in cases:
         kept = [e for d, e in enumerate(x.shape) if d not in axes]
         ref = out_like(kept)
         rk.reduce(abi.SUM, x, axes, False, ref)
         out = gpu(out_like(kept))
         abi.reduce(abi.SUM, gpu(x), axes, out)
-        assert_bits(host(out)[: ref.storage.size], ref.storage, f"small sum {axes}")
+        assert_bits(host(out)[: ref.storage.size], ref.storage, f"small sum {x.shape} {axes}")
