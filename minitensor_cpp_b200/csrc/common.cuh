@@ -105,6 +105,16 @@ inline FastDiv make_fastdiv(uint32_t d) {
 }
 
 #ifdef __CUDACC__
+// Asynchronous 4-byte global -> shared copy (sm_80+ cp.async): a thread issues
+// any number of them back to back and waits once, so staging loops do not
+// pay one memory latency per element.
+__device__ __forceinline__ void cp_async4(float *smem, const float *gmem) {
+    const unsigned int dst = static_cast<unsigned int>(__cvta_generic_to_shared(smem));
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(dst), "l"(gmem) : "memory");
+}
+// Waits for every cp.async the calling thread issued.
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t fastdiv(uint32_t n, const FastDiv &f) {
     if (f.d <= 1) return n;
     uint32_t t = __umulhi(n, f.mul);

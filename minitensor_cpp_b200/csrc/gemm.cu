@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(128) k_gemm_small_exact(const GemmProblem p) {
 
 // Small problems with a long contraction: a 16x16 output tile per CTA, the A
 // and B panels of the tile staged in shared memory by all 256 threads at once
-// (coalesced along whichever axis has unit stride), then each thread runs its
+// (asynchronous copies, coalesced along whichever axis has unit stride), then each thread runs its
 // output's k loop in the reference's order from shared memory.  The loads of a
 // panel are all in flight together, so the latency of memory is paid once per
 // chunk of kSmallKc k values instead of once per sixteen.
@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(256) k_gemm_small_staged(const GemmProblem p) 
     __shared__ float As[kSmallKc * kSmallPad];  // As[k * pad + m]
     __shared__ float Bs[kSmallKc * kSmallPad];  // Bs[k * pad + n]
     const int t = threadIdx.x;
-    const int tm = t / kSmallT, tn = t % kSmallT;
+    const int tm = t / kSmallT, tn = t % kSmallT;  // this thread's output in the tile
     const long long m0 = static_cast<long long>(blockIdx.y) * kSmallT;
     const long long n0 = static_cast<long long>(blockIdx.x) * kSmallT;
     long long ao = p.a_off, bo = p.b_off, co = p.c_off;
@@ -218,17 +218,27 @@ __global__ void __launch_bounds__(256) k_gemm_small_staged(const GemmProblem p) 
     float acc = 0.0f;
     for (long long k0 = 0; k0 < p.K; k0 += kSmallKc) {
         const int kn = static_cast<int>(p.K - k0 < kSmallKc ? p.K - k0 : kSmallKc);
-        const int na = mt * kn, nb = nt * kn;
-        for (int i = t; i < na; i += 256) {
-            const int m = a_kfast ? i / kn : i % mt;
-            const int k = a_kfast ? i % kn : i / mt;
-            As[k * kSmallPad + m] = __ldg(p.A + ao + (m0 + m) * p.a_rs + (k0 + k) * p.a_cs);
+        // coalesced along whichever axis has unit stride; no division per element
+        const int lane = t % 32, warp = t / 32;
+        if (a_kfast) {
+            for (int m = warp; m < mt; m += 8)
+                for (int k = lane; k < kn; k += 32)
+                    cp_async4(&As[k * kSmallPad + m], p.A + ao + (m0 + m) * p.a_rs + (k0 + k) * p.a_cs);
+        } else {
+            const int m = t % kSmallT;
+            for (int k = t / kSmallT; k < kn; k += 256 / kSmallT)
+                if (m < mt) cp_async4(&As[k * kSmallPad + m], p.A + ao + (m0 + m) * p.a_rs + (k0 + k) * p.a_cs);
         }
-        for (int i = t; i < nb; i += 256) {
-            const int n = b_kfast ? i / kn : i % nt;
-            const int k = b_kfast ? i % kn : i / nt;
-            Bs[k * kSmallPad + n] = __ldg(p.B + bo + (k0 + k) * p.b_rs + (n0 + n) * p.b_cs);
+        if (b_kfast) {
+            for (int n = warp; n < nt; n += 8)
+                for (int k = lane; k < kn; k += 32)
+                    cp_async4(&Bs[k * kSmallPad + n], p.B + bo + (k0 + k) * p.b_rs + (n0 + n) * p.b_cs);
+        } else {
+            const int n = t % kSmallT;
+            for (int k = t / kSmallT; k < kn; k += 256 / kSmallT)
+                if (n < nt) cp_async4(&Bs[k * kSmallPad + n], p.B + bo + (k0 + k) * p.b_rs + (n0 + n) * p.b_cs);
         }
+        cp_async_wait_all();
         __syncthreads();
         if (tm < mt && tn < nt) {
             // the reference's rounding and order: float product, float sum, k ascending

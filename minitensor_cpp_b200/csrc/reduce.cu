@@ -614,9 +614,9 @@ constexpr int kStagedFloats = 12288;  // 48 KB of shared memory per CTA
 
 // Small reductions whose outputs each read many elements (bias gradients,
 // means): a CTA stages the inputs of up to G consecutive outputs in shared
-// memory with all of its threads, coalesced along the kept axis when that is
-// contiguous and along the reduced axis otherwise, so the loads are in flight
-// together.  Then one thread per output combines its elements from shared
+// memory with all of its threads (asynchronous copies, coalesced along the
+// kept axis when that is contiguous and along the reduced axis otherwise), so
+// the loads are in flight together.  Then one thread per output combines its elements from shared
 // memory in the reference's order, exactly as k_exact_small does from memory.
 template <int OP>
 __global__ void __launch_bounds__(256) k_exact_staged(const RedArgs a, int G) {
@@ -624,24 +624,40 @@ __global__ void __launch_bounds__(256) k_exact_staged(const RedArgs a, int G) {
     const long long o0 = static_cast<long long>(blockIdx.x) * G;
     const int gn = static_cast<int>(a.nout - o0 < G ? a.nout - o0 : G);
     const int gp = G == 1 ? 1 : G + 1;
-    const long long R = a.R;
-    const bool kept_fast = a.krank > 0 && a.kstr[a.krank - 1] == 1 && gn > 1;
-    const long long total = static_cast<long long>(gn) * R;
-    for (long long i = threadIdx.x; i < total; i += blockDim.x) {
-        const long long g = kept_fast ? i % gn : i / R;
-        const long long r = kept_fast ? i / gn : i % R;
-        const long long off = kept_offset(a, static_cast<unsigned int>(o0 + g)) + reduced_offset(a, r);
-        tile[r * gp + g] = __ldg(a.in + off);
+    const int R = static_cast<int>(a.R);  // <= 8192
+    const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+    const bool one_axis = a.rrank == 1;
+    const long long rs = a.rstr[0];
+    if (a.krank > 0 && a.kstr[a.krank - 1] == 1 && gn > 1) {
+        // consecutive outputs are contiguous: lanes take outputs, warps take rows
+        if (lane < gn) {
+            const long long base = kept_offset(a, static_cast<unsigned int>(o0 + lane));
+            for (int r = warp; r < R; r += 8) {
+                const long long off = one_axis ? base + r * rs : base + reduced_offset(a, r);
+                cp_async4(&tile[r * gp + lane], a.in + off);
+            }
+        }
+    } else {
+        // lanes walk the reduced elements of one output, warps take outputs
+        for (int g = warp; g < gn; g += 8) {
+            const long long base = kept_offset(a, static_cast<unsigned int>(o0 + g));
+            for (int r = lane; r < R; r += 32) {
+                const long long off = one_axis ? base + r * rs : base + reduced_offset(a, r);
+                cp_async4(&tile[r * gp + g], a.in + off);
+            }
+        }
     }
+    cp_async_wait_all();
     __syncthreads();
     const int t = threadIdx.x;
     if (t >= gn) return;
     const long long o = o0 + t;
+    const float *col = tile + t;
     if constexpr (OP == MTC_OP_LOGSUMEXP) {
         float mx = -INFINITY;
         bool nan = false;
-        for (long long r = 0; r < R; ++r) {
-            const float x = tile[r * gp + t];
+        for (int r = 0; r < R; ++r) {
+            const float x = col[r * gp];
             if (x != x) nan = true;
             else mx = (mx < x) ? x : mx;  // std::max(mx, x)
         }
@@ -652,13 +668,22 @@ __global__ void __launch_bounds__(256) k_exact_staged(const RedArgs a, int G) {
             result = mx;
         } else {
             float s = 0.0f;
-            for (long long r = 0; r < R; ++r) s = __fadd_rn(s, expf(__fsub_rn(tile[r * gp + t], mx)));
+            for (int r = 0; r < R; ++r) s = __fadd_rn(s, expf(__fsub_rn(col[r * gp], mx)));
             result = __fadd_rn(mx, logf(s));
         }
         static_cast<float *>(a.out)[a.out_off + o] = result;
     } else {
         State s = Reducer<OP>::init();
-        for (long long r = 0; r < R; ++r) Reducer<OP>::add(s, tile[r * gp + t], r);
+        int r = 0;
+        // eight shared-memory reads ahead of the in-order updates
+        for (; r + 8 <= R; r += 8) {
+            float x[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) x[u] = col[(r + u) * gp];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) Reducer<OP>::add(s, x[u], r + u);
+        }
+        for (; r < R; ++r) Reducer<OP>::add(s, col[r * gp], r);
         store_result<OP>(a, o, s);
     }
 }

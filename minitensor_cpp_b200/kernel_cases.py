@@ -6,6 +6,7 @@
     python -m minitensor_cpp_b200.kernel_cases log_softmax --n 8192
     python -m minitensor_cpp_b200.kernel_cases gather --rows 16777216 --cols 64
     python -m minitensor_cpp_b200.kernel_cases adamw --numel 150823912
+    python -m minitensor_cpp_b200.kernel_cases spiral --steps 500 [--eager]
 
 Each case allocates its operands on cuda:0 with torch (device memory only),
 calls the C ABI `--reps` times back to back (prepared calls) on the current stream, synchronises, checks
@@ -137,8 +138,29 @@ def case_adamw(a, torch, stream):
     return {"ms": ms, "gbs": 28.0 * n / ms / 1e6}
 
 
+def case_spiral(a, torch, stream):
+    """The spiral MLP (300 points, 2-64-64-3, Adam) through MiniTensor's API:
+    --warm-steps untimed steps, then --steps timed ones (host clock; the call
+    returns after the final parameters are on the host).  Plans repeat from
+    step to step, so they are replayed as CUDA graphs unless --eager."""
+    from .frontend import Frontend
+
+    fe = Frontend()
+    fe.set_graphs(not a.eager)
+    fe.spiral_train(0, a.warm_steps, loss_every=0)
+    n0 = abi.launch_count()
+    fe.reset_stats()
+    _, secs = fe.spiral_train(0, a.steps, loss_every=0)
+    st = fe.stats()
+    return {"ms_per_step": secs * 1e3 / max(a.steps, 1), "samples_per_s": 300 * a.steps / secs,
+            "launches_per_step": (abi.launch_count() - n0) / max(a.steps, 1),
+            "replays": st["graph_replays"], "evaluations": st["evaluations"],
+            "plan_us_per_step": st["plan_ns"] / 1e3 / max(a.steps, 1),
+            "execute_us_per_step": st["execute_ns"] / 1e3 / max(a.steps, 1)}
+
+
 CASES = {"gemm": case_gemm, "chain": case_chain, "reduce": case_reduce, "log_softmax": case_log_softmax,
-         "gather": case_gather, "adamw": case_adamw}
+         "gather": case_gather, "adamw": case_adamw, "spiral": case_spiral}
 
 
 def main(argv=None) -> int:
@@ -157,6 +179,9 @@ def main(argv=None) -> int:
     p.add_argument("--reps", type=int, default=3)
     p.add_argument("--numel", type=int, default=150823912, help="adamw: parameter count")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--steps", type=int, default=500, help="spiral: timed training steps")
+    p.add_argument("--warm-steps", type=int, default=20, help="spiral: untimed training steps first")
+    p.add_argument("--eager", action="store_true", help="spiral: no plan replay")
     p.add_argument("--warm-s", type=float, default=0.3, help="untimed calls before timing (0 under a profiler)")
     a = p.parse_args(argv)
     global WARM_S
