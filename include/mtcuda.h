@@ -311,6 +311,9 @@ int mtc_graph_destroy(mtc_graph *graph);
  * mtc_alloc would.  MTC_OK when it was free, reusable on `stream` and large
  * enough; MTC_ERR_UNSUPPORTED (nothing changes) otherwise. */
 int mtc_pool_take(int device, void *ptr, size_t bytes, void *stream);
+/* mtc_pool_take for `n` blocks at once, under one lock: all are taken
+ * (MTC_OK) or none (MTC_ERR_UNSUPPORTED; *failed = the first that was not free). */
+int mtc_pool_take_many(int device, void *const *ptrs, const size_t *bytes, int32_t n, void *stream, int32_t *failed);
 /* Adds `delta` to the protection count of the pool block at `ptr`.  While the
  * count is positive the block, once released, is kept for mtc_pool_take
  * (the replays of the graphs that use it) instead of being handed to other

@@ -226,11 +226,10 @@ int pool_protect(int device, void *ptr, int delta) {
     return MTC_OK;
 }
 
-int pool_take(int device, void *ptr, size_t bytes, cudaStream_t stream) {
-    DevicePool &pool = pool_of(device);
+// Takes the free block at `ptr` back for a request of `bytes` on `stream`;
+// the caller holds pool.mu.
+int take_locked(DevicePool &pool, int device, void *ptr, size_t bytes, cudaStream_t stream) {
     const size_t want = round_request(bytes);
-    std::lock_guard<std::mutex> lock(pool.mu);
-    if (!pool.pending.empty()) collect_pending(pool);
     auto f = pool.free_at.find(ptr);
     if (f == pool.free_at.end()) return fail(MTC_ERR_UNSUPPORTED, "device %d: %p is not a free block", device, ptr);
     DevicePool::FreeList *fl = f->second.first;
@@ -244,6 +243,35 @@ int pool_take(int device, void *ptr, size_t bytes, cudaStream_t stream) {
     pool.cached -= b.size;
     b.stream = stream;
     pool.live.emplace(b.ptr, b);
+    return MTC_OK;
+}
+
+int pool_take(int device, void *ptr, size_t bytes, cudaStream_t stream) {
+    DevicePool &pool = pool_of(device);
+    std::lock_guard<std::mutex> lock(pool.mu);
+    if (!pool.pending.empty()) collect_pending(pool);
+    return take_locked(pool, device, ptr, bytes, stream);
+}
+
+// Takes all of `n` blocks or none.
+int pool_take_many(int device, void *const *ptrs, const size_t *bytes, int n, cudaStream_t stream, int *failed) {
+    DevicePool &pool = pool_of(device);
+    std::lock_guard<std::mutex> lock(pool.mu);
+    if (!pool.pending.empty()) collect_pending(pool);
+    for (int i = 0; i < n; ++i) {
+        const int rc = take_locked(pool, device, ptrs[i], bytes[i], stream);
+        if (rc == MTC_OK) continue;
+        *failed = i;
+        // hand back what was taken, to this stream's free list (or parked)
+        for (int j = 0; j < i; ++j) {
+            auto it = pool.live.find(ptrs[j]);
+            Block b = it->second;
+            pool.live.erase(it);
+            pool.cached += b.size;
+            pool.put_free(stream, b);
+        }
+        return rc;
+    }
     return MTC_OK;
 }
 
@@ -663,6 +691,16 @@ int mtc_pool_take(int device, void *ptr, size_t bytes, void *stream) {
     if (device < 0) return fail(MTC_ERR_INVALID_ARGUMENT, "negative device index");
     if (ptr == nullptr || bytes == 0) return fail(MTC_ERR_INVALID_ARGUMENT, "nothing to take");
     return pool_take(device, ptr, bytes, static_cast<cudaStream_t>(stream));
+}
+
+int mtc_pool_take_many(int device, void *const *ptrs, const size_t *bytes, int32_t n, void *stream, int32_t *failed) {
+    clear_error();
+    if (device < 0 || n < 0 || (n > 0 && (ptrs == nullptr || bytes == nullptr)))
+        return fail(MTC_ERR_INVALID_ARGUMENT, "bad block list");
+    int bad = -1;
+    const int rc = pool_take_many(device, ptrs, bytes, n, static_cast<cudaStream_t>(stream), &bad);
+    if (failed) *failed = bad;
+    return rc;
 }
 
 int mtc_pool_protect(int device, void *ptr, int32_t delta) {

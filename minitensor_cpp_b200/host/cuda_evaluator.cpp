@@ -84,6 +84,59 @@ constexpr std::uint32_t kScatterAddId = 0x0209;
 bool is_unary_id(std::uint32_t id) { return id >= 0x0101 && id <= 0x0108; }
 bool is_binary_id(std::uint32_t id) { return id >= 0x0110 && id <= 0x0114; }
 
+// Open-addressing map from graph values to plan positions.  A plan visits a
+// few hundred values per evaluation; std::unordered_map's node allocations and
+// the copy of the planner's map cost a third of the host time of planning.
+class ValueIndex {
+  public:
+    // Position of `v`, or nullptr when absent.
+    int *find(const Value *v) {
+        if (keys_.empty()) return nullptr;
+        for (std::size_t i = slot(v);; i = (i + 1) & mask_) {
+            if (keys_[i] == v) return &vals_[i];
+            if (keys_[i] == nullptr) return nullptr;
+        }
+    }
+    const int *find(const Value *v) const { return const_cast<ValueIndex *>(this)->find(v); }
+    // Inserts (v, value) when absent; returns the stored value and whether it was inserted.
+    std::pair<int *, bool> emplace(const Value *v, int value) {
+        if (2 * (size_ + 1) > keys_.size()) grow();
+        for (std::size_t i = slot(v);; i = (i + 1) & mask_) {
+            if (keys_[i] == v) return {&vals_[i], false};
+            if (keys_[i] == nullptr) {
+                keys_[i] = v;
+                vals_[i] = value;
+                ++size_;
+                return {&vals_[i], true};
+            }
+        }
+    }
+
+  private:
+    std::size_t slot(const Value *v) const {
+        auto x = static_cast<std::uint64_t>(reinterpret_cast<std::uintptr_t>(v));
+        x ^= x >> 33;
+        x *= 0xff51afd7ed558ccdULL;
+        x ^= x >> 33;
+        return static_cast<std::size_t>(x) & mask_;
+    }
+    void grow() {
+        std::vector<const Value *> keys = std::move(keys_);
+        std::vector<int> vals = std::move(vals_);
+        const std::size_t cap = keys.empty() ? 256 : 2 * keys.size();
+        keys_.assign(cap, nullptr);
+        vals_.assign(cap, 0);
+        mask_ = cap - 1;
+        size_ = 0;
+        for (std::size_t i = 0; i < keys.size(); ++i)
+            if (keys[i] != nullptr) emplace(keys[i], vals[i]);
+    }
+    std::vector<const Value *> keys_;
+    std::vector<int> vals_;
+    std::size_t size_ = 0;
+    std::size_t mask_ = 0;
+};
+
 struct Step {
     ValueRef output;
     const Node *node = nullptr;
@@ -95,8 +148,7 @@ struct Step {
     bool folded = false;   // constant folded into the clusters of its consumers
     bool materialize = false;
     int cluster = -1;
-    std::vector<int> consumers;
-    int internal_refs = 0;
+    int internal_refs = 0;  // input slots of planned nodes that read this value
 };
 
 struct Cluster {
@@ -115,18 +167,19 @@ class Planner {
         return std::move(plan_);
     }
 
-    const std::unordered_map<const Value *, int> &index() const { return index_; }
+    // Plan position of every planned value (moved out: call once, after build).
+    ValueIndex take_index() { return std::move(index_); }
 
   private:
     void visit(const ValueRef &value) {
         if (!value) throw std::invalid_argument{"cannot evaluate an empty value"};
         if (value->materialization() != nullptr) return;
-        auto it = state_.find(value.get());
-        if (it != state_.end()) {
-            if (it->second == 0) throw std::logic_error{"cycle in computation graph"};
+        // -1 while the value's inputs are being visited, then its plan position
+        auto [pos, fresh] = index_.emplace(value.get(), -1);
+        if (!fresh) {
+            if (*pos < 0) throw std::logic_error{"cycle in computation graph"};
             return;
         }
-        state_.emplace(value.get(), 0);
         const NodeRef &node = value->producer_ref();
         if (!node) throw std::runtime_error{"cannot evaluate unmaterialized leaf"};
         for (const ValueRef &input : node->inputs()) visit(input);
@@ -136,10 +189,7 @@ class Planner {
         const Primitive &primitive = node->primitive();
         const TensorSpec &spec = value->spec();
         step.on_cuda = spec.device.type() == DeviceType::Cuda;
-        if (primitive.requires_kernel_support()) {
-            step.runtime = &runtimes_.get(spec.device);
-            step.kernel = &kernels_.get(KernelKey{primitive.id(), spec.device.type()});
-        }
+        if (primitive.requires_kernel_support()) lookup(primitive, spec.device, step);
         if (step.on_cuda) {
             has_cuda_ = true;
             const std::uint32_t id = primitive.id().value();
@@ -147,15 +197,36 @@ class Planner {
             step.fusible = f32 && (is_unary_id(id) || is_binary_id(id));
             step.constant = f32 && id == kFullId;
         }
-        index_.emplace(value.get(), static_cast<int>(plan_.size()));
+        *index_.find(value.get()) = static_cast<int>(plan_.size());
         plan_.push_back(std::move(step));
-        state_[value.get()] = 1;
     }
+
+    // The registries' runtime and kernel for (primitive, device), remembered
+    // for this plan: a plan has a few hundred nodes but a few dozen kinds.
+    void lookup(const Primitive &primitive, const Device &device, Step &step) {
+        const std::uint32_t id = primitive.id().value();
+        for (const Known &k : known_)
+            if (k.id == id && k.device == device) {
+                step.runtime = k.runtime;
+                step.kernel = k.kernel;
+                return;
+            }
+        step.runtime = &runtimes_.get(device);
+        step.kernel = &kernels_.get(KernelKey{primitive.id(), device.type()});
+        known_.push_back(Known{id, device, step.runtime, step.kernel});
+    }
+
+    struct Known {
+        std::uint32_t id;
+        Device device;
+        DeviceRuntime *runtime;
+        const KernelFn *kernel;
+    };
 
     const RuntimeRegistry &runtimes_;
     const KernelRegistry &kernels_;
-    std::unordered_map<const Value *, int> state_;
-    std::unordered_map<const Value *, int> index_;
+    ValueIndex index_;
+    std::vector<Known> known_;
     std::vector<Step> plan_;
     bool has_cuda_ = false;
 };
@@ -305,6 +376,9 @@ struct Recording {
     // requests, so the outputs are free whenever the plan comes back.
     std::vector<void *> protected_blocks;
     std::size_t protected_bytes = 0;
+    // the output blocks a replay takes back, in one allocator call
+    std::vector<void *> take_ptrs;
+    std::vector<std::size_t> take_bytes;
     Recording() = default;
     Recording(const Recording &) = delete;
     Recording &operator=(const Recording &) = delete;
@@ -386,21 +460,30 @@ class FusedEvaluator {
             raise_device_errors(static_cast<int>(s.output->spec().device.index()), false);
             break;
         }
-        index_cache_ = planner.index();
+        index_cache_ = planner.take_index();
         ++evaluator_stats().evaluations;
-        const auto &index = index_cache_;
-        // consumers, graph-internal references and roots
-        for (int i = 0; i < static_cast<int>(plan_.size()); ++i) {
+        // consumers (one flat array, ascending per producer), graph-internal
+        // references and roots
+        const int n = static_cast<int>(plan_.size());
+        cons_off_.assign(static_cast<std::size_t>(n) + 1, 0);
+        for (int i = 0; i < n; ++i)
             for (const ValueRef &in : plan_[i].node->inputs()) {
-                auto it = index.find(in.get());
-                if (it == index.end()) continue;
-                plan_[it->second].consumers.push_back(i);
-                ++plan_[it->second].internal_refs;
+                const int pi = plan_index(in.get());
+                if (pi >= 0) ++cons_off_[static_cast<std::size_t>(pi) + 1];
             }
-        }
+        for (int i = 0; i < n; ++i) cons_off_[i + 1] += cons_off_[i];
+        cons_.assign(static_cast<std::size_t>(cons_off_[n]), 0);
+        std::vector<int> fill(cons_off_.begin(), cons_off_.end() - 1);
+        for (int i = 0; i < n; ++i)
+            for (const ValueRef &in : plan_[i].node->inputs()) {
+                const int pi = plan_index(in.get());
+                if (pi < 0) continue;
+                cons_[fill[pi]++] = i;
+                ++plan_[pi].internal_refs;
+            }
         for (const ValueRef &r : roots) {
-            auto it = index.find(r.get());
-            if (it != index.end()) plan_[it->second].materialize = true;
+            const int pi = plan_index(r.get());
+            if (pi >= 0) plan_[pi].materialize = true;
         }
         for (Step &s : plan_) {
             // the step itself holds one reference; anything beyond the graph's own
@@ -419,10 +502,16 @@ class FusedEvaluator {
     }
 
   private:
-    bool consumers_in_one_cluster(const Step &s, int &target) const {
+    // The planned consumers of step i, in plan order.
+    std::span<const int> consumers(int i) const {
+        return {cons_.data() + cons_off_[i], static_cast<std::size_t>(cons_off_[i + 1] - cons_off_[i])};
+    }
+
+    bool consumers_in_one_cluster(int i, int &target) const {
         target = -1;
-        if (s.consumers.empty()) return false;
-        for (int c : s.consumers) {
+        const auto cs_of = consumers(i);
+        if (cs_of.empty()) return false;
+        for (int c : cs_of) {
             const Step &cs = plan_[c];
             if (!cs.fusible || cs.cluster < 0) return false;
             if (target == -1) target = cs.cluster;
@@ -435,15 +524,15 @@ class FusedEvaluator {
         for (int i = static_cast<int>(plan_.size()) - 1; i >= 0; --i) {
             Step &s = plan_[i];
             if (s.constant && !s.materialize) {
-                bool all_fused = !s.consumers.empty();
-                for (int c : s.consumers) all_fused = all_fused && plan_[c].fusible && plan_[c].cluster >= 0;
+                bool all_fused = !consumers(i).empty();
+                for (int c : consumers(i)) all_fused = all_fused && plan_[c].fusible && plan_[c].cluster >= 0;
                 s.folded = all_fused;
                 continue;
             }
             if (!s.fusible) continue;
             int target = -1;
             const Shape &shape = s.output->spec().shape;
-            if (consumers_in_one_cluster(s, target) && clusters_[target].shape == shape && can_grow(target, i)) {
+            if (consumers_in_one_cluster(i, target) && clusters_[target].shape == shape && can_grow(target, i)) {
                 clusters_[target].members.push_back(i);
                 s.cluster = target;
             } else {
@@ -456,7 +545,7 @@ class FusedEvaluator {
                 s.materialize = true;  // the cluster's result is always written
             }
             // a member consumed outside its cluster must be written
-            for (int c : s.consumers)
+            for (int c : consumers(i))
                 if (plan_[c].cluster != s.cluster) s.materialize = true;
         }
     }
@@ -712,8 +801,8 @@ class FusedEvaluator {
     }
 
     int plan_index(const Value *v) const {
-        const auto it = index_cache_.find(v);
-        return it == index_cache_.end() ? -1 : it->second;
+        const int *p = index_cache_.find(v);
+        return p == nullptr ? -1 : *p;
     }
 
     // ---------------------------------------------------------- recording --
@@ -725,7 +814,7 @@ class FusedEvaluator {
         leaf_values_.clear();
         int device = -1;
         std::size_t out_bytes = 0;
-        std::unordered_map<const Value *, int> leaf_slot;
+        ValueIndex leaf_slot;
         w.bytes.reserve(plan_.size() * 64);
         for (int i = 0; i < static_cast<int>(plan_.size()); ++i) {
             const Step &s = plan_[i];
@@ -767,7 +856,7 @@ class FusedEvaluator {
                     w.shape(in->spec().shape);
                     w.layout(m->layout());
                 }
-                w.pod(static_cast<std::int32_t>(-2 - slot->second));
+                w.pod(static_cast<std::int32_t>(-2 - *slot));
             }
             if (s.materialize && s.kernel != nullptr) out_bytes += dense_size_bytes(spec);
         }
@@ -898,6 +987,11 @@ class FusedEvaluator {
             rec->protect(const_cast<void *>(leaves[i]), b != nullptr ? b->size_bytes() : 0);
         }
         rec->leaves = leaves;
+        for (const Install &in : installs_) {
+            if (in.view || in.bytes == 0) continue;
+            rec->take_ptrs.push_back(in.ptr);
+            rec->take_bytes.push_back(in.bytes);
+        }
         rec->installs = std::move(installs_);
         rec->constants = std::move(constants_);
         rec->index_kernels = index_kernels_;
@@ -913,13 +1007,16 @@ class FusedEvaluator {
     bool replay(Recording &r, CudaRuntime &rt) {
         const int device = rt.index();
         void *stream = rt.stream();
+        // every output block at once, or none (some value still holds one)
+        int32_t failed = -1;
+        if (!r.take_ptrs.empty() &&
+            mtc_pool_take_many(device, r.take_ptrs.data(), r.take_bytes.data(), static_cast<int32_t>(r.take_ptrs.size()),
+                               stream, &failed) != MTC_OK)
+            return false;
         std::vector<BufferRef> taken(r.installs.size());
         for (std::size_t k = 0; k < r.installs.size(); ++k) {
             const Install &in = r.installs[k];
-            if (in.view) continue;
-            // blocks taken so far go back to the pool with `taken` on failure
-            if (in.bytes != 0 && mtc_pool_take(device, in.ptr, in.bytes, stream) != MTC_OK) return false;
-            taken[k] = rt.adopt(in.ptr, in.bytes);
+            if (!in.view) taken[k] = rt.adopt(in.bytes != 0 ? in.ptr : nullptr, in.bytes);
         }
         for (FusedConstants &fc : r.constants) {
             bool changed = false;
@@ -959,7 +1056,9 @@ class FusedEvaluator {
     const KernelRegistry &kernels_;
     std::vector<Step> plan_;
     std::vector<Cluster> clusters_;
-    std::unordered_map<const Value *, int> index_cache_;
+    ValueIndex index_cache_;
+    std::vector<int> cons_off_;  // consumers of step i: cons_[cons_off_[i] .. cons_off_[i + 1])
+    std::vector<int> cons_;
     bool index_kernels_ = false;
     DeviceRuntime *index_runtime_ = nullptr;
     // recording state
