@@ -251,12 +251,24 @@ class Planner {
 // the earlier recording read.  The two recordings then alternate: every later
 // step finds its leaves where one of them expects them.
 
+// Appends plain values to a byte key.  Writes go through a cursor into a
+// buffer grown by doubling: a plan key takes a few thousand small writes.
 struct KeyWriter {
     std::string bytes;
+    std::size_t used = 0;
     template <typename T>
     void pod(const T &v) {
-        bytes.append(reinterpret_cast<const char *>(&v), sizeof(T));
+        if (bytes.size() - used < sizeof(T)) bytes.resize(bytes.empty() ? 4096 : 2 * bytes.size());
+        std::memcpy(bytes.data() + used, &v, sizeof(T));
+        used += sizeof(T);
     }
+    void raw(const void *p, std::size_t n) {
+        while (bytes.size() - used < n) bytes.resize(bytes.empty() ? 4096 : 2 * bytes.size());
+        std::memcpy(bytes.data() + used, p, n);
+        used += n;
+    }
+    // The key: the bytes written so far.
+    void finish() { bytes.resize(used); }
     void shape(const Shape &s) {
         pod(static_cast<std::uint32_t>(s.rank()));
         for (Extent e : s.dimensions()) pod(static_cast<std::int64_t>(e));
@@ -335,9 +347,13 @@ bool write_parameters(const Primitive &primitive, std::uint32_t id, bool folded,
     case 0x0202:
     case 0x0204:
     case 0x0401: return true;
-    default:
+    default: {
         if (is_unary_id(id) || is_binary_id(id)) return true;
-        return ext::write_primitive_key(primitive, w.bytes);
+        std::string ext_key;
+        if (!ext::write_primitive_key(primitive, ext_key)) return false;
+        w.raw(ext_key.data(), ext_key.size());
+        return true;
+    }
     }
 }
 
@@ -815,7 +831,7 @@ class FusedEvaluator {
         int device = -1;
         std::size_t out_bytes = 0;
         ValueIndex leaf_slot;
-        w.bytes.reserve(plan_.size() * 64);
+        w.bytes.resize(plan_.size() * 64);
         for (int i = 0; i < static_cast<int>(plan_.size()); ++i) {
             const Step &s = plan_[i];
             if (!s.on_cuda) return trace_graph("not recorded", "a step runs on the host"), false;
@@ -863,6 +879,7 @@ class FusedEvaluator {
         if (rt == nullptr || device < 0) return trace_graph("not recorded", "no device runtime"), false;
         if (out_bytes > evaluator_options().graph_max_bytes) return false;  // launch overhead does not matter
         w.pod(device);
+        w.finish();
         return true;
     }
 
