@@ -280,8 +280,9 @@ def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
                 ms = _time_ms(abi.matmul(V(a), V(b), V(c), algo, prepare=True), reps=3)
                 out[f"gemm_simt_{tag}_4096_TFLOPs"] = 2 * m ** 3 / (ms * 1e-3) / 1e12
     out["gemm_8192_frac_of_3xtf32"] = out["gemm_8192_TFLOPs"] / peak3
-    # the same 8192^3 GEMM with the other kernel variants / shared-memory rings
-    for variant in ("32x2", "pair16x6", "pair32x3"):
+    # the same 8192^3 GEMM with each kernel variant / shared-memory ring forced
+    # (the default picks the CTA pair at this size)
+    for variant in ("16x4", "32x2", "pair16x6", "pair32x3"):
         os.environ["MTC_TC_PIPELINE"] = variant
         try:
             ms = _time_ms(abi.matmul(V(a), V(b), V(c), prepare=True), reps=3)
