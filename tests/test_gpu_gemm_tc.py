@@ -14,18 +14,24 @@ pytestmark = pytest.mark.gpu
 F = np.float32
 
 
-@pytest.fixture(autouse=True, params=["16x4", "16x4-0", "16x4-ab", "32x2", "pair16x6", "pair32x3"])
+@pytest.fixture(autouse=True, params=["auto", "16x4", "16x4-0", "16x4-ab", "32x2", "pair16x6", "pair32x3"])
 def pipeline(request, monkeypatch):
     """Every kernel and ring: the single-CTA kernel with 4 stages of BK=16 (64-byte
     swizzle) or 2 of BK=32 (128-byte swizzle), reading a K-contiguous A raw (lo
     computed in shared memory; the default), splitting every operand first
-    ("-0"), or reading both K-contiguous operands raw ("-ab"); and the CTA-pair
-    kernel with 6 stages of BK=16 or 3 of BK=32."""
+    ("-0"), or reading both K-contiguous operands raw ("-ab"); the CTA-pair
+    kernel (split operands) with 6 stages of BK=16 or 3 of BK=32; and the
+    default choice between them ("auto")."""
     name = request.param
     pipe, _, direct = name.partition("-")
-    monkeypatch.setenv("MTC_TC_PIPELINE", pipe)
+    if pipe != "auto":
+        monkeypatch.setenv("MTC_TC_PIPELINE", pipe)
+    else:
+        monkeypatch.delenv("MTC_TC_PIPELINE", raising=False)
     if direct:
         monkeypatch.setenv("MTC_TC_DIRECT", direct)
+    else:
+        monkeypatch.delenv("MTC_TC_DIRECT", raising=False)
     return name
 
 
@@ -143,3 +149,13 @@ def test_auto_uses_tensor_cores_for_large_problems(cuda):
     simt_got, _ = _run(rng.standard_normal(M * K).astype(F), [M, K], [K, 1], rng.standard_normal(K * N).astype(F),
                        [K, N], [N, 1], algo=abi.GEMM_SIMT)
     assert got.shape == exp.shape
+
+
+def test_many_tiles_per_cluster(cuda):
+    """Enough 256x256 tiles that the default picks the CTA pair and each pair
+    runs several tiles (both TMEM accumulators, every ring phase), with ragged
+    row tiles and a K tail."""
+    rng = np.random.default_rng(14)
+    M, N, K = 2600, 2560, 300
+    _run(rng.standard_normal(M * K).astype(F), [M, K], [K, 1], rng.standard_normal(K * N).astype(F), [K, N],
+         [N, 1], out_offset=2)
