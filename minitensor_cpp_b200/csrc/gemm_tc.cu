@@ -1201,15 +1201,18 @@ int launch_pair(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float 
 // single-CTA kernel reads a K-contiguous A raw (no split pack for it);
 // MTC_TC_DIRECT selects the raw operands explicitly ("0", "a", "b", "ab").
 //
-// Unset: the CTA pair ("pair16x6") when its 256 x 256 tiles give every pair of
-// SMs at least one tile, else "16x4" (which also splits K for problems with
-// few tiles).  Each CTA of a pair stages half of the B tile, so the pair reads
-// half as much shared memory per MMA; on the wide-MLP training step it ran
-// 14 % more GEMM work per clock than the single-CTA kernel, and the step 4.5 %
-// faster, although it packs A as well.
+// Unset: "16x4" when A can be read raw (the single-CTA kernel then streams A
+// once instead of a split hi/lo copy), or when the CTA pair's 256 x 256 tiles
+// would leave pairs of SMs idle (it also splits K for problems with few
+// tiles); otherwise the CTA pair ("pair16x6").  Each CTA of a pair stages half
+// of the B tile, so the pair reads half as much shared memory per MMA.
+// Measured per GEMM of the wide-MLP training step (ncu, one pass):
+//   weight gradients (both operands packed, K = 65536): pair 24 ms, single 31-34 ms;
+//   forward / input gradients (raw A, K = 8192): single 28-30 ms and 57-62 GB of
+//   DRAM traffic, pair (A packed) 30-33 ms and 105-121 GB.
 enum class TcKernel { Deep, Wide, PairDeep, PairWide };
 
-TcKernel selected_kernel(const GemmProblem &p) {
+TcKernel selected_kernel(const GemmProblem &p, bool a_raw) {
     const char *sel = std::getenv("MTC_TC_PIPELINE");
     if (sel != nullptr) {
         if (std::strcmp(sel, "16x4") == 0) return TcKernel::Deep;
@@ -1217,6 +1220,7 @@ TcKernel selected_kernel(const GemmProblem &p) {
         if (std::strcmp(sel, "pair16x6") == 0) return TcKernel::PairDeep;
         if (std::strcmp(sel, "pair32x3") == 0) return TcKernel::PairWide;
     }
+    if (a_raw) return TcKernel::Deep;
     const int64_t pair_tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256) * p.batch;
     return 2 * pair_tiles >= sm_count(current_device()) ? TcKernel::PairDeep : TcKernel::Deep;
 }
@@ -1267,6 +1271,14 @@ void choose_direct(const GemmProblem &p, TcKernel k, bool &ad, bool &bd, TcOpera
     bd = (mask > 0 && (mask & 2)) && direct_operand(p.B, p.b_off, p.b_cs, p.b_rs, p.N, p, p.b_bs, b_raw);
 }
 
+// Whether the single-CTA kernel would read A raw under the current policy.
+bool a_readable_raw(const GemmProblem &p) {
+    const int mask = direct_mask(TcKernel::Deep);
+    if (mask == 0 || (mask > 0 && !(mask & 1))) return false;
+    TcOperand unused;
+    return direct_operand(p.A, p.a_off, p.a_rs, p.a_cs, p.M, p, p.a_bs, unused);
+}
+
 }  // namespace
 
 int gemm_3xtf32(const GemmProblem &p, cudaStream_t stream) {
@@ -1276,7 +1288,7 @@ int gemm_3xtf32(const GemmProblem &p, cudaStream_t stream) {
     const int64_t Kp = (p.K + 3) / 4 * 4;  // 16-byte row pitch for the tensor maps
     if (Kp >= (int64_t{1} << 31) || p.M >= (int64_t{1} << 31) || p.N >= (int64_t{1} << 31))
         return fail(MTC_ERR_UNSUPPORTED, "extent beyond the tensor-map range");
-    const TcKernel k = selected_kernel(p);
+    const TcKernel k = selected_kernel(p, a_readable_raw(p));
     bool ad, bd;
     TcOperand a_raw, b_raw;
     choose_direct(p, k, ad, bd, a_raw, b_raw);
@@ -1364,7 +1376,7 @@ int gemm_3xtf32_static(const GemmProblem &p, cudaStream_t stream) {
                     need, kStaticWorkspaceFloats);
     float *ws = nullptr;
     MTC_TRY(static_workspace(&ws));
-    const TcKernel k = selected_kernel(p);
+    const TcKernel k = selected_kernel(p, a_readable_raw(p));
     bool ad, bd;
     TcOperand a_raw, b_raw;
     choose_direct(p, k, ad, bd, a_raw, b_raw);
