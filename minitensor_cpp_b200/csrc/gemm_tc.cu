@@ -79,6 +79,7 @@ struct TcArgs {
     int splits;
     int64_t kb_per_split;
     float *ws;
+    int group;  // row tiles per column sweep of the tile order (L2 reuse)
 };
 
 // Tile and K-block range of work unit u.
@@ -198,8 +199,8 @@ __device__ __forceinline__ void tile_coords(const TcArgs &a, int64_t t, int &tm,
     const int64_t per_batch = static_cast<int64_t>(a.tiles_m) * a.tiles_n;
     tb = static_cast<int>(t / per_batch);
     const int64_t r = t - tb * per_batch;
-    // grouped rasterisation: 8 row tiles share each column sweep for L2 reuse
-    constexpr int G = 8;
+    // grouped rasterisation: `group` row tiles share each column sweep for L2 reuse
+    const int G = a.group;
     const int64_t group_span = static_cast<int64_t>(G) * a.tiles_n;
     const int group = static_cast<int>(r / group_span);
     const int first_m = group * G;
@@ -1082,6 +1083,14 @@ int launch_tc_variant(const CUtensorMap &m_ahi, const CUtensorMap &m_alo, const 
 
 // Tensor maps over the two operands and the persistent GEMM launch with
 // pipeline shape P (allocates nothing).
+// Row tiles per column sweep of the persistent tile order (environment
+// override for measurements).
+int tile_group(const char *env, int fallback) {
+    const char *v = std::getenv(env);
+    const int g = v != nullptr ? std::atoi(v) : fallback;
+    return g >= 1 && g <= 256 ? g : fallback;
+}
+
 template <class P>
 int launch_tc(const GemmProblem &p, int64_t Kp, const TcOperand &A, const TcOperand &B, cudaStream_t stream,
               int splits = 1, float *split_ws = nullptr) {
@@ -1110,6 +1119,7 @@ int launch_tc(const GemmProblem &p, int64_t Kp, const TcOperand &A, const TcOper
     for (int d = 0; d < p.batch_rank && vec; ++d) vec = (p.c_bs[d] % 4) == 0;
     a.vec_store = vec ? 1 : 0;
     a.err = device_error_word();
+    a.group = tile_group("MTC_TC_GROUP", 24);
     const int64_t kblocks = (Kp + P::BK - 1) / P::BK;
     a.splits = 1;
     a.kb_per_split = kblocks;
@@ -1171,6 +1181,7 @@ int launch_pair(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float 
     a.N = p.N;
     a.Kp = Kp;
     a.batch = p.batch;
+    a.group = tile_group("MTC_TC_PAIR_GROUP", 8);
     a.tiles_m = static_cast<int>((p.M + 255) / 256);
     a.tiles_n = static_cast<int>((p.N + 255) / 256);
     a.total_tiles = static_cast<int64_t>(a.tiles_m) * a.tiles_n * p.batch;
