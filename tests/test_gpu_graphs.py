@@ -155,3 +155,38 @@ def test_recorded_fused_kernel_takes_new_constants(cuda):
         assert launches.value == 1
     finally:
         L.mtc_graph_destroy(g)
+
+
+def test_pool_take_many_is_all_or_none(cuda):
+    L = abi.lib()
+    s = _stream()
+    blocks = [_alloc(1 << 16, s) for _ in range(3)]
+    for p in blocks[:2]:
+        abi.check(L.mtc_free(0, ctypes.c_void_p(p), ctypes.c_void_p(s)), "free")
+    ptrs = (ctypes.c_void_p * 3)(*blocks)
+    sizes = (ctypes.c_size_t * 3)(*(1 << 16 for _ in range(3)))
+    failed = ctypes.c_int32(-1)
+    # the third block is still live: nothing is taken
+    assert L.mtc_pool_take_many(0, ptrs, sizes, 3, ctypes.c_void_p(s), ctypes.byref(failed)) != 0
+    assert failed.value == 2
+    abi.check(L.mtc_pool_take_many(0, ptrs, sizes, 2, ctypes.c_void_p(s), ctypes.byref(failed)), "take two")
+    for p in blocks:
+        abi.check(L.mtc_free(0, ctypes.c_void_p(p), ctypes.c_void_p(s)), "free")
+
+
+def test_protected_blocks_wait_for_a_take_by_address(cuda):
+    L = abi.lib()
+    s = _stream()
+    abi.check(L.mtc_pool_trim(0), "trim")
+    a = _alloc(3 << 20, s)
+    abi.check(L.mtc_pool_protect(0, ctypes.c_void_p(a), 1), "protect")
+    abi.check(L.mtc_free(0, ctypes.c_void_p(a), ctypes.c_void_p(s)), "free")
+    b = _alloc(3 << 20, s)  # same size, same stream: a protected block is not handed out
+    assert b != a
+    abi.check(L.mtc_pool_take(0, ctypes.c_void_p(a), 3 << 20, ctypes.c_void_p(s)), "take the protected block")
+    abi.check(L.mtc_free(0, ctypes.c_void_p(a), ctypes.c_void_p(s)), "free")
+    abi.check(L.mtc_pool_protect(0, ctypes.c_void_p(a), -1), "unprotect")
+    abi.check(L.mtc_free(0, ctypes.c_void_p(b), ctypes.c_void_p(s)), "free")
+    c = _alloc(3 << 20, s)  # unprotected again: an ordinary cached block
+    assert c in (a, b)
+    abi.check(L.mtc_free(0, ctypes.c_void_p(c), ctypes.c_void_p(s)), "free")
