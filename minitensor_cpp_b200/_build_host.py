@@ -35,7 +35,12 @@ INCLUDE = ROOT / "include"
 REFERENCE = Path(os.environ.get("MINITENSOR_REFERENCE", "/root/reference"))
 
 CXX = os.environ.get("CXX", "g++")
-CXXFLAGS = ["-std=c++20", "-O3", "-DNDEBUG", "-fPIC", "-Wall", "-Wno-unused-parameter"]
+# -fno-semantic-interposition: the library binds its own symbols (-Bsymbolic),
+# so the compiler may inline calls between functions of one translation unit
+# that -fPIC would otherwise treat as interposable (building a lazy graph makes
+# many such small calls).
+CXXFLAGS = ["-std=c++20", "-O3", "-DNDEBUG", "-fPIC", "-Wall", "-Wno-unused-parameter", "-fno-semantic-interposition"]
+LDFLAGS: list[str] = []
 
 # (file, anchor, replacement) edits; each anchor must occur exactly once.
 EDITS = [
@@ -127,7 +132,7 @@ def build(verbose: bool = False) -> Path | None:
     for src in ref_sources:
         obj = BUILD / "ref" / (str(src.relative_to(work / "src")).replace("/", "__") + ".o")
         objs.append(obj)
-        if _newer(obj, [src]):
+        if _newer(obj, [src, Path(__file__)]):
             obj.parent.mkdir(parents=True, exist_ok=True)
             jobs.append([CXX, *CXXFLAGS, *includes, "-c", str(src), "-o", str(obj)])
     for name in HOST_SOURCES:
@@ -142,7 +147,7 @@ def build(verbose: bool = False) -> Path | None:
                 print(proc.stderr)
     mtcuda = LIB / "libmtcuda.so"
     if _newer(lib, objs + [mtcuda]):
-        _run([CXX, "-shared", "-Wl,-Bsymbolic", "-o", str(lib), *map(str, objs), f"-L{LIB}", "-lmtcuda",
+        _run([CXX, "-shared", *LDFLAGS, "-Wl,-Bsymbolic", "-o", str(lib), *map(str, objs), f"-L{LIB}", "-lmtcuda",
               "-Wl,-rpath,$ORIGIN"])
     return lib
 
