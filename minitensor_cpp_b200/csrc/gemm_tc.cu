@@ -1181,7 +1181,7 @@ int launch_pair(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float 
     a.N = p.N;
     a.Kp = Kp;
     a.batch = p.batch;
-    a.group = tile_group("MTC_TC_PAIR_GROUP", 8);
+    a.group = tile_group("MTC_TC_PAIR_GROUP", 16);
     a.tiles_m = static_cast<int>((p.M + 255) / 256);
     a.tiles_n = static_cast<int>((p.N + 255) / 256);
     a.total_tiles = static_cast<int64_t>(a.tiles_m) * a.tiles_n * p.batch;
