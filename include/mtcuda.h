@@ -143,6 +143,19 @@ int mtc_copy_from_host(int device, void *dst, const void *src, size_t bytes, voi
 int mtc_copy_to_host(int device, void *dst, const void *src, size_t bytes, void *stream);
 /* Wait for all work queued on `stream`. */
 int mtc_stream_synchronize(void *stream);
+/* Streams and events for callers that overlap their own host transfers with
+ * work queued on the device stream (an input pipeline: the next batch's copy
+ * runs while the current step computes).  No reference counterpart: the
+ * reference copies and evaluates synchronously on one host thread.
+ * mtc_stream_create makes a stream that does not synchronise with the legacy
+ * default stream; mtc_event_create an event without timing.  A wait on an
+ * event that was never recorded returns at once. */
+int mtc_stream_create(int device, void **stream);
+int mtc_stream_destroy(int device, void *stream);
+int mtc_event_create(int device, void **event);
+int mtc_event_destroy(int device, void *event);
+int mtc_event_record(void *event, void *stream);
+int mtc_stream_wait_event(void *stream, void *event);
 /* Bytes held from the driver by / handed out from the caching allocator. */
 int mtc_pool_stats(int device, uint64_t *reserved_bytes, uint64_t *used_bytes);
 /* Return cached-but-unused blocks to the driver (synchronises the device).

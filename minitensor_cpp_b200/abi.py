@@ -159,6 +159,12 @@ def _declare(L):
         "mtc_pool_stats": ([c_int, P(ctypes.c_uint64), P(ctypes.c_uint64)], c_int),
         "mtc_pool_trim": ([c_int], c_int),
         "mtc_pool_take": ([c_int, c_vp, c_sz, c_vp], c_int),
+        "mtc_stream_create": ([c_int, P(c_vp)], c_int),
+        "mtc_stream_destroy": ([c_int, c_vp], c_int),
+        "mtc_event_create": ([c_int, P(c_vp)], c_int),
+        "mtc_event_destroy": ([c_int, c_vp], c_int),
+        "mtc_event_record": ([c_vp, c_vp], c_int),
+        "mtc_stream_wait_event": ([c_vp, c_vp], c_int),
         "mtc_pool_protect": ([c_int, c_vp, c_i32], c_int),
         "mtc_pool_take_many": ([c_int, P(c_vp), P(c_sz), c_i32, c_vp, P(c_i32)], c_int),
         "mtc_capture_begin": ([c_int, c_vp], c_int),
@@ -206,7 +212,8 @@ def _declare(L):
 EXPORTED = (
     "mtc_last_error", "mtc_version", "mtc_device_count", "mtc_device_sm_count", "mtc_set_device", "mtc_device_stream", "mtc_alloc",
     "mtc_free", "mtc_copy_from_host", "mtc_copy_to_host", "mtc_stream_synchronize", "mtc_pool_stats", "mtc_pool_trim",
-    "mtc_pool_take", "mtc_pool_take_many", "mtc_pool_protect", "mtc_capture_begin", "mtc_capture_end", "mtc_capture_fused_count", "mtc_graph_launch",
+    "mtc_stream_create", "mtc_stream_destroy", "mtc_event_create", "mtc_event_destroy", "mtc_event_record",
+    "mtc_stream_wait_event", "mtc_pool_take", "mtc_pool_take_many", "mtc_pool_protect", "mtc_capture_begin", "mtc_capture_end", "mtc_capture_fused_count", "mtc_graph_launch",
     "mtc_graph_set_constants", "mtc_graph_launches", "mtc_graph_destroy",
     "mtc_check_device_errors", "mtc_watch_device_errors", "mtc_poll_device_errors", "mtc_selftest_bounded_wait", "mtc_unary", "mtc_binary", "mtc_fused", "mtc_copy", "mtc_concat", "mtc_index_scatter",
     "mtc_gather", "mtc_gather_scatter_add", "mtc_reduce", "mtc_log_softmax", "mtc_matmul", "mtc_fill", "mtc_uniform",

@@ -686,6 +686,60 @@ int mtc_pool_stats(int device, uint64_t *reserved_bytes, uint64_t *used_bytes) {
     return MTC_OK;
 }
 
+int mtc_stream_create(int device, void **stream) {
+    clear_error();
+    if (stream == nullptr) return fail(MTC_ERR_INVALID_ARGUMENT, "null stream slot");
+    DeviceState *st = nullptr;
+    MTC_TRY(ensure_device(device, &st));
+    DeviceGuard guard(device);
+    MTC_TRY(guard.rc);
+    cudaStream_t s = nullptr;
+    MTC_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+    *stream = s;
+    return MTC_OK;
+}
+
+int mtc_stream_destroy(int device, void *stream) {
+    if (stream == nullptr) return MTC_OK;
+    DeviceGuard guard(device);
+    MTC_TRY(guard.rc);
+    MTC_CUDA_TRY(cudaStreamDestroy(static_cast<cudaStream_t>(stream)));
+    return MTC_OK;
+}
+
+int mtc_event_create(int device, void **event) {
+    clear_error();
+    if (event == nullptr) return fail(MTC_ERR_INVALID_ARGUMENT, "null event slot");
+    DeviceGuard guard(device);
+    MTC_TRY(guard.rc);
+    cudaEvent_t e = nullptr;
+    MTC_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    *event = e;
+    return MTC_OK;
+}
+
+int mtc_event_destroy(int device, void *event) {
+    if (event == nullptr) return MTC_OK;
+    DeviceGuard guard(device);
+    MTC_TRY(guard.rc);
+    MTC_CUDA_TRY(cudaEventDestroy(static_cast<cudaEvent_t>(event)));
+    return MTC_OK;
+}
+
+int mtc_event_record(void *event, void *stream) {
+    clear_error();
+    if (event == nullptr) return fail(MTC_ERR_INVALID_ARGUMENT, "null event");
+    MTC_CUDA_TRY(cudaEventRecord(static_cast<cudaEvent_t>(event), static_cast<cudaStream_t>(stream)));
+    return MTC_OK;
+}
+
+int mtc_stream_wait_event(void *stream, void *event) {
+    clear_error();
+    if (event == nullptr) return fail(MTC_ERR_INVALID_ARGUMENT, "null event");
+    MTC_CUDA_TRY(cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), static_cast<cudaEvent_t>(event), 0));
+    return MTC_OK;
+}
+
 int mtc_pool_take(int device, void *ptr, size_t bytes, void *stream) {
     clear_error();
     if (device < 0) return fail(MTC_ERR_INVALID_ARGUMENT, "negative device index");

@@ -34,7 +34,9 @@
 #include "ops_ext.hpp"
 #include "tensor/backend/cpu/cpu_buffer.hpp"
 #include "tensor/execution/environment.hpp"
+#include "tensor/graph/leaf.hpp"
 #include "tensor/graph/value.hpp"
+#include "tensor/storage/dense_size.hpp"
 #include "tensor/storage/materialization.hpp"
 #include "tensor/tensor_access.hpp"
 #endif
@@ -246,6 +248,22 @@ struct MlpTrainer {
     int world = 1;
     std::optional<mt::Tensor> x_resident;
     std::optional<mt::Tensor> y_resident;
+#ifndef MTB_CPU_ONLY
+    // Input pipeline of step_host on a CUDA device: two device slots for a
+    // batch (x and labels) filled on a copy stream, so the next batch's copy
+    // runs while the device stream still computes the previous step.
+    struct InputSlot {
+        std::optional<mt::Tensor> x, y;
+        void *copied = nullptr;  // event: the slot holds its batch (copy stream)
+        void *free = nullptr;    // event: the step that read the slot has run (device stream)
+    };
+    InputSlot slots[2];
+    int next_slot = 0;
+    std::int64_t slot_batch = -1;
+    void *copy_stream = nullptr;
+    void *loss_ready = nullptr;  // event: the step's loss is computed
+    bool mark_loss = false;      // record loss_ready once the loss is queued
+#endif
 
     MlpTrainer(mt::Device dev, std::vector<mt::Extent> widths, uint64_t seed, float lr)
         : device{dev}, model{std::move(widths)},
@@ -262,10 +280,38 @@ struct MlpTrainer {
         }
     }
 
-    float step(const mt::Tensor &x, const mt::Tensor &y, bool read_loss) {
+    ~MlpTrainer() {
+#ifndef MTB_CPU_ONLY
+        if (copy_stream == nullptr) return;
+        const int dev = static_cast<int>(device.index());
+        (void)mtc_stream_synchronize(copy_stream);
+        for (InputSlot &sl : slots) {
+            (void)mtc_event_destroy(dev, sl.copied);
+            (void)mtc_event_destroy(dev, sl.free);
+        }
+        (void)mtc_event_destroy(dev, loss_ready);
+        (void)mtc_stream_destroy(dev, copy_stream);
+#endif
+    }
+
+    // early_loss: read the loss as soon as it is computed (a CUDA device): the
+    // forward pass is evaluated first and marked, and the read waits for that
+    // mark only, so the host returns while the device runs the backward pass
+    // and the optimizer.  Otherwise the loss is read after the whole step.
+    float step(const mt::Tensor &x, const mt::Tensor &y, bool read_loss, bool early_loss = false) {
         StepTrace trace;
         const mt::Tensor logits = mt::nn::forward(model, params, x);
         const mt::Tensor loss = mt::nn::categorical_cross_entropy_with_logits(logits, y);
+#ifndef MTB_CPU_ONLY
+        early_loss = early_loss && read_loss && device.type() == mt::DeviceType::Cuda && copy_stream != nullptr;
+        if (early_loss && world == 1) {
+            mt::eval(loss);  // materialises the loss; the graph stays for the gradients
+            mark_loss_ready();
+        }
+        mark_loss = early_loss && world > 1;  // the first layer of the exchange materialises it
+#else
+        early_loss = false;
+#endif
         auto grads = mt::nn::parameter_gradients(loss, params);
         trace.mark("graph");
         if (world > 1) allreduce(grads, loss);
@@ -277,10 +323,91 @@ struct MlpTrainer {
         trace.mark("evaluate parameters");
         state = mt::nn::leafify_optimizer_state(std::move(next_state));
         trace.mark("evaluate state");
-        const float value = read_loss ? mt::item<float>(loss) : 0.0F;
+        float value = 0.0F;
+#ifndef MTB_CPU_ONLY
+        if (early_loss) value = read_marked_loss(loss);
+        else
+#endif
+            if (read_loss) value = mt::item<float>(loss);
         trace.mark("loss");
         return value;
     }
+
+#ifndef MTB_CPU_ONLY
+    mt::detail::cuda::CudaRuntime &cuda_runtime() const {
+        return dynamic_cast<mt::detail::cuda::CudaRuntime &>(mt::detail::environment().runtime_for(device));
+    }
+
+    void mark_loss_ready() {
+        mt::detail::cuda::check(mtc_event_record(loss_ready, cuda_runtime().stream()), "loss mark");
+    }
+
+    // The loss, read on the copy stream once the device stream passed the mark.
+    float read_marked_loss(const mt::Tensor &loss) {
+        mt::Tensor l = loss;
+        const void *src = dense_region(l);
+        float value = 0.0F;
+        const int dev = static_cast<int>(device.index());
+        mt::detail::cuda::check(mtc_stream_wait_event(copy_stream, loss_ready), "loss wait");
+        mt::detail::cuda::check(mtc_copy_to_host(dev, &value, src, sizeof(float), copy_stream), "loss read");
+        // an index error of this or an earlier step whose snapshot has arrived
+        mt::detail::cuda::raise_device_errors(dev, false);
+        return value;
+    }
+
+    // One step from host inputs through the input pipeline: the batch is copied
+    // into the next slot on the copy stream (after the step that last read that
+    // slot), the device stream waits for the copy, and the loss is read early.
+    float step_pipelined(const float *x, const std::int64_t *labels, std::int64_t batch) {
+        const int dev = static_cast<int>(device.index());
+        const mt::Extent in = params.parameters().get(order.front()).value.shape()[1];
+        auto &rt = cuda_runtime();
+        if (copy_stream == nullptr) {
+            mt::detail::cuda::check(mtc_stream_create(dev, &copy_stream), "copy stream");
+            mt::detail::cuda::check(mtc_event_create(dev, &loss_ready), "event");
+            for (InputSlot &sl : slots) {
+                mt::detail::cuda::check(mtc_event_create(dev, &sl.copied), "event");
+                mt::detail::cuda::check(mtc_event_create(dev, &sl.free), "event");
+            }
+        }
+        if (batch != slot_batch) {
+            // (re)allocate the slots for this batch size, after all earlier use
+            mt::detail::cuda::check(mtc_stream_synchronize(rt.stream()), "stream");
+            for (InputSlot &sl : slots) {
+                sl.x = device_leaf(mt::detail::TensorSpec{mt::Shape{batch, in}, mt::DType::Float32, device}, rt);
+                sl.y = device_leaf(mt::detail::TensorSpec{mt::Shape{batch}, mt::DType::Int64, device}, rt);
+            }
+            slot_batch = batch;
+        }
+        InputSlot &sl = slots[next_slot];
+        next_slot ^= 1;
+        const std::size_t xb = static_cast<std::size_t>(batch * in) * sizeof(float);
+        const std::size_t yb = static_cast<std::size_t>(batch) * sizeof(std::int64_t);
+        mt::detail::cuda::check(mtc_stream_wait_event(copy_stream, sl.free), "slot wait");
+        mt::Tensor xs = *sl.x, ys = *sl.y;
+        mt::detail::cuda::check(mtc_copy_from_host(dev, dense_region(xs), x, xb, copy_stream), "input copy");
+        mt::detail::cuda::check(mtc_copy_from_host(dev, dense_region_i64(ys), labels, yb, copy_stream), "label copy");
+        mt::detail::cuda::check(mtc_event_record(sl.copied, copy_stream), "copy mark");
+        mt::detail::cuda::check(mtc_stream_wait_event(rt.stream(), sl.copied), "copy wait");
+        const float l = step(xs, ys, true, true);
+        mt::detail::cuda::check(mtc_event_record(sl.free, rt.stream()), "slot mark");
+        return l;
+    }
+
+    // A materialised leaf over a fresh device buffer of the spec's dense size.
+    static mt::Tensor device_leaf(mt::detail::TensorSpec spec, mt::detail::cuda::CudaRuntime &rt) {
+        mt::detail::BufferRef buffer = rt.allocate(mt::detail::dense_size_bytes(spec));
+        mt::detail::Materialization m(std::move(buffer), mt::detail::Layout::contiguous(spec.shape));
+        return mt::detail::TensorAccess::make(mt::detail::make_materialized_leaf(std::move(spec), std::move(m)));
+    }
+
+    static void *dense_region_i64(mt::Tensor &t) {
+        const auto *m = mt::detail::TensorAccess::value(t)->materialization();
+        auto *cb = dynamic_cast<mt::detail::cuda::CudaBuffer *>(m->buffer_ref().get());
+        if (cb == nullptr) throw std::logic_error{"label storage is not a device buffer"};
+        return static_cast<std::int64_t *>(cb->data()) + m->layout().offset();
+    }
+#endif
 
     // Data-parallel gradient exchange.  Each gradient's dense storage region is
     // summed over the ranks in place and scaled by 1/world, then the unchanged
@@ -308,6 +435,7 @@ struct MlpTrainer {
                 for (const auto &id : layers[l]) roots.push_back(grads.at(id));
                 std::vector<mt::Tensor> leaves = mt::leafify(roots);
                 const std::size_t skip = l + 1 == layers.size() ? 1 : 0;
+                if (skip == 1 && mark_loss) mark_loss_ready();
                 std::vector<void *> buffers;
                 std::vector<std::size_t> counts;
                 for (std::size_t i = 0; i < layers[l].size(); ++i) {
@@ -422,6 +550,13 @@ int mtb_mlp_step_resident(void *handle, int32_t read_loss, float *loss) {
 int mtb_mlp_step_host(void *handle, const float *x, const int64_t *labels, int64_t batch, float *loss) {
     return guarded([&] {
         auto *t = static_cast<MlpTrainer *>(handle);
+#ifndef MTB_CPU_ONLY
+        if (t->device.type() == mt::DeviceType::Cuda) {
+            const float l = t->step_pipelined(x, labels, batch);
+            if (loss) *loss = l;
+            return;
+        }
+#endif
         const mt::Extent in = t->params.parameters().get(t->order.front()).value.shape()[1];
         const mt::Tensor xt = mt::from_data(std::span<const float>(x, static_cast<std::size_t>(batch * in)),
                                             mt::Shape{batch, in}, t->device);

@@ -112,3 +112,26 @@ def test_gather_index_error_through_the_api(fe, ref):
             lib.gather_rows(dev, table, bad)
         out = lib.gather_rows(dev, table, good)
         np.testing.assert_array_equal(out, table[good])
+
+
+def test_pipelined_host_steps_match_resident_steps(fe):
+    """step_host copies each batch into one of two device slots on a copy
+    stream and reads the loss as soon as the forward pass has computed it.
+    Losses and parameters must equal those of steps on the same batches loaded
+    synchronously (load_batch + step_resident), bit for bit, including when
+    the batch size changes (the slots are reallocated)."""
+    rng = np.random.default_rng(17)
+    fin, hid, cls = 96, 160, 10
+    batches = []
+    for n in (256, 256, 256, 128, 128):
+        batches.append((rng.standard_normal((n, fin)).astype(F), rng.integers(0, cls, n).astype(np.int64)))
+    a = MlpTrainer(fe, 0, fin, hid, 3, cls, seed=11, lr=1e-3)
+    b = MlpTrainer(fe, 0, fin, hid, 3, cls, seed=11, lr=1e-3)
+    for x, y in batches:
+        a.load_batch(x.ctypes.data, y.ctypes.data, x.shape[0])
+        la = a.step_resident(read_loss=True)
+        lb = b.step_host(x.ctypes.data, y.ctypes.data, x.shape[0])
+        assert np.float32(la).view(np.uint32) == np.float32(lb).view(np.uint32), (la, lb)
+    np.testing.assert_array_equal(a.parameters().view(np.uint32), b.parameters().view(np.uint32))
+    a.close()
+    b.close()
