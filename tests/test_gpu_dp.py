@@ -71,6 +71,9 @@ def _rank_main(rank, world, port, out_path):
         ys = np.ascontiguousarray(y[rank * shard:(rank + 1) * shard])
         tr.load_batch(xs.ctypes.data, ys.ctypes.data, shard)
         losses = [tr.step_resident(read_loss=True) for _ in range(STEPS)]
+        # one more step from host memory: the input pipeline, with the loss read
+        # right after the first layer of the gradient exchange
+        losses.append(tr.step_host(xs.ctypes.data, ys.ctypes.data, shard))
         np.savez(out_path, losses=np.array(losses, dtype=np.float64), params=tr.parameters())
         tr.close()
         dist.barrier()
@@ -104,11 +107,12 @@ def test_two_gpu_training_matches_one_gpu(cuda, tmp_path):
     single = MlpTrainer(fe, 0, WIDTHS[0], WIDTHS[1], WIDTHS[2], WIDTHS[3], seed=9, lr=LR)
     x, y = _data()
     single.load_batch(x.ctypes.data, y.ctypes.data, BATCH)
-    losses = np.array([single.step_resident(read_loss=True) for _ in range(STEPS)])
+    losses = [single.step_resident(read_loss=True) for _ in range(STEPS)]
+    losses = np.array(losses + [single.step_host(x.ctypes.data, y.ctypes.data, BATCH)])
     mean_rank_loss = (r0["losses"] + r1["losses"]) / 2
     np.testing.assert_allclose(mean_rank_loss, losses, rtol=1e-5, atol=1e-6)
     diff = np.abs(single.parameters() - r0["params"])
     # Adam may flip the sign of an update whose gradient is within rounding of zero (moves 2*lr)
-    assert diff.max() <= STEPS * 2 * LR + 1e-6
+    assert diff.max() <= (STEPS + 1) * 2 * LR + 1e-6
     assert np.mean(diff > 1e-5) < 0.02, float(np.mean(diff > 1e-5))
     single.close()
