@@ -176,7 +176,8 @@ def reduce_argmax(x: np.ndarray, axis: int, keep_dim: bool = False) -> np.ndarra
 def log_softmax(x: np.ndarray, axis: int) -> np.ndarray:
     """x - logsumexp(x, {axis}, keep_dim=true): the reference composite (Subtract of LogSumExp)."""
     x = np.asarray(x, dtype=F32)
-    return (x - reduce_logsumexp(x, [axis], keep_dim=True)).astype(F32)
+    with np.errstate(invalid="ignore"):  # a row of -inf (or +inf) gives NaN, as in IEEE arithmetic
+        return (x - reduce_logsumexp(x, [axis], keep_dim=True)).astype(F32)
 
 
 # ------------------------------------------------------------------ matmul --

@@ -188,3 +188,41 @@ def test_random_creation_matches_reference(n):
     nkey = tuple(int(x) for x in CASES[f"random_{n}/nkey"])
     assert_bits(mo.uniform(n, -2.0, 3.0, ukey), CASES[f"random_{n}/uniform"], "uniform")
     assert_ulp(mo.normal(n, 0.5, 2.0, nkey), CASES[f"random_{n}/normal"], 1, "normal")
+
+
+# ---- ops with no reference kernel (max, argmax, log-softmax): hand answers ----
+
+NINF = F(-np.inf)
+
+
+def test_max_known_answers():
+    x = np.array([[1, 3, 2], [NINF, -5, NINF], [7, np.nan, 9]], dtype=F)
+    assert_bits(mo.reduce_max(x, [1]), np.array([3, -5, np.nan], dtype=F), "max axis 1")
+    assert_bits(mo.reduce_max(x, [0]), np.array([7, np.nan, 9], dtype=F), "max axis 0")
+    assert mo.reduce_max(x, [1], keep_dim=True).shape == (3, 1)
+    assert_bits(mo.reduce_max(np.zeros((2, 0), F), [1]), np.array([NINF, NINF], dtype=F), "empty axis")
+    assert_bits(mo.reduce_max(x[:2], [0, 1]), np.array(3, dtype=F), "all axes")
+
+
+def test_argmax_known_answers():
+    x = np.array([[2, 5, 5, 1], [1, np.nan, 9, np.nan], [NINF, NINF, NINF, NINF]], dtype=F)
+    # first maximum wins a tie; the first NaN is the maximum; an all -inf row gives 0
+    assert_bits(mo.reduce_argmax(x, 1), np.array([1, 1, 0], dtype=np.int64), "argmax axis 1")
+    assert_bits(mo.reduce_argmax(x, 0), np.array([0, 1, 1, 1], dtype=np.int64), "argmax axis 0")
+    assert mo.reduce_argmax(x, 0, keep_dim=True).shape == (1, 4)
+
+
+def test_log_softmax_known_answers():
+    # softmax of [0, ln 2, ln 3] is [1/6, 2/6, 3/6]
+    x = np.array([[0, np.log(2), np.log(3)], [NINF, 0, NINF]], dtype=F)
+    want = np.array([np.log([1 / 6, 1 / 3, 1 / 2]), [-np.inf, 0, -np.inf]], dtype=F)
+    assert_ulp(mo.log_softmax(x, 1), want, 2, "log_softmax")
+    # large equal logits stay finite; the composite x - logsumexp(x) rounds
+    # logsumexp near 1001, so the error is one spacing there, not ulps of ln 3
+    big = mo.log_softmax(np.full((1, 3), 1000, F), 1)
+    assert np.all(np.abs(big.astype(np.float64) + np.log(3)) <= np.spacing(F(1001)))
+    # the composite: x - logsumexp(x) with the reference's logsumexp, bit for bit
+    y = CASES["reduce_lse_special/x"].reshape(5, 3)
+    with np.errstate(invalid="ignore"):
+        composite = (y - mo.reduce_logsumexp(y, [1], keep_dim=True)).astype(F)
+    assert_bits(mo.log_softmax(y, 1), composite, "composite")
