@@ -63,6 +63,10 @@ class Frontend:
             fn = getattr(L, name)
             fn.argtypes = args
             fn.restype = res
+        # only the backend library has the operations it adds to MiniTensor
+        if hasattr(L, "mtb_added_ops"):
+            L.mtb_added_ops.argtypes = [ctypes.c_int, i64, i64, P(f32), i32, P(f32), P(f32), P(i64), P(f32)]
+            L.mtb_added_ops.restype = ctypes.c_int
 
     def _check(self, rc: int, what: str):
         if rc == 0:
@@ -108,6 +112,22 @@ class Frontend:
                                              i.size, i.ctypes.data_as(P(ctypes.c_int64)),
                                              out.ctypes.data_as(P(ctypes.c_float))), "gather_rows")
         return out
+
+    def added_ops(self, device: int, x: np.ndarray, axis: int):
+        """relu(x), and max, argmax and log-softmax of x along `axis`, through the
+        operations this backend adds to MiniTensor's API."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows, cols = x.shape
+        relu = np.empty_like(x)
+        lsm = np.empty_like(x)
+        reduced = cols if axis == 0 else rows
+        mx = np.empty(reduced, dtype=np.float32)
+        am = np.empty(reduced, dtype=np.int64)
+        P = ctypes.POINTER
+        f = lambda a: a.ctypes.data_as(P(ctypes.c_float))
+        self._check(self.lib.mtb_added_ops(device, rows, cols, f(x), axis, f(relu), f(mx),
+                                           am.ctypes.data_as(P(ctypes.c_int64)), f(lsm)), "added_ops")
+        return relu, mx, am, lsm
 
     def stats(self) -> dict:
         buf = (ctypes.c_uint64 * 12)()

@@ -3,8 +3,9 @@
 // sigmoid, its reductions sum and logsumexp); the benchmark workloads need them.
 //
 //  relu(x)            composite (x + |x|) * 0.5 of reference ops: exact ReLU in
-//                     float32 (-0 -> +0, NaN propagates), differentiable through
-//                     the reference's own VJP rules (gradient 0.5 at 0), and one
+//                     float32 for finite x (-0 -> +0), NaN propagates, and -inf
+//                     gives NaN (-inf + inf); differentiable through the
+//                     reference's own VJP rules (gradient 0.5 at 0), and one
 //                     fused kernel on the GPU.
 //  max(x, axes)       new primitive 0x0380: NaN propagates, empty -> -inf.
 //  argmax(x, axis)    new primitive 0x0381: Int64 index of the first maximum; a

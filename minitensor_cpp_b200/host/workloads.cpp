@@ -660,6 +660,30 @@ int mtb_gather_rows(int device, int64_t rows, int64_t cols, const float *table, 
     });
 }
 
+#ifndef MTB_CPU_ONLY
+// The operations this backend adds (ops_ext.hpp) on a [rows, cols] matrix,
+// through MiniTensor's API: relu(x), and max, argmax and log-softmax along
+// `axis` (0 or 1).  max_out and argmax_out hold the reduced extent, the other
+// two rows * cols values.
+int mtb_added_ops(int device, int64_t rows, int64_t cols, const float *x, int32_t axis, float *relu_out,
+                  float *max_out, int64_t *argmax_out, float *log_softmax_out) {
+    return guarded([&] {
+        if (axis != 0 && axis != 1) throw std::invalid_argument{"axis must be 0 or 1"};
+        const mt::Device dev = device_of(device);
+        const mt::Tensor X = mt::from_data(std::span<const float>(x, static_cast<std::size_t>(rows * cols)),
+                                           mt::Shape{rows, cols}, dev);
+        const std::vector<float> r = mt::to_vector(mt::b200::relu(X));
+        const std::vector<float> m = mt::to_vector(mt::b200::max(X, {axis}));
+        const std::vector<std::int64_t> a = mt::to_vector<std::int64_t>(mt::b200::argmax(X, axis));
+        const std::vector<float> l = mt::to_vector(mt::b200::log_softmax(X, axis));
+        std::copy(r.begin(), r.end(), relu_out);
+        std::copy(m.begin(), m.end(), max_out);
+        std::copy(a.begin(), a.end(), argmax_out);
+        std::copy(l.begin(), l.end(), log_softmax_out);
+    });
+}
+#endif
+
 void mtb_evaluator_stats(uint64_t *out12) {
 #ifndef MTB_CPU_ONLY
     const auto &s = mt::detail::cuda::evaluator_stats();

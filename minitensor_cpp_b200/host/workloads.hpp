@@ -64,6 +64,14 @@ int mtb_chain(int device, int64_t n, int64_t m, const float *a, const float *b_s
 int mtb_gather_rows(int device, int64_t rows, int64_t cols, const float *table, int64_t n, const int64_t *index,
                     float *out);
 
+// The operations this backend adds (relu, max, argmax, log-softmax) on a
+// [rows, cols] matrix through the public API; the reductions run along `axis`
+// (0 or 1).  relu_out and log_softmax_out hold rows * cols values, max_out and
+// argmax_out the extent of the other axis.  Not in the CPU-only build: the
+// unmodified reference has none of these operations.
+int mtb_added_ops(int device, int64_t rows, int64_t cols, const float *x, int32_t axis, float *relu_out,
+                  float *max_out, int64_t *argmax_out, float *log_softmax_out);
+
 // Counters of the fusing evaluator (zeros in the CPU-only build):
 // kernel_steps, fused_launches, fused_nodes, folded_constants, view_steps, evaluations,
 // and host nanoseconds spent planning, issuing kernels and in the index-error check.

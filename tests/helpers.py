@@ -50,7 +50,36 @@ def assert_rel_sqrtk(actual, expected, k: int, scale=None, what: str = ""):
     assert (a[~finite & ~np.isnan(e)] == e[~finite & ~np.isnan(e)]).all(), f"{what}: infinities differ"
     s = np.abs(e) if scale is None else np.asarray(scale, dtype=np.float64)
     tol = 1e-5 * np.sqrt(max(k, 1)) * np.maximum(s, 1e-30)
-    err = np.abs(a - e)
+    with np.errstate(invalid="ignore"):  # inf - inf at the infinities checked above
+        err = np.abs(a - e)
     bad = finite & (err > tol)
     assert not bad.any(), (f"{what}: {int(bad.sum())} elements exceed 1e-5*sqrt({k}); worst ratio "
                            f"{float(np.max(np.where(finite, err / tol, 0))):.3g}")
+
+
+def check_added_ops(fe, device: int, x: np.ndarray, axis: int):
+    """relu, max, argmax and log-softmax through the front-end's added operations
+    against the oracle: bit for bit, log-softmax within the logsumexp bound
+    (1e-5*sqrt(K) of |lse|)."""
+    from oracle import mt_oracle as mo
+
+    relu, mx, am, lsm = fe.added_ops(device, x, axis)
+    with np.errstate(invalid="ignore"):  # -inf + inf is NaN in the composite as in the kernel
+        want_relu = ((x + np.abs(x)) * F32(0.5)).astype(F32)
+    assert_bits(relu, want_relu, f"relu device {device}")
+    assert_bits(mx, mo.reduce_max(x, [axis]), f"max axis {axis} device {device}")
+    assert_bits(am, mo.reduce_argmax(x, axis), f"argmax axis {axis} device {device}")
+    lse = mo.reduce_logsumexp(x, [axis], keep_dim=True)
+    scale = np.broadcast_to(np.abs(lse), x.shape)
+    assert_rel_sqrtk(lsm, mo.log_softmax(x, axis), x.shape[axis], scale, f"log_softmax axis {axis} device {device}")
+
+
+def added_ops_input(rows: int, cols: int, seed: int) -> np.ndarray:
+    """Uniform values with a tie, a NaN, a row of -inf and a -0 planted."""
+    rng = np.random.default_rng(seed)
+    x = rng.uniform(-10, 10, (rows, cols)).astype(F32)
+    x[1, 2] = x[1, 5] = F32(50)  # a tie along axis 1
+    x[3, 4] = F32(np.nan)
+    x[5, :] = F32(-np.inf)
+    x[2, 0] = F32(-0.0)
+    return x

@@ -68,3 +68,14 @@ def test_gather_rows_and_index_error_on_the_cpu_device():
         np.testing.assert_array_equal(fe.gather_rows(-1, table, idx), table[idx])
         with pytest.raises(IndexError):
             fe.gather_rows(-1, table, np.array([15], dtype=np.int64))
+
+
+@pytest.mark.parametrize("axis", [0, 1])
+def test_added_operations_on_the_cpu_device(fe, axis):
+    """relu, max, argmax and log-softmax (the operations this backend adds, with
+    their CPU kernels) through MiniTensor's API, against the oracle."""
+    from helpers import added_ops_input, check_added_ops
+
+    check_added_ops(fe, -1, added_ops_input(9, 13, seed=4), axis)
+    with pytest.raises(ValueError):
+        fe.added_ops(-1, np.zeros((2, 2), F), 2)

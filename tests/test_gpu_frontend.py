@@ -135,3 +135,13 @@ def test_pipelined_host_steps_match_resident_steps(fe):
     np.testing.assert_array_equal(a.parameters().view(np.uint32), b.parameters().view(np.uint32))
     a.close()
     b.close()
+
+
+@pytest.mark.parametrize("axis", [0, 1])
+@pytest.mark.parametrize("rows, cols", [(9, 13), (1024, 3000)])
+def test_added_operations_on_the_cuda_device(fe, axis, rows, cols):
+    """relu, max, argmax and log-softmax through MiniTensor's API on the GPU (the
+    evaluator fuses relu; the reductions run the CUDA kernels), against the oracle."""
+    from helpers import added_ops_input, check_added_ops
+
+    check_added_ops(fe, 0, added_ops_input(rows, cols, seed=5), axis)
