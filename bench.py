@@ -9,6 +9,7 @@ training iteration (forward, backward, all-reduce, Adam update, leafify) of the
 unchanged MiniTensor front-end running on the CUDA backend.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --case gemm|chain|reduce|log_softmax|gather|scatter_add|concat|uniform|normal|adamw|spiral ...
 
 `value` times K steps on device-resident inputs (CUDA events on the backend's
 stream, barrier + synchronize on both sides, max over ranks).  `e2e` times steps
@@ -188,6 +189,154 @@ def _worker(args):
     return cpu_reference_sample(batch, steps)
 
 
+# ------------------------------------------------------- single-kernel cases --
+# `python bench.py --case NAME [options]` runs one kernel of the backend alone
+# on cuda:0 (operands made with torch, device memory only), for ncu captures
+# and for timing one kernel: the set-up call, --warm-s seconds of untimed calls,
+# then --reps calls back to back (prepared ABI calls) between two CUDA events on
+# the current stream.  It prints one JSON line with the mean time per call.
+# Under a profiler pass --warm-s 0 --reps 1: the launches are then the set-up
+# call and one timed call.
+
+def _case_ms(fn, reps: int, warm_s: float) -> float:
+    import torch
+
+    fn()  # set-up call: NVRTC / tensor-map preparation, not timed
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()  # untimed calls so the SM clock has left idle
+    while time.perf_counter() - t0 < warm_s:
+        fn()
+        torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        fn()
+    stop.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(stop) / reps
+
+
+def adamw_program(lr=1e-3, b1=0.9, b2=0.999, eps=1e-8, c1=0.1, c2=0.001):
+    """AdamW's per-parameter update as one fused program: registers 0..3 are
+    p, g, m, v; outputs p', m', v' (the evaluator builds the same cluster for
+    AdamW::update_parameter, src/nn/optimizers/adamw.cpp:67-97)."""
+    from minitensor_cpp_b200 import abi
+
+    C, M, A, D, S = abi.CONST, abi.MULTIPLY, abi.ADD, abi.DIVIDE, abi.SUBTRACT
+    prog = [(C, 4, 0, 0, b1), (M, 5, 4, 2, 0.0), (C, 6, 0, 0, 1 - b1), (M, 7, 6, 1, 0.0), (A, 8, 5, 7, 0.0),
+            (C, 9, 0, 0, b2), (M, 10, 9, 3, 0.0), (C, 11, 0, 0, 1 - b2), (M, 12, 11, 1, 0.0), (M, 13, 12, 1, 0.0),
+            (A, 14, 10, 13, 0.0), (C, 15, 0, 0, c1), (D, 16, 8, 15, 0.0), (C, 17, 0, 0, c2), (D, 18, 14, 17, 0.0),
+            (C, 21, 0, 0, lr), (M, 22, 21, 16, 0.0), (abi.SQRT, 23, 18, 0, 0.0), (C, 24, 0, 0, eps),
+            (A, 25, 23, 24, 0.0), (D, 26, 22, 25, 0.0), (S, 27, 0, 26, 0.0)]
+    return prog, [27, 8, 14]
+
+
+def _case(a) -> dict:
+    """One kernel case; returns its figures (ms per call and the rate)."""
+    import torch
+
+    from minitensor_cpp_b200 import abi
+
+    V = abi.View.of
+    g = torch.Generator(device="cuda").manual_seed(a.seed)
+    run = lambda call: _case_ms(call, a.reps, a.warm_s)
+    if a.case == "gemm":
+        algo = {"auto": abi.GEMM_AUTO, "simt": abi.GEMM_SIMT, "3xtf32": abi.GEMM_3XTF32,
+                "simt_ffma": abi.GEMM_SIMT_FFMA}[a.algo]
+        m = a.m or a.n
+        lead = (a.batch,) if a.batch > 1 else ()
+        A = torch.randn(*lead, a.k, m, device="cuda", generator=g).transpose(-1, -2) if a.at else \
+            torch.randn(*lead, m, a.k, device="cuda", generator=g)
+        B = torch.randn(*lead, a.n, a.k, device="cuda", generator=g).transpose(-1, -2) if a.bt else \
+            torch.randn(*lead, a.k, a.n, device="cuda", generator=g)
+        C = torch.empty(*lead, m, a.n, device="cuda")
+        ms = run(abi.matmul(V(A), V(B), V(C), algo, prepare=True))
+        return {"ms": ms, "tflops": 2.0 * a.batch * m * a.n * a.k / ms / 1e9}
+    if a.case == "chain":
+        n = a.n
+        u = lambda *s: torch.rand(*s, device="cuda", generator=g) * 2 - 1
+        A, Bs, row, col = u(n, n), u(n, n), u(1, n), u(n, 1)
+        E, Y = torch.empty(n, 1, device="cuda"), torch.empty(n, n, device="cuda")
+        abi.fused([(abi.NEGATE, 1, 0, 0, 0.0), (abi.EXP, 2, 1, 0, 0.0)], [V(col)], [2], [V(E)])
+        prog = [(abi.MULTIPLY, 4, 0, 1, 0.0), (abi.ADD, 5, 4, 2, 0.0), (abi.RELU, 6, 5, 0, 0.0),
+                (abi.MULTIPLY, 7, 6, 3, 0.0)]
+        ms = run(abi.fused(prog, [V(A), V(Bs.t()), V(row), V(E)], [7], [V(Y)], prepare=True))
+        return {"ms": ms, "gbs": 4.0 * (3 * n * n + 2 * n) / ms / 1e6}
+    if a.case in ("reduce", "log_softmax"):
+        X = torch.rand(a.n, a.m or a.n, device="cuda", generator=g) * 2 - 1
+        if a.case == "log_softmax":
+            Y = torch.empty_like(X)
+            ms = run(abi.log_softmax(V(X), 1, V(Y), prepare=True))
+            return {"ms": ms, "gbs": X.numel() * 8.0 / ms / 1e6}
+        op = {"sum": abi.SUM, "max": abi.MAX, "argmax": abi.ARGMAX, "lse": abi.LOGSUMEXP}[a.op]
+        O = torch.empty(X.shape[1 - a.axis], device="cuda", dtype=torch.int64 if a.op == "argmax" else torch.float32)
+        ms = run(abi.reduce(op, V(X), [a.axis], V(O), prepare=True))
+        return {"ms": ms, "gbs": X.numel() * 4.0 / ms / 1e6}
+    if a.case in ("gather", "scatter_add"):
+        # row gather / scatter-add: the Int64 index column broadcast over the row width
+        T = torch.randn(a.rows, a.cols, device="cuda", generator=g)
+        idx = torch.randint(0, a.rows, (a.rows,), device="cuda", generator=g, dtype=torch.int64)
+        O = torch.empty(a.rows, a.cols, device="cuda")
+        vi = abi.View(idx, (a.rows, a.cols), (1, 0), 0)
+        if a.case == "gather":
+            ms = run(abi.gather(V(T), vi, 0, V(O), prepare=True))
+        else:
+            U = torch.floor(torch.rand(a.rows, a.cols, device="cuda", generator=g) * 16 - 8)
+            ms = run(abi.gather_scatter_add(V(U), vi, 0, V(O), prepare=True))
+        return {"ms": ms, "gbs": (2.0 * a.rows * a.cols * 4 + a.rows * 8) / ms / 1e6}
+    if a.case == "concat":
+        parts = [torch.randn(a.n, a.k, device="cuda", generator=g) for _ in range(4)]
+        D = torch.empty((4 * a.n, a.k) if a.axis == 0 else (a.n, 4 * a.k), device="cuda")
+        ms = run(abi.concat([V(p) for p in parts], a.axis, V(D), prepare=True))
+        return {"ms": ms, "gbs": 2.0 * 4 * a.n * a.k * 4 / ms / 1e6}
+    if a.case in ("uniform", "normal"):
+        O = torch.empty(a.numel, device="cuda")
+        fn = abi.uniform if a.case == "uniform" else abi.normal
+        lo_hi = (-1.0, 1.0) if a.case == "uniform" else (0.0, 1.0)
+        call = lambda: fn(V(O), *lo_hi, (a.seed, 7))
+        ms = run(call)
+        return {"ms": ms, "gbs": 4.0 * a.numel / ms / 1e6}
+    if a.case == "adamw":
+        n = a.numel
+        p, gr, m = (torch.randn(n, device="cuda", generator=g) for _ in range(3))
+        v = torch.rand(n, device="cuda", generator=g)
+        outs = [torch.empty(n, device="cuda") for _ in range(3)]
+        prog, regs = adamw_program()
+        ms = run(abi.fused(prog, [V(t) for t in (p, gr, m, v)], regs, [V(t) for t in outs], prepare=True))
+        return {"ms": ms, "gbs": 28.0 * n / ms / 1e6}
+    if a.case == "spiral":
+        from minitensor_cpp_b200.frontend import Frontend
+
+        fe = Frontend()
+        fe.set_graphs(not a.eager)
+        fe.spiral_train(0, 20, loss_every=0)
+        n0 = abi.launch_count()
+        fe.reset_stats()
+        _, secs = fe.spiral_train(0, a.spiral_steps, loss_every=0)
+        st = fe.stats()
+        steps = max(a.spiral_steps, 1)
+        return {"ms_per_step": secs * 1e3 / steps, "samples_per_s": 300 * steps / secs,
+                "launches_per_step": (abi.launch_count() - n0) / steps, "replays": st["graph_replays"],
+                "evaluations": st["evaluations"], "plan_us_per_step": st["plan_ns"] / 1e3 / steps,
+                "execute_us_per_step": st["execute_ns"] / 1e3 / steps}
+    raise SystemExit(f"unknown case {a.case}")
+
+
+def run_case(a) -> None:
+    import torch
+
+    from minitensor_cpp_b200 import abi
+
+    if not torch.cuda.is_available():
+        raise SystemExit("--case needs a CUDA device")
+    torch.cuda.set_device(0)
+    abi.lib()
+    res = _case(a)
+    abi.check_device_errors(0)
+    keys = ("m", "n", "k", "batch", "at", "bt", "algo", "op", "axis", "rows", "cols", "numel", "reps", "eager")
+    print(json.dumps({"case": a.case, **{k: getattr(a, k) for k in keys}, **res}))
+
+
 # ------------------------------------------------------------ micro (N=1) --
 
 def _time_ms(fn, reps=10, groups=3, warm=2) -> float:
@@ -253,8 +402,6 @@ def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
     ms = _time_ms(abi.log_softmax(V(Y), 1, V(Z), prepare=True))
     out["log_softmax_axis1_GBps"] = gbs(8 * n * n, ms)
     # the fused AdamW update of all 150.8 M parameters: p, g, m, v read; p', m', v' written
-    from minitensor_cpp_b200.kernel_cases import adamw_program
-
     npar = sum(a * b + b for a, b in zip(WIDTHS[:-1], WIDTHS[1:]))
     st = [torch.randn(npar, device="cuda", generator=g) for _ in range(3)] + [torch.rand(npar, device="cuda")]
     res = [torch.empty(npar, device="cuda") for _ in range(3)]
@@ -323,21 +470,26 @@ def micro_benchmarks(hbm_gbs: float, tf32_tflops: float) -> dict:
     from minitensor_cpp_b200.frontend import Frontend
 
     fe = Frontend()
-    steps = 500
+    steps = 3000  # long enough for several clock samples (200 ms apart) per leg
     # eager: every step re-planned and its kernels launched one by one
     graphs = fe.set_graphs(False)
     fe.spiral_train(0, 20, loss_every=0)  # warm-up: NVRTC programs and allocator blocks
-    _, secs = fe.spiral_train(0, steps, loss_every=0)
+    with ClockSampler(0) as ck:
+        _, secs = fe.spiral_train(0, steps, loss_every=0)
     out["spiral_eager_samples_per_s"] = 300 * steps / secs
+    out["spiral_eager_sm_mhz"] = ck.summary()["sm_mhz"] or 0.0
     # default: the repeated step plan is recorded once and replayed as a CUDA graph
     fe.set_graphs(True)
     fe.spiral_train(0, 20, loss_every=0)
     n0 = abi.launch_count()
     fe.reset_stats()
-    _, secs = fe.spiral_train(0, steps, loss_every=0)
+    with ClockSampler(0) as ck:
+        _, secs = fe.spiral_train(0, steps, loss_every=0)
     st = fe.stats()
     fe.set_graphs(graphs)
     out["spiral_train_samples_per_s"] = 300 * steps / secs
+    out["spiral_train_sm_mhz"] = ck.summary()["sm_mhz"] or 0.0
+    out["spiral_host_us_per_step"] = (st["plan_ns"] + st["execute_ns"] + st["check_ns"]) / 1e3 / steps
     out["spiral_launches_per_step"] = (abi.launch_count() - n0) / steps
     out["spiral_replayed_steps_frac"] = st["graph_replays"] / max(st["evaluations"], 1)
     # -- the broadcast chain and its reductions end to end through the API: host
@@ -470,6 +622,7 @@ def run_ours(args) -> None:
     launches0 = abi.launch_count()
     abi.profile_gemm(reset=True)
     abi.profile_enable(True)
+    tr.profile(True)
     barrier()
     torch.cuda.synchronize()
     tr.synchronize()
@@ -482,11 +635,19 @@ def run_ours(args) -> None:
         tr.synchronize()
         torch.cuda.synchronize()
     abi.profile_enable(False)
+    phase_ms = tr.profile(False)
     launches = abi.launch_count() - launches0
     ms_local = start.elapsed_time(stop)
     ms = max_over_ranks(ms_local)
     barrier()
     gemm_n, gemm_ms, gemm_flops = abi.profile_gemm(reset=True)
+    # device milliseconds per step on this rank: the GEMMs, and (N > 1) the
+    # phases around the gradient exchange; the slowest rank's figures are kept
+    phases = {"gemm": gemm_ms / args.steps, "step": phase_ms[0] / args.steps}
+    if world > 1:
+        phases.update({"forward_backward": phase_ms[1] / args.steps, "exposed_allreduce": phase_ms[2] / args.steps,
+                       "optimizer": phase_ms[3] / args.steps})
+    phases = {k: max_over_ranks(v) for k, v in phases.items()}
 
     # ---- e2e: host buffers through the public API, loss read back every step
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
@@ -543,7 +704,8 @@ def run_ours(args) -> None:
     cpu = None
     if world == 1 and not args.skip_cpu:
         s = cpu_reference_sample(args.cpu_batch, 1)
-        cpu = {"value": s["samples"] / s["seconds"], "unit": "samples/s", "cores": 1, "kind": "reference",
+        cpu = {"value": s["samples"] / s["seconds"], "unit": "samples/s", "cores": 1, "host_cores": os.cpu_count(),
+               "kind": "reference",
                "sample": f"1 training step at batch {args.cpu_batch} (same model, Adam) on the reference CPU "
                          f"backend, {s['seconds']:.1f} s"}
         if not args.skip_micro:
@@ -568,6 +730,7 @@ def run_ours(args) -> None:
                 "h2d_bytes_per_step": world * (x.numel() * 4 + y.numel() * 8),
                 "d2h_bytes_per_step": world * 4},
         "gpu_launches": launches,
+        "phases_ms_per_step": {k: round(v, 3) for k, v in phases.items()},
         "roofline": roofline,
         "cpu_baseline": cpu,
         "clocks": clocks.summary(),
@@ -621,7 +784,8 @@ def run_reference(args) -> None:
         "dtype": "f32",
         "data": "synthetic (seeded N(0,1) inputs, uniform Int64 labels)",
         "config": config(args.gpus),
-        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": workers, "kind": "reference",
+        "cpu_baseline": {"value": value, "unit": "samples/s", "cores": workers, "host_cores": cores,
+                         "kind": "reference",
                          "sample": f"{workers} single-threaded reference processes x {steps} training step at "
                                    f"batch {batch} each (the reference is single-threaded); wall {wall:.1f} s"},
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -639,7 +803,31 @@ def main() -> None:
     p.add_argument("--cpu-batch", type=int, default=4)
     p.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline sample")
     p.add_argument("--skip-micro", action="store_true", help="omit the kernel microbenchmarks (N=1 only)")
+    c = p.add_argument_group("single-kernel cases (--case)")
+    c.add_argument("--case", choices=("gemm", "chain", "reduce", "log_softmax", "gather", "scatter_add", "concat",
+                                      "uniform", "normal", "adamw", "spiral"),
+                   help="run one kernel alone on cuda:0 and print its time (for ncu captures)")
+    c.add_argument("--m", type=int, default=0, help="gemm: rows of A (default --n); reduce: columns")
+    c.add_argument("--n", type=int, default=8192)
+    c.add_argument("--k", type=int, default=8192)
+    c.add_argument("--batch", type=int, default=1)
+    c.add_argument("--at", action="store_true", help="gemm: A is the transposed view of a [k, m] tensor")
+    c.add_argument("--bt", action="store_true", help="gemm: B is the transposed view of an [n, k] tensor")
+    c.add_argument("--algo", default="3xtf32", choices=("auto", "simt", "3xtf32", "simt_ffma"))
+    c.add_argument("--op", default="sum", choices=("sum", "max", "argmax", "lse"))
+    c.add_argument("--axis", type=int, default=0)
+    c.add_argument("--rows", type=int, default=1 << 24)
+    c.add_argument("--cols", type=int, default=64)
+    c.add_argument("--numel", type=int, default=150823912, help="adamw / uniform / normal: element count")
+    c.add_argument("--reps", type=int, default=3)
+    c.add_argument("--seed", type=int, default=0)
+    c.add_argument("--spiral-steps", type=int, default=500)
+    c.add_argument("--eager", action="store_true", help="spiral: no plan replay")
+    c.add_argument("--warm-s", type=float, default=0.3, help="untimed calls first (0 under a profiler)")
     args = p.parse_args()
+    if args.case:
+        run_case(args)
+        return
     if args.warmup < 3:
         p.error("--warmup must be at least 3")
     if args.impl == "reference":

@@ -156,6 +156,11 @@ int mtc_event_create(int device, void **event);
 int mtc_event_destroy(int device, void *event);
 int mtc_event_record(void *event, void *stream);
 int mtc_stream_wait_event(void *stream, void *event);
+/* Events that record a time stamp, for measuring phases of work on a stream;
+ * mtc_event_elapsed waits for `stop` and gives the milliseconds between the two
+ * recordings.  No reference counterpart. */
+int mtc_event_create_timed(int device, void **event);
+int mtc_event_elapsed(void *start, void *stop, float *milliseconds);
 /* Bytes held from the driver by / handed out from the caching allocator. */
 int mtc_pool_stats(int device, uint64_t *reserved_bytes, uint64_t *used_bytes);
 /* Return cached-but-unused blocks to the driver (synchronises the device).
@@ -232,6 +237,15 @@ int mtc_gather(const mtc_desc *src, const mtc_desc *idx, int64_t axis, const mtc
  * (integer-valued updates below 2^24), otherwise equal up to summation order. */
 int mtc_gather_scatter_add(const mtc_desc *upd, const mtc_desc *idx, int64_t axis, const mtc_desc *out,
                            void *stream);
+
+/* out[..idx[..i..]..] += upd[..i..] WITHOUT clearing out first: the updates are
+ * added to the values already there (float32 atomics, so duplicate indices
+ * accumulate in an unspecified order).  No reference counterpart: the fusing
+ * evaluator uses it for the gather VJP's scatter-add (rules/manipulation.cpp:81-91)
+ * when its only consumer is an elementwise Add that becomes the scatter's
+ * target, so the [B, C] zero fill and its read-back disappear. */
+int mtc_gather_scatter_add_into(const mtc_desc *upd, const mtc_desc *idx, int64_t axis, const mtc_desc *out,
+                                void *stream);
 
 /* -------------------------------------------------------- reductions (A8, A9) -- */
 
@@ -343,6 +357,12 @@ int mtc_profile_enable(int on);
  * time (ms, from the events; synchronises them) and algorithmic FLOPs (2*M*N*K
  * per batch entry).  reset != 0 clears the totals afterwards. */
 int mtc_profile_gemm(uint64_t *launches, double *milliseconds, double *flops, int reset);
+
+/* Matmul calls since process start by the kernel family that ran them:
+ * *tensor_core counts calls served by the tcgen05 3xTF32 kernels, *simt those
+ * served by the SIMT kernels (exact or FFMA).  Lets a caller confirm which path
+ * MTC_GEMM_AUTO took.  No reference counterpart (the reference has one CPU loop). */
+int mtc_gemm_path_counts(uint64_t *tensor_core, uint64_t *simt);
 
 /* -------------------------------------------------- data parallel (config 5) --
  * Gradient all-reduce between the ranks of a data-parallel job, one process per

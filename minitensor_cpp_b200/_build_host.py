@@ -1,7 +1,8 @@
 """Builds libminitensor_b200.so: MiniTensor's front-end with the CUDA backend.
 
 The MiniTensor sources are compiled from the reference tree (read-only) with the
-two edits a new device type needs, which no plugin can avoid:
+two edits a new device type needs, which no plugin can avoid, and one that lets
+the backend's new operations carry gradients:
 
 1. include/minitensor/types.hpp: `DeviceType::Cuda` and the `Device::cuda(i)`
    factory (the enum has only `Cpu` and Device's constructor is private,
@@ -11,6 +12,10 @@ two edits a new device type needs, which no plugin can avoid:
    runtime and kernels (environment.cpp:16-20), and `evaluate` first offers the
    roots to `evaluate_with_backend_extensions` (environment.cpp:22-26).  Both
    hooks are weak symbols, so the edited file still links without a backend.
+3. src/tensor/autograd/vjp_registry.cpp: the registry, built once from the
+   reference's own rule sets, also calls `register_backend_vjps(registry)`
+   (weak) after them, so relu (an operation this backend adds) has a VJP rule.
+   The registry is a sealed function-local static (vjp_registry.cpp:36-48).
 
 The edits are applied to a private working copy under the system temp
 directory (never inside this repository); the objects and the library land in
@@ -32,7 +37,8 @@ HOST = PKG / "host"
 LIB = PKG / "lib"
 BUILD = ROOT / "_build" / "host"
 INCLUDE = ROOT / "include"
-REFERENCE = Path(os.environ.get("MINITENSOR_REFERENCE", "/root/reference"))
+# the MiniTensor sources: $MINITENSOR_REFERENCE, else the checkout "reference" beside this repository
+REFERENCE = Path(os.environ.get("MINITENSOR_REFERENCE", ROOT.parent / "reference"))
 
 CXX = os.environ.get("CXX", "g++")
 # -fno-semantic-interposition: the library binds its own symbols (-Bsymbolic),
@@ -70,6 +76,17 @@ EDITS = [
      "void ExecutionEnvironment::evaluate(std::span<const ValueRef> roots)\n{\n"
      "    if (evaluate_with_backend_extensions != nullptr && "
      "evaluate_with_backend_extensions(runtimes_, kernels_, roots))\n    {\n        return;\n    }\n"),
+    ("src/tensor/autograd/vjp_registry.cpp",
+     "namespace minitensor::detail\n{\nvoid VjpRegistry::register_erased",
+     "namespace minitensor::detail\n{\n"
+     "// Optional rules of a device backend's own operations (weak: absent without one).\n"
+     "[[gnu::weak]] void register_backend_vjps(VjpRegistry &registry);\n\n"
+     "void VjpRegistry::register_erased"),
+    ("src/tensor/autograd/vjp_registry.cpp",
+     "        register_reduction_vjps(result);\n        return result;",
+     "        register_reduction_vjps(result);\n"
+     "        if (register_backend_vjps != nullptr)\n        {\n            register_backend_vjps(result);\n        }\n"
+     "        return result;"),
 ]
 
 HOST_SOURCES = ["cuda_runtime.cpp", "cuda_kernels.cpp", "cuda_evaluator.cpp", "extensions.cpp", "ops_ext.cpp",

@@ -165,6 +165,8 @@ def _declare(L):
         "mtc_event_destroy": ([c_int, c_vp], c_int),
         "mtc_event_record": ([c_vp, c_vp], c_int),
         "mtc_stream_wait_event": ([c_vp, c_vp], c_int),
+        "mtc_event_create_timed": ([c_int, P(c_vp)], c_int),
+        "mtc_event_elapsed": ([c_vp, c_vp, P(c_f)], c_int),
         "mtc_pool_protect": ([c_int, c_vp, c_i32], c_int),
         "mtc_pool_take_many": ([c_int, P(c_vp), P(c_sz), c_i32, c_vp, P(c_i32)], c_int),
         "mtc_capture_begin": ([c_int, c_vp], c_int),
@@ -186,6 +188,7 @@ def _declare(L):
         "mtc_index_scatter": ([P(Desc), P(Desc), P(Desc), c_vp], c_int),
         "mtc_gather": ([P(Desc), P(Desc), c_i64, P(Desc), c_vp], c_int),
         "mtc_gather_scatter_add": ([P(Desc), P(Desc), c_i64, P(Desc), c_vp], c_int),
+        "mtc_gather_scatter_add_into": ([P(Desc), P(Desc), c_i64, P(Desc), c_vp], c_int),
         "mtc_reduce": ([c_i32, P(Desc), P(c_i64), c_i32, P(Desc), c_vp], c_int),
         "mtc_log_softmax": ([P(Desc), c_i64, P(Desc), c_vp], c_int),
         "mtc_matmul": ([P(Desc), P(Desc), P(Desc), c_i32, c_vp], c_int),
@@ -196,6 +199,7 @@ def _declare(L):
         "mtc_launch_count": ([P(ctypes.c_uint64)], c_int),
         "mtc_profile_enable": ([c_int], c_int),
         "mtc_profile_gemm": ([P(ctypes.c_uint64), P(ctypes.c_double), P(ctypes.c_double), c_int], c_int),
+        "mtc_gemm_path_counts": ([P(ctypes.c_uint64), P(ctypes.c_uint64)], c_int),
         "mtc_comm_unique_id": ([c_vp, c_sz], c_int),
         "mtc_comm_init": ([c_int, c_int, c_int, c_vp, c_sz, P(c_vp)], c_int),
         "mtc_comm_allreduce_f32": ([c_vp, P(c_vp), P(c_sz), c_i32, c_f, c_vp], c_int),
@@ -213,11 +217,11 @@ EXPORTED = (
     "mtc_last_error", "mtc_version", "mtc_device_count", "mtc_device_sm_count", "mtc_set_device", "mtc_device_stream", "mtc_alloc",
     "mtc_free", "mtc_copy_from_host", "mtc_copy_to_host", "mtc_stream_synchronize", "mtc_pool_stats", "mtc_pool_trim",
     "mtc_stream_create", "mtc_stream_destroy", "mtc_event_create", "mtc_event_destroy", "mtc_event_record",
-    "mtc_stream_wait_event", "mtc_pool_take", "mtc_pool_take_many", "mtc_pool_protect", "mtc_capture_begin", "mtc_capture_end", "mtc_capture_fused_count", "mtc_graph_launch",
+    "mtc_stream_wait_event", "mtc_event_create_timed", "mtc_event_elapsed", "mtc_pool_take", "mtc_pool_take_many", "mtc_pool_protect", "mtc_capture_begin", "mtc_capture_end", "mtc_capture_fused_count", "mtc_graph_launch",
     "mtc_graph_set_constants", "mtc_graph_launches", "mtc_graph_destroy",
     "mtc_check_device_errors", "mtc_watch_device_errors", "mtc_poll_device_errors", "mtc_selftest_bounded_wait", "mtc_unary", "mtc_binary", "mtc_fused", "mtc_copy", "mtc_concat", "mtc_index_scatter",
-    "mtc_gather", "mtc_gather_scatter_add", "mtc_reduce", "mtc_log_softmax", "mtc_matmul", "mtc_fill", "mtc_uniform",
-    "mtc_normal", "mtc_launch_count", "mtc_profile_enable", "mtc_profile_gemm", "mtc_comm_unique_id", "mtc_comm_init", "mtc_comm_allreduce_f32", "mtc_comm_allreduce_f32_async", "mtc_comm_wait", "mtc_comm_destroy",
+    "mtc_gather", "mtc_gather_scatter_add", "mtc_gather_scatter_add_into", "mtc_reduce", "mtc_log_softmax", "mtc_matmul", "mtc_fill", "mtc_uniform",
+    "mtc_normal", "mtc_launch_count", "mtc_profile_enable", "mtc_profile_gemm", "mtc_gemm_path_counts", "mtc_comm_unique_id", "mtc_comm_init", "mtc_comm_allreduce_f32", "mtc_comm_allreduce_f32_async", "mtc_comm_wait", "mtc_comm_destroy",
 )
 
 
@@ -354,6 +358,13 @@ def profile_gemm(reset: bool = True):
     n, ms, fl = ctypes.c_uint64(0), ctypes.c_double(0.0), ctypes.c_double(0.0)
     check(lib().mtc_profile_gemm(ctypes.byref(n), ctypes.byref(ms), ctypes.byref(fl), int(reset)))
     return n.value, ms.value, fl.value
+
+
+def gemm_path_counts():
+    """(tensor-core calls, SIMT calls) of mtc_matmul since the process started."""
+    tc, simt = ctypes.c_uint64(0), ctypes.c_uint64(0)
+    check(lib().mtc_gemm_path_counts(ctypes.byref(tc), ctypes.byref(simt)))
+    return tc.value, simt.value
 
 
 def check_device_errors(device: int = 0, stream=None) -> None:

@@ -18,16 +18,29 @@ __device__ __forceinline__ void record_device_error(int code, long long detail) 
 }
 
 // Device address of the error word on the current device (kernels in other
-// files receive it as an argument).
-unsigned long long *device_error_word() {
+// files receive it as an argument), looked up once per device.  MTC_OK, or
+// MTC_ERR_RUNTIME (and *out = nullptr) when the address cannot be had: callers
+// then refuse to launch, because a kernel that gives up a bounded wait writes
+// through this pointer.
+int device_error_word(unsigned long long **out) {
+    static std::mutex mu;
     static unsigned long long *words[64] = {};
+    *out = nullptr;
     const int dev = current_device();
-    if (dev < 0 || dev >= 64) return nullptr;
+    if (dev < 0 || dev >= 64) return fail(MTC_ERR_RUNTIME, "device index %d outside the supported range", dev);
+    std::lock_guard<std::mutex> lock(mu);
     if (words[dev] == nullptr) {
         void *p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_device_error) == cudaSuccess) words[dev] = static_cast<unsigned long long *>(p);
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_device_error);
+        if (e != cudaSuccess || p == nullptr) {
+            cudaGetLastError();
+            return fail(MTC_ERR_RUNTIME, "cudaGetSymbolAddress of the device error word failed: %s",
+                        cudaGetErrorString(e));
+        }
+        words[dev] = static_cast<unsigned long long *>(p);
     }
-    return words[dev];
+    *out = words[dev];
+    return MTC_OK;
 }
 
 namespace {
@@ -221,6 +234,287 @@ __global__ void __launch_bounds__(256) k_scatter_add_rows16(const MoveArgs a, lo
     }
 }
 
+// ------------------------------------------------ rank-2 row gather / scatter --
+// The iteration space [rows, W] after simplification: the inner axis contiguous
+// in the table / target and the updates / output, the Int64 index broadcast
+// along it (stride 0), so index j of row r selects a whole row of `row_vec`
+// 16-byte vectors.  A half-warp (16 lanes) owns ROWS_PER_HALF rows per step and
+// issues all of their loads before any store, so every lane keeps several
+// 16-byte loads in flight (Little's law at ~6.5 TB/s needs tens of KB in flight
+// per SM for random 256-byte rows).
+
+constexpr int kRowsPerHalf = 4;
+
+// Rank-2 row operands from their own descriptors (logical row order kept):
+// `rows` rows of row_vec 16-byte vectors; element offsets and row strides.
+struct RowArgs {
+    char *out;                // gather: output; scatter: target
+    const char *in;           // gather: table; scatter: updates
+    const long long *idx;
+    long long out_off, out_rs, in_off, in_rs, idx_off, idx_rs;
+    long long rows;           // gather: output rows; scatter: update rows
+    long long extent;         // gather: table rows; scatter: target rows
+    int row_vec;
+};
+
+__device__ __forceinline__ const uint4 *row_in(const RowArgs &a, long long r, int c) {
+    return reinterpret_cast<const uint4 *>(a.in + (a.in_off + r * a.in_rs) * 4) + c;
+}
+__device__ __forceinline__ uint4 *row_out(const RowArgs &a, long long r, int c) {
+    return reinterpret_cast<uint4 *>(a.out + (a.out_off + r * a.out_rs) * 4) + c;
+}
+
+__global__ void __launch_bounds__(256) k_gather_rows2(const RowArgs a) {
+    const int lane = threadIdx.x & 15;
+    const long long half = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
+    const long long halves = (static_cast<long long>(gridDim.x) * blockDim.x) >> 4;
+    for (long long r0 = half * kRowsPerHalf; r0 < a.rows; r0 += halves * kRowsPerHalf) {
+        long long j[kRowsPerHalf];
+        bool ok[kRowsPerHalf];
+#pragma unroll
+        for (int u = 0; u < kRowsPerHalf; ++u) {
+            const long long r = r0 + u;
+            j[u] = r < a.rows ? __ldg(a.idx + a.idx_off + r * a.idx_rs) : 0;
+            ok[u] = r < a.rows && j[u] >= 0 && j[u] < a.extent;
+            if (r < a.rows && !ok[u] && lane == 0) record_device_error(MTC_ERR_OUT_OF_RANGE, j[u]);
+        }
+        for (int c = lane; c < a.row_vec; c += 16) {
+            uint4 v[kRowsPerHalf];
+#pragma unroll
+            for (int u = 0; u < kRowsPerHalf; ++u)
+                if (ok[u]) v[u] = __ldg(row_in(a, j[u], c));
+#pragma unroll
+            for (int u = 0; u < kRowsPerHalf; ++u)
+                if (ok[u]) __stcs(row_out(a, r0 + u, c), v[u]);
+        }
+    }
+}
+
+// Scatter-add as a segment sum.  out[t] = sum of upd[i] over the rows i with
+// idx[i] = t, added in ascending i starting from +0 -- the reference's order
+// (zero-filled target, then += in the iteration order of the updates), so the
+// result is the reference's bit for bit whatever the values.  Steps:
+//   count  : counts[t] = number of rows i with idx[i] = t (atomics on 4 bytes)
+//   scan   : starts = exclusive prefix sum of counts (two levels of blocks)
+//   fill   : perm[starts[t] .. starts[t+1]) = the rows i of target t
+//   sort   : each segment sorted ascending (in-thread up to 32 rows; a CTA
+//            bitonic sort in shared memory up to kLongSegment rows)
+//   sum    : every target row written once (zeros for rows no index names),
+//            so the target needs no zero fill and is never read back.
+// Scratch: counts, starts (T + 1 each), perm (n), block sums, the long-segment list.
+
+constexpr int kScanItems = 8;                       // per thread
+constexpr int kScanBlock = 256 * kScanItems;        // counts per scan block
+constexpr int kLongSegment = 4096;                  // longest segment sorted in shared memory
+
+__global__ void __launch_bounds__(256) k_seg_count(const RowArgs a, int *counts) {
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.rows;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long j = __ldg(a.idx + a.idx_off + i * a.idx_rs);
+        if (j < 0 || j >= a.extent) {
+            record_device_error(MTC_ERR_OUT_OF_RANGE, j);
+            continue;
+        }
+        atomicAdd(counts + j, 1);
+    }
+}
+
+// Block-local exclusive scan of kScanBlock counts; block totals to `sums`.
+__global__ void __launch_bounds__(256) k_scan_blocks(const int *in, int *out, long long len, int *sums) {
+    __shared__ int warp_tot[8];
+    const long long base = static_cast<long long>(blockIdx.x) * kScanBlock + threadIdx.x * kScanItems;
+    int v[kScanItems];
+    int run = 0;
+#pragma unroll
+    for (int q = 0; q < kScanItems; ++q) {
+        v[q] = base + q < len ? in[base + q] : 0;
+        const int t = v[q];
+        v[q] = run;
+        run += t;
+    }
+    // exclusive scan of the per-thread totals across the block
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int inc = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+    }
+    if (lane == 31) warp_tot[warp] = inc;
+    __syncthreads();
+    int warp_off = 0;
+    for (int w = 0; w < warp; ++w) warp_off += warp_tot[w];
+    const int excl = warp_off + inc - run;
+#pragma unroll
+    for (int q = 0; q < kScanItems; ++q)
+        if (base + q < len) out[base + q] = v[q] + excl;
+    if (threadIdx.x == 255) sums[blockIdx.x] = warp_off + inc;
+}
+
+// Exclusive scan of up to 256 * 64 block totals in one CTA, in place.
+__global__ void __launch_bounds__(256) k_scan_totals(int *sums, int n) {
+    __shared__ int warp_tot[8];
+    constexpr int kItems = 64;
+    const int base = threadIdx.x * kItems;
+    int run = 0;
+    for (int q = 0; q < kItems; ++q)
+        if (base + q < n) run += sums[base + q];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int inc = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+    }
+    if (lane == 31) warp_tot[warp] = inc;
+    __syncthreads();
+    int off = 0;
+    for (int w = 0; w < warp; ++w) off += warp_tot[w];
+    off += inc - run;
+    for (int q = 0; q < kItems; ++q) {
+        if (base + q < n) {
+            const int t = sums[base + q];
+            sums[base + q] = off;
+            off += t;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) k_scan_add(int *out, long long len, const int *sums) {
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < len) out[i] += sums[i / kScanBlock];
+}
+
+// perm[starts[j] + slot] = i, slots taken from the back of each segment by
+// counting its remaining count down (order within a segment fixed by the sort).
+__global__ void __launch_bounds__(256) k_seg_fill(const RowArgs a, int *counts, const int *starts, int *perm) {
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.rows;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long j = __ldg(a.idx + a.idx_off + i * a.idx_rs);
+        if (j < 0 || j >= a.extent) continue;
+        const int slot = atomicSub(counts + j, 1) - 1;
+        perm[starts[j] + slot] = static_cast<int>(i);
+    }
+}
+
+// Sorts the segments of up to 32 rows in place, one thread per target; longer
+// segments (up to kLongSegment) go to a list for k_seg_sort_long.
+__global__ void __launch_bounds__(256) k_seg_sort(const int *starts, int *perm, long long targets, int *long_list,
+                                                  int *long_count, int long_capacity) {
+    for (long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; t < targets;
+         t += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const int s = starts[t], e = starts[t + 1];
+        const int len = e - s;
+        if (len < 2) continue;
+        if (len > 32) {
+            const int k = atomicAdd(long_count, 1);
+            if (k < long_capacity) long_list[k] = static_cast<int>(t);
+            continue;
+        }
+        int *p = perm + s;
+        for (int q = 1; q < len; ++q) {
+            const int key = p[q];
+            int w = q - 1;
+            while (w >= 0 && p[w] > key) {
+                p[w + 1] = p[w];
+                --w;
+            }
+            p[w + 1] = key;
+        }
+    }
+}
+
+// Bitonic sort of one long segment per CTA iteration in shared memory (padded
+// with INT_MAX to a power of two); segments above kLongSegment stay in fill order.
+__global__ void __launch_bounds__(256) k_seg_sort_long(const int *starts, int *perm, const int *long_list,
+                                                       const int *long_count, int long_capacity) {
+    __shared__ int keys[kLongSegment];
+    const int count = min(*long_count, long_capacity);
+    for (int e = blockIdx.x; e < count; e += gridDim.x) {
+        const int t = long_list[e];
+        const int s = starts[t], len = starts[t + 1] - s;
+        if (len > kLongSegment) continue;
+        int n2 = 64;
+        while (n2 < len) n2 <<= 1;
+        for (int q = threadIdx.x; q < n2; q += blockDim.x) keys[q] = q < len ? perm[s + q] : 0x7fffffff;
+        __syncthreads();
+        for (int k = 2; k <= n2; k <<= 1) {
+            for (int jj = k >> 1; jj > 0; jj >>= 1) {
+                for (int q = threadIdx.x; q < n2; q += blockDim.x) {
+                    const int partner = q ^ jj;
+                    if (partner > q) {
+                        const bool up = (q & k) == 0;
+                        const int x = keys[q], y = keys[partner];
+                        if ((x > y) == up) {
+                            keys[q] = y;
+                            keys[partner] = x;
+                        }
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        for (int q = threadIdx.x; q < len; q += blockDim.x) perm[s + q] = keys[q];
+        __syncthreads();
+    }
+}
+
+// out[t] = +0 + upd[perm[s]] + upd[perm[s + 1]] + ... for every target row t.
+// A warp owns 32 consecutive target rows: lane l loads starts[t0 + l] and the
+// first update index of that row in two coalesced loads (perm is ordered by
+// target), then the half-warps copy-and-add two rows at a time, eight rows in
+// flight per warp; rows with several updates add the rest in order after.
+constexpr int kSumRowsInFlight = 8;
+
+__global__ void __launch_bounds__(256) k_seg_sum(const RowArgs a, const int *starts, const int *perm) {
+    const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
+    const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const long long warps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+    const long long targets = a.extent;
+    for (long long t0 = warp * 32; t0 < targets; t0 += warps * 32) {
+        const long long t = t0 + lane;
+        const int s = t < targets ? __ldg(starts + t) : 0;
+        const int e = t < targets ? __ldg(starts + t + 1) : 0;
+        const int first = s < e ? __ldg(perm + s) : 0;
+        const int rows = static_cast<int>(targets - t0 < 32 ? targets - t0 : 32);  // warp-uniform
+        for (int q0 = 0; q0 < rows; q0 += kSumRowsInFlight) {
+            // every lane takes part in the shuffles: they sit outside lane-dependent branches
+            int fq[kSumRowsInFlight / 2], len[kSumRowsInFlight / 2], sq[kSumRowsInFlight / 2];
+#pragma unroll
+            for (int u = 0; u < kSumRowsInFlight / 2; ++u) {
+                const int q = q0 + 2 * u + half;  // this half-warp's row
+                const int qs = q < 32 ? q : 31;
+                fq[u] = __shfl_sync(0xffffffffu, first, qs);
+                len[u] = __shfl_sync(0xffffffffu, e - s, qs);
+                sq[u] = __shfl_sync(0xffffffffu, s, qs);
+                if (q >= rows) len[u] = -1;  // no such row
+            }
+            for (int c = hl; c < a.row_vec; c += 16) {
+                uint4 v[kSumRowsInFlight / 2];
+#pragma unroll
+                for (int u = 0; u < kSumRowsInFlight / 2; ++u)
+                    if (len[u] > 0) v[u] = __ldg(row_in(a, fq[u], c));
+#pragma unroll
+                for (int u = 0; u < kSumRowsInFlight / 2; ++u) {
+                    if (len[u] < 0) continue;
+                    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    if (len[u] > 0)
+                        acc = make_float4(__fadd_rn(0.0f, __uint_as_float(v[u].x)), __fadd_rn(0.0f, __uint_as_float(v[u].y)),
+                                          __fadd_rn(0.0f, __uint_as_float(v[u].z)), __fadd_rn(0.0f, __uint_as_float(v[u].w)));
+                    for (int k = sq[u] + 1; k < sq[u] + len[u]; ++k) {
+                        const uint4 w = __ldg(row_in(a, __ldg(perm + k), c));
+                        acc.x = __fadd_rn(acc.x, __uint_as_float(w.x));
+                        acc.y = __fadd_rn(acc.y, __uint_as_float(w.y));
+                        acc.z = __fadd_rn(acc.z, __uint_as_float(w.z));
+                        acc.w = __fadd_rn(acc.w, __uint_as_float(w.w));
+                    }
+                    __stcs(reinterpret_cast<float4 *>(row_out(a, t0 + q0 + 2 * u + half, c)), acc);
+                }
+            }
+        }
+    }
+}
+
 int grid_for(long long work, int per_block = 256) {
     const int sms = sm_count(current_device());
     long long b = (work + per_block - 1) / per_block;
@@ -241,6 +535,113 @@ void fill_divs(MoveArgs &a, const IterSpace &s) {
 
 bool aligned16(const void *p, long long off_elems, int elem) {
     return (reinterpret_cast<uintptr_t>(static_cast<const char *>(p) + off_elems * elem) % 16) == 0;
+}
+
+// Rank-2 row operands along axis 0 with the index broadcast along the row
+// (table / target, updates or output, and indices all [rows, W] views whose
+// inner axis is contiguous, 16-byte aligned rows of whole vectors): the row
+// gather and the segment-sum scatter-add.  `in` is the table (gather) or the
+// updates (scatter); `indexed` is the operand the index selects rows of.
+bool row_operands(const mtc_desc &out, const mtc_desc &in, const mtc_desc &idx, const mtc_desc &indexed, int64_t axis,
+                  RowArgs &r) {
+    if (axis != 0 || out.rank != 2 || in.rank != 2 || idx.rank != 2) return false;
+    const int64_t w = idx.shape[1];
+    if (w < 4 || w % 4 != 0 || out.shape[1] != w || in.shape[1] != w) return false;
+    if (out.strides[1] != 1 || in.strides[1] != 1 || idx.strides[1] != 0) return false;
+    if (!aligned16(out.data, out.offset, 4) || !aligned16(in.data, in.offset, 4)) return false;
+    if (out.strides[0] % 4 != 0 || in.strides[0] % 4 != 0) return false;
+    std::memset(&r, 0, sizeof(r));
+    r.out = static_cast<char *>(out.data);
+    r.in = static_cast<const char *>(in.data);
+    r.idx = static_cast<const long long *>(idx.data);
+    r.out_off = out.offset;
+    r.out_rs = out.strides[0];
+    r.in_off = in.offset;
+    r.in_rs = in.strides[0];
+    r.idx_off = idx.offset;
+    r.idx_rs = idx.strides[0];
+    r.rows = idx.shape[0];
+    r.extent = indexed.shape[0];
+    r.row_vec = static_cast<int>(w / 4);
+    return w / 4 < (int64_t{1} << 30);
+}
+
+int row_gather(const RowArgs &r, cudaStream_t st) {
+    if (r.rows == 0) return MTC_OK;
+    k_gather_rows2<<<grid_for(r.rows * 4), 256, 0, st>>>(r);  // 16 lanes per kRowsPerHalf rows
+    return check_launch("row gather");
+}
+
+// Segment-sum scatter-add (see k_seg_sum); MTC_ERR_UNSUPPORTED when the sizes
+// exceed the int32 bookkeeping or the two-level scan (the caller then takes
+// the atomic kernel).
+int segment_scatter_add(const RowArgs &r, cudaStream_t st) {
+    const long long T = r.extent, n = r.rows;
+    if (n >= (int64_t{1} << 31) - 1 || T + 1 > static_cast<long long>(kScanBlock) * 256 * 64)
+        return fail(MTC_ERR_UNSUPPORTED, "scatter-add beyond the segment path's sizes");
+    if (T == 0) {
+        if (n > 0) {  // every index is out of range: record it like the other paths
+            k_seg_count<<<grid_for(n), 256, 0, st>>>(r, nullptr);
+            return check_launch("segment scatter-add count");
+        }
+        return MTC_OK;
+    }
+    const long long nblk = (T + 1 + kScanBlock - 1) / kScanBlock;
+    const long long cap = n / 33 + 1;
+    // counts | starts | perm | block sums | long-segment list | long-segment count
+    const size_t words = static_cast<size_t>(2 * (T + 1) + (n > 0 ? n : 1) + nblk + cap + 1);
+    void *scratch = nullptr;
+    MTC_TRY(scratch_alloc(words * sizeof(int), st, &scratch));
+    int *counts = static_cast<int *>(scratch);
+    int *starts = counts + (T + 1);
+    int *perm = starts + (T + 1);
+    int *sums = perm + (n > 0 ? n : 1);
+    int *long_list = sums + nblk;
+    int *long_count = long_list + cap;
+    int rc = MTC_OK;
+    auto launched = [&](const char *what) {
+        if (rc == MTC_OK) rc = check_launch(what);
+    };
+    if (cudaMemsetAsync(counts, 0, static_cast<size_t>(T + 1) * sizeof(int), st) != cudaSuccess ||
+        cudaMemsetAsync(long_count, 0, sizeof(int), st) != cudaSuccess) {
+        rc = fail(MTC_ERR_RUNTIME, "segment scatter-add: clearing the counters failed: %s",
+                  cudaGetErrorString(cudaGetLastError()));
+    }
+    if (rc == MTC_OK && n > 0) {
+        k_seg_count<<<grid_for(n), 256, 0, st>>>(r, counts);
+        launched("segment scatter-add count");
+    }
+    if (rc == MTC_OK) {
+        k_scan_blocks<<<static_cast<unsigned>(nblk), 256, 0, st>>>(counts, starts, T + 1, sums);
+        launched("segment scatter-add scan");
+    }
+    if (rc == MTC_OK) {
+        k_scan_totals<<<1, 256, 0, st>>>(sums, static_cast<int>(nblk));
+        launched("segment scatter-add scan totals");
+    }
+    if (rc == MTC_OK) {
+        k_scan_add<<<static_cast<unsigned>((T + 1 + 255) / 256), 256, 0, st>>>(starts, T + 1, sums);
+        launched("segment scatter-add scan offsets");
+    }
+    if (rc == MTC_OK && n > 0) {
+        k_seg_fill<<<grid_for(n), 256, 0, st>>>(r, counts, starts, perm);
+        launched("segment scatter-add fill");
+        if (rc == MTC_OK) {
+            k_seg_sort<<<grid_for(T), 256, 0, st>>>(starts, perm, T, long_list, long_count, static_cast<int>(cap));
+            launched("segment scatter-add sort");
+        }
+        if (rc == MTC_OK) {
+            k_seg_sort_long<<<sm_count(current_device()) * 2, 256, 0, st>>>(starts, perm, long_list, long_count,
+                                                                              static_cast<int>(cap));
+            launched("segment scatter-add long sort");
+        }
+    }
+    if (rc == MTC_OK) {
+        k_seg_sum<<<grid_for(T), 256, 0, st>>>(r, starts, perm);  // a warp per 32 target rows
+        launched("segment scatter-add sum");
+    }
+    scratch_free(scratch, st);
+    return rc;
 }
 
 // Strided copy of src into dst (same shape, same dtype).
@@ -370,6 +771,52 @@ int index_space(const mtc_desc &indexed, const mtc_desc &walked, const mtc_desc 
     return MTC_OK;
 }
 
+// out = 0 first when `clear`, then out[..idx..] += upd.
+int scatter_add_impl(const mtc_desc *upd, const mtc_desc *idx, int64_t axis, const mtc_desc *out, bool clear,
+                     cudaStream_t st) {
+    MTC_TRY(validate(upd, "updates"));
+    MTC_TRY(validate(idx, "indices"));
+    MTC_TRY(validate(out, "output"));
+    if (idx->dtype != MTC_INT64) return fail(MTC_ERR_INVALID_ARGUMENT, "scatter indices must be Int64");
+    if (upd->dtype != MTC_FLOAT32 || out->dtype != MTC_FLOAT32)
+        return fail(MTC_ERR_LOGIC, "scatter-add requires Float32");
+    if (upd->rank != idx->rank || upd->rank != out->rank || !same_shape(*upd, *idx))
+        return fail(MTC_ERR_INVALID_ARGUMENT, "scatter-add shapes are inconsistent");
+    if (axis < 0 || axis >= out->rank) return fail(MTC_ERR_OUT_OF_RANGE, "scatter-add axis out of range");
+    RowArgs ra;
+    if (clear && row_operands(*out, *upd, *idx, *out, axis, ra)) {
+        const int rc = segment_scatter_add(ra, st);
+        if (rc != MTC_ERR_UNSUPPORTED) return rc;
+        clear_error();
+    }
+    if (clear) {
+        const float zero = 0.0f;
+        MTC_TRY(fill_impl(*out, &zero, st));
+    }
+    MoveArgs a;
+    IterSpace s;
+    MTC_TRY(index_space(*out, *upd, *idx, axis, true, a, s));
+    if (s.numel == 0) return MTC_OK;
+    a.ptr[0] = static_cast<char *>(out->data);
+    a.ptr[1] = static_cast<char *>(const_cast<void *>(upd->data));
+    a.ptr[2] = static_cast<char *>(const_cast<void *>(idx->data));
+    const int r = s.rank;
+    if (r >= 2 && s.stride[0][r - 1] == 1 && s.stride[1][r - 1] == 1 && s.stride[2][r - 1] == 0 &&
+        (s.shape[r - 1] * 4) % 16 == 0 && (a.axis_stride * 4) % 16 == 0) {
+        bool ok = aligned16(out->data, 0, 4) && aligned16(upd->data, 0, 4);
+        for (int d = 0; d < r - 1 && ok; ++d) ok = (s.stride[0][d] * 4) % 16 == 0 && (s.stride[1][d] * 4) % 16 == 0;
+        ok = ok && (s.offset[0] * 4) % 16 == 0 && (s.offset[1] * 4) % 16 == 0;
+        if (ok) {
+            const long long rows = s.numel / s.shape[r - 1];
+            const long long row_vec = s.shape[r - 1] / 4;
+            k_scatter_add_rows16<<<grid_for(rows * row_vec), 256, 0, st>>>(a, rows, row_vec);
+            return check_launch("row scatter-add");
+        }
+    }
+    k_scatter_add<<<grid_for(s.numel), 256, 0, st>>>(a);
+    return check_launch("scatter-add");
+}
+
 }  // namespace
 }  // namespace mtc
 
@@ -451,6 +898,9 @@ int mtc_gather(const mtc_desc *src, const mtc_desc *idx, int64_t axis, const mtc
     for (int d = 0; d < src->rank; ++d)
         if (d != axis && idx->shape[d] != src->shape[d])
             return fail(MTC_ERR_INVALID_ARGUMENT, "gather index extent differs from source off the axis");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    RowArgs rows;
+    if (src->dtype == MTC_FLOAT32 && row_operands(*out, *src, *idx, *src, axis, rows)) return row_gather(rows, st);
     MoveArgs a;
     IterSpace s;
     MTC_TRY(index_space(*src, *out, *idx, axis, false, a, s));
@@ -458,7 +908,6 @@ int mtc_gather(const mtc_desc *src, const mtc_desc *idx, int64_t axis, const mtc
     a.ptr[0] = static_cast<char *>(out->data);
     a.ptr[1] = static_cast<char *>(const_cast<void *>(src->data));
     a.ptr[2] = static_cast<char *>(const_cast<void *>(idx->data));
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int r = s.rank;
     const int es = static_cast<int>(dtype_size(src->dtype));
     if (r >= 2 && es == 4 && s.stride[0][r - 1] == 1 && s.stride[1][r - 1] == 1 && s.stride[2][r - 1] == 0 &&
@@ -480,40 +929,13 @@ int mtc_gather(const mtc_desc *src, const mtc_desc *idx, int64_t axis, const mtc
 
 int mtc_gather_scatter_add(const mtc_desc *upd, const mtc_desc *idx, int64_t axis, const mtc_desc *out, void *stream) {
     clear_error();
-    MTC_TRY(validate(upd, "updates"));
-    MTC_TRY(validate(idx, "indices"));
-    MTC_TRY(validate(out, "output"));
-    if (idx->dtype != MTC_INT64) return fail(MTC_ERR_INVALID_ARGUMENT, "scatter indices must be Int64");
-    if (upd->dtype != MTC_FLOAT32 || out->dtype != MTC_FLOAT32)
-        return fail(MTC_ERR_LOGIC, "scatter-add requires Float32");
-    if (upd->rank != idx->rank || upd->rank != out->rank || !same_shape(*upd, *idx))
-        return fail(MTC_ERR_INVALID_ARGUMENT, "scatter-add shapes are inconsistent");
-    if (axis < 0 || axis >= out->rank) return fail(MTC_ERR_OUT_OF_RANGE, "scatter-add axis out of range");
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const float zero = 0.0f;
-    MTC_TRY(fill_impl(*out, &zero, st));
-    MoveArgs a;
-    IterSpace s;
-    MTC_TRY(index_space(*out, *upd, *idx, axis, true, a, s));
-    if (s.numel == 0) return MTC_OK;
-    a.ptr[0] = static_cast<char *>(out->data);
-    a.ptr[1] = static_cast<char *>(const_cast<void *>(upd->data));
-    a.ptr[2] = static_cast<char *>(const_cast<void *>(idx->data));
-    const int r = s.rank;
-    if (r >= 2 && s.stride[0][r - 1] == 1 && s.stride[1][r - 1] == 1 && s.stride[2][r - 1] == 0 &&
-        (s.shape[r - 1] * 4) % 16 == 0 && (a.axis_stride * 4) % 16 == 0) {
-        bool ok = aligned16(out->data, 0, 4) && aligned16(upd->data, 0, 4);
-        for (int d = 0; d < r - 1 && ok; ++d) ok = (s.stride[0][d] * 4) % 16 == 0 && (s.stride[1][d] * 4) % 16 == 0;
-        ok = ok && (s.offset[0] * 4) % 16 == 0 && (s.offset[1] * 4) % 16 == 0;
-        if (ok) {
-            const long long rows = s.numel / s.shape[r - 1];
-            const long long row_vec = s.shape[r - 1] / 4;
-            k_scatter_add_rows16<<<grid_for(rows * row_vec), 256, 0, st>>>(a, rows, row_vec);
-            return check_launch("row scatter-add");
-        }
-    }
-    k_scatter_add<<<grid_for(s.numel), 256, 0, st>>>(a);
-    return check_launch("scatter-add");
+    return scatter_add_impl(upd, idx, axis, out, true, static_cast<cudaStream_t>(stream));
+}
+
+int mtc_gather_scatter_add_into(const mtc_desc *upd, const mtc_desc *idx, int64_t axis, const mtc_desc *out,
+                                void *stream) {
+    clear_error();
+    return scatter_add_impl(upd, idx, axis, out, false, static_cast<cudaStream_t>(stream));
 }
 
 int mtc_check_device_errors(int device, void *stream, int64_t *detail) {

@@ -51,7 +51,7 @@ template <> __device__ __forceinline__ float mtc_unary<0x0108>(float x) {
     return __fdiv_rn(e, __fadd_rn(1.0f, e));
 }
 template <> __device__ __forceinline__ float mtc_unary<0x0180>(float x) {
-    // relu: NaN propagates, -0 -> +0 (equal to the composite (x + |x|) * 0.5)
+    // relu: max(x, 0) for every input; NaN propagates, -0 and -inf give +0
     return x > 0.0f ? x : (x != x ? x : 0.0f);
 }
 

@@ -9,6 +9,8 @@
 // so it matches the CPU to rounding, not bit for bit.
 #include <cstring>
 
+#include <atomic>
+
 #include "gemm.cuh"
 
 namespace mtc {
@@ -344,6 +346,11 @@ static int build_problem(const mtc_desc &lhs, const mtc_desc &rhs, const mtc_des
 
 using namespace mtc;
 
+namespace {
+// matmul calls served by each kernel family (mtc_gemm_path_counts)
+std::atomic<uint64_t> g_tc_calls{0}, g_simt_calls{0};
+}  // namespace
+
 extern "C" int mtc_matmul(const mtc_desc *lhs, const mtc_desc *rhs, const mtc_desc *out, int32_t algo, void *stream) {
     clear_error();
     MTC_TRY(validate(lhs, "lhs"));
@@ -364,6 +371,7 @@ extern "C" int mtc_matmul(const mtc_desc *lhs, const mtc_desc *rhs, const mtc_de
         return fail(MTC_ERR_INVALID_ARGUMENT, "unknown matmul algorithm %d", algo);
     void *mark = profiling() ? profile_begin(s) : nullptr;
     int rc;
+    bool used_tensor_cores = false;
     // AUTO: tensor cores for problems large enough to amortise the split pack,
     // otherwise the exact-order SIMT kernel (bit-identical to the CPU reference)
     const double macs = double(p.M) * double(p.N) * double(p.K) * double(p.batch);
@@ -374,13 +382,22 @@ extern "C" int mtc_matmul(const mtc_desc *lhs, const mtc_desc *rhs, const mtc_de
         rc = gemm_simt(p, s, false);
     } else {
         rc = gemm_3xtf32(p, s);
+        used_tensor_cores = rc == MTC_OK;
         if (rc == MTC_ERR_UNSUPPORTED && algo == MTC_GEMM_AUTO) {
             clear_error();
             rc = gemm_simt(p, s, true);
         }
     }
     if (mark != nullptr) profile_end(mark, s, 2.0 * double(p.M) * double(p.N) * double(p.K) * double(p.batch));
+    if (rc == MTC_OK) (used_tensor_cores ? g_tc_calls : g_simt_calls).fetch_add(1, std::memory_order_relaxed);
     return rc;
+}
+
+extern "C" int mtc_gemm_path_counts(uint64_t *tensor_core, uint64_t *simt) {
+    clear_error();
+    if (tensor_core) *tensor_core = g_tc_calls.load(std::memory_order_relaxed);
+    if (simt) *simt = g_simt_calls.load(std::memory_order_relaxed);
+    return MTC_OK;
 }
 
 extern "C" int mtc_matmul_3xtf32_static(const mtc_desc *lhs, const mtc_desc *rhs, const mtc_desc *out, void *stream) {

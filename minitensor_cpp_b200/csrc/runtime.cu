@@ -718,6 +718,26 @@ int mtc_event_create(int device, void **event) {
     return MTC_OK;
 }
 
+int mtc_event_create_timed(int device, void **event) {
+    clear_error();
+    if (event == nullptr) return fail(MTC_ERR_INVALID_ARGUMENT, "null event slot");
+    DeviceGuard guard(device);
+    MTC_TRY(guard.rc);
+    cudaEvent_t e = nullptr;
+    MTC_CUDA_TRY(cudaEventCreate(&e));
+    *event = e;
+    return MTC_OK;
+}
+
+int mtc_event_elapsed(void *start, void *stop, float *milliseconds) {
+    clear_error();
+    if (start == nullptr || stop == nullptr || milliseconds == nullptr)
+        return fail(MTC_ERR_INVALID_ARGUMENT, "null event or result");
+    MTC_CUDA_TRY(cudaEventSynchronize(static_cast<cudaEvent_t>(stop)));
+    MTC_CUDA_TRY(cudaEventElapsedTime(milliseconds, static_cast<cudaEvent_t>(start), static_cast<cudaEvent_t>(stop)));
+    return MTC_OK;
+}
+
 int mtc_event_destroy(int device, void *event) {
     if (event == nullptr) return MTC_OK;
     DeviceGuard guard(device);

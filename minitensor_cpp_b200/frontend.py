@@ -49,6 +49,15 @@ class Frontend:
             "mtb_mlp_step_host": ([vp, vp, vp, i64, P(f32)], ctypes.c_int),
             "mtb_mlp_parameters": ([vp, P(f32), i64], ctypes.c_int),
             "mtb_mlp_parameter_count": ([vp], i64),
+            "mtb_mlp_gradients": ([vp, P(f32), P(f32), i64], ctypes.c_int),
+            "mtb_mlp_use_sgd": ([vp, f32], ctypes.c_int),
+            "mtb_mlp_set_parameters": ([vp, P(f32), i64], ctypes.c_int),
+            "mtb_mlp_profile": ([vp, i32, P(ctypes.c_double)], ctypes.c_int),
+            "mtb_mlp_save": ([vp, ctypes.c_char_p], ctypes.c_int),
+            "mtb_mlp_load": ([vp, ctypes.c_char_p], ctypes.c_int),
+            "mtb_cross_entropy": ([ctypes.c_int, i64, i64, P(f32), i32, P(i64), P(f32), P(f32)], ctypes.c_int),
+            "mtb_optimizer_steps": ([ctypes.c_int, i32, i64, P(f32), i32, P(f32), f32, f32, f32, f32, f32, P(f32)],
+                                    ctypes.c_int),
             "mtb_mlp_synchronize": ([vp], ctypes.c_int),
             "mtb_mlp_materialize": ([vp], ctypes.c_int),
             "mtb_mlp_stream": ([vp], vp),
@@ -58,14 +67,20 @@ class Frontend:
             "mtb_evaluator_reset_stats": ([], None),
             "mtb_graph_cache_clear": ([], None),
             "mtb_set_graphs": ([ctypes.c_int], ctypes.c_int),
+            "mtb_set_fusion": ([ctypes.c_int], ctypes.c_int),
         }
         for name, (args, res) in sigs.items():
             fn = getattr(L, name)
             fn.argtypes = args
             fn.restype = res
         # only the backend library has the operations it adds to MiniTensor
+        if hasattr(L, "mtb_gather_eval_probe"):
+            L.mtb_gather_eval_probe.argtypes = [ctypes.c_int, i64, i64, P(f32), i64, P(i64), P(i32), P(i32)]
+            L.mtb_gather_eval_probe.restype = ctypes.c_int
+            L.mtb_set_index_checks.argtypes = [ctypes.c_int]
+            L.mtb_set_index_checks.restype = ctypes.c_int
         if hasattr(L, "mtb_added_ops"):
-            L.mtb_added_ops.argtypes = [ctypes.c_int, i64, i64, P(f32), i32, P(f32), P(f32), P(i64), P(f32)]
+            L.mtb_added_ops.argtypes = [ctypes.c_int, i64, i64, P(f32), i32, P(f32), P(f32), P(i64), P(f32), P(f32)]
             L.mtb_added_ops.restype = ctypes.c_int
 
     def _check(self, rc: int, what: str):
@@ -114,30 +129,82 @@ class Frontend:
         return out
 
     def added_ops(self, device: int, x: np.ndarray, axis: int):
-        """relu(x), and max, argmax and log-softmax of x along `axis`, through the
-        operations this backend adds to MiniTensor's API."""
+        """relu(x), and max, argmax and log-softmax of x along `axis`, and the
+        gradient of sum(relu(x)), through the operations this backend adds to
+        MiniTensor's API."""
         x = np.ascontiguousarray(x, dtype=np.float32)
         rows, cols = x.shape
         relu = np.empty_like(x)
         lsm = np.empty_like(x)
+        grad = np.empty_like(x)
         reduced = cols if axis == 0 else rows
         mx = np.empty(reduced, dtype=np.float32)
         am = np.empty(reduced, dtype=np.int64)
         P = ctypes.POINTER
         f = lambda a: a.ctypes.data_as(P(ctypes.c_float))
         self._check(self.lib.mtb_added_ops(device, rows, cols, f(x), axis, f(relu), f(mx),
-                                           am.ctypes.data_as(P(ctypes.c_int64)), f(lsm)), "added_ops")
-        return relu, mx, am, lsm
+                                           am.ctypes.data_as(P(ctypes.c_int64)), f(lsm), f(grad)), "added_ops")
+        return relu, mx, am, lsm, grad
+
+    def gather_eval_probe(self, device: int, table: np.ndarray, index: np.ndarray):
+        """(threw, materialized) of evaluating a row gather with mt::eval (see
+        workloads.hpp); a deferred index error raises IndexError from the read
+        that follows."""
+        t = np.ascontiguousarray(table, dtype=np.float32)
+        i = np.ascontiguousarray(index, dtype=np.int64)
+        threw, mat = ctypes.c_int32(0), ctypes.c_int32(0)
+        P = ctypes.POINTER
+        self._check(self.lib.mtb_gather_eval_probe(device, t.shape[0], t.shape[1], t.ctypes.data_as(P(ctypes.c_float)),
+                                                   i.size, i.ctypes.data_as(P(ctypes.c_int64)), ctypes.byref(threw),
+                                                   ctypes.byref(mat)), "gather_eval_probe")
+        return bool(threw.value), bool(mat.value)
+
+    def set_index_checks(self, mode: str) -> str:
+        """"off", "deferred" (default) or "sync"; returns the previous mode."""
+        names = ("off", "deferred", "sync")
+        return names[self.lib.mtb_set_index_checks(names.index(mode))]
+
+    def cross_entropy(self, device: int, logits: np.ndarray, targets: np.ndarray, class_axis: int = 1):
+        """(loss, d loss / d logits) of categorical_cross_entropy_with_logits on a
+        [rows, cols] matrix through the API."""
+        x = np.ascontiguousarray(logits, dtype=np.float32)
+        t = np.ascontiguousarray(targets, dtype=np.int64)
+        loss = ctypes.c_float(0.0)
+        grad = np.empty_like(x)
+        P = ctypes.POINTER
+        self._check(self.lib.mtb_cross_entropy(device, x.shape[0], x.shape[1], x.ctypes.data_as(P(ctypes.c_float)),
+                                               class_axis, t.ctypes.data_as(P(ctypes.c_int64)), ctypes.byref(loss),
+                                               grad.ctypes.data_as(P(ctypes.c_float))), "cross_entropy")
+        return loss.value, grad
+
+    def optimizer_steps(self, device: int, kind: str, params: np.ndarray, grads: np.ndarray, lr: float,
+                        weight_decay: float = 0.0, beta1: float = 0.9, beta2: float = 0.999,
+                        eps: float = 1e-8) -> np.ndarray:
+        """Parameters after len(grads) steps of AdamW ("adamw") or SGD ("sgd") on one
+        parameter vector through the API; grads is [steps, n]."""
+        p = np.ascontiguousarray(params, dtype=np.float32).reshape(-1)
+        g = np.ascontiguousarray(grads, dtype=np.float32).reshape(-1, p.size)
+        out = np.empty_like(p)
+        P = ctypes.POINTER
+        f = lambda a: a.ctypes.data_as(P(ctypes.c_float))
+        self._check(self.lib.mtb_optimizer_steps(device, {"adamw": 0, "sgd": 1}[kind], p.size, f(p), g.shape[0], f(g),
+                                                 lr, weight_decay, beta1, beta2, eps, f(out)), "optimizer_steps")
+        return out
 
     def stats(self) -> dict:
-        buf = (ctypes.c_uint64 * 12)()
+        buf = (ctypes.c_uint64 * 13)()
         self.lib.mtb_evaluator_stats(buf)
         keys = ("kernel_steps", "fused_launches", "fused_nodes", "folded_constants", "view_steps", "evaluations",
-                "plan_ns", "execute_ns", "check_ns", "graph_captures", "graph_replays", "graph_fallbacks")
+                "plan_ns", "execute_ns", "check_ns", "graph_captures", "graph_replays", "graph_fallbacks",
+                "scatters_deferred")
         return dict(zip(keys, list(buf)))
 
     def reset_stats(self):
         self.lib.mtb_evaluator_reset_stats()
+
+    def set_fusion(self, on: bool) -> bool:
+        """Turns elementwise fusion on or off; returns the previous setting."""
+        return bool(self.lib.mtb_set_fusion(1 if on else 0))
 
     def set_graphs(self, on: bool) -> bool:
         """Turns the replay of repeated evaluation plans on or off; returns the previous setting."""
@@ -207,6 +274,43 @@ class MlpTrainer:
         self.fe._check(self.fe.lib.mtb_mlp_parameters(self.h, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n),
                        "mlp_parameters")
         return out
+
+    def gradients(self):
+        """(loss, gradients) on the resident batch at the current parameters, without an
+        update; gradients in the order of parameters()."""
+        n = self.fe.lib.mtb_mlp_parameter_count(self.h)
+        out = np.empty(n, dtype=np.float32)
+        loss = ctypes.c_float(0.0)
+        self.fe._check(self.fe.lib.mtb_mlp_gradients(self.h, ctypes.byref(loss),
+                                                     out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n),
+                       "mlp_gradients")
+        return loss.value, out
+
+    def save(self, path) -> None:
+        """Writes the parameters under their tree paths to `path`."""
+        self.fe._check(self.fe.lib.mtb_mlp_save(self.h, os.fsencode(path)), "mlp_save")
+
+    def load(self, path) -> None:
+        """Replaces the parameters with those saved at `path` (matched by path)."""
+        self.fe._check(self.fe.lib.mtb_mlp_load(self.h, os.fsencode(path)), "mlp_load")
+
+    def profile(self, on: bool):
+        """Switches the device-time phase profile on or off; returns the
+        milliseconds summed since the last call: (steps, forward + backward,
+        exposed gradient exchange, optimizer)."""
+        ms = (ctypes.c_double * 4)()
+        self.fe._check(self.fe.lib.mtb_mlp_profile(self.h, int(on), ms), "mlp_profile")
+        return tuple(ms)
+
+    def set_parameters(self, values: np.ndarray):
+        """Replaces the parameters with `values` (the order of parameters())."""
+        v = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
+        self.fe._check(self.fe.lib.mtb_mlp_set_parameters(self.h, v.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                                          v.size), "mlp_set_parameters")
+
+    def use_sgd(self, lr: float):
+        """SGD(lr) replaces Adam for the following steps."""
+        self.fe._check(self.fe.lib.mtb_mlp_use_sgd(self.h, lr), "mlp_use_sgd")
 
     def synchronize(self):
         self.fe._check(self.fe.lib.mtb_mlp_synchronize(self.h), "mlp_synchronize")

@@ -87,6 +87,12 @@ bool evaluate_fused(const RuntimeRegistry &runtimes, const KernelRegistry &kerne
 struct EvaluatorOptions {
     bool fusion = true;
     bool check_index_errors = true;
+    // MTB_INDEX_CHECKS=sync: every gather / scatter-add kernel is checked before
+    // its output is installed (the stream is synchronised there), so an index
+    // outside its axis throws std::out_of_range with the node unmaterialised,
+    // as the reference's CPU kernel does (copy/loops.hpp:206-209).  Plans with
+    // index kernels are then not recorded for replay.
+    bool sync_index_checks = false;
     bool graphs = true;
     std::size_t graph_max_bytes = std::size_t(64) << 20;
 };
@@ -106,6 +112,7 @@ struct EvaluatorStats {
     std::uint64_t graph_captures = 0;  // plans recorded for replay
     std::uint64_t graph_replays = 0;   // evaluations run as one replay of a recorded plan
     std::uint64_t graph_fallbacks = 0; // recorded plans whose output blocks were in use (run eagerly)
+    std::uint64_t scatters_deferred = 0;  // scatter-adds added into their consumer's cluster output
 };
 EvaluatorStats &evaluator_stats();
 

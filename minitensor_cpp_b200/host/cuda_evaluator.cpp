@@ -62,7 +62,10 @@ EvaluatorOptions &evaluator_options() {
     static EvaluatorOptions options = [] {
         EvaluatorOptions o;
         if (const char *v = std::getenv("MTB_FUSION")) o.fusion = std::strcmp(v, "0") != 0;
-        if (const char *v = std::getenv("MTB_INDEX_CHECKS")) o.check_index_errors = std::strcmp(v, "0") != 0;
+        if (const char *v = std::getenv("MTB_INDEX_CHECKS")) {
+            o.check_index_errors = std::strcmp(v, "0") != 0;
+            o.sync_index_checks = std::strcmp(v, "sync") == 0;
+        }
         if (const char *v = std::getenv("MTB_GRAPHS")) o.graphs = std::strcmp(v, "0") != 0;
         if (const char *v = std::getenv("MTB_GRAPH_MAX_BYTES")) o.graph_max_bytes = std::strtoull(v, nullptr, 10);
         return o;
@@ -80,8 +83,10 @@ namespace {
 constexpr std::uint32_t kFullId = 0x0001;
 constexpr std::uint32_t kGatherId = 0x0208;
 constexpr std::uint32_t kScatterAddId = 0x0209;
+constexpr std::uint32_t kAddId = 0x0110;
 
-bool is_unary_id(std::uint32_t id) { return id >= 0x0101 && id <= 0x0108; }
+// reference unary ops 0x0101-0x0108 and this backend's relu 0x0180 (MTC_OP_RELU)
+bool is_unary_id(std::uint32_t id) { return (id >= 0x0101 && id <= 0x0108) || id == 0x0180; }
 bool is_binary_id(std::uint32_t id) { return id >= 0x0110 && id <= 0x0114; }
 
 // Open-addressing map from graph values to plan positions.  A plan visits a
@@ -148,6 +153,9 @@ struct Step {
     bool folded = false;   // constant folded into the clusters of its consumers
     bool materialize = false;
     int cluster = -1;
+    // a scatter-add deferred into the cluster rooted at this step: the cluster
+    // reads 0 in its place and the updates are then added into its output
+    int into = -1;
     int internal_refs = 0;  // input slots of planned nodes that read this value
 };
 
@@ -536,6 +544,31 @@ class FusedEvaluator {
         return true;
     }
 
+    // The gather VJP (rules/manipulation.cpp:81-91) with one index per position
+    // along its axis, whose output only an elementwise Add at a cluster's root
+    // reads -- in cross entropy, dLoss/dlogits = g * exp(x - lse) + scatter(-g):
+    // instead of zero-filling [B, C], scattering into it and reading it back,
+    // the cluster reads the constant 0 in its place and the updates are added
+    // into the cluster's output afterwards (mtc_gather_scatter_add_into).  Bit
+    // for bit the same: every target element receives at most one update, and
+    // (y + 0) + (0 + u) equals y + (0 + u) in float32, signed zeros included.
+    void defer_scatter(int i) {
+        Step &s = plan_[i];
+        if (!s.on_cuda || s.materialize || s.node->primitive().id().value() != kScatterAddId) return;
+        const auto cons = consumers(i);
+        if (cons.size() != 1) return;
+        const int c = cons.front();
+        const Step &cs = plan_[c];
+        if (cs.cluster < 0 || clusters_[cs.cluster].root != c || cs.node->primitive().id().value() != kAddId) return;
+        int uses = 0;
+        for (const ValueRef &in : cs.node->inputs()) uses += in.get() == s.output.get() ? 1 : 0;
+        if (uses != 1 || s.output->spec().shape != cs.output->spec().shape) return;
+        const auto &scatter = dynamic_cast<const GatherScatterAddPrimitive &>(s.node->primitive());
+        const auto ins = s.node->inputs();
+        if (ins.size() != 2 || ins[1]->spec().shape[scatter.axis()] != 1) return;
+        s.into = c;
+    }
+
     void form_clusters() {
         for (int i = static_cast<int>(plan_.size()) - 1; i >= 0; --i) {
             Step &s = plan_[i];
@@ -545,7 +578,10 @@ class FusedEvaluator {
                 s.folded = all_fused;
                 continue;
             }
-            if (!s.fusible) continue;
+            if (!s.fusible) {
+                defer_scatter(i);
+                continue;
+            }
             int target = -1;
             const Shape &shape = s.output->spec().shape;
             if (consumers_in_one_cluster(i, target) && clusters_[target].shape == shape && can_grow(target, i)) {
@@ -653,6 +689,10 @@ class FusedEvaluator {
             MutableTensorView out(spec, m);
             (*step.kernel)(*step.runtime, primitive, views, out);
         }
+        if (step.on_cuda && evaluator_options().sync_index_checks) {
+            const std::uint32_t id = primitive.id().value();
+            if (id == kGatherId || id == kScatterAddId) check_index_now(*step.runtime, id);
+        }
         install(pi, std::move(m), false);
         if (step.on_cuda) ++evaluator_stats().kernel_steps;
     }
@@ -667,6 +707,7 @@ class FusedEvaluator {
                 ++evaluator_stats().folded_constants;
                 continue;
             }
+            if (s.into >= 0) continue;  // added by its consumer's cluster launch
             const auto t0 = std::chrono::steady_clock::now();
             if (s.cluster >= 0) {
                 if (clusters_[s.cluster].root == i) launch_cluster(clusters_[s.cluster]);
@@ -682,6 +723,22 @@ class FusedEvaluator {
             }
         }
         if (!capturing_) watch_index_errors();
+    }
+
+    // Synchronous index check (MTB_INDEX_CHECKS=sync): waits for the kernel just
+    // queued and throws std::out_of_range before its output is installed.
+    static void check_index_now(DeviceRuntime &runtime, std::uint32_t id) {
+        auto &rt = dynamic_cast<CudaRuntime &>(runtime);
+        const auto c0 = std::chrono::steady_clock::now();
+        std::int64_t detail = 0;
+        const int rc = mtc_check_device_errors(rt.index(), rt.stream(), &detail);
+        evaluator_stats().check_ns += static_cast<std::uint64_t>(
+            std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now() - c0).count());
+        // the reference kernels' messages (copy/loops.hpp:208, :288)
+        if (rc == MTC_ERR_OUT_OF_RANGE)
+            throw std::out_of_range{id == kGatherId ? "gather index is out of range"
+                                                    : "gather scatter add index is out of range"};
+        check(rc, "device error check");
     }
 
     // Queues a snapshot of the device error word after an evaluation that ran
@@ -715,6 +772,7 @@ class FusedEvaluator {
         std::vector<int> out_steps;
         std::vector<int> const_steps;
         std::vector<float> const_values;
+        int deferred = -1;  // a scatter-add added into the root's output afterwards
         // external inputs
         for (int m : members) {
             for (const ValueRef &in : plan_[m].node->inputs()) {
@@ -722,7 +780,7 @@ class FusedEvaluator {
                 if (reg.count(v)) continue;
                 auto it = plan_index(v);
                 if (it >= 0 && plan_[it].cluster == plan_[m].cluster) continue;
-                if (it >= 0 && plan_[it].folded) continue;
+                if (it >= 0 && (plan_[it].folded || plan_[it].into >= 0)) continue;
                 const Materialization *mat = mat_of(v);
                 if (mat == nullptr) throw std::logic_error{"fused cluster has an unmaterialized input"};
                 reg.emplace(v, static_cast<int>(inputs.size()));
@@ -739,6 +797,16 @@ class FusedEvaluator {
             for (std::size_t k = 0; k < ins.size(); ++k) {
                 const Value *v = ins[k].get();
                 auto found = reg.find(v);
+                if (found == reg.end() && plan_index(v) >= 0 && plan_[plan_index(v)].into >= 0) {
+                    // a deferred scatter-add: 0 here, its updates added afterwards
+                    mtc_instr zi{};
+                    zi.op = MTC_OP_CONST;
+                    zi.dst = static_cast<int16_t>(next);
+                    zi.imm = 0.0f;
+                    program.push_back(zi);
+                    deferred = plan_index(v);
+                    found = reg.emplace(v, next++).first;
+                }
                 if (found == reg.end()) {
                     // a folded constant: emit it once
                     const int pi = plan_index(v);
@@ -769,6 +837,14 @@ class FusedEvaluator {
             run_unfused(members);
             return;
         }
+        const Materialization *scatter_upd = nullptr, *scatter_idx = nullptr;
+        if (deferred >= 0) {
+            const auto sin = plan_[deferred].node->inputs();
+            scatter_upd = mat_of(sin[0].get());
+            scatter_idx = mat_of(sin[1].get());
+            if (scatter_upd == nullptr || scatter_idx == nullptr)
+                throw std::logic_error{"deferred scatter-add has an unmaterialized input"};
+        }
         std::vector<Materialization> mats;
         std::vector<mtc_desc> outputs;
         std::vector<int32_t> out_regs;
@@ -791,6 +867,23 @@ class FusedEvaluator {
             return;
         }
         check(rc, "fused elementwise kernel");
+        if (deferred >= 0) {
+            const Step &sc = plan_[deferred];
+            const auto sin = sc.node->inputs();
+            const mtc_desc upd = make_desc(TensorView(sin[0]->spec(), *scatter_upd));
+            const mtc_desc idx = make_desc(TensorView(sin[1]->spec(), *scatter_idx));
+            std::size_t j = 0;
+            while (out_steps[j] != c.root) ++j;
+            const mtc_desc out = outputs[j];
+            const auto axis = static_cast<int64_t>(
+                dynamic_cast<const GatherScatterAddPrimitive &>(sc.node->primitive()).axis());
+            check(mtc_gather_scatter_add_into(&upd, &idx, axis, &out, runtime->stream()), "scatter-add into");
+            if (evaluator_options().sync_index_checks) check_index_now(*runtime, kScatterAddId);
+            index_kernels_ = true;
+            index_runtime_ = runtime;
+            ++evaluator_stats().kernel_steps;
+            ++evaluator_stats().scatters_deferred;
+        }
         if (capturing_) {
             int32_t recorded_after = 0;
             check(mtc_capture_fused_count(&recorded_after), "recording");
@@ -810,7 +903,13 @@ class FusedEvaluator {
         for (int m : members) {
             for (const ValueRef &in : plan_[m].node->inputs()) {
                 const int pi = plan_index(in.get());
-                if (pi >= 0 && plan_[pi].folded && mat_of(in.get()) == nullptr) execute_step(pi);
+                if (pi >= 0 && (plan_[pi].folded || plan_[pi].into >= 0) && mat_of(in.get()) == nullptr) {
+                    execute_step(pi);
+                    if (plan_[pi].into >= 0) {
+                        index_kernels_ = true;
+                        index_runtime_ = plan_[pi].runtime;
+                    }
+                }
             }
             execute_step(m);
         }
@@ -842,10 +941,12 @@ class FusedEvaluator {
             if (rt == nullptr && s.runtime != nullptr) rt = dynamic_cast<CudaRuntime *>(s.runtime);
             const Primitive &primitive = s.node->primitive();
             const std::uint32_t id = primitive.id().value();
+            if ((id == kGatherId || id == kScatterAddId) && evaluator_options().sync_index_checks)
+                return trace_graph("not recorded", "synchronous index checks"), false;
             w.pod(id);
             w.pod(static_cast<std::uint8_t>(spec.dtype));
             w.shape(spec.shape);
-            w.pod(static_cast<std::uint8_t>((s.materialize ? 1 : 0) | (s.folded ? 2 : 0)));
+            w.pod(static_cast<std::uint8_t>((s.materialize ? 1 : 0) | (s.folded ? 2 : 0) | (s.into >= 0 ? 4 : 0)));
             w.pod(static_cast<std::int32_t>(s.cluster));
             if (!write_parameters(primitive, id, s.folded, w)) {
                 trace_graph("not recorded, unknown primitive", std::string(primitive.name()).c_str());

@@ -1,7 +1,9 @@
-// New primitives (max, argmax, log-softmax), their CPU and CUDA kernels, and
-// the relu composite.  The CPU kernels walk the reference's own ReductionPlan
-// (src/tensor/backend/cpu/iteration/reduction.hpp:18-119) in its sequential
-// order, so they are the CPU definition the CUDA kernels are checked against.
+// New primitives (relu, max, argmax, log-softmax), their CPU and CUDA kernels,
+// and relu's VJP rule.  The CPU reduction kernels walk the reference's own
+// ReductionPlan (src/tensor/backend/cpu/iteration/reduction.hpp:18-119) in its
+// sequential order, and relu's CPU kernel runs the reference's unary loop
+// (src/tensor/backend/cpu/kernels/elementwise/loops.hpp:19-67), so they are
+// the CPU definition the CUDA kernels are checked against.
 #include "ops_ext.hpp"
 
 #include <algorithm>
@@ -17,6 +19,8 @@
 
 #include "cuda_backend.hpp"
 #include "tensor/apply_operation.hpp"
+#include "tensor/autograd/vjp_registry.hpp"
+#include "tensor/backend/cpu/kernels/elementwise/loops.hpp"
 #include "tensor/backend/cpu/detail/buffer_access.hpp"
 #include "tensor/backend/cpu/iteration/reduction.hpp"
 #include "tensor/core/axis.hpp"
@@ -39,6 +43,18 @@ std::vector<Shape::size_type> normalized_axes(std::span<const Axis> axes, Shape:
         throw std::invalid_argument{std::string(what) + " axes cannot contain duplicates"};
     return out;
 }
+
+class ReluPrimitive final : public Primitive {
+  public:
+    static constexpr PrimitiveId ID{0x0180};
+    [[nodiscard]] PrimitiveId id() const noexcept override { return ID; }
+    [[nodiscard]] std::string_view name() const noexcept override { return "relu"; }
+    [[nodiscard]] TensorSpec infer(std::span<const TensorSpec> inputs) const override {
+        if (inputs.size() != 1) throw std::invalid_argument{"relu requires a single input"};
+        if (!is_floating_point(inputs.front().dtype)) throw std::invalid_argument{"relu requires a floating-point input"};
+        return inputs.front();
+    }
+};
 
 class MaxPrimitive final : public Primitive {
   public:
@@ -109,6 +125,16 @@ class LogSoftmaxPrimitive final : public Primitive {
 };
 
 // ------------------------------------------------------------- CPU kernels --
+
+// max(x, 0): x above 0 passes, NaN propagates, everything else (-0, -inf) is +0.
+float relu_value(float x) { return x > 0.0F || std::isnan(x) ? x : 0.0F; }
+
+void cpu_relu(DeviceRuntime &, const Primitive &primitive, std::span<const TensorView> inputs,
+              MutableTensorView output) {
+    (void)dynamic_cast<const ReluPrimitive &>(primitive);
+    if (output.dtype() != DType::Float32) throw std::invalid_argument{"relu supports Float32"};
+    cpu::unary_elementwise<float>(inputs.front(), output, relu_value);
+}
 
 void cpu_max(DeviceRuntime &, const Primitive &primitive, std::span<const TensorView> inputs, MutableTensorView output) {
     const auto &p = dynamic_cast<const MaxPrimitive &>(primitive);
@@ -213,6 +239,15 @@ void cpu_log_softmax(DeviceRuntime &, const Primitive &primitive, std::span<cons
 
 // ------------------------------------------------------------ CUDA kernels --
 
+void cuda_relu(DeviceRuntime &rt, const Primitive &primitive, std::span<const TensorView> inputs,
+               MutableTensorView output) {
+    (void)dynamic_cast<const ReluPrimitive &>(primitive);
+    auto &cr = dynamic_cast<cuda::CudaRuntime &>(rt);
+    cr.activate();
+    const mtc_desc in = cuda::make_desc(inputs.front()), out = cuda::make_desc(output);
+    cuda::check(mtc_unary(MTC_OP_RELU, &in, &out, cr.stream()), "relu kernel");
+}
+
 void cuda_max(DeviceRuntime &rt, const Primitive &primitive, std::span<const TensorView> inputs,
               MutableTensorView output) {
     const auto &p = dynamic_cast<const MaxPrimitive &>(primitive);
@@ -247,6 +282,7 @@ void cuda_log_softmax(DeviceRuntime &rt, const Primitive &primitive, std::span<c
 
 bool write_primitive_key(const Primitive &primitive, std::string &key) {
     auto put = [&key](std::int64_t v) { key.append(reinterpret_cast<const char *>(&v), sizeof(v)); };
+    if (dynamic_cast<const ReluPrimitive *>(&primitive) != nullptr) return true;  // no parameters
     if (const auto *p = dynamic_cast<const MaxPrimitive *>(&primitive)) {
         put(static_cast<std::int64_t>(p->axes().size()));
         for (auto a : p->axes()) put(static_cast<std::int64_t>(a));
@@ -266,6 +302,8 @@ bool write_primitive_key(const Primitive &primitive, std::string &key) {
 }
 
 void register_extension_kernels(KernelRegistry &registry) {
+    registry.register_kernel({ReluPrimitive::ID, DeviceType::Cpu}, cpu_relu);
+    registry.register_kernel({ReluPrimitive::ID, DeviceType::Cuda}, cuda_relu);
     registry.register_kernel({MaxPrimitive::ID, DeviceType::Cpu}, cpu_max);
     registry.register_kernel({ArgMaxPrimitive::ID, DeviceType::Cpu}, cpu_argmax);
     registry.register_kernel({LogSoftmaxPrimitive::ID, DeviceType::Cpu}, cpu_log_softmax);
@@ -276,9 +314,28 @@ void register_extension_kernels(KernelRegistry &registry) {
 
 }  // namespace minitensor::detail::ext
 
+namespace minitensor::detail {
+
+// relu's VJP: the cotangent where the input is above 0, 0 where it is not
+// (the derivative at 0 is taken as 0), NaN where the input is NaN.  The step
+// (sign(x) + |sign(x)|) * 0.5 is built from reference ops, so the evaluator fuses
+// it with the product into one kernel.  Called by the reference's VJP registry
+// when it is built with this backend (the third edit of _build_host.py).
+void register_backend_vjps(VjpRegistry &registry) {
+    registry.register_rule<ext::ReluPrimitive>([](const ext::ReluPrimitive &, const VjpContext &context) {
+        if (context.inputs.size() != 1) throw std::logic_error{"relu VJP expects 1 input"};
+        const Tensor s = sign(context.inputs.front());
+        return VjpContributions{context.output_cotangent * ((s + abs(s)) * 0.5F)};
+    });
+}
+
+}  // namespace minitensor::detail
+
 namespace minitensor::b200 {
 
-Tensor relu(const Tensor &input) { return (input + abs(input)) * 0.5F; }
+Tensor relu(const Tensor &input) {
+    return detail::apply_operation(std::make_unique<detail::ext::ReluPrimitive>(), input);
+}
 
 Tensor max(const Tensor &input, std::span<const Axis> axes, bool keep_dim) {
     return detail::apply_operation(std::make_unique<detail::ext::MaxPrimitive>(axes, input.rank(), keep_dim), input);

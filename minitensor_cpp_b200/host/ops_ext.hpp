@@ -2,18 +2,18 @@
 // no ReLU, max, argmax or log-softmax primitive (its activations are tanh and
 // sigmoid, its reductions sum and logsumexp); the benchmark workloads need them.
 //
-//  relu(x)            composite (x + |x|) * 0.5 of reference ops: exact ReLU in
-//                     float32 for finite x (-0 -> +0), NaN propagates, and -inf
-//                     gives NaN (-inf + inf); differentiable through the
-//                     reference's own VJP rules (gradient 0.5 at 0), and one
-//                     fused kernel on the GPU.
+//  relu(x)            new primitive 0x0180: max(x, 0) for every float32 input
+//                     (x > 0 passes unchanged, -0 and -inf give +0, NaN
+//                     propagates); VJP cotangent * [x > 0] (0 at 0, NaN for a
+//                     NaN input).  Fused with its neighbours on the GPU.
 //  max(x, axes)       new primitive 0x0380: NaN propagates, empty -> -inf.
 //  argmax(x, axis)    new primitive 0x0381: Int64 index of the first maximum; a
 //                     NaN counts as the maximum.
 //  log_softmax(x, a)  new primitive 0x0382: x - logsumexp(x, {a}, keep_dim=true),
 //                     one pass over memory on the GPU.
-// None of the three new primitives has a VJP rule (they are not differentiated
-// by the workloads); grad() through them raises the reference's missing-rule error.
+// max, argmax and log-softmax have no VJP rule (the workloads do not
+// differentiate them); grad() through them raises the reference's missing-rule
+// error.
 #pragma once
 
 #include <initializer_list>
@@ -26,6 +26,10 @@
 namespace minitensor::detail {
 class KernelRegistry;
 class Primitive;
+class VjpRegistry;
+// relu's VJP rule; the reference's VJP registry calls this hook (weak there)
+// after its own rules when it is built with this backend.
+void register_backend_vjps(VjpRegistry &registry);
 }
 
 namespace minitensor::b200 {

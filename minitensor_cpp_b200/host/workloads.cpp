@@ -1,10 +1,13 @@
 // Benchmark and parity workloads over MiniTensor's public API (see workloads.hpp).
 #include "workloads.hpp"
 
+#include <array>
 #include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
+#include <unordered_map>
+#include <cstring>
 #include <limits>
 #include <memory>
 #include <optional>
@@ -16,13 +19,16 @@
 
 #include <minitensor/data.hpp>
 #include <minitensor/evaluation.hpp>
+#include <minitensor/autograd.hpp>
 #include <minitensor/nn/gradients.hpp>
 #include <minitensor/nn/leafification.hpp>
 #include <minitensor/nn/loss.hpp>
 #include <minitensor/nn/module.hpp>
 #include <minitensor/nn/modules/linear.hpp>
 #include <minitensor/nn/optimizers/adamw.hpp>
+#include <minitensor/nn/optimizers/sgd.hpp>
 #include <minitensor/nn/parameters.hpp>
+#include <minitensor/nn/parameters/parameter_tree.hpp>
 #include <minitensor/ops.hpp>
 #include <minitensor/random.hpp>
 #include <minitensor/tensor.hpp>
@@ -140,6 +146,22 @@ class DenseMlp final {
     std::vector<mt::nn::Linear> layers_;
 };
 
+// One parameter vector: the tree of the optimizer workload.
+class VectorTree final {
+  public:
+    explicit VectorTree(mt::nn::ParameterId id) : id_{std::move(id)} {}
+    [[nodiscard]] const mt::nn::ParameterId &id() const noexcept { return id_; }
+
+  private:
+    template <typename Self, typename Visitor>
+    static void visit_members(Self &self, Visitor &visitor) {
+        visitor.parameter("value", self.id_);
+    }
+
+    mt::nn::ParameterId id_;
+    friend class minitensor::nn::ParameterTreeAccess;
+};
+
 using Snapshot = mt::nn::ParameterSnapshot<DenseMlp::ParameterTree>;
 
 }  // namespace
@@ -248,6 +270,7 @@ struct MlpTrainer {
     int world = 1;
     std::optional<mt::Tensor> x_resident;
     std::optional<mt::Tensor> y_resident;
+    std::optional<mt::nn::SGD> sgd;  // set: SGD replaces Adam
 #ifndef MTB_CPU_ONLY
     // Input pipeline of step_host on a CUDA device: two device slots for a
     // batch (x and labels) filled on a copy stream, so the next batch's copy
@@ -263,6 +286,20 @@ struct MlpTrainer {
     void *copy_stream = nullptr;
     void *loss_ready = nullptr;  // event: the step's loss is computed
     bool mark_loss = false;      // record loss_ready once the loss is queued
+    // Phase profile (mtb_mlp_profile): timed events on the device stream at the
+    // step's start, before the wait for the gradient exchange, after it, and
+    // after the optimizer; read and released by mtb_mlp_profile_read.
+    bool profile = false;
+    std::vector<std::array<void *, 4>> phase_events;
+    void *phase_mark(int which) {
+        if (!profile || device.type() != mt::DeviceType::Cuda) return nullptr;
+        if (which == 0) phase_events.push_back({nullptr, nullptr, nullptr, nullptr});
+        void *&e = phase_events.back()[static_cast<std::size_t>(which)];
+        const int dev = static_cast<int>(device.index());
+        mt::detail::cuda::check(mtc_event_create_timed(dev, &e), "profile event");
+        mt::detail::cuda::check(mtc_event_record(e, cuda_runtime().stream()), "profile event");
+        return e;
+    }
 #endif
 
     MlpTrainer(mt::Device dev, std::vector<mt::Extent> widths, uint64_t seed, float lr)
@@ -294,12 +331,44 @@ struct MlpTrainer {
 #endif
     }
 
+#ifndef MTB_CPU_ONLY
+    // Device milliseconds of the profiled steps so far, summed: [0] the whole
+    // steps, [1] forward + backward up to the wait for the gradient exchange,
+    // [2] the exchange's exposed part (the device stream waiting for NCCL),
+    // [3] the optimizer after it.  With one rank only [0] is measured.  The
+    // events are released.
+    void profile_read(double *ms4) {
+        for (int k = 0; k < 4; ++k) ms4[k] = 0.0;
+        const int dev = static_cast<int>(device.index());
+        for (auto &ev : phase_events) {
+            float t = 0.0F;
+            if (ev[0] && ev[3]) {
+                mt::detail::cuda::check(mtc_event_elapsed(ev[0], ev[3], &t), "profile read");
+                ms4[0] += t;
+            }
+            for (int k = 0; k < 3; ++k) {
+                if (ev[static_cast<std::size_t>(k)] && ev[static_cast<std::size_t>(k) + 1]) {
+                    mt::detail::cuda::check(mtc_event_elapsed(ev[static_cast<std::size_t>(k)],
+                                                              ev[static_cast<std::size_t>(k) + 1], &t),
+                                            "profile read");
+                    ms4[k + 1] += t;
+                }
+            }
+            for (void *e : ev) (void)mtc_event_destroy(dev, e);
+        }
+        phase_events.clear();
+    }
+#endif
+
     // early_loss: read the loss as soon as it is computed (a CUDA device): the
     // forward pass is evaluated first and marked, and the read waits for that
     // mark only, so the host returns while the device runs the backward pass
     // and the optimizer.  Otherwise the loss is read after the whole step.
     float step(const mt::Tensor &x, const mt::Tensor &y, bool read_loss, bool early_loss = false) {
         StepTrace trace;
+#ifndef MTB_CPU_ONLY
+        phase_mark(0);
+#endif
         const mt::Tensor logits = mt::nn::forward(model, params, x);
         const mt::Tensor loss = mt::nn::categorical_cross_entropy_with_logits(logits, y);
 #ifndef MTB_CPU_ONLY
@@ -316,13 +385,25 @@ struct MlpTrainer {
         trace.mark("graph");
         if (world > 1) allreduce(grads, loss);
         trace.mark("allreduce");
-        auto [next_params, next_state] = optimizer.step(std::move(params), std::move(state), grads);
-        grads.clear();
-        trace.mark("optimizer graph");
-        params = mt::nn::leafify_parameter_values(std::move(next_params));
-        trace.mark("evaluate parameters");
-        state = mt::nn::leafify_optimizer_state(std::move(next_state));
-        trace.mark("evaluate state");
+        if (sgd) {
+            auto [next_params, sgd_state] = sgd->step(std::move(params), mt::nn::SGD::State{}, grads);
+            (void)sgd_state;
+            grads.clear();
+            trace.mark("optimizer graph");
+            params = mt::nn::leafify_parameter_values(std::move(next_params));
+            trace.mark("evaluate parameters");
+        } else {
+            auto [next_params, next_state] = optimizer.step(std::move(params), std::move(state), grads);
+            grads.clear();
+            trace.mark("optimizer graph");
+            params = mt::nn::leafify_parameter_values(std::move(next_params));
+            trace.mark("evaluate parameters");
+            state = mt::nn::leafify_optimizer_state(std::move(next_state));
+            trace.mark("evaluate state");
+        }
+#ifndef MTB_CPU_ONLY
+        phase_mark(3);
+#endif
         float value = 0.0F;
 #ifndef MTB_CPU_ONLY
         if (early_loss) value = read_marked_loss(loss);
@@ -331,6 +412,137 @@ struct MlpTrainer {
             if (read_loss) value = mt::item<float>(loss);
         trace.mark("loss");
         return value;
+    }
+
+    // Replaces every parameter's value with host values in the order of
+    // mtb_mlp_parameters (weight [out, in] then bias [out], layer by layer).
+    void set_parameters(const float *values, std::int64_t count) {
+        std::int64_t pos = 0;
+        std::vector<std::pair<mt::nn::ParameterId, std::int64_t>> offsets;
+        for (const auto &id : order) {
+            offsets.emplace_back(id, pos);
+            pos += static_cast<std::int64_t>(params.parameters().get(id).value.numel());
+        }
+        if (pos != count) throw std::invalid_argument{"parameter count differs from the model's"};
+        params = std::move(params).transform([&](mt::nn::ParameterId id, const mt::nn::ParameterState &state) {
+            for (const auto &[pid, off] : offsets) {
+                if (pid == id) {
+                    const auto n = static_cast<std::size_t>(state.value.numel());
+                    return mt::nn::ParameterState{
+                        mt::from_data(std::span<const float>(values + off, n), state.value.shape(), device),
+                        state.metadata};
+                }
+            }
+            return state;
+        });
+        params = mt::nn::leafify_parameter_values(std::move(params));
+    }
+
+    // Checkpoint of the parameters under their tree paths (layer0.weight, ...).
+    // Format, little-endian: "MTBCKPT1", u32 parameter count, then per parameter
+    // u32 path length, the path, u32 rank, i64 extents, float32 values.
+    void save(const char *file) const {
+        std::FILE *f = std::fopen(file, "wb");
+        if (f == nullptr) throw std::runtime_error{std::string("cannot open ") + file + " for writing"};
+        std::vector<std::pair<std::string, mt::nn::ParameterId>> named;
+        mt::nn::for_each_named_parameter(params.tree(), [&](std::string_view name, const mt::nn::ParameterId id) {
+            named.emplace_back(std::string(name), id);
+        });
+        bool ok = std::fwrite("MTBCKPT1", 1, 8, f) == 8;
+        const auto count = static_cast<std::uint32_t>(named.size());
+        ok = ok && std::fwrite(&count, sizeof(count), 1, f) == 1;
+        for (const auto &[name, id] : named) {
+            const mt::Tensor &v = params.value(id);
+            const std::vector<float> host = mt::to_vector(v);
+            const auto len = static_cast<std::uint32_t>(name.size());
+            const auto rank = static_cast<std::uint32_t>(v.rank());
+            ok = ok && std::fwrite(&len, sizeof(len), 1, f) == 1 && std::fwrite(name.data(), 1, len, f) == len &&
+                 std::fwrite(&rank, sizeof(rank), 1, f) == 1;
+            for (std::size_t d = 0; d < v.rank(); ++d) {
+                const auto extent = static_cast<std::int64_t>(v.shape()[d]);
+                ok = ok && std::fwrite(&extent, sizeof(extent), 1, f) == 1;
+            }
+            ok = ok && std::fwrite(host.data(), sizeof(float), host.size(), f) == host.size();
+        }
+        ok = std::fclose(f) == 0 && ok;
+        if (!ok) throw std::runtime_error{std::string("writing ") + file + " failed"};
+    }
+
+    // Replaces every parameter with the one saved under its path; the file must
+    // hold each of the model's parameters with the same shape.
+    void load(const char *file) {
+        std::FILE *f = std::fopen(file, "rb");
+        if (f == nullptr) throw std::runtime_error{std::string("cannot open ") + file};
+        struct Record {
+            std::vector<mt::Extent> shape;
+            std::vector<float> values;
+        };
+        std::unordered_map<std::string, Record> records;
+        char magic[8] = {};
+        std::uint32_t count = 0;
+        bool ok = std::fread(magic, 1, 8, f) == 8 && std::memcmp(magic, "MTBCKPT1", 8) == 0 &&
+                  std::fread(&count, sizeof(count), 1, f) == 1;
+        for (std::uint32_t k = 0; ok && k < count; ++k) {
+            std::uint32_t len = 0, rank = 0;
+            ok = std::fread(&len, sizeof(len), 1, f) == 1 && len < 4096;
+            std::string name(ok ? len : 0, '\0');
+            ok = ok && std::fread(name.data(), 1, len, f) == len && std::fread(&rank, sizeof(rank), 1, f) == 1 &&
+                 rank <= 8;
+            Record r;
+            std::size_t n = 1;
+            for (std::uint32_t d = 0; ok && d < rank; ++d) {
+                std::int64_t extent = 0;
+                ok = std::fread(&extent, sizeof(extent), 1, f) == 1 && extent >= 0 && extent < (std::int64_t{1} << 40);
+                r.shape.push_back(extent);
+                n *= static_cast<std::size_t>(extent);
+            }
+            if (!ok) break;
+            r.values.resize(n);
+            ok = std::fread(r.values.data(), sizeof(float), n, f) == n;
+            records.emplace(std::move(name), std::move(r));
+        }
+        std::fclose(f);
+        if (!ok) throw std::runtime_error{std::string(file) + " is not a complete checkpoint"};
+        std::unordered_map<mt::nn::ParameterId, const Record *> by_id;
+        mt::nn::for_each_named_parameter(params.tree(), [&](std::string_view name, const mt::nn::ParameterId id) {
+            const auto it = records.find(std::string(name));
+            if (it == records.end()) throw std::invalid_argument{"checkpoint has no parameter " + std::string(name)};
+            const mt::Tensor &v = params.value(id);
+            if (it->second.shape.size() != v.rank()) throw std::invalid_argument{"checkpoint shape differs: " + std::string(name)};
+            for (std::size_t d = 0; d < v.rank(); ++d)
+                if (it->second.shape[d] != v.shape()[d])
+                    throw std::invalid_argument{"checkpoint shape differs: " + std::string(name)};
+            by_id.emplace(id, &it->second);
+        });
+        params = std::move(params).transform([&](mt::nn::ParameterId id, const mt::nn::ParameterState &state) {
+            const auto it = by_id.find(id);
+            if (it == by_id.end()) return state;
+            return mt::nn::ParameterState{mt::from_data(std::span<const float>(it->second->values), state.value.shape(),
+                                                        device),
+                                          state.metadata};
+        });
+        params = mt::nn::leafify_parameter_values(std::move(params));
+    }
+
+    // Loss and parameter gradients on the resident batch at the current
+    // parameters (no update), evaluated together in one evaluation.
+    float gradients(float *out, std::int64_t capacity) {
+        if (!x_resident) throw std::logic_error{"no resident batch loaded"};
+        const mt::Tensor logits = mt::nn::forward(model, params, *x_resident);
+        const mt::Tensor loss = mt::nn::categorical_cross_entropy_with_logits(logits, *y_resident);
+        const auto grads = mt::nn::parameter_gradients(loss, params);
+        std::vector<mt::Tensor> roots{loss};
+        for (const auto &id : order) roots.push_back(grads.at(id));
+        const std::vector<mt::Tensor> leaves = mt::leafify(roots);
+        std::int64_t pos = 0;
+        for (std::size_t i = 0; i < order.size(); ++i) {
+            const std::vector<float> host = mt::to_vector(leaves[i + 1]);
+            if (pos + static_cast<std::int64_t>(host.size()) > capacity)
+                throw std::out_of_range{"gradient buffer too small"};
+            std::copy(host.begin(), host.end(), out + pos);
+            pos += static_cast<std::int64_t>(host.size());
+        }
+        return mt::item<float>(leaves[0]);
     }
 
 #ifndef MTB_CPU_ONLY
@@ -449,7 +661,9 @@ struct MlpTrainer {
                                                                      1.0F / world, rt.stream()),
                                         "gradient all-reduce");
             }
+            phase_mark(1);
             mt::detail::cuda::check(mtc_comm_wait(comm, rt.stream()), "gradient all-reduce wait");
+            phase_mark(2);
             return;
         }
         std::vector<mt::Tensor> roots{loss};
@@ -588,6 +802,45 @@ int mtb_mlp_parameters(void *handle, float *out, int64_t capacity) {
     });
 }
 
+int mtb_mlp_gradients(void *handle, float *loss, float *out, int64_t capacity) {
+    return guarded([&] {
+        auto *t = static_cast<MlpTrainer *>(handle);
+        const float l = t->gradients(out, capacity);
+        if (loss) *loss = l;
+    });
+}
+
+int mtb_mlp_profile(void *handle, int32_t on, double *ms4) {
+    return guarded([&] {
+        auto *t = static_cast<MlpTrainer *>(handle);
+#ifndef MTB_CPU_ONLY
+        if (ms4) t->profile_read(ms4);
+        t->profile = on != 0;
+#else
+        (void)t;
+        (void)on;
+        if (ms4)
+            for (int k = 0; k < 4; ++k) ms4[k] = 0.0;
+#endif
+    });
+}
+
+int mtb_mlp_save(void *handle, const char *path) {
+    return guarded([&] { static_cast<MlpTrainer *>(handle)->save(path); });
+}
+
+int mtb_mlp_load(void *handle, const char *path) {
+    return guarded([&] { static_cast<MlpTrainer *>(handle)->load(path); });
+}
+
+int mtb_mlp_set_parameters(void *handle, const float *values, int64_t count) {
+    return guarded([&] { static_cast<MlpTrainer *>(handle)->set_parameters(values, count); });
+}
+
+int mtb_mlp_use_sgd(void *handle, float lr) {
+    return guarded([&] { static_cast<MlpTrainer *>(handle)->sgd.emplace(lr); });
+}
+
 int mtb_mlp_materialize(void *handle) {
     return guarded([&] {
         auto *t = static_cast<MlpTrainer *>(handle);
@@ -660,18 +913,112 @@ int mtb_gather_rows(int device, int64_t rows, int64_t cols, const float *table, 
     });
 }
 
+int mtb_cross_entropy(int device, int64_t rows, int64_t cols, const float *logits, int32_t class_axis,
+                      const int64_t *targets, float *loss, float *grad) {
+    return guarded([&] {
+        if (class_axis != 0 && class_axis != 1) throw std::invalid_argument{"class axis must be 0 or 1"};
+        const mt::Device dev = device_of(device);
+        const mt::Tensor X = mt::from_data(std::span<const float>(logits, static_cast<std::size_t>(rows * cols)),
+                                           mt::Shape{rows, cols}, dev);
+        const int64_t n = class_axis == 0 ? cols : rows;
+        const mt::Tensor T = mt::from_data(std::span<const std::int64_t>(targets, static_cast<std::size_t>(n)),
+                                           mt::Shape{n}, dev);
+        const mt::Tensor L = mt::nn::categorical_cross_entropy_with_logits(X, T, class_axis);
+        if (grad) {
+            const std::vector<float> g = mt::to_vector(mt::grad(L, X).front());
+            std::copy(g.begin(), g.end(), grad);
+        }
+        if (loss) *loss = mt::item<float>(L);
+    });
+}
+
+int mtb_optimizer_steps(int device, int32_t kind, int64_t n, const float *params, int32_t steps, const float *grads,
+                        float lr, float weight_decay, float beta1, float beta2, float eps, float *out) {
+    return guarded([&] {
+        if (kind != 0 && kind != 1) throw std::invalid_argument{"optimizer kind must be 0 (AdamW) or 1 (SGD)"};
+        if (n < 0 || steps < 0) throw std::invalid_argument{"negative size"};
+        const mt::Device dev = device_of(device);
+        const auto count = static_cast<std::size_t>(n);
+        mt::nn::ParameterBuilder builder;
+        const mt::nn::ParameterId id =
+            builder.add(mt::nn::ParameterState{mt::from_data(std::span<const float>(params, count), mt::Shape{n}, dev)});
+        auto snapshot = std::move(builder).finish(VectorTree{id});
+        auto gradient_of = [&](int32_t step) {
+            mt::nn::ParameterGradients g;
+            g.emplace(id, mt::from_data(std::span<const float>(grads + static_cast<std::size_t>(step) * count, count),
+                                        mt::Shape{n}, dev));
+            return g;
+        };
+        if (kind == 0) {
+            const mt::nn::AdamW optimizer(lr, weight_decay, beta1, beta2, eps);
+            auto state = optimizer.initialize(snapshot);
+            for (int32_t s = 0; s < steps; ++s) {
+                auto [next, next_state] = optimizer.step(std::move(snapshot), std::move(state), gradient_of(s));
+                snapshot = mt::nn::leafify_parameter_values(std::move(next));
+                state = mt::nn::leafify_optimizer_state(std::move(next_state));
+            }
+        } else {
+            const mt::nn::SGD optimizer(lr);
+            for (int32_t s = 0; s < steps; ++s) {
+                auto [next, next_state] = optimizer.step(std::move(snapshot), optimizer.initialize(snapshot),
+                                                         gradient_of(s));
+                (void)next_state;
+                snapshot = mt::nn::leafify_parameter_values(std::move(next));
+            }
+        }
+        const std::vector<float> v = mt::to_vector(snapshot.value(id));
+        std::copy(v.begin(), v.end(), out);
+    });
+}
+
+#ifndef MTB_CPU_ONLY
+int mtb_gather_eval_probe(int device, int64_t rows, int64_t cols, const float *table, int64_t n, const int64_t *index,
+                          int32_t *threw, int32_t *materialized) {
+    return guarded([&] {
+        const mt::Device dev = device_of(device);
+        const mt::Tensor t = mt::from_data(std::span<const float>(table, static_cast<std::size_t>(rows * cols)),
+                                           mt::Shape{rows, cols}, dev);
+        const mt::Tensor i = mt::from_data(std::span<const std::int64_t>(index, static_cast<std::size_t>(n)),
+                                           mt::Shape{n, 1}, dev);
+        const mt::Tensor g = mt::gather(t, 0, mt::broadcast_to(i, mt::Shape{n, cols}));
+        *threw = 0;
+        try {
+            mt::eval(g);
+        } catch (const std::out_of_range &) {
+            *threw = 1;
+        }
+        *materialized = mt::detail::TensorAccess::value(g)->materialization() != nullptr ? 1 : 0;
+        if (*threw == 0) (void)mt::to_vector(g);  // a deferred index error surfaces at this read
+    });
+}
+
+int mtb_set_index_checks(int mode) {
+    auto &o = mt::detail::cuda::evaluator_options();
+    const int previous = !o.check_index_errors ? 0 : (o.sync_index_checks ? 2 : 1);
+    o.check_index_errors = mode != 0;
+    o.sync_index_checks = mode == 2;
+    return previous;
+}
+#endif
+
 #ifndef MTB_CPU_ONLY
 // The operations this backend adds (ops_ext.hpp) on a [rows, cols] matrix,
 // through MiniTensor's API: relu(x), and max, argmax and log-softmax along
-// `axis` (0 or 1).  max_out and argmax_out hold the reduced extent, the other
-// two rows * cols values.
+// `axis` (0 or 1), and (relu_grad_out, may be NULL) the gradient of
+// sum(relu(x)).  max_out and argmax_out hold the reduced extent, the others
+// rows * cols values.
 int mtb_added_ops(int device, int64_t rows, int64_t cols, const float *x, int32_t axis, float *relu_out,
-                  float *max_out, int64_t *argmax_out, float *log_softmax_out) {
+                  float *max_out, int64_t *argmax_out, float *log_softmax_out, float *relu_grad_out) {
     return guarded([&] {
         if (axis != 0 && axis != 1) throw std::invalid_argument{"axis must be 0 or 1"};
         const mt::Device dev = device_of(device);
         const mt::Tensor X = mt::from_data(std::span<const float>(x, static_cast<std::size_t>(rows * cols)),
                                            mt::Shape{rows, cols}, dev);
+        if (relu_grad_out) {
+            // d sum(relu(X)) / dX through the autograd engine and relu's VJP rule
+            const std::vector<float> g = mt::to_vector(mt::grad(mt::sum(mt::b200::relu(X)), X).front());
+            std::copy(g.begin(), g.end(), relu_grad_out);
+        }
         const std::vector<float> r = mt::to_vector(mt::b200::relu(X));
         const std::vector<float> m = mt::to_vector(mt::b200::max(X, {axis}));
         const std::vector<std::int64_t> a = mt::to_vector<std::int64_t>(mt::b200::argmax(X, axis));
@@ -684,29 +1031,41 @@ int mtb_added_ops(int device, int64_t rows, int64_t cols, const float *x, int32_
 }
 #endif
 
-void mtb_evaluator_stats(uint64_t *out12) {
+void mtb_evaluator_stats(uint64_t *out13) {
 #ifndef MTB_CPU_ONLY
     const auto &s = mt::detail::cuda::evaluator_stats();
-    out12[0] = s.kernel_steps;
-    out12[1] = s.fused_launches;
-    out12[2] = s.fused_nodes;
-    out12[3] = s.folded_constants;
-    out12[4] = s.view_steps;
-    out12[5] = s.evaluations;
-    out12[6] = s.plan_ns;
-    out12[7] = s.execute_ns;
-    out12[8] = s.check_ns;
-    out12[9] = s.graph_captures;
-    out12[10] = s.graph_replays;
-    out12[11] = s.graph_fallbacks;
+    out13[0] = s.kernel_steps;
+    out13[1] = s.fused_launches;
+    out13[2] = s.fused_nodes;
+    out13[3] = s.folded_constants;
+    out13[4] = s.view_steps;
+    out13[5] = s.evaluations;
+    out13[6] = s.plan_ns;
+    out13[7] = s.execute_ns;
+    out13[8] = s.check_ns;
+    out13[9] = s.graph_captures;
+    out13[10] = s.graph_replays;
+    out13[11] = s.graph_fallbacks;
+    out13[12] = s.scatters_deferred;
 #else
-    for (int i = 0; i < 12; ++i) out12[i] = 0;
+    for (int i = 0; i < 13; ++i) out13[i] = 0;
 #endif
 }
 
 void mtb_graph_cache_clear(void) {
 #ifndef MTB_CPU_ONLY
     mt::detail::cuda::clear_graph_cache();
+#endif
+}
+
+int mtb_set_fusion(int on) {
+#ifndef MTB_CPU_ONLY
+    const bool previous = mt::detail::cuda::evaluator_options().fusion;
+    mt::detail::cuda::evaluator_options().fusion = on != 0;
+    return previous ? 1 : 0;
+#else
+    (void)on;
+    return 0;
 #endif
 }
 

@@ -43,6 +43,31 @@ int mtb_mlp_step_resident(void *handle, int32_t read_loss, float *loss);
 int mtb_mlp_step_host(void *handle, const float *x, const int64_t *labels, int64_t batch, float *loss);
 // Copies the current parameters (layer by layer: weight [out, in] then bias [out]) to host.
 int mtb_mlp_parameters(void *handle, float *out, int64_t capacity);
+// Gradients of the loss on the resident batch at the current parameters, without
+// an update (nn::parameter_gradients): *loss receives the loss, `out` the
+// gradients in the order of mtb_mlp_parameters.
+int mtb_mlp_gradients(void *handle, float *loss, float *out, int64_t capacity);
+// Device-time profile of the training steps (CUDA device): ms4 (may be NULL)
+// receives the milliseconds summed over the steps profiled since the last call
+// -- [0] whole steps, [1] forward + backward up to the wait for the gradient
+// exchange, [2] the exchange's exposed part, [3] the optimizer -- and the
+// profile is then switched on or off.  With one rank only [0] is measured.
+int mtb_mlp_profile(void *handle, int32_t on, double *ms4);
+// Checkpoint of the parameters under their tree paths (nn::for_each_named_parameter,
+// include/minitensor/nn/parameters/parameter_tree.hpp:179-190: "layer0.weight",
+// "layer0.bias", ...).  File format, little-endian: "MTBCKPT1", u32 count, then
+// per parameter u32 path length, path, u32 rank, i64 extents, float32 values.
+// The optimizer state is not saved: AdamW::State keeps its moments private.
+int mtb_mlp_save(void *handle, const char *path);
+// Loads a checkpoint of mtb_mlp_save onto the trainer's device, matched by path;
+// every parameter of the model must be present with its shape.
+int mtb_mlp_load(void *handle, const char *path);
+// Replaces the parameters' values with `count` host values in the order of
+// mtb_mlp_parameters (the optimizer state is kept).
+int mtb_mlp_set_parameters(void *handle, const float *values, int64_t count);
+// Replaces the trainer's Adam with SGD(lr) (include/minitensor/nn/optimizers/sgd.hpp)
+// for the following steps.
+int mtb_mlp_use_sgd(void *handle, float lr);
 int64_t mtb_mlp_parameter_count(void *handle);
 // Evaluates the (lazily initialised) parameters and optimizer state.
 int mtb_mlp_materialize(void *handle);
@@ -64,23 +89,58 @@ int mtb_chain(int device, int64_t n, int64_t m, const float *a, const float *b_s
 int mtb_gather_rows(int device, int64_t rows, int64_t cols, const float *table, int64_t n, const int64_t *index,
                     float *out);
 
+// gather(table, 0, index broadcast along the row) evaluated with mt::eval and
+// not read back: *threw = 1 when that evaluation itself raised out_of_range,
+// *materialized = 1 when the result holds storage afterwards.  Without a throw
+// the result is then read (to_vector), which raises a deferred index error
+// (MTC_ERR_OUT_OF_RANGE).  Not in the CPU-only build.
+int mtb_gather_eval_probe(int device, int64_t rows, int64_t cols, const float *table, int64_t n, const int64_t *index,
+                          int32_t *threw, int32_t *materialized);
+// How the CUDA evaluator checks gather / scatter-add indices: 0 = not at all,
+// 1 = deferred to the next evaluation or read (default), 2 = synchronously
+// before the kernel's output is installed (as MTB_INDEX_CHECKS=sync).  Returns
+// the previous mode.  Not in the CPU-only build.
+int mtb_set_index_checks(int mode);
+
 // The operations this backend adds (relu, max, argmax, log-softmax) on a
 // [rows, cols] matrix through the public API; the reductions run along `axis`
-// (0 or 1).  relu_out and log_softmax_out hold rows * cols values, max_out and
-// argmax_out the extent of the other axis.  Not in the CPU-only build: the
-// unmodified reference has none of these operations.
+// (0 or 1).  relu_out, log_softmax_out and relu_grad_out (the gradient of
+// sum(relu(x)) through relu's VJP rule; may be NULL) hold rows * cols values,
+// max_out and argmax_out the extent of the other axis.  Not in the CPU-only
+// build: the unmodified reference has none of these operations.
 int mtb_added_ops(int device, int64_t rows, int64_t cols, const float *x, int32_t axis, float *relu_out,
-                  float *max_out, int64_t *argmax_out, float *log_softmax_out);
+                  float *max_out, int64_t *argmax_out, float *log_softmax_out, float *relu_grad_out);
+
+// categorical_cross_entropy_with_logits (src/nn/loss.cpp:41-57) of a [rows, cols]
+// logits matrix whose classes run along `class_axis` (0 or 1), with Int64
+// targets (one per row for axis 1, one per column for axis 0), through the API
+// on `device`: *loss receives the mean loss, grad (rows * cols, may be NULL)
+// its gradient with respect to the logits (autograd `grad`).
+int mtb_cross_entropy(int device, int64_t rows, int64_t cols, const float *logits, int32_t class_axis,
+                      const int64_t *targets, float *loss, float *grad);
+
+// `steps` optimizer steps on one parameter vector of n values through the API on
+// `device`: kind 0 = AdamW(lr, weight_decay, beta1, beta2, eps)
+// (src/nn/optimizers/adamw.cpp:53-97), kind 1 = SGD(lr) (sgd.hpp:30-39).
+// grads holds steps * n values (step s uses grads[s * n ...]); out receives the
+// parameters after the last step.  The parameters and the optimizer state are
+// leafified after every step, as a training loop does.
+int mtb_optimizer_steps(int device, int32_t kind, int64_t n, const float *params, int32_t steps, const float *grads,
+                        float lr, float weight_decay, float beta1, float beta2, float eps, float *out);
 
 // Counters of the fusing evaluator (zeros in the CPU-only build):
 // kernel_steps, fused_launches, fused_nodes, folded_constants, view_steps, evaluations,
-// and host nanoseconds spent planning, issuing kernels and in the index-error check.
-void mtb_evaluator_stats(uint64_t *out12);
+// host nanoseconds spent planning, issuing kernels and in the index-error check,
+// graph_captures, graph_replays, graph_fallbacks, scatters_deferred.
+void mtb_evaluator_stats(uint64_t *out13);
 void mtb_evaluator_reset_stats(void);
 // Destroys every plan recorded for replay.
 void mtb_graph_cache_clear(void);
 // Turns the replay of repeated plans on or off; returns the previous setting.
 int mtb_set_graphs(int on);
+// Turns elementwise fusion (and the scatter-add deferral) on or off; returns
+// the previous setting.
+int mtb_set_fusion(int on);
 // 1 when the library has the CUDA backend, 0 for the CPU-only build.
 int mtb_has_cuda(void);
 

@@ -59,14 +59,16 @@ def assert_rel_sqrtk(actual, expected, k: int, scale=None, what: str = ""):
 
 def check_added_ops(fe, device: int, x: np.ndarray, axis: int):
     """relu, max, argmax and log-softmax through the front-end's added operations
-    against the oracle: bit for bit, log-softmax within the logsumexp bound
-    (1e-5*sqrt(K) of |lse|)."""
+    against the oracle: relu bit for bit against max(x, 0) (NaN propagated) and
+    its gradient against the step [x > 0] (NaN where x is NaN), max and argmax
+    bit for bit, log-softmax within the logsumexp bound (1e-5*sqrt(K) of |lse|)."""
     from oracle import mt_oracle as mo
 
-    relu, mx, am, lsm = fe.added_ops(device, x, axis)
-    with np.errstate(invalid="ignore"):  # -inf + inf is NaN in the composite as in the kernel
-        want_relu = ((x + np.abs(x)) * F32(0.5)).astype(F32)
-    assert_bits(relu, want_relu, f"relu device {device}")
+    relu, mx, am, lsm, grad = fe.added_ops(device, x, axis)
+    assert_bits(relu, mo.unary(mo.RELU, x), f"relu device {device}")
+    assert_bits(relu, np.where(np.isnan(x), x, np.maximum(x, F32(0))) + F32(0), f"relu vs maximum, device {device}")
+    step = np.where(np.isnan(x), F32(np.nan), (x > 0).astype(F32))
+    assert_bits(grad, step, f"relu gradient device {device}")
     assert_bits(mx, mo.reduce_max(x, [axis]), f"max axis {axis} device {device}")
     assert_bits(am, mo.reduce_argmax(x, axis), f"argmax axis {axis} device {device}")
     lse = mo.reduce_logsumexp(x, [axis], keep_dim=True)
@@ -75,11 +77,15 @@ def check_added_ops(fe, device: int, x: np.ndarray, axis: int):
 
 
 def added_ops_input(rows: int, cols: int, seed: int) -> np.ndarray:
-    """Uniform values with a tie, a NaN, a row of -inf and a -0 planted."""
+    """Uniform values with a tie, a NaN, a row of -inf, a -0, 0 and values beyond
+    FLT_MAX / 2 planted."""
     rng = np.random.default_rng(seed)
     x = rng.uniform(-10, 10, (rows, cols)).astype(F32)
     x[1, 2] = x[1, 5] = F32(50)  # a tie along axis 1
     x[3, 4] = F32(np.nan)
     x[5, :] = F32(-np.inf)
     x[2, 0] = F32(-0.0)
+    x[2, 1] = F32(0.0)
+    x[4, 3] = F32(3e38)  # x + x overflows: a composite (x + |x|) / 2 would give inf
+    x[6, 1] = F32(-3e38)
     return x

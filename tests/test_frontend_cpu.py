@@ -79,3 +79,50 @@ def test_added_operations_on_the_cpu_device(fe, axis):
     check_added_ops(fe, -1, added_ops_input(9, 13, seed=4), axis)
     with pytest.raises(ValueError):
         fe.added_ops(-1, np.zeros((2, 2), F), 2)
+
+
+def _checkpoint_names(path):
+    """Parameter paths stored in a checkpoint of MlpTrainer.save."""
+    import struct
+
+    data = path.read_bytes()
+    assert data[:8] == b"MTBCKPT1"
+    (count,) = struct.unpack_from("<I", data, 8)
+    pos, names = 12, []
+    for _ in range(count):
+        (n,) = struct.unpack_from("<I", data, pos)
+        names.append(data[pos + 4:pos + 4 + n].decode())
+        pos += 4 + n
+        (rank,) = struct.unpack_from("<I", data, pos)
+        extents = struct.unpack_from(f"<{rank}q", data, pos + 4)
+        pos += 4 + 8 * rank + 4 * int(np.prod(extents))
+    assert pos == len(data)
+    return names
+
+
+def test_checkpoint_round_trip_between_builds(fe, ref, tmp_path):
+    """Parameters saved under their tree paths (for_each_named_parameter,
+    parameter_tree.hpp:179-190) by one build load bit for bit into the other;
+    a model of another shape is refused."""
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((16, 12)).astype(F)
+    y = rng.integers(0, 5, 16).astype(np.int64)
+    a = MlpTrainer(fe, -1, 12, 16, 2, 5, seed=3, lr=1e-2)
+    a.load_batch(x.ctypes.data, y.ctypes.data, 16)
+    for _ in range(2):
+        a.step_resident()
+    path = tmp_path / "mlp.ckpt"
+    a.save(path)
+    assert _checkpoint_names(path) == ["layer0.weight", "layer0.bias", "layer1.weight", "layer1.bias",
+                                       "layer2.weight", "layer2.bias"]
+    b = MlpTrainer(ref, -1, 12, 16, 2, 5, seed=99, lr=1e-2)
+    assert not np.array_equal(b.parameters(), a.parameters())
+    b.load(path)
+    np.testing.assert_array_equal(b.parameters().view(np.uint32), a.parameters().view(np.uint32))
+    b.save(tmp_path / "again.ckpt")
+    assert (tmp_path / "again.ckpt").read_bytes() == path.read_bytes()
+    other = MlpTrainer(fe, -1, 12, 24, 2, 5, seed=3, lr=1e-2)
+    with pytest.raises(ValueError):
+        other.load(path)
+    for t in (a, b, other):
+        t.close()

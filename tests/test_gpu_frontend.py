@@ -114,6 +114,56 @@ def test_gather_index_error_through_the_api(fe, ref):
         np.testing.assert_array_equal(out, table[good])
 
 
+def test_synchronous_index_check_installs_no_storage(fe):
+    """MTB_INDEX_CHECKS=sync (here switched on at run time): an out-of-range
+    gather index throws out_of_range from the evaluation itself and the gather
+    stays unmaterialised, as the reference's evaluator guarantees
+    (evaluator_test.cpp:199-216).  In the default deferred mode the evaluation
+    installs the value and the next read raises."""
+    rng = np.random.default_rng(37)
+    table = rng.standard_normal((1000, 64)).astype(F)
+    bad = np.array([3, 999, 1000, 7], dtype=np.int64)
+    good = rng.integers(0, 1000, 4096).astype(np.int64)
+    previous = fe.set_index_checks("sync")
+    try:
+        assert fe.gather_eval_probe(0, table, bad) == (True, False)
+        np.testing.assert_array_equal(fe.gather_rows(0, table, good), table[good])
+    finally:
+        fe.set_index_checks(previous)
+    assert previous == "deferred"
+    with pytest.raises(IndexError):
+        fe.gather_eval_probe(0, table, bad)
+    np.testing.assert_array_equal(fe.gather_rows(0, table, good), table[good])
+
+
+@pytest.mark.parametrize("class_axis", [1, 0])
+def test_cross_entropy_gradient_defers_its_scatter(fe, ref, class_axis):
+    """The gradient of categorical cross entropy (src/nn/loss.cpp:41-57) sums the
+    logsumexp VJP's g * exp(x - lse) and the gather VJP's scatter-add.  The
+    evaluator adds the scatter's updates into that sum's output instead of
+    materialising a zero-filled [B, C] tensor: bit for bit the same gradient as
+    the unfused evaluation, and within 1e-5*sqrt(C) of the reference's."""
+    from helpers import assert_bits
+
+    rng = np.random.default_rng(59 + class_axis)
+    x = (rng.standard_normal((2048, 1000)) * 3).astype(F)
+    t = rng.integers(0, 1000 if class_axis == 1 else 2048, x.shape[1 - class_axis])
+    fe.reset_stats()
+    lf, gf = fe.cross_entropy(0, x, t, class_axis)
+    assert fe.stats()["scatters_deferred"] >= 1
+    previous = fe.set_fusion(False)
+    try:
+        lu, gu = fe.cross_entropy(0, x, t, class_axis)
+    finally:
+        fe.set_fusion(previous)
+    assert np.float32(lf).view(np.uint32) == np.float32(lu).view(np.uint32)
+    assert_bits(gf, gu, "deferred vs unfused scatter")
+    lc, gc = ref.cross_entropy(-1, x, t, class_axis)
+    classes = x.shape[class_axis]
+    assert abs(lf - lc) <= 1e-5 * np.sqrt(classes) * abs(lc)
+    assert_rel_sqrtk(gf, gc, classes, np.abs(gc) + np.abs(gc).max() * 1e-3, "cross-entropy gradient")
+
+
 def test_pipelined_host_steps_match_resident_steps(fe):
     """step_host copies each batch into one of two device slots on a copy
     stream and reads the loss as soon as the forward pass has computed it.
@@ -145,3 +195,32 @@ def test_added_operations_on_the_cuda_device(fe, axis, rows, cols):
     from helpers import added_ops_input, check_added_ops
 
     check_added_ops(fe, 0, added_ops_input(rows, cols, seed=5), axis)
+
+
+def test_checkpoint_between_devices(fe, ref, tmp_path):
+    """Parameters saved on the GPU load bit for bit into the reference CPU trainer
+    and back; a step from the loaded parameters gives the same loss on both
+    (within 1e-5*sqrt(K)).  Adam's moments are not part of a checkpoint: both
+    trainers start them from zero."""
+    rng = np.random.default_rng(61)
+    batch, fin, hid, cls = 256, 96, 160, 10
+    x = rng.standard_normal((batch, fin)).astype(F)
+    y = rng.integers(0, cls, batch).astype(np.int64)
+    g = MlpTrainer(fe, 0, fin, hid, 2, cls, seed=13, lr=1e-3)
+    g.load_batch(x.ctypes.data, y.ctypes.data, batch)
+    for _ in range(3):
+        g.step_resident()
+    g.save(tmp_path / "gpu.ckpt")
+    c = MlpTrainer(ref, -1, fin, hid, 2, cls, seed=77, lr=1e-3)
+    c.load(tmp_path / "gpu.ckpt")
+    np.testing.assert_array_equal(c.parameters().view(np.uint32), g.parameters().view(np.uint32))
+    c.save(tmp_path / "cpu.ckpt")
+    g2 = MlpTrainer(fe, 0, fin, hid, 2, cls, seed=78, lr=1e-3)
+    g2.load(tmp_path / "cpu.ckpt")
+    np.testing.assert_array_equal(g2.parameters().view(np.uint32), g.parameters().view(np.uint32))
+    g2.load_batch(x.ctypes.data, y.ctypes.data, batch)
+    c.load_batch(x.ctypes.data, y.ctypes.data, batch)
+    lg, lc = g2.step_resident(read_loss=True), c.step_resident(read_loss=True)
+    assert abs(lg - lc) <= 1e-5 * np.sqrt(hid) * abs(lc), (lg, lc)
+    for t in (g, g2, c):
+        t.close()

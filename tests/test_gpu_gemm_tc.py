@@ -141,14 +141,25 @@ def test_large_values_and_specials_stay_finite(cuda):
 
 
 def test_auto_uses_tensor_cores_for_large_problems(cuda):
+    """MTC_GEMM_AUTO takes the tcgen05 path at 1024 x 512 x 512 (M*N*K = 2^28,
+    the threshold) and the exact SIMT kernel below it; the path counters show
+    which kernel family ran each call."""
     rng = np.random.default_rng(6)
-    M = N = K = 512
-    abi.profile_gemm(reset=True)
+    M, N, K = 1024, 512, 512
+    tc0, simt0 = abi.gemm_path_counts()
     got, exp = _run(rng.standard_normal(M * K).astype(F), [M, K], [K, 1], rng.standard_normal(K * N).astype(F),
                     [K, N], [N, 1], algo=abi.GEMM_AUTO)
-    simt_got, _ = _run(rng.standard_normal(M * K).astype(F), [M, K], [K, 1], rng.standard_normal(K * N).astype(F),
-                       [K, N], [N, 1], algo=abi.GEMM_SIMT)
-    assert got.shape == exp.shape
+    tc1, simt1 = abi.gemm_path_counts()
+    assert (tc1 - tc0, simt1 - simt0) == (1, 0), (tc1 - tc0, simt1 - simt0)
+    _run(rng.standard_normal(M * K).astype(F), [M, K], [K, 1], rng.standard_normal(K * N).astype(F), [K, N],
+         [N, 1], algo=abi.GEMM_SIMT)
+    tc2, simt2 = abi.gemm_path_counts()
+    assert (tc2 - tc1, simt2 - simt1) == (0, 1), (tc2 - tc1, simt2 - simt1)
+    # below 2^28 multiply-adds AUTO keeps the exact SIMT kernel
+    _run(rng.standard_normal(256 * 256).astype(F), [256, 256], [256, 1], rng.standard_normal(256 * 256).astype(F),
+         [256, 256], [256, 1], algo=abi.GEMM_AUTO)
+    tc3, simt3 = abi.gemm_path_counts()
+    assert (tc3 - tc2, simt3 - simt2) == (0, 1), (tc3 - tc2, simt3 - simt2)
 
 
 def test_many_tiles_per_cluster(cuda):

@@ -6,7 +6,8 @@ that must never wait on an allocation.  For them the 3xTF32 GEMM has a variant
 whose split operands live in a fixed 32 MiB static device array.  This file
 checks, through the C ABI, that two calls in a row give the results of the
 regular entry point (mtc_matmul with MTC_GEMM_3XTF32) within the GEMM parity
-bound, and that a problem too large for the array is rejected.  It is collected
+bound, that the calls take nothing from the backend's memory pool, and that a
+problem too large for the array is rejected.  It is collected
 last so a stop-at-first-failure run has already run every other test.
 """
 import ctypes
@@ -30,8 +31,17 @@ def _desc(t, shape=None, strides=None):
     return v.desc()
 
 
+def _pool():
+    """(reserved, used) bytes of the backend's caching allocator on device 0."""
+    reserved, used = ctypes.c_uint64(0), ctypes.c_uint64(0)
+    abi.check(abi.lib().mtc_pool_stats(0, ctypes.byref(reserved), ctypes.byref(used)), "pool stats")
+    return reserved.value, used.value
+
+
 def _both(a, b, a_view=None, b_view=None):
-    """C from the static-workspace entry point and from the regular one."""
+    """C from the static-workspace entry point and from the regular one; the
+    static call must leave the pool's reserved and used bytes unchanged (it is
+    made before the regular call, whose workspace comes from the pool)."""
     import torch
 
     A = torch.from_numpy(a).cuda()
@@ -44,8 +54,12 @@ def _both(a, b, a_view=None, b_view=None):
     c_regular = torch.full((m, n), -2.0, device="cuda")
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     lib = abi.lib()
+    torch.cuda.synchronize()
+    before = _pool()
     abi.check(lib.mtc_matmul_3xtf32_static(ctypes.byref(da), ctypes.byref(db), ctypes.byref(_desc(c_static)), stream),
               "static-workspace matmul")
+    torch.cuda.synchronize()
+    assert _pool() == before, f"the static-workspace call changed the pool: {before} -> {_pool()}"
     abi.check(lib.mtc_matmul(ctypes.byref(da), ctypes.byref(db), ctypes.byref(_desc(c_regular)), abi.GEMM_3XTF32,
                              stream), "regular matmul")
     torch.cuda.synchronize()
