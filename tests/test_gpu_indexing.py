@@ -138,3 +138,37 @@ def test_row_gather_views_and_errors(cuda, idx_step, off):
     abi.gather(T, I, 0, O)
     with pytest.raises(IndexError):
         abi.check_device_errors(0)
+
+
+def _into(upd, idx_view, axis, base):
+    import ctypes
+    import torch
+
+    U = _view(upd.reshape(-1), upd.shape, abi.contiguous_strides(list(upd.shape)))
+    O = _view(base.reshape(-1).copy(), base.shape, abi.contiguous_strides(list(base.shape)))
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    abi.check(abi.lib().mtc_gather_scatter_add_into(ctypes.byref(U.desc()), ctypes.byref(idx_view.desc()), axis,
+                                                    ctypes.byref(O.desc()), stream), "scatter-add into")
+    abi.check_device_errors(0)
+    return O.storage.cpu().numpy().reshape(base.shape)
+
+
+def test_scatter_add_into_existing_values(cuda):
+    """mtc_gather_scatter_add_into adds to the target's values instead of
+    clearing it: rows (a row index broadcast along the row, 128-bit reductions)
+    and one index per row along axis 1 (the cross-entropy gradient's shape)."""
+    rng = np.random.default_rng(12)
+    base = rng.standard_normal((300, 64)).astype(F)
+    upd = rng.standard_normal((200, 64)).astype(F)
+    idx = rng.choice(300, 200, replace=False)  # distinct rows: one update per element
+    got = _into(upd, _view(idx.astype(np.int64), (200, 64), (1, 0)), 0, base)
+    want = base.copy()
+    want[idx] = (want[idx] + upd).astype(F)
+    assert_bits(got, want, "row scatter-add into")
+    logits_grad = rng.standard_normal((128, 1000)).astype(F)
+    g = rng.standard_normal((128, 1)).astype(F)
+    t = rng.integers(0, 1000, 128)
+    got = _into(g, _view(t.astype(np.int64), (128, 1), (1, 1)), 1, logits_grad)
+    want = logits_grad.copy()
+    want[np.arange(128), t] = (want[np.arange(128), t] + g[:, 0]).astype(F)
+    assert_bits(got, want, "axis-1 scatter-add into")
