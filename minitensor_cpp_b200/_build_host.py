@@ -1,8 +1,9 @@
 """Builds libminitensor_b200.so: MiniTensor's front-end with the CUDA backend.
 
 The MiniTensor sources are compiled from the reference tree (read-only) with the
-two edits a new device type needs, which no plugin can avoid, and one that lets
-the backend's new operations carry gradients:
+two edits a new device type needs, which no plugin can avoid, one that lets
+the backend's new operations carry gradients, and one that lets a checkpoint
+hold the optimizer state:
 
 1. include/minitensor/types.hpp: `DeviceType::Cuda` and the `Device::cuda(i)`
    factory (the enum has only `Cpu` and Device's constructor is private,
@@ -16,6 +17,11 @@ the backend's new operations carry gradients:
    reference's own rule sets, also calls `register_backend_vjps(registry)`
    (weak) after them, so relu (an operation this backend adds) has a VJP rule.
    The registry is a sealed function-local static (vjp_registry.cpp:36-48).
+4. include/minitensor/nn/optimizers/adamw.hpp: `AdamW::State` befriends
+   `minitensor::nn::AdamWStateAccess`, so a checkpoint can hold the step count
+   and the moments, which the class keeps private (adamw.hpp:30-53) and the
+   reference cannot persist yet (`persistence::Record` is only declared,
+   random.hpp:13-16).
 
 The edits are applied to a private working copy under the system temp
 directory (never inside this repository); the objects and the library land in
@@ -82,6 +88,10 @@ EDITS = [
      "// Optional rules of a device backend's own operations (weak: absent without one).\n"
      "[[gnu::weak]] void register_backend_vjps(VjpRegistry &registry);\n\n"
      "void VjpRegistry::register_erased"),
+    ("include/minitensor/nn/optimizers/adamw.hpp",
+     "        friend class AdamW;\n        friend State leafify_optimizer_state(State state);",
+     "        friend class AdamW;\n        friend State leafify_optimizer_state(State state);\n"
+     "        friend struct AdamWStateAccess;  // checkpoints of the backend build"),
     ("src/tensor/autograd/vjp_registry.cpp",
      "        register_reduction_vjps(result);\n        return result;",
      "        register_reduction_vjps(result);\n"

@@ -49,6 +49,24 @@
 
 namespace mt = minitensor;
 
+#ifndef MTB_CPU_ONLY
+namespace minitensor::nn {
+// Step count and moments of AdamW::State, which keeps them private; the state
+// befriends this struct in the backend build (the fourth edit of the reference).
+struct AdamWStateAccess {
+    static std::uint64_t step(const AdamW::State &s) { return s.step_; }
+    static void set_step(AdamW::State &s, std::uint64_t step) { s.step_ = step; }
+    static const Tensor &first(const AdamW::State &s, const ParameterId &id) { return s.moments_.at(id).first; }
+    static const Tensor &second(const AdamW::State &s, const ParameterId &id) { return s.moments_.at(id).second; }
+    static void set_moments(AdamW::State &s, const ParameterId &id, Tensor first, Tensor second) {
+        auto &m = s.moments_.at(id);
+        m.first = std::move(first);
+        m.second = std::move(second);
+    }
+};
+}  // namespace minitensor::nn
+#endif
+
 namespace {
 
 thread_local std::string t_error;
@@ -319,8 +337,10 @@ struct MlpTrainer {
 
     ~MlpTrainer() {
 #ifndef MTB_CPU_ONLY
-        if (copy_stream == nullptr) return;
         const int dev = static_cast<int>(device.index());
+        for (auto &ev : phase_events)
+            for (void *e : ev) (void)mtc_event_destroy(dev, e);
+        if (copy_stream == nullptr) return;
         (void)mtc_stream_synchronize(copy_stream);
         for (InputSlot &sl : slots) {
             (void)mtc_event_destroy(dev, sl.copied);
@@ -448,7 +468,12 @@ struct MlpTrainer {
         mt::nn::for_each_named_parameter(params.tree(), [&](std::string_view name, const mt::nn::ParameterId id) {
             named.emplace_back(std::string(name), id);
         });
-        bool ok = std::fwrite("MTBCKPT1", 1, 8, f) == 8;
+#ifndef MTB_CPU_ONLY
+        const bool with_state = !sgd;  // Adam's step count and moments follow the parameters
+#else
+        const bool with_state = false;
+#endif
+        bool ok = std::fwrite(with_state ? "MTBCKPT2" : "MTBCKPT1", 1, 8, f) == 8;
         const auto count = static_cast<std::uint32_t>(named.size());
         ok = ok && std::fwrite(&count, sizeof(count), 1, f) == 1;
         for (const auto &[name, id] : named) {
@@ -464,6 +489,19 @@ struct MlpTrainer {
             }
             ok = ok && std::fwrite(host.data(), sizeof(float), host.size(), f) == host.size();
         }
+#ifndef MTB_CPU_ONLY
+        if (with_state) {
+            const std::uint64_t step = mt::nn::AdamWStateAccess::step(state);
+            ok = ok && std::fwrite(&step, sizeof(step), 1, f) == 1;
+            for (const auto &[name, id] : named) {
+                for (const mt::Tensor *m : {&mt::nn::AdamWStateAccess::first(state, id),
+                                            &mt::nn::AdamWStateAccess::second(state, id)}) {
+                    const std::vector<float> host = mt::to_vector(*m);
+                    ok = ok && std::fwrite(host.data(), sizeof(float), host.size(), f) == host.size();
+                }
+            }
+        }
+#endif
         ok = std::fclose(f) == 0 && ok;
         if (!ok) throw std::runtime_error{std::string("writing ") + file + " failed"};
     }
@@ -480,8 +518,11 @@ struct MlpTrainer {
         std::unordered_map<std::string, Record> records;
         char magic[8] = {};
         std::uint32_t count = 0;
-        bool ok = std::fread(magic, 1, 8, f) == 8 && std::memcmp(magic, "MTBCKPT1", 8) == 0 &&
+        bool ok = std::fread(magic, 1, 8, f) == 8 &&
+                  (std::memcmp(magic, "MTBCKPT1", 8) == 0 || std::memcmp(magic, "MTBCKPT2", 8) == 0) &&
                   std::fread(&count, sizeof(count), 1, f) == 1;
+        const bool with_state = ok && magic[7] == '2';
+        std::vector<std::string> order_in_file;
         for (std::uint32_t k = 0; ok && k < count; ++k) {
             std::uint32_t len = 0, rank = 0;
             ok = std::fread(&len, sizeof(len), 1, f) == 1 && len < 4096;
@@ -499,7 +540,22 @@ struct MlpTrainer {
             if (!ok) break;
             r.values.resize(n);
             ok = std::fread(r.values.data(), sizeof(float), n, f) == n;
+            order_in_file.push_back(name);
             records.emplace(std::move(name), std::move(r));
+        }
+        // optimizer state (version 2): the step count, then each parameter's
+        // first and second moments in the order of the parameters above
+        std::uint64_t adam_step = 0;
+        std::unordered_map<std::string, std::pair<std::vector<float>, std::vector<float>>> moments;
+        if (ok && with_state) {
+            ok = std::fread(&adam_step, sizeof(adam_step), 1, f) == 1;
+            for (const std::string &name : order_in_file) {
+                if (!ok) break;
+                const std::size_t n = records.at(name).values.size();
+                std::vector<float> m1(n), m2(n);
+                ok = std::fread(m1.data(), sizeof(float), n, f) == n && std::fread(m2.data(), sizeof(float), n, f) == n;
+                moments.emplace(name, std::make_pair(std::move(m1), std::move(m2)));
+            }
         }
         std::fclose(f);
         if (!ok) throw std::runtime_error{std::string(file) + " is not a complete checkpoint"};
@@ -522,6 +578,19 @@ struct MlpTrainer {
                                           state.metadata};
         });
         params = mt::nn::leafify_parameter_values(std::move(params));
+#ifndef MTB_CPU_ONLY
+        if (with_state && !sgd) {
+            mt::nn::for_each_named_parameter(params.tree(), [&](std::string_view name, const mt::nn::ParameterId id) {
+                const auto &mv = moments.at(std::string(name));
+                const mt::Shape shape = params.value(id).shape();
+                mt::nn::AdamWStateAccess::set_moments(state, id,
+                                                      mt::from_data(std::span<const float>(mv.first), shape, device),
+                                                      mt::from_data(std::span<const float>(mv.second), shape, device));
+            });
+            mt::nn::AdamWStateAccess::set_step(state, adam_step);
+            state = mt::nn::leafify_optimizer_state(std::move(state));
+        }
+#endif
     }
 
     // Loss and parameter gradients on the resident batch at the current

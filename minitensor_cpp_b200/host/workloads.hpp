@@ -55,12 +55,17 @@ int mtb_mlp_gradients(void *handle, float *loss, float *out, int64_t capacity);
 int mtb_mlp_profile(void *handle, int32_t on, double *ms4);
 // Checkpoint of the parameters under their tree paths (nn::for_each_named_parameter,
 // include/minitensor/nn/parameters/parameter_tree.hpp:179-190: "layer0.weight",
-// "layer0.bias", ...).  File format, little-endian: "MTBCKPT1", u32 count, then
-// per parameter u32 path length, path, u32 rank, i64 extents, float32 values.
-// The optimizer state is not saved: AdamW::State keeps its moments private.
+// "layer0.bias", ...).  File format, little-endian: "MTBCKPT1" or "MTBCKPT2",
+// u32 count, then per parameter u32 path length, path, u32 rank, i64 extents,
+// float32 values.  Version 2 (the backend build with Adam) continues with the
+// u64 step count and each parameter's first and second moments (float32, in
+// the parameters' order); the build against the unmodified reference cannot
+// reach AdamW::State's private moments and writes version 1.
 int mtb_mlp_save(void *handle, const char *path);
 // Loads a checkpoint of mtb_mlp_save onto the trainer's device, matched by path;
-// every parameter of the model must be present with its shape.
+// every parameter of the model must be present with its shape.  A version-2
+// file also restores Adam's step count and moments (backend build), so the
+// following steps equal those of an uninterrupted run bit for bit.
 int mtb_mlp_load(void *handle, const char *path);
 // Replaces the parameters' values with `count` host values in the order of
 // mtb_mlp_parameters (the optimizer state is kept).

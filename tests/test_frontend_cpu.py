@@ -82,28 +82,34 @@ def test_added_operations_on_the_cpu_device(fe, axis):
 
 
 def _checkpoint_names(path):
-    """Parameter paths stored in a checkpoint of MlpTrainer.save."""
+    """Format version and parameter paths of a checkpoint of MlpTrainer.save
+    (version 2 carries Adam's step count and moments after the parameters)."""
     import struct
 
     data = path.read_bytes()
-    assert data[:8] == b"MTBCKPT1"
+    assert data[:7] == b"MTBCKPT" and data[7:8] in (b"1", b"2")
+    version = int(data[7:8])
     (count,) = struct.unpack_from("<I", data, 8)
-    pos, names = 12, []
+    pos, names, sizes = 12, [], []
     for _ in range(count):
         (n,) = struct.unpack_from("<I", data, pos)
         names.append(data[pos + 4:pos + 4 + n].decode())
         pos += 4 + n
         (rank,) = struct.unpack_from("<I", data, pos)
         extents = struct.unpack_from(f"<{rank}q", data, pos + 4)
-        pos += 4 + 8 * rank + 4 * int(np.prod(extents))
+        sizes.append(int(np.prod(extents)))
+        pos += 4 + 8 * rank + 4 * sizes[-1]
+    if version == 2:
+        pos += 8 + 2 * 4 * sum(sizes)
     assert pos == len(data)
-    return names
+    return version, names
 
 
 def test_checkpoint_round_trip_between_builds(fe, ref, tmp_path):
     """Parameters saved under their tree paths (for_each_named_parameter,
     parameter_tree.hpp:179-190) by one build load bit for bit into the other;
-    a model of another shape is refused."""
+    a model of another shape is refused.  The backend build adds Adam's state
+    (version 2); the build against the unmodified reference writes version 1."""
     rng = np.random.default_rng(4)
     x = rng.standard_normal((16, 12)).astype(F)
     y = rng.integers(0, 5, 16).astype(np.int64)
@@ -113,16 +119,45 @@ def test_checkpoint_round_trip_between_builds(fe, ref, tmp_path):
         a.step_resident()
     path = tmp_path / "mlp.ckpt"
     a.save(path)
-    assert _checkpoint_names(path) == ["layer0.weight", "layer0.bias", "layer1.weight", "layer1.bias",
-                                       "layer2.weight", "layer2.bias"]
+    assert _checkpoint_names(path) == (2, ["layer0.weight", "layer0.bias", "layer1.weight", "layer1.bias",
+                                           "layer2.weight", "layer2.bias"])
     b = MlpTrainer(ref, -1, 12, 16, 2, 5, seed=99, lr=1e-2)
     assert not np.array_equal(b.parameters(), a.parameters())
     b.load(path)
     np.testing.assert_array_equal(b.parameters().view(np.uint32), a.parameters().view(np.uint32))
     b.save(tmp_path / "again.ckpt")
-    assert (tmp_path / "again.ckpt").read_bytes() == path.read_bytes()
+    assert _checkpoint_names(tmp_path / "again.ckpt")[0] == 1
+    c = MlpTrainer(fe, -1, 12, 16, 2, 5, seed=98, lr=1e-2)
+    c.load(tmp_path / "again.ckpt")
+    np.testing.assert_array_equal(c.parameters().view(np.uint32), a.parameters().view(np.uint32))
     other = MlpTrainer(fe, -1, 12, 24, 2, 5, seed=3, lr=1e-2)
     with pytest.raises(ValueError):
         other.load(path)
-    for t in (a, b, other):
+    for t in (a, b, c, other):
+        t.close()
+
+
+def test_resume_from_checkpoint_is_bit_identical(fe, tmp_path):
+    """With Adam's step count and moments in the checkpoint (version 2), three
+    steps, a save, a load into a fresh trainer and two more steps give the
+    parameters of five uninterrupted steps bit for bit."""
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((16, 12)).astype(F)
+    y = rng.integers(0, 5, 16).astype(np.int64)
+    full = MlpTrainer(fe, -1, 12, 16, 2, 5, seed=3, lr=1e-2)
+    part = MlpTrainer(fe, -1, 12, 16, 2, 5, seed=3, lr=1e-2)
+    for t in (full, part):
+        t.load_batch(x.ctypes.data, y.ctypes.data, 16)
+    for _ in range(5):
+        full.step_resident()
+    for _ in range(3):
+        part.step_resident()
+    part.save(tmp_path / "step3.ckpt")
+    resumed = MlpTrainer(fe, -1, 12, 16, 2, 5, seed=7, lr=1e-2)
+    resumed.load(tmp_path / "step3.ckpt")
+    resumed.load_batch(x.ctypes.data, y.ctypes.data, 16)
+    for _ in range(2):
+        resumed.step_resident()
+    np.testing.assert_array_equal(resumed.parameters().view(np.uint32), full.parameters().view(np.uint32))
+    for t in (full, part, resumed):
         t.close()

@@ -200,8 +200,8 @@ def test_added_operations_on_the_cuda_device(fe, axis, rows, cols):
 def test_checkpoint_between_devices(fe, ref, tmp_path):
     """Parameters saved on the GPU load bit for bit into the reference CPU trainer
     and back; a step from the loaded parameters gives the same loss on both
-    (within 1e-5*sqrt(K)).  Adam's moments are not part of a checkpoint: both
-    trainers start them from zero."""
+    (within 1e-5*sqrt(K)).  The reference build cannot hold Adam's moments
+    (version-1 checkpoint), so here both trainers start them from zero."""
     rng = np.random.default_rng(61)
     batch, fin, hid, cls = 256, 96, 160, 10
     x = rng.standard_normal((batch, fin)).astype(F)
@@ -223,4 +223,31 @@ def test_checkpoint_between_devices(fe, ref, tmp_path):
     lg, lc = g2.step_resident(read_loss=True), c.step_resident(read_loss=True)
     assert abs(lg - lc) <= 1e-5 * np.sqrt(hid) * abs(lc), (lg, lc)
     for t in (g, g2, c):
+        t.close()
+
+
+def test_resume_from_checkpoint_on_cuda(fe, tmp_path):
+    """Adam's step count and moments travel with the parameters (version-2
+    checkpoint): three steps, save, load into a fresh GPU trainer, two more
+    steps equal five uninterrupted steps bit for bit."""
+    rng = np.random.default_rng(67)
+    batch, fin, hid, cls = 256, 96, 160, 10
+    x = rng.standard_normal((batch, fin)).astype(F)
+    y = rng.integers(0, cls, batch).astype(np.int64)
+    full = MlpTrainer(fe, 0, fin, hid, 2, cls, seed=21, lr=1e-3)
+    part = MlpTrainer(fe, 0, fin, hid, 2, cls, seed=21, lr=1e-3)
+    for t in (full, part):
+        t.load_batch(x.ctypes.data, y.ctypes.data, batch)
+    for _ in range(5):
+        full.step_resident()
+    for _ in range(3):
+        part.step_resident()
+    part.save(tmp_path / "step3.ckpt")
+    resumed = MlpTrainer(fe, 0, fin, hid, 2, cls, seed=22, lr=1e-3)
+    resumed.load(tmp_path / "step3.ckpt")
+    resumed.load_batch(x.ctypes.data, y.ctypes.data, batch)
+    for _ in range(2):
+        resumed.step_resident()
+    np.testing.assert_array_equal(resumed.parameters().view(np.uint32), full.parameters().view(np.uint32))
+    for t in (full, part, resumed):
         t.close()
