@@ -55,16 +55,20 @@ def config(n_gpus: int) -> dict:
         "flop_per_step": flops_per_sample() * GLOBAL_BATCH,
         "parallelism": f"dp{n_gpus}",
         "l2": "inputs and weights larger than the 126 MB L2 (no flush needed)",
+        "batches": f"{BATCHES} distinct seeded batches per rank, resident; step s uses batch s mod {BATCHES}",
     }
 
 
 # ---------------------------------------------------------------- helpers --
 
-def make_batch(rank: int, batch: int):
+BATCHES = 4  # distinct seeded batches per rank, cycled step by step
+
+
+def make_batch(rank: int, batch: int, index: int = 0):
     import numpy as np
     import torch
 
-    rng = np.random.default_rng([SEED, rank])
+    rng = np.random.default_rng([SEED, rank, index])
     x = torch.empty((batch, WIDTHS[0]), dtype=torch.float32, pin_memory=True)
     y = torch.empty((batch,), dtype=torch.int64, pin_memory=True)
     x.numpy()[:] = rng.standard_normal((batch, WIDTHS[0]), dtype=np.float32)
@@ -162,8 +166,9 @@ def read_traffic(name: str):
     return None
 
 
-def cpu_reference_sample(batch: int, steps: int) -> dict:
-    """The reference CPU backend (oracle/_ref) training the same model on one core."""
+def cpu_reference_sample(batch: int, steps: int, warm: int = 0) -> dict:
+    """The reference CPU backend (oracle/_ref) training the same model on one core:
+    `warm` untimed steps, then `steps` timed ones."""
     import numpy as np
 
     from minitensor_cpp_b200.frontend import Frontend, MlpTrainer
@@ -176,6 +181,8 @@ def cpu_reference_sample(batch: int, steps: int) -> dict:
     x = rng.standard_normal((batch, WIDTHS[0]), dtype=np.float32)
     y = rng.integers(0, WIDTHS[-1], batch).astype(np.int64)
     tr.load_batch(x.ctypes.data, y.ctypes.data, batch)
+    for _ in range(warm):
+        tr.step_resident(read_loss=True)
     t0 = time.perf_counter()
     for _ in range(steps):
         tr.step_resident(read_loss=True)
@@ -185,8 +192,8 @@ def cpu_reference_sample(batch: int, steps: int) -> dict:
 
 
 def _worker(args):
-    batch, steps = args
-    return cpu_reference_sample(batch, steps)
+    batch, steps, warm = args
+    return cpu_reference_sample(batch, steps, warm)
 
 
 # ------------------------------------------------------- single-kernel cases --
@@ -599,8 +606,12 @@ def run_ours(args) -> None:
         abi.check(abi.lib().mtc_comm_init(local, rank, world, uid, 128, ctypes.byref(comm)), "nccl init")
         tr.set_comm(comm, world)
 
-    x, y = make_batch(rank, batch)
-    tr.load_batch(x.data_ptr(), y.data_ptr(), batch)
+    # BATCHES distinct batches, resident in the trainer's slots: step s of every
+    # loop uses batch s mod BATCHES (the benchmark draws fresh inputs each step)
+    host = [make_batch(rank, batch, k) for k in range(BATCHES)]
+    for k, (xk, yk) in enumerate(host):
+        tr.load_batch_slot(k, xk.data_ptr(), yk.data_ptr(), batch)
+    tr.use_slot(0)
     stream = torch.cuda.ExternalStream(tr.stream(), device=torch.device("cuda", local))
 
     def barrier():
@@ -614,7 +625,8 @@ def run_ours(args) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
+    for w in range(args.warmup):
+        tr.use_slot(w % BATCHES)
         tr.step_resident(read_loss=False)
     tr.synchronize()
 
@@ -629,7 +641,8 @@ def run_ours(args) -> None:
     with ClockSampler(local) as clocks:
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
-        for _ in range(args.steps):
+        for k in range(args.steps):
+            tr.use_slot(k % BATCHES)
             tr.step_resident(read_loss=False)
         stop.record(stream)
         tr.synchronize()
@@ -653,7 +666,7 @@ def run_ours(args) -> None:
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
     # one untimed host step first: it sets up the input pipeline (copy stream,
     # events, the two device slots of a batch), like the warm-up steps above
-    tr.step_host(x.data_ptr(), y.data_ptr(), batch)
+    tr.step_host(host[0][0].data_ptr(), host[0][1].data_ptr(), batch)
     tr.synchronize()
     barrier()
     torch.cuda.synchronize()
@@ -661,8 +674,9 @@ def run_ours(args) -> None:
     e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
     loss = 0.0
-    for _ in range(e2e_steps):
-        loss = tr.step_host(x.data_ptr(), y.data_ptr(), batch)
+    for k in range(e2e_steps):
+        xk, yk = host[k % BATCHES]
+        loss = tr.step_host(xk.data_ptr(), yk.data_ptr(), batch)
     e_stop.record(stream)
     tr.synchronize()
     e2e_ms = max_over_ranks(e_start.elapsed_time(e_stop))
@@ -727,7 +741,7 @@ def run_ours(args) -> None:
         "tflops": flops_per_sample() * GLOBAL_BATCH * args.steps / (ms * 1e-3) / 1e12,
         "e2e": {"value": GLOBAL_BATCH * e2e_steps / (e2e_ms * 1e-3), "unit": "samples/s",
                 "steps": e2e_steps, "wall_s": wall_e2e, "last_loss": loss,
-                "h2d_bytes_per_step": world * (x.numel() * 4 + y.numel() * 8),
+                "h2d_bytes_per_step": world * (host[0][0].numel() * 4 + host[0][1].numel() * 8),
                 "d2h_bytes_per_step": world * 4},
         "gpu_launches": launches,
         "phases_ms_per_step": {k: round(v, 3) for k, v in phases.items()},
@@ -759,17 +773,22 @@ def run_reference(args) -> None:
         avail_gb = 64.0
     # each single-threaded reference process holds the 151M-parameter model,
     # its Adam moments and the step's intermediates (~10 GB peak)
-    workers = max(1, min(cores, int(avail_gb // 12), 16))
+    workers = max(1, min(cores, int(avail_gb // 12), 16, args.steps))
     batch = args.cpu_batch
-    steps = 1  # one ~30-60 s training step per worker bounds the whole run to minutes
+    # the --steps timed steps (and one untimed step per worker when --warmup is
+    # given) are shared out over the workers: a step at batch 4 takes about 12 s,
+    # so the whole run stays within a couple of minutes
+    shares = [args.steps // workers + (1 if k < args.steps % workers else 0) for k in range(workers)]
+    warm = 1 if args.warmup > 0 else 0
     ctx = mp.get_context("spawn")
     t0 = time.perf_counter()
     with ctx.Pool(workers) as pool:
-        results = pool.map(_worker, [(batch, steps)] * workers)
+        results = pool.map(_worker, [(batch, n, warm) for n in shares])
     wall = time.perf_counter() - t0
     samples = sum(r["samples"] for r in results)
     busiest = max(r["seconds"] for r in results)
     value = samples / busiest
+    steps = sum(shares)
     line = {
         "metric": METRIC,
         "value": value,
@@ -777,8 +796,7 @@ def run_reference(args) -> None:
         "impl": "reference",
         "n_gpus": args.gpus,
         "steps": steps,
-        "steps_requested": args.steps,
-        "warmup": 0,
+        "warmup": warm * workers,
         "higher_is_better": True,
         "scaling": "strong",
         "dtype": "f32",
@@ -786,8 +804,10 @@ def run_reference(args) -> None:
         "config": config(args.gpus),
         "cpu_baseline": {"value": value, "unit": "samples/s", "cores": workers, "host_cores": cores,
                          "kind": "reference",
-                         "sample": f"{workers} single-threaded reference processes x {steps} training step at "
-                                   f"batch {batch} each (the reference is single-threaded); wall {wall:.1f} s"},
+                         "sample": f"{steps} training steps at batch {batch} shared over {workers} single-threaded "
+                                   f"reference processes (the reference is single-threaded), each after "
+                                   f"{warm} untimed step; samples / the slowest process's timed seconds; "
+                                   f"wall {wall:.1f} s"},
         "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -45,6 +45,8 @@ class Frontend:
             "mtb_mlp_set_comm": ([vp, vp, i32], ctypes.c_int),
             "mtb_mlp_set_host_allreduce": ([vp, HOST_ALLREDUCE, i32], ctypes.c_int),
             "mtb_mlp_load_batch": ([vp, vp, vp, i64], ctypes.c_int),
+            "mtb_mlp_load_batch_slot": ([vp, i32, vp, vp, i64], ctypes.c_int),
+            "mtb_mlp_use_slot": ([vp, i32], ctypes.c_int),
             "mtb_mlp_step_resident": ([vp, i32, P(f32)], ctypes.c_int),
             "mtb_mlp_step_host": ([vp, vp, vp, i64, P(f32)], ctypes.c_int),
             "mtb_mlp_parameters": ([vp, P(f32), i64], ctypes.c_int),
@@ -257,6 +259,14 @@ class MlpTrainer:
 
     def load_batch(self, x_ptr: int, y_ptr: int, batch: int):
         self.fe._check(self.fe.lib.mtb_mlp_load_batch(self.h, x_ptr, y_ptr, batch), "mlp_load_batch")
+
+    def load_batch_slot(self, slot: int, x_ptr: int, y_ptr: int, batch: int):
+        """Uploads a batch into resident slot `slot` (not made current)."""
+        self.fe._check(self.fe.lib.mtb_mlp_load_batch_slot(self.h, slot, x_ptr, y_ptr, batch), "mlp_load_batch_slot")
+
+    def use_slot(self, slot: int):
+        """Makes resident slot `slot` the batch of the following steps (no copy)."""
+        self.fe._check(self.fe.lib.mtb_mlp_use_slot(self.h, slot), "mlp_use_slot")
 
     def step_resident(self, read_loss: bool = False) -> float:
         loss = ctypes.c_float(0.0)

@@ -288,6 +288,9 @@ struct MlpTrainer {
     int world = 1;
     std::optional<mt::Tensor> x_resident;
     std::optional<mt::Tensor> y_resident;
+    // further resident batches (mtb_mlp_load_batch_slot); mtb_mlp_use_slot makes
+    // one of them the resident batch without a copy
+    std::vector<std::pair<mt::Tensor, mt::Tensor>> batch_slots;
     std::optional<mt::nn::SGD> sgd;  // set: SGD replaces Adam
 #ifndef MTB_CPU_ONLY
     // Input pipeline of step_host on a CUDA device: two device slots for a
@@ -818,6 +821,30 @@ int mtb_mlp_load_batch(void *handle, const float *x, const int64_t *labels, int6
                                       mt::Shape{batch, in}, t->device);
         t->y_resident = mt::from_data(std::span<const std::int64_t>(labels, static_cast<std::size_t>(batch)),
                                       mt::Shape{batch}, t->device);
+    });
+}
+
+int mtb_mlp_load_batch_slot(void *handle, int32_t slot, const float *x, const int64_t *labels, int64_t batch) {
+    return guarded([&] {
+        auto *t = static_cast<MlpTrainer *>(handle);
+        if (slot < 0 || slot > 64) throw std::out_of_range{"batch slot outside 0..64"};
+        const mt::Extent in = t->params.parameters().get(t->order.front()).value.shape()[1];
+        mt::Tensor xt = mt::from_data(std::span<const float>(x, static_cast<std::size_t>(batch * in)),
+                                      mt::Shape{batch, in}, t->device);
+        mt::Tensor yt = mt::from_data(std::span<const std::int64_t>(labels, static_cast<std::size_t>(batch)),
+                                      mt::Shape{batch}, t->device);
+        mt::eval({xt, yt});
+        while (static_cast<int32_t>(t->batch_slots.size()) <= slot) t->batch_slots.emplace_back(xt, yt);
+        t->batch_slots[static_cast<std::size_t>(slot)] = {std::move(xt), std::move(yt)};
+    });
+}
+
+int mtb_mlp_use_slot(void *handle, int32_t slot) {
+    return guarded([&] {
+        auto *t = static_cast<MlpTrainer *>(handle);
+        if (slot < 0 || slot >= static_cast<int32_t>(t->batch_slots.size())) throw std::out_of_range{"no such batch slot"};
+        t->x_resident = t->batch_slots[static_cast<std::size_t>(slot)].first;
+        t->y_resident = t->batch_slots[static_cast<std::size_t>(slot)].second;
     });
 }
 

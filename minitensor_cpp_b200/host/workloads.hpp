@@ -36,6 +36,11 @@ int mtb_mlp_set_comm(void *handle, void *comm, int32_t world);
 int mtb_mlp_set_host_allreduce(void *handle, int (*sum_in_place)(void *, size_t), int32_t world);
 // Upload one batch (host memory; copied to the device) that mtb_mlp_step_resident reuses.
 int mtb_mlp_load_batch(void *handle, const float *x, const int64_t *labels, int64_t batch);
+// Upload a batch into resident slot `slot` (0..64) without making it current;
+// mtb_mlp_use_slot makes a slot the resident batch (no copy), so a timed loop
+// can cycle through several device-resident batches.
+int mtb_mlp_load_batch_slot(void *handle, int32_t slot, const float *x, const int64_t *labels, int64_t batch);
+int mtb_mlp_use_slot(void *handle, int32_t slot);
 // One training step on the resident batch; *loss receives the step's loss when read_loss != 0.
 int mtb_mlp_step_resident(void *handle, int32_t read_loss, float *loss);
 // One end-to-end training step from host buffers: the batch is copied host -> device,
