@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "gemm.cuh"
 
 namespace mtc {
 namespace {
@@ -75,11 +76,20 @@ __global__ void k_scale(float *p, long long n, float s) {
     } while (0)
 
 // Grouped in-place sum of the buffers over the ranks on stream `s`, then x scale.
+// A scale of 1 / ranks with a power-of-two rank count is folded into the
+// reduction as ncclAvg (NCCL multiplies each contribution by 1 / ranks before
+// summing floats; with a power of two that multiplication is exact outside
+// the subnormal range, so the result equals the sum scaled afterwards bit for
+// bit) and no scale kernel runs.
 int allreduce_on(Comm *c, void *const *buffers, const size_t *counts, int32_t n, float scale, cudaStream_t s) {
+    const bool pow2 = c->n_ranks > 1 && (c->n_ranks & (c->n_ranks - 1)) == 0;
+    const bool avg = pow2 && scale == 1.0f / static_cast<float>(c->n_ranks);
+    if (avg) scale = 1.0f;
     MTC_NCCL_TRY(nccl().group_start());
     for (int i = 0; i < n; ++i) {
         if (counts[i] == 0) continue;
-        ncclResult_t r = nccl().all_reduce(buffers[i], buffers[i], counts[i], ncclFloat32, ncclSum, c->comm, s);
+        ncclResult_t r = nccl().all_reduce(buffers[i], buffers[i], counts[i], ncclFloat32, avg ? ncclAvg : ncclSum,
+                                           c->comm, s);
         if (r != ncclSuccess) {
             nccl().group_end();
             return fail(MTC_ERR_RUNTIME, "ncclAllReduce failed: %s", nccl().error_string(r));
@@ -136,6 +146,7 @@ int mtc_comm_init(int device, int rank, int n_ranks, const void *id, size_t id_b
         return fail(MTC_ERR_RUNTIME, "ncclCommInitRank failed: %s", nccl().error_string(r));
     }
     *comm = c;
+    gemm_note_collectives();
     return MTC_OK;
 }
 

@@ -329,8 +329,9 @@ __global__ void __launch_bounds__(256) k_scatter_rows2(const RowArgs a) {
 // result is the reference's bit for bit whatever the values.  Steps:
 //   count  : counts[t] = number of rows i with idx[i] = t, and rank[i] = the
 //            slot row i took (returning atomics on the L2-resident counts)
-//   scan   : starts = exclusive prefix sum of counts, in place (two levels)
-//   fill   : perm[starts[idx[i]] + rank[i]] = i (plain stores)
+//   scan   : block-local exclusive prefix sums of the counts in place, and
+//            the scanned block totals; start(t) = starts[t] + sums[t / kScanBlock]
+//   fill   : perm[start(idx[i]) + rank[i]] = i (plain stores)
 //   sort   : each segment sorted ascending (in-thread up to 32 rows; a CTA
 //            bitonic sort in shared memory up to kLongSegment rows)
 //   sum    : every target row written once (zeros for rows no index names),
@@ -344,6 +345,8 @@ constexpr int kLongSegment = 4096;                  // longest segment sorted in
 // counts[j] += 1 for every update row i with idx[i] = j; rank[i] = the slot i
 // took within its target's segment (a returning atomic on the L2-resident
 // counts), -1 for an index outside the target.  rank may be null (no slots).
+// (Counting in slices of the targets, so that each launch's counts stay in
+// L2, measured no faster at 2^24 rows: the returning atomics bound it.)
 __global__ void __launch_bounds__(256) k_seg_count(const RowArgs a, int *counts, int *rank) {
     for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.rows;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -390,59 +393,76 @@ __global__ void __launch_bounds__(256) k_scan_blocks(const int *in, int *out, lo
     if (threadIdx.x == 255) sums[blockIdx.x] = warp_off + inc;
 }
 
-// Exclusive scan of up to 256 * 64 block totals in one CTA, in place.
-__global__ void __launch_bounds__(256) k_scan_totals(int *sums, int n) {
-    __shared__ int warp_tot[8];
-    constexpr int kItems = 64;
-    const int base = threadIdx.x * kItems;
-    int run = 0;
-    for (int q = 0; q < kItems; ++q)
-        if (base + q < n) run += sums[base + q];
+// Exclusive scan of the n block totals in one CTA, in place: 4 consecutive
+// totals a thread (16-byte coalesced loads), 4096 a pass, carried across passes.
+// A target's start is then starts[t] + sums[t / kScanBlock] (seg_start).
+__global__ void __launch_bounds__(1024) k_scan_totals(int *sums, int n) {
+    __shared__ int warp_tot[32];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int inc = run;
+    int carry = 0;
+    for (int base = 0; base < n; base += 1024 * 4) {
+        const int i0 = base + static_cast<int>(threadIdx.x) * 4;
+        int v[4];
+        int run = 0;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += y;
-    }
-    if (lane == 31) warp_tot[warp] = inc;
-    __syncthreads();
-    int off = 0;
-    for (int w = 0; w < warp; ++w) off += warp_tot[w];
-    off += inc - run;
-    for (int q = 0; q < kItems; ++q) {
-        if (base + q < n) {
-            const int t = sums[base + q];
-            sums[base + q] = off;
-            off += t;
+        for (int q = 0; q < 4; ++q) {
+            const int t = i0 + q < n ? sums[i0 + q] : 0;
+            v[q] = run;
+            run += t;
         }
+        int inc = run;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += y;
+        }
+        if (lane == 31) warp_tot[warp] = inc;
+        __syncthreads();
+        if (warp == 0) {
+            int x = warp_tot[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
+            }
+            warp_tot[lane] = x;  // inclusive over the warps
+        }
+        __syncthreads();
+        const int excl = carry + (warp > 0 ? warp_tot[warp - 1] : 0) + inc - run;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (i0 + q < n) sums[i0 + q] = v[q] + excl;
+        carry += warp_tot[31];
+        __syncthreads();  // warp_tot is rewritten by the next pass
     }
 }
 
-__global__ void __launch_bounds__(256) k_scan_add(int *out, long long len, const int *sums) {
-    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i < len) out[i] += sums[i / kScanBlock];
+// Start of target t's segment in perm (t = targets gives the end of the last).
+__device__ __forceinline__ int seg_start(const int *starts, const int *sums, long long t) {
+    return __ldg(starts + t) + __ldg(sums + t / kScanBlock);
 }
 
-// perm[starts[j] + rank[i]] = i: every update row in the slot the count pass
-// gave it (no atomics; the order within a segment is fixed by the sort).
-__global__ void __launch_bounds__(256) k_seg_fill(const RowArgs a, const int *rank, const int *starts, int *perm) {
+// perm[starts[j] + rank[i]] = i for the update rows whose target j lies in
+// [lo, hi): every update row in the slot the count pass gave it (no atomics;
+// the order within a segment is fixed by the sort).  Run over slices of the
+// targets, the randomly addressed parts of starts and perm stay in L2.
+__global__ void __launch_bounds__(256) k_seg_fill(const RowArgs a, const int *rank, const int *starts,
+                                                  const int *sums, int *perm, long long lo, long long hi) {
     for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < a.rows;
          i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int r = rank[i];
-        if (r < 0) continue;
         const long long j = __ldg(a.idx + a.idx_off + i * a.idx_rs);
-        perm[starts[j] + r] = static_cast<int>(i);
+        if (j < lo || j >= hi) continue;  // also every index outside the target
+        perm[seg_start(starts, sums, j) + __ldcs(rank + i)] = static_cast<int>(i);
     }
 }
 
 // Sorts the segments of up to 32 rows in place, one thread per target; longer
 // segments (up to kLongSegment) go to a list for k_seg_sort_long.
-__global__ void __launch_bounds__(256) k_seg_sort(const int *starts, int *perm, long long targets, int *long_list,
-                                                  int *long_count, int long_capacity) {
+__global__ void __launch_bounds__(256) k_seg_sort(const int *starts, const int *sums, int *perm, long long targets,
+                                                  int *long_list, int *long_count, int long_capacity) {
     for (long long t = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; t < targets;
          t += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int s = starts[t], e = starts[t + 1];
+        const int s = seg_start(starts, sums, t), e = seg_start(starts, sums, t + 1);
         const int len = e - s;
         if (len < 2) continue;
         if (len > 32) {
@@ -465,13 +485,13 @@ __global__ void __launch_bounds__(256) k_seg_sort(const int *starts, int *perm, 
 
 // Bitonic sort of one long segment per CTA iteration in shared memory (padded
 // with INT_MAX to a power of two); segments above kLongSegment stay in fill order.
-__global__ void __launch_bounds__(256) k_seg_sort_long(const int *starts, int *perm, const int *long_list,
-                                                       const int *long_count, int long_capacity) {
+__global__ void __launch_bounds__(256) k_seg_sort_long(const int *starts, const int *sums, int *perm,
+                                                       const int *long_list, const int *long_count, int long_capacity) {
     __shared__ int keys[kLongSegment];
     const int count = min(*long_count, long_capacity);
     for (int e = blockIdx.x; e < count; e += gridDim.x) {
         const int t = long_list[e];
-        const int s = starts[t], len = starts[t + 1] - s;
+        const int s = seg_start(starts, sums, t), len = seg_start(starts, sums, t + 1) - s;
         if (len > kLongSegment) continue;
         int n2 = 64;
         while (n2 < len) n2 <<= 1;
@@ -498,28 +518,6 @@ __global__ void __launch_bounds__(256) k_seg_sort_long(const int *starts, int *p
     }
 }
 
-// out[t] = +0 + upd[perm[s]] + upd[perm[s + 1]] + ... for every target row t.
-// A warp owns 32 consecutive target rows: lane l holds the segment bounds of
-// row t0 + l and its first three update indices (coalesced loads, perm being
-// ordered by target; the next chunk's are loaded while this one is summed).
-// The half-warps then sum two rows at a time, four rows each per burst, with
-// all of a row's first three update rows in flight together; only rows with
-// four or more updates (about 2 % for uniform indices) loop for the rest.
-struct SegHead {
-    int s, len, p0, p1, p2;
-};
-
-__device__ __forceinline__ SegHead seg_head(const int *starts, const int *perm, long long t, long long targets) {
-    SegHead h{0, 0, 0, 0, 0};
-    if (t >= targets) return h;
-    h.s = __ldg(starts + t);
-    h.len = __ldg(starts + t + 1) - h.s;
-    if (h.len > 0) h.p0 = __ldg(perm + h.s);
-    if (h.len > 1) h.p1 = __ldg(perm + h.s + 1);
-    if (h.len > 2) h.p2 = __ldg(perm + h.s + 2);
-    return h;
-}
-
 __device__ __forceinline__ void add4(float4 &acc, const uint4 w) {
     acc.x = __fadd_rn(acc.x, __uint_as_float(w.x));
     acc.y = __fadd_rn(acc.y, __uint_as_float(w.y));
@@ -527,52 +525,63 @@ __device__ __forceinline__ void add4(float4 &acc, const uint4 w) {
     acc.w = __fadd_rn(acc.w, __uint_as_float(w.w));
 }
 
-template <int kSumRowsPerHalf>
-__global__ void __launch_bounds__(256) k_seg_sum(const RowArgs a, const int *starts, const int *perm) {
-    // kSumRowsPerHalf = 4 (measured at 2^24 rows: 2.77 ms, against 2.81 / 3.17 ms
-    // for 1 / 2 and 4.1 ms for a variant staging the rows in shared memory by cp.async)
-    const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
-    const long long warp = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const long long warps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+// out[t] = +0 + upd[perm[s]] + upd[perm[s + 1]] + ... for every target row t,
+// walking the sorted update list: a half-warp owns kWalkTargets consecutive
+// target rows and consumes their update rows in list order, four rows in
+// flight per lane at a time whatever the segment lengths; a row is stored as
+// soon as its segment ends (zeros for rows no index names).  Measured at 2^24
+// rows of 64 floats: 1.56 ms (5.6 TB/s), against 1.88 ms for a warp per 32
+// target rows with each row's first three updates prefetched (two to four rows
+// in flight per lane), and 1.67 ms when the walk also sorted each group of up
+// to 16 updates in registers (a bitonic network over the half-warp) in place of
+// the segment sort.
+constexpr int kWalkTargets = 8;  // target rows per half-warp step (at most 15)
+
+__global__ void __launch_bounds__(256) k_seg_walk(const RowArgs a, const int *starts, const int *sums, const int *perm) {
+    const int hl = threadIdx.x & 15;
+    const unsigned hmask = 0xffffu << (threadIdx.x & 16);
+    const long long half = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
+    const long long halves = (static_cast<long long>(gridDim.x) * blockDim.x) >> 4;
     const long long targets = a.extent;
-    long long t0 = warp * 32;
-    SegHead head = seg_head(starts, perm, t0 + lane, targets);
-    for (; t0 < targets; t0 += warps * 32) {
-        const SegHead next = seg_head(starts, perm, t0 + warps * 32 + lane, targets);  // in flight meanwhile
-        const int rows = static_cast<int>(targets - t0 < 32 ? targets - t0 : 32);  // warp-uniform
-        for (int q0 = 0; q0 < rows; q0 += 2 * kSumRowsPerHalf) {
-            SegHead h[kSumRowsPerHalf];
+    for (long long t0 = half * kWalkTargets; t0 < targets; t0 += halves * kWalkTargets) {
+        const int g = static_cast<int>(targets - t0 < kWalkTargets ? targets - t0 : kWalkTargets);
+        // lane l: the start of target t0 + l; lane g: the end of target t0 + g - 1
+        const int sb = hl <= g ? seg_start(starts, sums, t0 + hl) : 0;
+        const int e_beg = __shfl_sync(hmask, sb, 0, 16);
+        const int e_end = __shfl_sync(hmask, sb, g, 16);
+        for (int c0 = 0; c0 < a.row_vec; c0 += 16) {
+            const int c = c0 + hl;
+            const bool col = c < a.row_vec;
+            int q = 0;                                        // current target of the group
+            int seg_end = __shfl_sync(hmask, sb, 1, 16);      // end of target t0 + q
+            float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            for (int e = e_beg; e < e_end; e += 4) {
+                const int nb = e_end - e < 4 ? e_end - e : 4;  // uniform in the half-warp
+                const int pl = hl < nb ? __ldg(perm + e + hl) : 0;
+                int p[4];
+                uint4 v[4];
 #pragma unroll
-            for (int u = 0; u < kSumRowsPerHalf; ++u) {
-                const int q = q0 + 2 * u + half;
-                const int qs = q < 32 ? q : 31;
-                h[u].s = __shfl_sync(0xffffffffu, head.s, qs);
-                h[u].len = q < rows ? __shfl_sync(0xffffffffu, head.len, qs) : -1;
-                h[u].p0 = __shfl_sync(0xffffffffu, head.p0, qs);
-                h[u].p1 = __shfl_sync(0xffffffffu, head.p1, qs);
-                h[u].p2 = __shfl_sync(0xffffffffu, head.p2, qs);
+                for (int u = 0; u < 4; ++u) p[u] = __shfl_sync(hmask, pl, u, 16);
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (u < nb && col) v[u] = __ldg(row_in(a, p[u], c));
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    if (u >= nb) break;
+                    while (e + u >= seg_end) {  // finish the targets that end before this entry
+                        if (col) __stcs(reinterpret_cast<float4 *>(row_out(a, t0 + q, c)), acc);
+                        acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                        ++q;
+                        seg_end = __shfl_sync(hmask, sb, q + 1, 16);
+                    }
+                    if (col) add4(acc, v[u]);
+                }
             }
-            for (int c = hl; c < a.row_vec; c += 16) {
-                uint4 v0[kSumRowsPerHalf], v1[kSumRowsPerHalf], v2[kSumRowsPerHalf];
-#pragma unroll
-                for (int u = 0; u < kSumRowsPerHalf; ++u) {
-                    if (h[u].len > 0) v0[u] = __ldg(row_in(a, h[u].p0, c));
-                    if (h[u].len > 1) v1[u] = __ldg(row_in(a, h[u].p1, c));
-                    if (h[u].len > 2) v2[u] = __ldg(row_in(a, h[u].p2, c));
-                }
-#pragma unroll
-                for (int u = 0; u < kSumRowsPerHalf; ++u) {
-                    if (h[u].len < 0) continue;  // beyond the targets
-                    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-                    if (h[u].len > 0) add4(acc, v0[u]);
-                    if (h[u].len > 1) add4(acc, v1[u]);
-                    if (h[u].len > 2) add4(acc, v2[u]);
-                    for (int k = h[u].s + 3; k < h[u].s + h[u].len; ++k) add4(acc, __ldg(row_in(a, __ldg(perm + k), c)));
-                    __stcs(reinterpret_cast<float4 *>(row_out(a, t0 + q0 + 2 * u + half, c)), acc);
-                }
+            for (; q < g; ++q) {
+                if (col) __stcs(reinterpret_cast<float4 *>(row_out(a, t0 + q, c)), acc);
+                acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
             }
         }
-        head = next;
     }
 }
 
@@ -633,7 +642,7 @@ int row_gather(const RowArgs &r, cudaStream_t st) {
     return check_launch("row gather");
 }
 
-// Segment-sum scatter-add (see k_seg_sum); MTC_ERR_UNSUPPORTED when the sizes
+// Segment-sum scatter-add (see k_seg_walk); MTC_ERR_UNSUPPORTED when the sizes
 // exceed the int32 bookkeeping or the two-level scan (the caller then takes
 // the atomic kernel).
 int segment_scatter_add(const RowArgs &r, cudaStream_t st) {
@@ -679,28 +688,33 @@ int segment_scatter_add(const RowArgs &r, cudaStream_t st) {
         launched("segment scatter-add scan");
     }
     if (rc == MTC_OK) {
-        k_scan_totals<<<1, 256, 0, st>>>(sums, static_cast<int>(nblk));
+        k_scan_totals<<<1, 1024, 0, st>>>(sums, static_cast<int>(nblk));
         launched("segment scatter-add scan totals");
     }
-    if (rc == MTC_OK) {
-        k_scan_add<<<static_cast<unsigned>((T + 1 + 255) / 256), 256, 0, st>>>(starts, T + 1, sums);
-        launched("segment scatter-add scan offsets");
-    }
     if (rc == MTC_OK && n > 0) {
-        k_seg_fill<<<grid_for(n), 256, 0, st>>>(r, rank, starts, perm);
-        launched("segment scatter-add fill");
+        // slices of the targets whose starts and perm regions (4 bytes per target
+        // and per update) take at most 64 MB together, half of the 126 MB L2:
+        // at 2^24 rows two slices took the fill from 0.50 to 0.23 ms (four: 0.25)
+        const long long slice_bytes = 64ll << 20;
+        const long long slices = ((T + n) * 4 + slice_bytes - 1) / slice_bytes;
+        const long long per = (T + slices - 1) / slices;
+        for (long long lo = 0; lo < T && rc == MTC_OK; lo += per) {
+            k_seg_fill<<<grid_for(n), 256, 0, st>>>(r, rank, starts, sums, perm, lo, lo + per < T ? lo + per : T);
+            launched("segment scatter-add fill");
+        }
         if (rc == MTC_OK) {
-            k_seg_sort<<<grid_for(T), 256, 0, st>>>(starts, perm, T, long_list, long_count, static_cast<int>(cap));
+            k_seg_sort<<<grid_for(T), 256, 0, st>>>(starts, sums, perm, T, long_list, long_count,
+                                                   static_cast<int>(cap));
             launched("segment scatter-add sort");
         }
         if (rc == MTC_OK) {
-            k_seg_sort_long<<<sm_count(current_device()) * 2, 256, 0, st>>>(starts, perm, long_list, long_count,
-                                                                              static_cast<int>(cap));
+            k_seg_sort_long<<<sm_count(current_device()) * 2, 256, 0, st>>>(starts, sums, perm, long_list,
+                                                                              long_count, static_cast<int>(cap));
             launched("segment scatter-add long sort");
         }
     }
     if (rc == MTC_OK) {
-        k_seg_sum<4><<<grid_for(T), 256, 0, st>>>(r, starts, perm);  // a warp per 32 target rows
+        k_seg_walk<<<grid_for(T * 16 / kWalkTargets), 256, 0, st>>>(r, starts, sums, perm);  // 16 lanes a group
         launched("segment scatter-add sum");
     }
     scratch_free(scratch, st);

@@ -31,5 +31,9 @@ int gemm_simt(const GemmProblem &p, cudaStream_t stream, bool exact);
 // The tensor-core path with its split operands in a fixed static device array
 // (no allocation); rejects problems whose workspace exceeds that array.
 int gemm_3xtf32_static(const GemmProblem &p, cudaStream_t stream);
+// Called when the process creates a collective communicator: from then on the
+// tensor-core GEMMs hand out their work units at run time, since collective
+// kernels on other streams may hold some SMs while a GEMM starts.
+void gemm_note_collectives();
 
 }  // namespace mtc

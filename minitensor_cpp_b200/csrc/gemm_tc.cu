@@ -27,6 +27,7 @@
 // device error word and leaves its loops (no hang).
 #include <cuda.h>
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -53,7 +54,7 @@ struct TcPipe {
     static constexpr int A_BYTES = TC_BM * BK * 4;
     static constexpr int B_BYTES = TC_BN * BK * 4;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 512;
     // smem descriptor layout code (tcgen05): 2 = 128-byte swizzle, 4 = 64-byte swizzle
     static constexpr uint64_t LAYOUT = BK == 32 ? 2ull : 4ull;
     // byte distance between 8-row core-matrix groups: 8 rows x one swizzle row
@@ -85,7 +86,15 @@ struct TcArgs {
     int64_t kb_per_split;
     float *ws;
     int group;  // row tiles per column sweep of the tile order (L2 reuse)
+    // Work units are handed out at run time: each CTA (CTA pair) starts with the
+    // unit of its own index, then takes the next from this counter (zeroed
+    // before the launch), so a CTA that starts late -- its SM still busy with
+    // another kernel, e.g. a collective on another stream -- takes fewer units
+    // instead of holding up the whole GEMM.  Null: static round-robin.
+    unsigned long long *counter;
 };
+
+constexpr int kUnitRing = 4;  // units published ahead of the slowest role
 
 // Tile and K-block range of work unit u.
 __device__ __forceinline__ void unit_range(const TcArgs &a, int64_t u, int64_t kblocks, int64_t &t, int &split,
@@ -134,6 +143,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     }
     *abort_flag = 1;
     return false;
+}
+
+// The unit after `u` for a CTA (or CTA pair) among `workers`.
+__device__ __forceinline__ int64_t next_unit(const TcArgs &a, int64_t u, int64_t workers) {
+    return a.counter != nullptr ? workers + static_cast<int64_t>(atomicAdd(a.counter, 1ull)) : u + workers;
+}
+
+// Reads entry i of the unit ring once the producer has published it.  The
+// caller arrives on unit_empty after every thread of its group has read it.
+__device__ __forceinline__ bool unit_take(uint64_t *unit_full, const volatile int64_t *ring, int64_t i,
+                                          volatile int *abort_flag, int64_t &u) {
+    const int r = static_cast<int>(i % kUnitRing);
+    if (!mbar_wait(&unit_full[r], static_cast<uint32_t>(i / kUnitRing) & 1u, abort_flag)) return false;
+    u = ring[r];
+    return true;
 }
 
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z) {
@@ -243,6 +267,12 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
     uint64_t *conv = drain + 1;                  // [TC_STAGES] lo slots written (DIRECT)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(conv + TC_STAGES);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    // unit ring: the producer publishes every work unit it takes; the MMA issuer,
+    // the epilogue warps and the converter warps read the same sequence
+    uint64_t *unit_full = reinterpret_cast<uint64_t *>(tmem_slot + 2);  // [kUnitRing]
+    uint64_t *unit_empty = unit_full + kUnitRing;                        // [kUnitRing]
+    volatile int64_t *unit_ring = reinterpret_cast<volatile int64_t *>(unit_empty + kUnitRing);
+    const int64_t units = args.total_tiles * args.splits;
     // bytes the TMA delivers per stage: raw operands fill one slot, packed ones two
     constexpr uint32_t kStageTx = (AD ? TC_A_BYTES : 2 * TC_A_BYTES) + (BD ? TC_B_BYTES : 2 * TC_B_BYTES);
 
@@ -259,6 +289,10 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 128);
+        }
+        for (int r = 0; r < kUnitRing; ++r) {
+            mbar_init(&unit_full[r], 1);
+            mbar_init(&unit_empty[r], DIRECT ? 9 : 5);  // MMA issuer, 4 epilogue (+ 4 converter) warps
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -279,7 +313,17 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
         if (lane == 0) {
             int64_t it = 0;
             bool ok = true;
-            for (int64_t u = blockIdx.x; u < args.total_tiles * args.splits && ok; u += gridDim.x) {
+            int64_t u = blockIdx.x;
+            for (int64_t i = 0; ok; ++i) {
+                const int r = static_cast<int>(i % kUnitRing);
+                if (!mbar_wait(&unit_empty[r], (static_cast<uint32_t>(i / kUnitRing) & 1u) ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                unit_ring[r] = u;
+                mbar_arrive(&unit_full[r]);
+                if (u >= units) break;
+                const int64_t next = next_unit(args, u, gridDim.x);  // its latency overlaps this unit's loads
                 int64_t t, kb0, kb1;
                 int split;
                 unit_range(args, u, kblocks, t, split, kb0, kb1);
@@ -300,6 +344,7 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
                     tma_load_3d(st + 2 * TC_A_BYTES, &tm_bhi, &full[s], kx, tn * TC_BN, tb);
                     if (!BD) tma_load_3d(st + 2 * TC_A_BYTES + TC_B_BYTES, &tm_blo, &full[s], kx, tn * TC_BN, tb);
                 }
+                u = next;
             }
             if (!ok) atomicCAS(args.err, 0ull, static_cast<unsigned long long>(kErrTimeout));
             // drain: every issued stage must have landed before the CTA exits
@@ -313,9 +358,15 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             int64_t it = 0;
-            int64_t local = 0;
             bool ok = true;
-            for (int64_t u = blockIdx.x; u < args.total_tiles * args.splits && ok; u += gridDim.x, ++local) {
+            for (int64_t local = 0; ok; ++local) {
+                int64_t u;
+                if (!unit_take(unit_full, unit_ring, local, abort_flag, u)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive(&unit_empty[local % kUnitRing]);
+                if (u >= units) break;
                 int64_t t, kb0, kb1;
                 int split;
                 unit_range(args, u, kblocks, t, split, kb0, kb1);
@@ -366,7 +417,15 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
         const int ct = threadIdx.x - TC_THREADS;  // 0..127
         int64_t it = 0;
         bool ok = true;
-        for (int64_t u = blockIdx.x; u < args.total_tiles * args.splits && ok; u += gridDim.x) {
+        for (int64_t i = 0; ok; ++i) {
+            int64_t u;
+            if (!unit_take(unit_full, unit_ring, i, abort_flag, u)) {
+                ok = false;
+                break;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&unit_empty[i % kUnitRing]);
+            if (u >= units) break;
             int64_t t, kb0, kb1;
             int split;
             unit_range(args, u, kblocks, t, split, kb0, kb1);
@@ -404,8 +463,15 @@ __global__ void __launch_bounds__(DIRECT ? TC_THREADS + 128 : TC_THREADS, 1)
         // epilogue: warps 2..5 cover TMEM lane quadrants (warp % 4)
         const int quadrant = warp % 4;
         const int row_in_tile = quadrant * 32 + lane;
-        int64_t local = 0;
-        for (int64_t u = blockIdx.x; u < args.total_tiles * args.splits; u += gridDim.x, ++local) {
+        for (int64_t local = 0;; ++local) {
+            int64_t u;
+            if (!unit_take(unit_full, unit_ring, local, abort_flag, u)) {
+                atomicCAS(args.err, 0ull, static_cast<unsigned long long>(kErrTimeout));
+                break;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&unit_empty[local % kUnitRing]);
+            if (u >= units) break;
             int64_t t, kb0, kb1;
             int split;
             unit_range(args, u, kblocks, t, split, kb0, kb1);
@@ -494,6 +560,39 @@ __global__ void __launch_bounds__(256) k_splitk_reduce(const TcArgs a) {
     }
 }
 
+// The same reduction four columns at a time (N a multiple of 4, C rows
+// contiguous and 16-byte aligned): a CTA row per output row, 128-bit loads
+// and stores, no per-element index division.
+__global__ void __launch_bounds__(256) k_splitk_reduce4(const TcArgs a) {
+    const int64_t rows = a.batch * a.M;
+    const int64_t nv = a.N / 4;
+    const int64_t plane4 = rows * nv;
+    const float4 *ws4 = reinterpret_cast<const float4 *>(a.ws);
+    for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+        const int64_t m = r % a.M;
+        int64_t rem = r / a.M;
+        int64_t co = a.c_off + m * a.c_rs;
+        for (int d = a.batch_rank - 1; d >= 0; --d) {
+            const int64_t c = rem % a.batch_shape[d];
+            rem /= a.batch_shape[d];
+            co += c * a.c_bs[d];
+        }
+        float4 *dst = reinterpret_cast<float4 *>(a.C + co);
+        for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < nv;
+             c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+            float4 acc = ws4[r * nv + c];
+            for (int s = 1; s < a.splits; ++s) {
+                const float4 v = ws4[s * plane4 + r * nv + c];
+                acc.x = __fadd_rn(acc.x, v.x);
+                acc.y = __fadd_rn(acc.y, v.y);
+                acc.z = __fadd_rn(acc.z, v.z);
+                acc.w = __fadd_rn(acc.w, v.w);
+            }
+            dst[c] = acc;
+        }
+    }
+}
+
 // ------------------------------------------------------- CTA-pair kernel --
 // The same 3xTF32 product with tcgen05.mma.cta_group::2: a cluster of two CTAs
 // on two SMs computes one 256x256 tile.  Each CTA stages its own 128 rows of A
@@ -516,7 +615,7 @@ struct PairPipe {
     static constexpr int A_BYTES = 128 * BK * 4;  // this CTA's 128 rows of A
     static constexpr int B_BYTES = 128 * BK * 4;  // this CTA's 128 columns of B
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 512;
     static constexpr uint64_t LAYOUT = BK == 32 ? 2ull : 4ull;
     static constexpr uint64_t SBO = 8ull * BK * 4;
     static_assert(BK == 16 || BK == 32, "BK is one 64- or 128-byte swizzle row");
@@ -544,6 +643,29 @@ __device__ __forceinline__ uint32_t peer_addr(const void *p, uint32_t rank) {
 
 __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Bounded wait with cluster-scope acquire: for barriers another CTA of the
+// cluster arrives on after writing this CTA's shared memory.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+    for (long long i = 0; i < kWaitLimit; ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if ((i & 1023) == 1023 && *abort_flag) return false;
+    }
+    *abort_flag = 1;
+    return false;
+}
+
+__device__ __forceinline__ void st_cluster_s64(uint32_t cluster_addr, int64_t v) {
+    asm volatile("st.shared::cluster.s64 [%0], %1;" ::"r"(cluster_addr), "l"(v) : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
@@ -604,6 +726,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     uint64_t *drain = acc_empty + 2;     // [1]  leader's: all MMAs complete
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    // unit ring in both CTAs, written by the leader's producer; unit_empty is the
+    // leader's: its MMA issuer and epilogue warps, the peer's producer and
+    // epilogue warps arrive once they have read an entry
+    uint64_t *unit_full = reinterpret_cast<uint64_t *>(tmem_slot + 2);  // [kUnitRing]
+    uint64_t *unit_empty = unit_full + kUnitRing;                        // [kUnitRing] (leader's)
+    volatile int64_t *unit_ring = reinterpret_cast<volatile int64_t *>(unit_empty + kUnitRing);
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
@@ -612,6 +740,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     const int64_t cluster = blockIdx.x / 2;
     const int64_t clusters = gridDim.x / 2;
     const int64_t kblocks = (args.Kp + P::BK - 1) / P::BK;
+    // the entry's unit, and the release of its slot (the leader's barrier)
+    auto take = [&](int64_t i, int64_t &u) -> bool {
+        const int r = static_cast<int>(i % kUnitRing);
+        const uint32_t par = static_cast<uint32_t>(i / kUnitRing) & 1u;
+        if (!(leader ? mbar_wait(&unit_full[r], par, abort_flag) : mbar_wait_cluster(&unit_full[r], par, abort_flag)))
+            return false;
+        u = unit_ring[r];
+        return true;
+    };
+    auto release = [&](int64_t i) {
+        const int r = static_cast<int>(i % kUnitRing);
+        if (leader) mbar_arrive(&unit_empty[r]);
+        else mbar_arrive_remote(peer_addr(&unit_empty[r], 0));
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -621,6 +763,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 8);  // 4 epilogue warps x 2 CTAs
+        }
+        for (int r = 0; r < kUnitRing; ++r) {
+            mbar_init(&unit_full[r], 1);
+            mbar_init(&unit_empty[r], 10);  // leader: MMA issuer + 4 epilogue warps; peer: producer + 4
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -642,7 +788,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
         if (lane == 0) {
             int64_t it = 0;
             bool ok = true;
-            for (int64_t t = cluster; t < args.total_tiles && ok; t += clusters) {
+            int64_t t = cluster;  // leader: the unit it publishes next
+            for (int64_t i = 0; ok; ++i) {
+                int64_t next = 0;
+                if (leader) {
+                    const int r = static_cast<int>(i % kUnitRing);
+                    if (!mbar_wait_cluster(&unit_empty[r], (static_cast<uint32_t>(i / kUnitRing) & 1u) ^ 1u,
+                                           abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    unit_ring[r] = t;
+                    st_cluster_s64(peer_addr(const_cast<int64_t *>(&unit_ring[r]), 1), t);
+                    mbar_arrive(&unit_full[r]);
+                    mbar_arrive_remote(peer_addr(&unit_full[r], 1));  // release: the remote store lands first
+                    if (t >= args.total_tiles) break;
+                    next = next_unit(args, t, clusters);
+                } else {
+                    if (!take(i, t)) {
+                        ok = false;
+                        break;
+                    }
+                    release(i);
+                    if (t >= args.total_tiles) break;
+                }
                 int tm, tn, tb;
                 pair_tile_coords(args, t, tm, tn, tb);
                 const int a_row = tm * 256 + static_cast<int>(rank) * 128;
@@ -663,6 +832,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
                     tma_load_3d_pair(st + 2 * P::A_BYTES, &tm_bhi, fb, kx, b_row, tb);
                     tma_load_3d_pair(st + 2 * P::A_BYTES + P::B_BYTES, &tm_blo, fb, kx, b_row, tb);
                 }
+                if (leader) t = next;
             }
             if (!ok) atomicCAS(args.err, 0ull, static_cast<unsigned long long>(kErrTimeout));
             if (leader) {  // every stage issued by the pair has landed before the cluster exits
@@ -677,9 +847,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
     } else if (warp == 1) {
         if (lane == 0 && leader) {
             int64_t it = 0;
-            int64_t local = 0;
             bool ok = true;
-            for (int64_t t = cluster; t < args.total_tiles && ok; t += clusters, ++local) {
+            for (int64_t local = 0; ok; ++local) {
+                int64_t t;
+                if (!take(local, t)) {
+                    ok = false;
+                    break;
+                }
+                release(local);
+                if (t >= args.total_tiles) break;
                 const int b = static_cast<int>(local & 1);
                 const uint32_t use = static_cast<uint32_t>(local >> 1);
                 if (!mbar_wait(&acc_empty[b], (use & 1u) ^ 1u, abort_flag)) {
@@ -725,8 +901,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TC_THREADS, 1)
         const int row_in_tile = static_cast<int>(rank) * 128 + quadrant * 32 + lane;
         const uint32_t acc_empty_leader0 = peer_addr(&acc_empty[0], 0);
         const uint32_t acc_empty_leader1 = peer_addr(&acc_empty[1], 0);
-        int64_t local = 0;
-        for (int64_t t = cluster; t < args.total_tiles; t += clusters, ++local) {
+        for (int64_t local = 0;; ++local) {
+            int64_t t;
+            if (!take(local, t)) {
+                atomicCAS(args.err, 0ull, static_cast<unsigned long long>(kErrTimeout));
+                break;
+            }
+            __syncwarp();
+            if (lane == 0) release(local);
+            if (t >= args.total_tiles) break;
             const int b = static_cast<int>(local & 1);
             const uint32_t use = static_cast<uint32_t>(local >> 1);
             if (!mbar_wait(&acc_full[b], use & 1u, abort_flag)) {
@@ -1098,7 +1281,7 @@ int tile_group(const char *env, int fallback) {
 
 template <class P>
 int launch_tc(const GemmProblem &p, int64_t Kp, const TcOperand &A, const TcOperand &B, cudaStream_t stream,
-              int splits = 1, float *split_ws = nullptr) {
+              int splits, float *split_ws, unsigned long long *counter) {
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
     MTC_TRY(operand_maps<P>(A, p.M, p.batch, TC_BM, m_ahi, m_alo));
     MTC_TRY(operand_maps<P>(B, p.N, p.batch, TC_BN, m_bhi, m_blo));
@@ -1133,6 +1316,7 @@ int launch_tc(const GemmProblem &p, int64_t Kp, const TcOperand &A, const TcOper
         a.splits = static_cast<int>((kblocks + a.kb_per_split - 1) / a.kb_per_split);
         a.ws = split_ws;
     }
+    a.counter = counter;
     int rc;
     switch ((A.direct ? 1 : 0) | (B.direct ? 2 : 0)) {
     case 0: rc = launch_tc_variant<P, 0>(m_ahi, m_alo, m_bhi, m_blo, a, stream); break;
@@ -1141,6 +1325,13 @@ int launch_tc(const GemmProblem &p, int64_t Kp, const TcOperand &A, const TcOper
     default: rc = launch_tc_variant<P, 3>(m_ahi, m_alo, m_bhi, m_blo, a, stream); break;
     }
     if (rc != MTC_OK || a.splits == 1) return rc;
+    if (a.vec_store && a.N % 4 == 0) {
+        const int64_t rows = a.batch * a.M;
+        const int64_t bx = (a.N / 4 + 255) / 256;
+        const dim3 grid(static_cast<unsigned>(bx < 64 ? bx : 64), static_cast<unsigned>(rows < 65535 ? rows : 65535));
+        k_splitk_reduce4<<<grid, 256, 0, stream>>>(a);
+        return check_launch("3xTF32 split-K reduction");
+    }
     const int64_t total = a.batch * a.M * a.N;
     int64_t blocks = (total + 255) / 256;
     if (blocks > 148 * 8) blocks = 148 * 8;
@@ -1176,7 +1367,7 @@ int pair_clusters(int *out) {
 // The CTA-pair kernel: 256x256 tiles, each CTA stages 128 rows of A and 128 of B.
 template <class P>
 int launch_pair(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float *bhi, float *blo,
-                cudaStream_t stream) {
+                cudaStream_t stream, unsigned long long *counter) {
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
     MTC_TRY(operand_maps<P>(packed_operand(ahi, alo, Kp, p.M), p.M, p.batch, 128, m_ahi, m_alo));
     MTC_TRY(operand_maps<P>(packed_operand(bhi, blo, Kp, p.N), p.N, p.batch, 128, m_bhi, m_blo));
@@ -1205,6 +1396,7 @@ int launch_pair(const GemmProblem &p, int64_t Kp, float *ahi, float *alo, float 
     MTC_TRY(device_error_word(&a.err));
     int max_clusters = 0;
     MTC_TRY(pair_clusters<P>(&max_clusters));
+    a.counter = counter;
     const int64_t clusters = a.total_tiles < max_clusters ? a.total_tiles : max_clusters;
     k_gemm_3xtf32_pair<P><<<static_cast<unsigned>(2 * clusters), TC_THREADS, P::SMEM_BYTES, stream>>>(
         m_ahi, m_alo, m_bhi, m_blo, a);
@@ -1252,8 +1444,11 @@ int direct_mask(TcKernel k) {
 
 // Packs the operands that cannot be read raw into `ws` (2 * batch * rows * Kp
 // floats each), then launches the selected kernel.
+// `counter`: 8 bytes of device memory for the run-time unit hand-out, zeroed
+// here on the stream before the launch; null keeps the static round-robin.
 int run_tc(const GemmProblem &p, int64_t Kp, TcKernel k, bool a_direct, bool b_direct, const TcOperand &a_raw,
-           const TcOperand &b_raw, float *ws, cudaStream_t stream, int splits = 1, float *split_ws = nullptr) {
+           const TcOperand &b_raw, float *ws, cudaStream_t stream, int splits = 1, float *split_ws = nullptr,
+           unsigned long long *counter = nullptr) {
     const size_t a_elems = a_direct ? 0 : static_cast<size_t>(p.batch * p.M * Kp);
     const size_t b_elems = b_direct ? 0 : static_cast<size_t>(p.batch * p.N * Kp);
     float *ahi = ws, *alo = ws + a_elems, *bhi = alo + a_elems, *blo = bhi + b_elems;
@@ -1266,11 +1461,12 @@ int run_tc(const GemmProblem &p, int64_t Kp, TcKernel k, bool a_direct, bool b_d
     HostSpan span("3xTF32 tensor maps and launch");
     const TcOperand A = a_direct ? a_raw : packed_operand(ahi, alo, Kp, p.M);
     const TcOperand B = b_direct ? b_raw : packed_operand(bhi, blo, Kp, p.N);
+    if (counter != nullptr) MTC_CUDA_TRY(cudaMemsetAsync(counter, 0, sizeof(*counter), stream));
     switch (k) {
-    case TcKernel::Wide: return launch_tc<PipeWide>(p, Kp, A, B, stream, splits, split_ws);
-    case TcKernel::PairDeep: return launch_pair<PairDeep>(p, Kp, ahi, alo, bhi, blo, stream);
-    case TcKernel::PairWide: return launch_pair<PairWide>(p, Kp, ahi, alo, bhi, blo, stream);
-    default: return launch_tc<PipeDeep>(p, Kp, A, B, stream, splits, split_ws);
+    case TcKernel::Wide: return launch_tc<PipeWide>(p, Kp, A, B, stream, splits, split_ws, counter);
+    case TcKernel::PairDeep: return launch_pair<PairDeep>(p, Kp, ahi, alo, bhi, blo, stream, counter);
+    case TcKernel::PairWide: return launch_pair<PairWide>(p, Kp, ahi, alo, bhi, blo, stream, counter);
+    default: return launch_tc<PipeDeep>(p, Kp, A, B, stream, splits, split_ws, counter);
     }
 }
 
@@ -1295,7 +1491,25 @@ bool a_readable_raw(const GemmProblem &p) {
     return direct_operand(p.A, p.a_off, p.a_rs, p.a_cs, p.M, p, p.a_bs, unused);
 }
 
+// Work units handed out at run time (TcArgs::counter) or round-robin.  Measured
+// on one B200 with a kernel holding 16 SMs for 2 ms launched just before an
+// 8192^3 GEMM: round-robin 4.0 -> 6.9 ms (the late CTAs' fixed shares finish
+// last), run-time hand-out 4.0 -> 4.7 ms.  Alone, the hand-out was 0.5-1.5 %
+// slower on the training step's large GEMMs (its waves spread a little wider),
+// so it is used once a communicator exists in the process, i.e. when NCCL
+// kernels may share the SMs.  MTC_TC_SCHEDULE=static / dynamic overrides.
+std::atomic<bool> g_collectives{false};
+
+bool run_time_units() {
+    const char *v = std::getenv("MTC_TC_SCHEDULE");
+    if (v != nullptr && std::strcmp(v, "static") == 0) return false;
+    if (v != nullptr && std::strcmp(v, "dynamic") == 0) return true;
+    return g_collectives.load(std::memory_order_relaxed);
+}
+
 }  // namespace
+
+void gemm_note_collectives() { g_collectives.store(true, std::memory_order_relaxed); }
 
 int gemm_3xtf32(const GemmProblem &p, cudaStream_t stream) {
     if (p.M < 64 || p.N < 64 || p.K < 16) return fail(MTC_ERR_UNSUPPORTED, "problem too small for the tensor-core path");
@@ -1328,13 +1542,18 @@ int gemm_3xtf32(const GemmProblem &p, cudaStream_t stream) {
         }
     }
     const size_t split_elems = splits > 1 ? static_cast<size_t>(splits) * p.batch * p.M * p.N : 0;
+    // workspace: the unit counter (256 bytes, keeping the packs 256-byte aligned),
+    // the split operands, the split-K partial tiles
     void *scratch = nullptr;
-    if (a_elems + b_elems + split_elems > 0) {
+    {
         HostSpan span("3xTF32 workspace allocation");
-        MTC_TRY(scratch_alloc((2 * a_elems + 2 * b_elems + split_elems) * sizeof(float) + 1024, stream, &scratch));
+        MTC_TRY(scratch_alloc(256 + (2 * a_elems + 2 * b_elems + split_elems) * sizeof(float) + 1024, stream,
+                              &scratch));
     }
-    float *split_ws = splits > 1 ? static_cast<float *>(scratch) + 2 * a_elems + 2 * b_elems : nullptr;
-    const int rc = run_tc(p, Kp, k, ad, bd, a_raw, b_raw, static_cast<float *>(scratch), stream, splits, split_ws);
+    unsigned long long *counter = run_time_units() ? static_cast<unsigned long long *>(scratch) : nullptr;
+    float *ws = reinterpret_cast<float *>(static_cast<char *>(scratch) + 256);
+    float *split_ws = splits > 1 ? ws + 2 * a_elems + 2 * b_elems : nullptr;
+    const int rc = run_tc(p, Kp, k, ad, bd, a_raw, b_raw, ws, stream, splits, split_ws, counter);
     {
         HostSpan span("3xTF32 workspace release");
         scratch_free(scratch, stream);

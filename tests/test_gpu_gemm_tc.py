@@ -128,7 +128,8 @@ def test_split_k_when_tiles_do_not_fill_the_gpu(cuda):
     bt, M, N, K = 2, 200, 300, 1000
     a = rng.standard_normal(bt * M * K).astype(F)
     b = rng.standard_normal(bt * K * N).astype(F)
-    _run(a, [bt, M, K], [M * K, K, 1], b, [bt, K, N], [K * N, N, 1], out_offset=5)
+    _run(a, [bt, M, K], [M * K, K, 1], b, [bt, K, N], [K * N, N, 1], out_offset=5)  # element-wise reduction
+    _run(a, [bt, M, K], [M * K, K, 1], b, [bt, K, N], [K * N, N, 1], out_offset=4)  # 128-bit reduction
     _run(a[: M * K], [M, K], [K, 1], b[: K * N], [K, N], [1, K])  # one tile column, transposed B
 
 
