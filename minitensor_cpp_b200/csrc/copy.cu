@@ -537,7 +537,9 @@ __device__ __forceinline__ void add4(float4 &acc, const uint4 w) {
 // the segment sort.
 constexpr int kWalkTargets = 8;  // target rows per half-warp step (at most 15)
 
-__global__ void __launch_bounds__(256) k_seg_walk(const RowArgs a, const int *starts, const int *sums, const int *perm) {
+template <int kBatch, int kMinBlocks>
+__global__ void __launch_bounds__(256, kMinBlocks) k_seg_walk(const RowArgs a, const int *starts, const int *sums,
+                                                              const int *perm) {
     const int hl = threadIdx.x & 15;
     const unsigned hmask = 0xffffu << (threadIdx.x & 16);
     const long long half = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
@@ -555,18 +557,18 @@ __global__ void __launch_bounds__(256) k_seg_walk(const RowArgs a, const int *st
             int q = 0;                                        // current target of the group
             int seg_end = __shfl_sync(hmask, sb, 1, 16);      // end of target t0 + q
             float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            for (int e = e_beg; e < e_end; e += 4) {
-                const int nb = e_end - e < 4 ? e_end - e : 4;  // uniform in the half-warp
+            for (int e = e_beg; e < e_end; e += kBatch) {
+                const int nb = e_end - e < kBatch ? e_end - e : kBatch;  // uniform in the half-warp
                 const int pl = hl < nb ? __ldg(perm + e + hl) : 0;
-                int p[4];
-                uint4 v[4];
+                int p[kBatch];
+                uint4 v[kBatch];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) p[u] = __shfl_sync(hmask, pl, u, 16);
+                for (int u = 0; u < kBatch; ++u) p[u] = __shfl_sync(hmask, pl, u, 16);
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
+                for (int u = 0; u < kBatch; ++u)
                     if (u < nb && col) v[u] = __ldg(row_in(a, p[u], c));
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
+                for (int u = 0; u < kBatch; ++u) {
                     if (u >= nb) break;
                     while (e + u >= seg_end) {  // finish the targets that end before this entry
                         if (col) __stcs(reinterpret_cast<float4 *>(row_out(a, t0 + q, c)), acc);
@@ -714,7 +716,15 @@ int segment_scatter_add(const RowArgs &r, cudaStream_t st) {
         }
     }
     if (rc == MTC_OK) {
-        k_seg_walk<<<grid_for(T * 16 / kWalkTargets), 256, 0, st>>>(r, starts, sums, perm);  // 16 lanes a group
+        const char *wv = std::getenv("MTC_SEG_WALK");
+        const int wk = wv ? std::atoi(wv) : 0;
+        const int wgrid = grid_for(T * 16 / kWalkTargets);  // 16 lanes a group
+        if (wk == 45) k_seg_walk<4, 5><<<wgrid, 256, 0, st>>>(r, starts, sums, perm);
+        else if (wk == 81) k_seg_walk<8, 1><<<wgrid, 256, 0, st>>>(r, starts, sums, perm);
+        else if (wk == 83) k_seg_walk<8, 3><<<wgrid, 256, 0, st>>>(r, starts, sums, perm);
+        else if (wk == 26) k_seg_walk<2, 6><<<wgrid, 256, 0, st>>>(r, starts, sums, perm);
+        else if (wk == 41) k_seg_walk<4, 1><<<wgrid, 256, 0, st>>>(r, starts, sums, perm);
+        else k_seg_walk<4, 4><<<wgrid, 256, 0, st>>>(r, starts, sums, perm);
         launched("segment scatter-add sum");
     }
     scratch_free(scratch, st);
