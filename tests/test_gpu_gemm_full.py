@@ -32,7 +32,8 @@ from oracle import mt_oracle as mo
 
 pytestmark = pytest.mark.gpu
 
-POLICIES = (None, "pair16x6")
+# kernel choice ("MTC_TC_PIPELINE") and, after "/", the work-unit schedule
+POLICIES = (None, "pair16x6", "/dynamic", "pair16x6/dynamic")
 ROWS = 64
 ORACLE_ROWS = 4
 
@@ -48,8 +49,11 @@ def _run_policy(A, B, C, policy):
     import torch
 
     old = os.environ.pop("MTC_TC_PIPELINE", None)
-    if policy is not None:
-        os.environ["MTC_TC_PIPELINE"] = policy
+    pipe, _, sched = (policy or "").partition("/")
+    if pipe:
+        os.environ["MTC_TC_PIPELINE"] = pipe
+    if sched:
+        os.environ["MTC_TC_SCHEDULE"] = sched
     try:
         tc0, _ = abi.gemm_path_counts()
         abi.matmul(A, B, C, abi.GEMM_AUTO)
@@ -58,6 +62,7 @@ def _run_policy(A, B, C, policy):
         tc1, _ = abi.gemm_path_counts()
     finally:
         os.environ.pop("MTC_TC_PIPELINE", None)
+        os.environ.pop("MTC_TC_SCHEDULE", None)
         if old is not None:
             os.environ["MTC_TC_PIPELINE"] = old
     assert tc1 - tc0 == 1, "the problem did not run on the tensor-core path"

@@ -1,7 +1,7 @@
 """Parity of the tcgen05 3xTF32 tensor-core GEMM (forced, no SIMT fallback)
 against the float32 oracle: |C - C_ref| <= 1e-5 * sqrt(K) * (|A| |B|)_ij, the
 normwise per-element form of the 1e-5*sqrt(K) relative bound.  Every case runs
-with each kernel variant and shared-memory ring."""
+with each kernel variant and shared-memory ring, under both work-unit schedules."""
 import numpy as np
 import pytest
 
@@ -33,6 +33,15 @@ def pipeline(request, monkeypatch):
     else:
         monkeypatch.delenv("MTC_TC_DIRECT", raising=False)
     return name
+
+
+@pytest.fixture(autouse=True, params=["static", "dynamic"])
+def schedule(request, monkeypatch):
+    """Work units round-robin (the default of a process without a communicator)
+    or handed out at run time from a per-launch counter (the default once NCCL
+    is in use): the same tiles, so the same results."""
+    monkeypatch.setenv("MTC_TC_SCHEDULE", request.param)
+    return request.param
 
 
 def _run(a_st, a_shape, a_strides, b_st, b_shape, b_strides, out_offset=0, algo=abi.GEMM_3XTF32):
