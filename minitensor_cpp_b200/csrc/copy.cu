@@ -534,12 +534,14 @@ __device__ __forceinline__ void add4(float4 &acc, const uint4 w) {
 // target rows with each row's first three updates prefetched (two to four rows
 // in flight per lane), and 1.67 ms when the walk also sorted each group of up
 // to 16 updates in registers (a bitonic network over the half-warp) in place of
-// the segment sort.
+// the segment sort.  Four rows a batch at 64 registers (4 CTAs of 256 per SM)
+// measured best: 2 rows at 40 registers 2.37 ms for the whole scatter-add, 4
+// at 48 (spilling) 2.20, 4 at 72 2.45, 8 at 80 2.27, 8 at 94 2.62, against 2.16.
 constexpr int kWalkTargets = 8;  // target rows per half-warp step (at most 15)
 
-template <int kBatch, int kMinBlocks>
-__global__ void __launch_bounds__(256, kMinBlocks) k_seg_walk(const RowArgs a, const int *starts, const int *sums,
-                                                              const int *perm) {
+__global__ void __launch_bounds__(256, 4) k_seg_walk(const RowArgs a, const int *starts, const int *sums,
+                                                     const int *perm) {
+    constexpr int kBatch = 4;
     const int hl = threadIdx.x & 15;
     const unsigned hmask = 0xffffu << (threadIdx.x & 16);
     const long long half = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 4;
@@ -716,15 +718,7 @@ int segment_scatter_add(const RowArgs &r, cudaStream_t st) {
         }
     }
     if (rc == MTC_OK) {
-        const char *wv = std::getenv("MTC_SEG_WALK");
-        const int wk = wv ? std::atoi(wv) : 0;
-        const int wgrid = grid_for(T * 16 / kWalkTargets);  // 16 lanes a group
-        if (wk == 45) k_seg_walk<4, 5><<<wgrid, 256, 0, st>>>(r, starts, sums, perm);
-        else if (wk == 81) k_seg_walk<8, 1><<<wgrid, 256, 0, st>>>(r, starts, sums, perm);
-        else if (wk == 83) k_seg_walk<8, 3><<<wgrid, 256, 0, st>>>(r, starts, sums, perm);
-        else if (wk == 26) k_seg_walk<2, 6><<<wgrid, 256, 0, st>>>(r, starts, sums, perm);
-        else if (wk == 41) k_seg_walk<4, 1><<<wgrid, 256, 0, st>>>(r, starts, sums, perm);
-        else k_seg_walk<4, 4><<<wgrid, 256, 0, st>>>(r, starts, sums, perm);
+        k_seg_walk<<<grid_for(T * 16 / kWalkTargets), 256, 0, st>>>(r, starts, sums, perm);  // 16 lanes a group
         launched("segment scatter-add sum");
     }
     scratch_free(scratch, st);
