@@ -437,9 +437,10 @@ __global__ void __launch_bounds__(1024) k_scan_totals(int *sums, int n) {
     }
 }
 
-// Start of target t's segment in perm (t = targets gives the end of the last).
+// Start of target t's segment in perm (t = targets gives the end of the last);
+// sums is null when starts already holds the final offsets.
 __device__ __forceinline__ int seg_start(const int *starts, const int *sums, long long t) {
-    return __ldg(starts + t) + __ldg(sums + t / kScanBlock);
+    return __ldg(starts + t) + (sums != nullptr ? __ldg(sums + t / kScanBlock) : 0);
 }
 
 // perm[starts[j] + rank[i]] = i for the update rows whose target j lies in
@@ -523,6 +524,180 @@ __device__ __forceinline__ void add4(float4 &acc, const uint4 w) {
     acc.y = __fadd_rn(acc.y, __uint_as_float(w.y));
     acc.z = __fadd_rn(acc.z, __uint_as_float(w.z));
     acc.w = __fadd_rn(acc.w, __uint_as_float(w.w));
+}
+
+// ---- bucketed prelude (targets from 2^22 to 2^26 rows) -------------------
+// The same starts and sorted perm, built without global atomics: a counting
+// sort by target in two levels whose counters live in shared memory.
+//   hist : per chunk of kChunk updates, how many fall in each bucket of
+//          kBucketRows target rows, written bucket-major
+//   scan : of that matrix (the scan kernels above) -> where each chunk's
+//          updates of each bucket go
+//   part : each chunk stages its updates by bucket in shared memory and writes
+//          (update row, target row within the bucket) runs to their places
+//   sort : a CTA per bucket counts its target rows in shared memory, scans,
+//          writes starts, places the update rows into perm and sorts each
+//          segment (the long ones go to k_seg_sort_long as before)
+constexpr int kBucketShift = 14;
+constexpr int kBucketRows = 1 << kBucketShift;     // target rows a bucket
+constexpr int kChunk = 16384;                      // updates a partition CTA
+constexpr int kMaxBuckets = 4096;                  // so targets <= 2^26
+constexpr int kPartThreads = 1024;
+constexpr int kPerThread = kChunk / kPartThreads;  // 16
+constexpr size_t kPartSmem = kChunk * sizeof(int2) + 2 * kMaxBuckets * sizeof(int) + 32 * sizeof(int);
+constexpr size_t kBktSortSmem = kBucketRows * sizeof(int) + 32 * sizeof(int);
+
+// Exclusive scan of v[0, len) in shared memory by a CTA of kPartThreads threads
+// (len <= 16 * kPartThreads); returns the total.  wtot: 32 ints of shared scratch.
+__device__ int block_exclusive_scan(int *v, int len, int *wtot) {
+    const int per = (len + kPartThreads - 1) / kPartThreads;
+    const int b0 = static_cast<int>(threadIdx.x) * per;
+    int run = 0;
+    for (int q = 0; q < per; ++q)
+        if (b0 + q < len) run += v[b0 + q];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int inc = run;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+    }
+    if (lane == 31) wtot[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        int x = wtot[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        wtot[lane] = x;
+    }
+    __syncthreads();
+    int off = (warp > 0 ? wtot[warp - 1] : 0) + inc - run;
+    for (int q = 0; q < per; ++q) {
+        if (b0 + q < len) {
+            const int t = v[b0 + q];
+            v[b0 + q] = off;
+            off += t;
+        }
+    }
+    const int total = wtot[31];
+    __syncthreads();
+    return total;
+}
+
+__global__ void __launch_bounds__(kPartThreads) k_bkt_hist(const RowArgs a, int *hist, int nb, long long chunks) {
+    __shared__ int h[kMaxBuckets];
+    for (int b = threadIdx.x; b < nb; b += kPartThreads) h[b] = 0;
+    __syncthreads();
+    const long long base = static_cast<long long>(blockIdx.x) * kChunk;
+    for (int k = threadIdx.x; k < kChunk; k += kPartThreads) {
+        const long long i = base + k;
+        if (i >= a.rows) break;
+        const long long j = __ldg(a.idx + a.idx_off + i * a.idx_rs);
+        if (j < 0 || j >= a.extent) {
+            record_device_error(MTC_ERR_OUT_OF_RANGE, j);
+            continue;
+        }
+        atomicAdd(&h[j >> kBucketShift], 1);
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < nb; b += kPartThreads) hist[static_cast<long long>(b) * chunks + blockIdx.x] = h[b];
+}
+
+// off / off_sums: the scanned histogram (offset of chunk c's bucket-b updates
+// at b * chunks + c, plus its scan block's sum).
+__global__ void __launch_bounds__(kPartThreads) k_bkt_part(const RowArgs a, const int *off, const int *off_sums,
+                                                           int2 *pairs, int nb, long long chunks) {
+    extern __shared__ __align__(16) unsigned char bkt_smem[];
+    int2 *stage = reinterpret_cast<int2 *>(bkt_smem);     // kChunk: the chunk's updates by bucket
+    int *h = reinterpret_cast<int *>(stage + kChunk);      // counts, then chunk-local offsets
+    int *goff = h + kMaxBuckets;                           // the chunk's place in each bucket
+    int *wtot = goff + kMaxBuckets;
+    const long long c = blockIdx.x;
+    for (int b = threadIdx.x; b < nb; b += kPartThreads) {
+        h[b] = 0;
+        const long long x = static_cast<long long>(b) * chunks + c;
+        goff[b] = off[x] + off_sums[x / kScanBlock];
+    }
+    __syncthreads();
+    const long long base = c * kChunk;
+    int ii[kPerThread], jj[kPerThread], rr[kPerThread];
+#pragma unroll
+    for (int q = 0; q < kPerThread; ++q) {
+        const long long i = base + threadIdx.x + q * kPartThreads;
+        jj[q] = -1;
+        ii[q] = 0;
+        rr[q] = 0;
+        if (i < a.rows) {
+            const long long j = __ldg(a.idx + a.idx_off + i * a.idx_rs);
+            if (j >= 0 && j < a.extent) {  // the histogram pass recorded the others
+                jj[q] = static_cast<int>(j);
+                ii[q] = static_cast<int>(i);
+                rr[q] = atomicAdd(&h[j >> kBucketShift], 1);
+            }
+        }
+    }
+    __syncthreads();
+    const int valid = block_exclusive_scan(h, nb, wtot);
+#pragma unroll
+    for (int q = 0; q < kPerThread; ++q)
+        if (jj[q] >= 0) stage[h[jj[q] >> kBucketShift] + rr[q]] = make_int2(ii[q], jj[q]);
+    __syncthreads();
+    for (int p = threadIdx.x; p < valid; p += kPartThreads) {
+        const int2 e = stage[p];
+        const int b = e.y >> kBucketShift;
+        pairs[goff[b] + (p - h[b])] = make_int2(e.x, e.y & (kBucketRows - 1));
+    }
+}
+
+__global__ void __launch_bounds__(kPartThreads) k_bkt_sort(const int2 *pairs, const int *off, const int *off_sums,
+                                                           long long chunks, int nb, long long targets, int *starts,
+                                                           int *perm, int *long_list, int *long_count,
+                                                           int long_capacity) {
+    extern __shared__ __align__(16) unsigned char bkt_smem[];
+    int *cnt = reinterpret_cast<int *>(bkt_smem);  // kBucketRows
+    int *wtot = cnt + kBucketRows;
+    const int b = blockIdx.x;
+    const long long t0 = static_cast<long long>(b) << kBucketShift;
+    const int wt = static_cast<int>(targets - t0 < kBucketRows ? targets - t0 : kBucketRows);
+    const long long x0 = static_cast<long long>(b) * chunks, x1 = x0 + chunks;
+    const int beg = off[x0] + off_sums[x0 / kScanBlock];
+    const int end = off[x1] + off_sums[x1 / kScanBlock];
+    for (int t = threadIdx.x; t < wt; t += kPartThreads) cnt[t] = 0;
+    __syncthreads();
+    for (int e = beg + static_cast<int>(threadIdx.x); e < end; e += kPartThreads) atomicAdd(&cnt[pairs[e].y], 1);
+    __syncthreads();
+    block_exclusive_scan(cnt, wt, wtot);
+    for (int t = threadIdx.x; t < wt; t += kPartThreads) starts[t0 + t] = beg + cnt[t];
+    if (b == nb - 1 && threadIdx.x == 0) starts[targets] = end;
+    __syncthreads();  // every start is read before the placement moves cnt on
+    for (int e = beg + static_cast<int>(threadIdx.x); e < end; e += kPartThreads) {
+        const int2 pe = pairs[e];
+        perm[beg + atomicAdd(&cnt[pe.y], 1)] = pe.x;
+    }
+    __syncthreads();
+    // cnt[t] is now the end of segment t within the bucket; sort each segment
+    for (int t = threadIdx.x; t < wt; t += kPartThreads) {
+        const int s0 = t == 0 ? 0 : cnt[t - 1];
+        const int len = cnt[t] - s0;
+        if (len > 32) {
+            const int k = atomicAdd(long_count, 1);
+            if (k < long_capacity) long_list[k] = static_cast<int>(t0 + t);
+        } else if (len > 1) {
+            int *pp = perm + beg + s0;
+            for (int q = 1; q < len; ++q) {
+                const int key = pp[q];
+                int w = q - 1;
+                while (w >= 0 && pp[w] > key) {
+                    pp[w + 1] = pp[w];
+                    --w;
+                }
+                pp[w + 1] = key;
+            }
+        }
+    }
 }
 
 // out[t] = +0 + upd[perm[s]] + upd[perm[s + 1]] + ... for every target row t,
@@ -649,8 +824,83 @@ int row_gather(const RowArgs &r, cudaStream_t st) {
 // Segment-sum scatter-add (see k_seg_walk); MTC_ERR_UNSUPPORTED when the sizes
 // exceed the int32 bookkeeping or the two-level scan (the caller then takes
 // the atomic kernel).
+// The bucketed prelude (k_bkt_*) and the walk, for 2^22 <= T <= 2^26 target rows.
+int bucketed_scatter_add(const RowArgs &r, cudaStream_t st) {
+    const long long T = r.extent, n = r.rows;
+    const int nb = static_cast<int>((T + kBucketRows - 1) / kBucketRows);
+    const long long chunks = (n + kChunk - 1) / kChunk;
+    const long long hlen = static_cast<long long>(nb) * chunks + 1;  // + the total after the scan
+    const long long hblk = (hlen + kScanBlock - 1) / kScanBlock;
+    const long long cap = n / 33 + 1;
+    // hist (scanned in place) | hist block sums | starts (T + 1) | perm (n) | long list | count | pairs (n int2)
+    size_t words = static_cast<size_t>(hlen + hblk + (T + 1) + n + cap + 1);
+    words = (words + 1) & ~size_t(1);  // 8-byte alignment of the pairs
+    void *scratch = nullptr;
+    MTC_TRY(scratch_alloc(words * sizeof(int) + static_cast<size_t>(n) * sizeof(int2), st, &scratch));
+    int *hist = static_cast<int *>(scratch);
+    int *hsums = hist + hlen;
+    int *starts = hsums + hblk;
+    int *perm = starts + (T + 1);
+    int *long_list = perm + n;
+    int *long_count = long_list + cap;
+    int2 *pairs = reinterpret_cast<int2 *>(static_cast<int *>(scratch) + words);
+    int rc = MTC_OK;
+    auto launched = [&](const char *what) {
+        if (rc == MTC_OK) rc = check_launch(what);
+    };
+    if (cudaMemsetAsync(hist + hlen - 1, 0, sizeof(int), st) != cudaSuccess ||
+        cudaMemsetAsync(long_count, 0, sizeof(int), st) != cudaSuccess ||
+        cudaFuncSetAttribute(k_bkt_part, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kPartSmem)) != cudaSuccess ||
+        cudaFuncSetAttribute(k_bkt_sort, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kBktSortSmem)) != cudaSuccess) {
+        rc = fail(MTC_ERR_RUNTIME, "bucketed scatter-add set-up failed: %s", cudaGetErrorString(cudaGetLastError()));
+    }
+    if (rc == MTC_OK) {
+        k_bkt_hist<<<static_cast<unsigned>(chunks), kPartThreads, 0, st>>>(r, hist, nb, chunks);
+        launched("bucketed scatter-add histogram");
+    }
+    if (rc == MTC_OK) {
+        k_scan_blocks<<<static_cast<unsigned>(hblk), 256, 0, st>>>(hist, hist, hlen, hsums);
+        launched("bucketed scatter-add scan");
+    }
+    if (rc == MTC_OK) {
+        k_scan_totals<<<1, 1024, 0, st>>>(hsums, static_cast<int>(hblk));
+        launched("bucketed scatter-add scan totals");
+    }
+    if (rc == MTC_OK) {
+        k_bkt_part<<<static_cast<unsigned>(chunks), kPartThreads, kPartSmem, st>>>(r, hist, hsums, pairs, nb, chunks);
+        launched("bucketed scatter-add partition");
+    }
+    if (rc == MTC_OK) {
+        k_bkt_sort<<<static_cast<unsigned>(nb), kPartThreads, kBktSortSmem, st>>>(
+            pairs, hist, hsums, chunks, nb, T, starts, perm, long_list, long_count, static_cast<int>(cap));
+        launched("bucketed scatter-add bucket sort");
+    }
+    if (rc == MTC_OK) {
+        k_seg_sort_long<<<sm_count(current_device()) * 2, 256, 0, st>>>(starts, nullptr, perm, long_list, long_count,
+                                                                          static_cast<int>(cap));
+        launched("bucketed scatter-add long sort");
+    }
+    if (rc == MTC_OK) {
+        k_seg_walk<<<grid_for(T * 16 / kWalkTargets), 256, 0, st>>>(r, starts, nullptr, perm);
+        launched("bucketed scatter-add sum");
+    }
+    scratch_free(scratch, st);
+    return rc;
+}
+
 int segment_scatter_add(const RowArgs &r, cudaStream_t st) {
     const long long T = r.extent, n = r.rows;
+    {
+        const char *bv = std::getenv("MTC_SEG_BUCKETS");  // measurement switch: "0" keeps the atomic count
+        const bool allow = bv == nullptr || bv[0] != '0';
+        if (allow && T >= (1ll << 22) && T <= static_cast<long long>(kMaxBuckets) * kBucketRows && n > 0 &&
+            n < (int64_t{1} << 31) - 1 && ((n + kChunk - 1) / kChunk) * ((T + kBucketRows - 1) / kBucketRows) <
+                                              (int64_t{1} << 30) &&
+            (n + kChunk - 1) / kChunk < 65536 * 32)
+            return bucketed_scatter_add(r, st);
+    }
     if (n >= (int64_t{1} << 31) - 1 || T + 1 > static_cast<long long>(kScanBlock) * 256 * 64)
         return fail(MTC_ERR_UNSUPPORTED, "scatter-add beyond the segment path's sizes");
     if (T == 0) {

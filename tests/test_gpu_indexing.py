@@ -107,6 +107,51 @@ def test_strided_offset_views_and_padding(cuda):
     assert (pad == -5.0).all(), "wrote outside the target view"
 
 
+@pytest.mark.parametrize("width", [8, 64])
+def test_bucketed_prelude_for_large_targets(cuda, width):
+    """From 2^22 target rows the segments are built by a two-level counting sort
+    with shared-memory counters (buckets of 2^14 rows, chunks of 2^14 updates):
+    a partial last bucket, duplicates, a 3000-update segment (the long sort),
+    non-integer values, and the same bits as the oracle."""
+    rng = np.random.default_rng(31)
+    targets = (1 << 22) + 12345
+    n = 3_000_000 if width == 8 else 600_000
+    idx = rng.integers(0, targets, n)
+    idx[rng.choice(n, 3000, replace=False)] = targets - 1  # long segment in the last bucket
+    upd = rng.standard_normal((n, width)).astype(F)
+    got, _ = _scatter_fast(upd, idx, targets, width)
+    want = np.zeros((targets, width), F)
+    np.add.at(want, idx, upd)
+    assert_bits(got, want, f"bucketed scatter-add width {width}")
+
+
+def test_bucketed_prelude_reports_out_of_range(cuda):
+    rng = np.random.default_rng(32)
+    targets = 1 << 22
+    idx = rng.integers(0, targets, 50_000)
+    idx[777] = targets
+    upd = rng.standard_normal((len(idx), 4)).astype(F)
+    with pytest.raises(IndexError):
+        _scatter_fast(upd, idx, targets, 4)
+    idx[777] = 5
+    got, _ = _scatter_fast(upd, idx, targets, 4)
+    want = np.zeros((targets, 4), F)
+    np.add.at(want, idx, upd)
+    assert_bits(got, want, "bucketed scatter-add after an index error")
+
+
+def _scatter_fast(upd, idx, targets, width):
+    """_scatter for large contiguous cases (no padding, no per-row host loop)."""
+    import torch
+
+    U = abi.View(torch.from_numpy(np.ascontiguousarray(upd)).cuda(), (len(idx), width), (width, 1), 0)
+    I = abi.View(torch.from_numpy(idx.astype(np.int64)).cuda(), (len(idx), width), (1, 0), 0)
+    O = abi.View(torch.full((targets * width,), -5.0, device="cuda"), (targets, width), (width, 1), 0)
+    abi.gather_scatter_add(U, I, 0, O)
+    abi.check_device_errors(0)
+    return O.storage.cpu().numpy().reshape(targets, width), None
+
+
 def test_out_of_range_index_is_reported(cuda):
     rng = np.random.default_rng(10)
     upd = rng.standard_normal((64, 8)).astype(F)
