@@ -2,6 +2,7 @@
 // basic-index scatter, Int64 gather and gather-scatter-add, fill.
 // Reference: src/tensor/backend/cpu/kernels/copy/loops.hpp:22-303 and
 // creation/loops.hpp:21-37.
+#include <climits>
 #include <cstdlib>
 #include <atomic>
 #include <cstring>
@@ -528,7 +529,10 @@ __device__ __forceinline__ void add4(float4 &acc, const uint4 w) {
 
 // ---- bucketed prelude (targets from 2^22 to 2^26 rows) -------------------
 // The same starts and sorted perm, built without global atomics: a counting
-// sort by target in two levels whose counters live in shared memory.
+// sort by target in two levels whose counters live in shared memory.  At 2^24
+// rows of 64 floats: hist 53 us, scan 16, part 116, sort 160, against count
+// 206, scan 48, fill 233, sort 113 for the atomic prelude (0.35 / 0.60 ms;
+// the whole scatter-add 1.92 / 2.17 ms).
 //   hist : per chunk of kChunk updates, how many fall in each bucket of
 //          kBucketRows target rows, written bucket-major
 //   scan : of that matrix (the scan kernels above) -> where each chunk's
@@ -538,14 +542,16 @@ __device__ __forceinline__ void add4(float4 &acc, const uint4 w) {
 //   sort : a CTA per bucket counts its target rows in shared memory, scans,
 //          writes starts, places the update rows into perm and sorts each
 //          segment (the long ones go to k_seg_sort_long as before)
-constexpr int kBucketShift = 14;
+constexpr int kBucketShift = 13;
 constexpr int kBucketRows = 1 << kBucketShift;     // target rows a bucket
-constexpr int kChunk = 16384;                      // updates a partition CTA
-constexpr int kMaxBuckets = 4096;                  // so targets <= 2^26
+constexpr int kChunk = 8192;                       // updates a partition CTA
+constexpr int kMaxBuckets = 8192;                  // so targets <= 2^26
 constexpr int kPartThreads = 1024;
-constexpr int kPerThread = kChunk / kPartThreads;  // 16
-constexpr size_t kPartSmem = kChunk * sizeof(int2) + 2 * kMaxBuckets * sizeof(int) + 32 * sizeof(int);
-constexpr size_t kBktSortSmem = kBucketRows * sizeof(int) + 32 * sizeof(int);
+constexpr int kPerThread = kChunk / kPartThreads;  // 8
+constexpr int kStageCap = 16384;                   // a bucket's updates placed and sorted in shared memory
+// partition smem: the stage, then 2 * nb counters and offsets, then 32 ints
+constexpr size_t part_smem(int nb) { return kChunk * sizeof(int2) + (2 * static_cast<size_t>(nb) + 32) * sizeof(int); }
+constexpr size_t kBktSortSmem = (kBucketRows + kStageCap + 32) * sizeof(int);
 
 // Exclusive scan of v[0, len) in shared memory by a CTA of kPartThreads threads
 // (len <= 16 * kPartThreads); returns the total.  wtot: 32 ints of shared scratch.
@@ -592,15 +598,17 @@ __global__ void __launch_bounds__(kPartThreads) k_bkt_hist(const RowArgs a, int 
     for (int b = threadIdx.x; b < nb; b += kPartThreads) h[b] = 0;
     __syncthreads();
     const long long base = static_cast<long long>(blockIdx.x) * kChunk;
-    for (int k = threadIdx.x; k < kChunk; k += kPartThreads) {
-        const long long i = base + k;
-        if (i >= a.rows) break;
-        const long long j = __ldg(a.idx + a.idx_off + i * a.idx_rs);
-        if (j < 0 || j >= a.extent) {
-            record_device_error(MTC_ERR_OUT_OF_RANGE, j);
-            continue;
-        }
-        atomicAdd(&h[j >> kBucketShift], 1);
+    long long jv[kPerThread];  // all of a thread's index loads in flight before its first count
+#pragma unroll
+    for (int q = 0; q < kPerThread; ++q) {
+        const long long i = base + threadIdx.x + q * kPartThreads;
+        jv[q] = i < a.rows ? __ldg(a.idx + a.idx_off + i * a.idx_rs) : LLONG_MIN;
+    }
+#pragma unroll
+    for (int q = 0; q < kPerThread; ++q) {
+        if (jv[q] == LLONG_MIN) continue;
+        if (jv[q] < 0 || jv[q] >= a.extent) record_device_error(MTC_ERR_OUT_OF_RANGE, jv[q]);
+        else atomicAdd(&h[jv[q] >> kBucketShift], 1);
     }
     __syncthreads();
     for (int b = threadIdx.x; b < nb; b += kPartThreads) hist[static_cast<long long>(b) * chunks + blockIdx.x] = h[b];
@@ -612,9 +620,9 @@ __global__ void __launch_bounds__(kPartThreads) k_bkt_part(const RowArgs a, cons
                                                            int2 *pairs, int nb, long long chunks) {
     extern __shared__ __align__(16) unsigned char bkt_smem[];
     int2 *stage = reinterpret_cast<int2 *>(bkt_smem);     // kChunk: the chunk's updates by bucket
-    int *h = reinterpret_cast<int *>(stage + kChunk);      // counts, then chunk-local offsets
-    int *goff = h + kMaxBuckets;                           // the chunk's place in each bucket
-    int *wtot = goff + kMaxBuckets;
+    int *h = reinterpret_cast<int *>(stage + kChunk);      // nb counts, then chunk-local offsets
+    int *goff = h + nb;                                    // nb: the chunk's place in each bucket
+    int *wtot = goff + nb;
     const long long c = blockIdx.x;
     for (int b = threadIdx.x; b < nb; b += kPartThreads) {
         h[b] = 0;
@@ -623,27 +631,22 @@ __global__ void __launch_bounds__(kPartThreads) k_bkt_part(const RowArgs a, cons
     }
     __syncthreads();
     const long long base = c * kChunk;
-    int ii[kPerThread], jj[kPerThread], rr[kPerThread];
+    int jj[kPerThread], rr[kPerThread];
 #pragma unroll
-    for (int q = 0; q < kPerThread; ++q) {
+    for (int q = 0; q < kPerThread; ++q) {  // the loads first, all in flight
         const long long i = base + threadIdx.x + q * kPartThreads;
-        jj[q] = -1;
-        ii[q] = 0;
-        rr[q] = 0;
-        if (i < a.rows) {
-            const long long j = __ldg(a.idx + a.idx_off + i * a.idx_rs);
-            if (j >= 0 && j < a.extent) {  // the histogram pass recorded the others
-                jj[q] = static_cast<int>(j);
-                ii[q] = static_cast<int>(i);
-                rr[q] = atomicAdd(&h[j >> kBucketShift], 1);
-            }
-        }
+        const long long j = i < a.rows ? __ldg(a.idx + a.idx_off + i * a.idx_rs) : -1;
+        jj[q] = j >= 0 && j < a.extent ? static_cast<int>(j) : -1;  // the histogram pass recorded the others
     }
+#pragma unroll
+    for (int q = 0; q < kPerThread; ++q) rr[q] = jj[q] >= 0 ? atomicAdd(&h[jj[q] >> kBucketShift], 1) : 0;
     __syncthreads();
     const int valid = block_exclusive_scan(h, nb, wtot);
 #pragma unroll
     for (int q = 0; q < kPerThread; ++q)
-        if (jj[q] >= 0) stage[h[jj[q] >> kBucketShift] + rr[q]] = make_int2(ii[q], jj[q]);
+        if (jj[q] >= 0)
+            stage[h[jj[q] >> kBucketShift] + rr[q]] =
+                make_int2(static_cast<int>(base + threadIdx.x + q * kPartThreads), jj[q]);
     __syncthreads();
     for (int p = threadIdx.x; p < valid; p += kPartThreads) {
         const int2 e = stage[p];
@@ -652,30 +655,72 @@ __global__ void __launch_bounds__(kPartThreads) k_bkt_part(const RowArgs a, cons
     }
 }
 
+// Insertion sort of a short segment (at most 32 entries) in place.
+template <class P>
+__device__ __forceinline__ void sort_short(P pp, int len) {
+    for (int q = 1; q < len; ++q) {
+        const int key = pp[q];
+        int w = q - 1;
+        while (w >= 0 && pp[w] > key) {
+            pp[w + 1] = pp[w];
+            --w;
+        }
+        pp[w + 1] = key;
+    }
+}
+
+// A CTA per bucket: counts its target rows in shared memory, scans them into
+// starts, places the update rows (in shared memory when the bucket holds at
+// most kStageCap updates, else straight into perm) and sorts each segment.
+// Segments above 32 updates go to the long list, sorted in perm afterwards.
 __global__ void __launch_bounds__(kPartThreads) k_bkt_sort(const int2 *pairs, const int *off, const int *off_sums,
                                                            long long chunks, int nb, long long targets, int *starts,
                                                            int *perm, int *long_list, int *long_count,
                                                            int long_capacity) {
     extern __shared__ __align__(16) unsigned char bkt_smem[];
     int *cnt = reinterpret_cast<int *>(bkt_smem);  // kBucketRows
-    int *wtot = cnt + kBucketRows;
+    int *stage = cnt + kBucketRows;                // kStageCap
+    int *wtot = stage + kStageCap;
     const int b = blockIdx.x;
     const long long t0 = static_cast<long long>(b) << kBucketShift;
     const int wt = static_cast<int>(targets - t0 < kBucketRows ? targets - t0 : kBucketRows);
     const long long x0 = static_cast<long long>(b) * chunks, x1 = x0 + chunks;
     const int beg = off[x0] + off_sums[x0 / kScanBlock];
     const int end = off[x1] + off_sums[x1 / kScanBlock];
+    const bool staged = end - beg <= kStageCap;  // uniform in the CTA
     for (int t = threadIdx.x; t < wt; t += kPartThreads) cnt[t] = 0;
     __syncthreads();
-    for (int e = beg + static_cast<int>(threadIdx.x); e < end; e += kPartThreads) atomicAdd(&cnt[pairs[e].y], 1);
+    constexpr int kIn = 8;  // pair loads in flight per thread
+    for (int e0 = beg; e0 < end; e0 += kIn * kPartThreads) {
+        int y[kIn];
+#pragma unroll
+        for (int u = 0; u < kIn; ++u) {
+            const int e = e0 + static_cast<int>(threadIdx.x) + u * kPartThreads;
+            y[u] = e < end ? pairs[e].y : -1;
+        }
+#pragma unroll
+        for (int u = 0; u < kIn; ++u)
+            if (y[u] >= 0) atomicAdd(&cnt[y[u]], 1);
+    }
     __syncthreads();
     block_exclusive_scan(cnt, wt, wtot);
     for (int t = threadIdx.x; t < wt; t += kPartThreads) starts[t0 + t] = beg + cnt[t];
     if (b == nb - 1 && threadIdx.x == 0) starts[targets] = end;
     __syncthreads();  // every start is read before the placement moves cnt on
-    for (int e = beg + static_cast<int>(threadIdx.x); e < end; e += kPartThreads) {
-        const int2 pe = pairs[e];
-        perm[beg + atomicAdd(&cnt[pe.y], 1)] = pe.x;
+    for (int e0 = beg; e0 < end; e0 += kIn * kPartThreads) {
+        int2 pe[kIn];
+#pragma unroll
+        for (int u = 0; u < kIn; ++u) {
+            const int e = e0 + static_cast<int>(threadIdx.x) + u * kPartThreads;
+            pe[u] = e < end ? pairs[e] : make_int2(0, -1);
+        }
+#pragma unroll
+        for (int u = 0; u < kIn; ++u) {
+            if (pe[u].y < 0) continue;
+            const int p = atomicAdd(&cnt[pe[u].y], 1);
+            if (staged) stage[p] = pe[u].x;
+            else perm[beg + p] = pe[u].x;
+        }
     }
     __syncthreads();
     // cnt[t] is now the end of segment t within the bucket; sort each segment
@@ -686,17 +731,13 @@ __global__ void __launch_bounds__(kPartThreads) k_bkt_sort(const int2 *pairs, co
             const int k = atomicAdd(long_count, 1);
             if (k < long_capacity) long_list[k] = static_cast<int>(t0 + t);
         } else if (len > 1) {
-            int *pp = perm + beg + s0;
-            for (int q = 1; q < len; ++q) {
-                const int key = pp[q];
-                int w = q - 1;
-                while (w >= 0 && pp[w] > key) {
-                    pp[w + 1] = pp[w];
-                    --w;
-                }
-                pp[w + 1] = key;
-            }
+            if (staged) sort_short(stage + s0, len);
+            else sort_short(perm + beg + s0, len);
         }
+    }
+    if (staged) {
+        __syncthreads();
+        for (int e = threadIdx.x; e < end - beg; e += kPartThreads) perm[beg + e] = stage[e];
     }
 }
 
@@ -851,7 +892,7 @@ int bucketed_scatter_add(const RowArgs &r, cudaStream_t st) {
     if (cudaMemsetAsync(hist + hlen - 1, 0, sizeof(int), st) != cudaSuccess ||
         cudaMemsetAsync(long_count, 0, sizeof(int), st) != cudaSuccess ||
         cudaFuncSetAttribute(k_bkt_part, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kPartSmem)) != cudaSuccess ||
+                             static_cast<int>(part_smem(kMaxBuckets))) != cudaSuccess ||
         cudaFuncSetAttribute(k_bkt_sort, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kBktSortSmem)) != cudaSuccess) {
         rc = fail(MTC_ERR_RUNTIME, "bucketed scatter-add set-up failed: %s", cudaGetErrorString(cudaGetLastError()));
@@ -869,7 +910,8 @@ int bucketed_scatter_add(const RowArgs &r, cudaStream_t st) {
         launched("bucketed scatter-add scan totals");
     }
     if (rc == MTC_OK) {
-        k_bkt_part<<<static_cast<unsigned>(chunks), kPartThreads, kPartSmem, st>>>(r, hist, hsums, pairs, nb, chunks);
+        k_bkt_part<<<static_cast<unsigned>(chunks), kPartThreads, part_smem(nb), st>>>(r, hist, hsums, pairs, nb,
+                                                                                        chunks);
         launched("bucketed scatter-add partition");
     }
     if (rc == MTC_OK) {

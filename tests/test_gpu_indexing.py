@@ -110,14 +110,17 @@ def test_strided_offset_views_and_padding(cuda):
 @pytest.mark.parametrize("width", [8, 64])
 def test_bucketed_prelude_for_large_targets(cuda, width):
     """From 2^22 target rows the segments are built by a two-level counting sort
-    with shared-memory counters (buckets of 2^14 rows, chunks of 2^14 updates):
-    a partial last bucket, duplicates, a 3000-update segment (the long sort),
-    non-integer values, and the same bits as the oracle."""
+    with shared-memory counters (buckets of 2^13 rows, chunks of 2^14 updates):
+    a partial last bucket, duplicates, a 3000-update segment (the long sort), a
+    bucket holding more updates than its shared-memory stage (placed and sorted
+    in global memory), non-integer values, and the same bits as the oracle."""
     rng = np.random.default_rng(31)
     targets = (1 << 22) + 12345
     n = 3_000_000 if width == 8 else 600_000
     idx = rng.integers(0, targets, n)
-    idx[rng.choice(n, 3000, replace=False)] = targets - 1  # long segment in the last bucket
+    picked = rng.choice(n, 23000, replace=False)
+    idx[picked[:3000]] = targets - 1  # long segment in the last bucket
+    idx[picked[3000:]] = 7 * 8192 + rng.integers(0, 100, 20000)  # 20000 updates in bucket 7
     upd = rng.standard_normal((n, width)).astype(F)
     got, _ = _scatter_fast(upd, idx, targets, width)
     want = np.zeros((targets, width), F)
