@@ -554,13 +554,23 @@ constexpr size_t part_smem(int nb) { return kChunk * sizeof(int2) + (2 * static_
 constexpr size_t kBktSortSmem = (kBucketRows + kStageCap + 32) * sizeof(int);
 
 // Exclusive scan of v[0, len) in shared memory by a CTA of kPartThreads threads
-// (len <= 16 * kPartThreads); returns the total.  wtot: 32 ints of shared scratch.
+// (len <= 16 * kPartThreads, v 16-byte aligned); returns the total.  Each
+// thread owns a run of a multiple of 4 entries, read and written as int4 (a
+// scalar run of 8 per thread made the bucket sort shared-memory-bound through
+// 8-way bank conflicts).  wtot: 32 ints of shared scratch.
 __device__ int block_exclusive_scan(int *v, int len, int *wtot) {
-    const int per = (len + kPartThreads - 1) / kPartThreads;
+    const int per = ((len + kPartThreads - 1) / kPartThreads + 3) & ~3;
     const int b0 = static_cast<int>(threadIdx.x) * per;
     int run = 0;
-    for (int q = 0; q < per; ++q)
-        if (b0 + q < len) run += v[b0 + q];
+    for (int q = 0; q < per; q += 4) {
+        if (b0 + q + 3 < len) {
+            const int4 x = *reinterpret_cast<const int4 *>(v + b0 + q);
+            run += x.x + x.y + x.z + x.w;
+        } else {
+            for (int k = q; k < q + 4; ++k)
+                if (b0 + k < len) run += v[b0 + k];
+        }
+    }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int inc = run;
 #pragma unroll
@@ -581,11 +591,21 @@ __device__ int block_exclusive_scan(int *v, int len, int *wtot) {
     }
     __syncthreads();
     int off = (warp > 0 ? wtot[warp - 1] : 0) + inc - run;
-    for (int q = 0; q < per; ++q) {
-        if (b0 + q < len) {
-            const int t = v[b0 + q];
-            v[b0 + q] = off;
-            off += t;
+    for (int q = 0; q < per; q += 4) {
+        if (b0 + q + 3 < len) {
+            int4 x = *reinterpret_cast<const int4 *>(v + b0 + q);
+            const int a0 = off, a1 = a0 + x.x, a2 = a1 + x.y, a3 = a2 + x.z;
+            off = a3 + x.w;
+            x = make_int4(a0, a1, a2, a3);
+            *reinterpret_cast<int4 *>(v + b0 + q) = x;
+        } else {
+            for (int k = q; k < q + 4; ++k) {
+                if (b0 + k < len) {
+                    const int t = v[b0 + k];
+                    v[b0 + k] = off;
+                    off += t;
+                }
+            }
         }
     }
     const int total = wtot[31];
@@ -593,7 +613,7 @@ __device__ int block_exclusive_scan(int *v, int len, int *wtot) {
     return total;
 }
 
-__global__ void __launch_bounds__(kPartThreads) k_bkt_hist(const RowArgs a, int *hist, int nb, long long chunks) {
+__global__ void __launch_bounds__(kPartThreads, 2) k_bkt_hist(const RowArgs a, int *hist, int nb, long long chunks) {
     __shared__ int h[kMaxBuckets];
     for (int b = threadIdx.x; b < nb; b += kPartThreads) h[b] = 0;
     __syncthreads();
@@ -616,7 +636,7 @@ __global__ void __launch_bounds__(kPartThreads) k_bkt_hist(const RowArgs a, int 
 
 // off / off_sums: the scanned histogram (offset of chunk c's bucket-b updates
 // at b * chunks + c, plus its scan block's sum).
-__global__ void __launch_bounds__(kPartThreads) k_bkt_part(const RowArgs a, const int *off, const int *off_sums,
+__global__ void __launch_bounds__(kPartThreads, 2) k_bkt_part(const RowArgs a, const int *off, const int *off_sums,
                                                            int2 *pairs, int nb, long long chunks) {
     extern __shared__ __align__(16) unsigned char bkt_smem[];
     int2 *stage = reinterpret_cast<int2 *>(bkt_smem);     // kChunk: the chunk's updates by bucket
@@ -673,7 +693,7 @@ __device__ __forceinline__ void sort_short(P pp, int len) {
 // starts, places the update rows (in shared memory when the bucket holds at
 // most kStageCap updates, else straight into perm) and sorts each segment.
 // Segments above 32 updates go to the long list, sorted in perm afterwards.
-__global__ void __launch_bounds__(kPartThreads) k_bkt_sort(const int2 *pairs, const int *off, const int *off_sums,
+__global__ void __launch_bounds__(kPartThreads, 2) k_bkt_sort(const int2 *pairs, const int *off, const int *off_sums,
                                                            long long chunks, int nb, long long targets, int *starts,
                                                            int *perm, int *long_list, int *long_count,
                                                            int long_capacity) {
@@ -766,6 +786,7 @@ __global__ void __launch_bounds__(256, 4) k_seg_walk(const RowArgs a, const int 
     for (long long t0 = half * kWalkTargets; t0 < targets; t0 += halves * kWalkTargets) {
         const int g = static_cast<int>(targets - t0 < kWalkTargets ? targets - t0 : kWalkTargets);
         // lane l: the start of target t0 + l; lane g: the end of target t0 + g - 1
+        // (loading the next group's bounds a group ahead measured no faster)
         const int sb = hl <= g ? seg_start(starts, sums, t0 + hl) : 0;
         const int e_beg = __shfl_sync(hmask, sb, 0, 16);
         const int e_end = __shfl_sync(hmask, sb, g, 16);
