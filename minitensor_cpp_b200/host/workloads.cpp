@@ -419,15 +419,10 @@ struct MlpTrainer {
             auto [next_params, next_state] = optimizer.step(std::move(params), std::move(state), grads);
             grads.clear();
             trace.mark("optimizer graph");
-#ifndef MTB_CPU_ONLY
-            leafify_step(std::move(next_params), std::move(next_state));
-            trace.mark("evaluate parameters and state");
-#else
             params = mt::nn::leafify_parameter_values(std::move(next_params));
             trace.mark("evaluate parameters");
             state = mt::nn::leafify_optimizer_state(std::move(next_state));
             trace.mark("evaluate state");
-#endif
         }
 #ifndef MTB_CPU_ONLY
         phase_mark(3);
@@ -441,37 +436,6 @@ struct MlpTrainer {
         trace.mark("loss");
         return value;
     }
-
-#ifndef MTB_CPU_ONLY
-    // The updated parameters and Adam's moments materialised in ONE evaluation,
-    // where the reference's leafify_parameter_values and leafify_optimizer_state
-    // take two: in two, the first writes p' and the second recomputes m' and v'
-    // from g, m and v (40 bytes a parameter); in one, each parameter's update is
-    // one fused cluster with the three outputs (28 bytes).  Same values: the
-    // same operations in the same order, only materialised together.
-    void leafify_step(Snapshot next_params, mt::nn::AdamW::State next_state) {
-        std::vector<mt::Tensor> roots;
-        std::vector<mt::nn::ParameterId> ids;
-        for (const auto &entry : next_params.parameters()) {
-            ids.push_back(entry.first);
-            roots.push_back(entry.second.value);
-        }
-        const std::size_t np = roots.size();
-        for (const auto &id : ids) {
-            roots.push_back(mt::nn::AdamWStateAccess::first(next_state, id));
-            roots.push_back(mt::nn::AdamWStateAccess::second(next_state, id));
-        }
-        std::vector<mt::Tensor> leaves = mt::leafify(roots);
-        std::size_t k = 0;
-        params = std::move(next_params).transform([&](mt::nn::ParameterId, const mt::nn::ParameterState &ps) {
-            return mt::nn::ParameterState{std::move(leaves[k++]), ps.metadata};
-        });
-        for (std::size_t q = 0; q < ids.size(); ++q)
-            mt::nn::AdamWStateAccess::set_moments(next_state, ids[q], std::move(leaves[np + 2 * q]),
-                                                  std::move(leaves[np + 2 * q + 1]));
-        state = std::move(next_state);
-    }
-#endif
 
     // Replaces every parameter's value with host values in the order of
     // mtb_mlp_parameters (weight [out, in] then bias [out], layer by layer).
