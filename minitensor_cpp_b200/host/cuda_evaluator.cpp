@@ -617,18 +617,22 @@ class FusedEvaluator {
         for (int m : c.members)
             if (plan_[m].materialize) ++outputs;
         if (outputs > MTC_MAX_FUSED_OUTPUTS) return false;
-        std::vector<const Value *> external;
+        std::vector<const Value *> external, constants;
         auto note_inputs = [&](int m) {
             for (const ValueRef &in : plan_[m].node->inputs()) {
                 const Value *v = in.get();
                 const int pi = plan_index(v);
-                if (pi >= 0 && (pi == candidate || plan_[pi].cluster == cluster || plan_[pi].constant)) continue;
-                if (std::find(external.begin(), external.end(), v) == external.end()) external.push_back(v);
+                if (pi >= 0 && (pi == candidate || plan_[pi].cluster == cluster)) continue;
+                auto &set = pi >= 0 && plan_[pi].constant ? constants : external;
+                if (std::find(set.begin(), set.end(), v) == set.end()) set.push_back(v);
             }
         };
         for (int m : c.members) note_inputs(m);
         note_inputs(candidate);
-        return static_cast<int>(external.size()) <= MTC_MAX_FUSED_OPERANDS;
+        // the program: one instruction per member and per folded constant
+        const std::size_t instructions = c.members.size() + 1 + constants.size();
+        return static_cast<int>(external.size()) <= MTC_MAX_FUSED_OPERANDS &&
+               instructions <= static_cast<std::size_t>(MTC_MAX_FUSED_INSTRUCTIONS);
     }
 
     // --------------------------------------------------------- eager steps --
