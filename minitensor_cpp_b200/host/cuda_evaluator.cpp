@@ -164,6 +164,9 @@ struct Cluster {
     std::vector<int> members;  // step indices, added in reverse plan order
     int root = -1;             // last member in plan order: the launch point
     Shape shape;
+    int outputs = 0;                     // members written
+    std::vector<const Value *> external;  // distinct values read from outside the members
+    std::vector<const Value *> constants; // distinct Full inputs (folded into the program)
 };
 
 class Planner {
@@ -585,17 +588,26 @@ class FusedEvaluator {
             }
             int target = -1;
             const Shape &shape = s.output->spec().shape;
-            if (consumers_in_one_cluster(i, target) && clusters_[target].shape == shape && can_grow(target, i)) {
-                clusters_[target].members.push_back(i);
+            Budget b;
+            if (consumers_in_one_cluster(i, target) && clusters_[target].shape == shape && can_grow(target, i, b)) {
+                Cluster &c = clusters_[target];
+                c.members.push_back(i);
+                c.external = std::move(b.external);
+                c.constants = std::move(b.constants);
+                if (s.materialize) ++c.outputs;
                 s.cluster = target;
             } else {
+                s.materialize = true;  // the cluster's result is always written
+                b = with_member(-1, i);
                 Cluster c;
                 c.root = i;
                 c.shape = shape;
                 c.members.push_back(i);
+                c.outputs = 1;
+                c.external = std::move(b.external);
+                c.constants = std::move(b.constants);
                 clusters_.push_back(std::move(c));
                 s.cluster = static_cast<int>(clusters_.size()) - 1;
-                s.materialize = true;  // the cluster's result is always written
             }
             // a member consumed outside its cluster must be written
             for (int c : consumers(i))
@@ -604,34 +616,45 @@ class FusedEvaluator {
     }
 
     // Operand budget: the distinct values the cluster would read from outside
-    // itself once the candidate joins (constants fold into the program).  The
-    // earlier count, every input of every member less one per member, split
-    // AdamW's update (four external tensors, about sixteen operations) into
-    // four kernels moving about 51 bytes a parameter instead of one moving 28.
-    // A cluster that still ends up over budget at launch (a constant that was
-    // not folded) runs unfused.
-    bool can_grow(int cluster, int candidate) const {
+    // itself once the candidate joins (constants fold into the program), its
+    // outputs and its program length.  The earlier count, every input of every
+    // member less one per member, split AdamW's update (four external tensors,
+    // about sixteen operations) into four kernels moving about 51 bytes a
+    // parameter instead of one moving 28.  A cluster that still ends up over
+    // budget at launch (a constant that was not folded) runs unfused.  The
+    // lists are kept per cluster and updated as members join, since planning
+    // runs for every evaluation, replayed ones included.
+    struct Budget {
+        std::vector<const Value *> external, constants;
+    };
+
+    // The budget of `c` (cluster index, or -1 for a new cluster) with step i added.
+    Budget with_member(int c, int i) const {
+        Budget b;
+        if (c >= 0) {
+            b.external = clusters_[c].external;
+            b.constants = clusters_[c].constants;
+            const Value *own = plan_[i].output.get();  // now produced inside
+            b.external.erase(std::remove(b.external.begin(), b.external.end(), own), b.external.end());
+        }
+        for (const ValueRef &in : plan_[i].node->inputs()) {
+            const Value *v = in.get();
+            const int pi = plan_index(v);
+            if (pi >= 0 && c >= 0 && plan_[pi].cluster == c) continue;
+            auto &set = pi >= 0 && plan_[pi].constant ? b.constants : b.external;
+            if (std::find(set.begin(), set.end(), v) == set.end()) set.push_back(v);
+        }
+        return b;
+    }
+
+    bool can_grow(int cluster, int candidate, Budget &b) const {
         const Cluster &c = clusters_[cluster];
         if (c.members.size() + 1 > 48) return false;
-        int outputs = plan_[candidate].materialize ? 1 : 0;
-        for (int m : c.members)
-            if (plan_[m].materialize) ++outputs;
-        if (outputs > MTC_MAX_FUSED_OUTPUTS) return false;
-        std::vector<const Value *> external, constants;
-        auto note_inputs = [&](int m) {
-            for (const ValueRef &in : plan_[m].node->inputs()) {
-                const Value *v = in.get();
-                const int pi = plan_index(v);
-                if (pi >= 0 && (pi == candidate || plan_[pi].cluster == cluster)) continue;
-                auto &set = pi >= 0 && plan_[pi].constant ? constants : external;
-                if (std::find(set.begin(), set.end(), v) == set.end()) set.push_back(v);
-            }
-        };
-        for (int m : c.members) note_inputs(m);
-        note_inputs(candidate);
+        if (c.outputs + (plan_[candidate].materialize ? 1 : 0) > MTC_MAX_FUSED_OUTPUTS) return false;
+        b = with_member(cluster, candidate);
         // the program: one instruction per member and per folded constant
-        const std::size_t instructions = c.members.size() + 1 + constants.size();
-        return static_cast<int>(external.size()) <= MTC_MAX_FUSED_OPERANDS &&
+        const std::size_t instructions = c.members.size() + 1 + b.constants.size();
+        return static_cast<int>(b.external.size()) <= MTC_MAX_FUSED_OPERANDS &&
                instructions <= static_cast<std::size_t>(MTC_MAX_FUSED_INSTRUCTIONS);
     }
 
