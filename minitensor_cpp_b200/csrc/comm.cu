@@ -5,6 +5,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -168,7 +169,16 @@ int mtc_comm_allreduce_f32_async(void *comm, void *const *buffers, const size_t 
     MTC_TRY(need_nccl());
     if (c->side == nullptr) {
         MTC_CUDA_TRY(cudaSetDevice(c->device));
-        MTC_CUDA_TRY(cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking));
+        // The reductions run at the device's highest stream priority: when a
+        // layer's gradients are done, its all-reduce and the next GEMM become
+        // ready together, and the block scheduler then seats the reduction's
+        // CTAs first instead of leaving them behind a GEMM that fills every SM.
+        // MTC_COMM_PRIORITY=normal keeps the default priority (measurements).
+        int least = 0, greatest = 0;
+        MTC_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+        const char *pr = std::getenv("MTC_COMM_PRIORITY");
+        const bool high = pr == nullptr || std::strcmp(pr, "normal") != 0;
+        MTC_CUDA_TRY(cudaStreamCreateWithPriority(&c->side, cudaStreamNonBlocking, high ? greatest : least));
         MTC_CUDA_TRY(cudaEventCreateWithFlags(&c->ready, cudaEventDisableTiming));
         MTC_CUDA_TRY(cudaEventCreateWithFlags(&c->done, cudaEventDisableTiming));
     }
